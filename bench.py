@@ -1,0 +1,460 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE layer of Qwen3.6-35B-A3B (lightreason edge35b).
+
+Metric: MoE-layer us/step at decode, tokens/s at prefill, and
+the fraction of the HBM / tensor-core roofline.  The JSON line's `value` is
+whole-job throughput in tokens/s; `ms_per_step` gives the step time.
+
+Default workload (no flags): BASELINE configs[1], one MoE layer at the
+speculative-verify width T=16 with seeded synthetic weights and N(0,1)
+activations.
+  * value: device-timed steps with every input already resident in HBM;
+  * e2e:   the same step through the C ABI (moe_layer_forward) with HOST
+           buffers -- activations copied in from pinned memory and the result
+           read back each step, and all 256 experts resident in pinned host
+           RAM, of which only the union of selected experts is gathered into
+           HBM slots every step (configs[1]'s gather + compute);
+  * roofline: the dominant kernel of `value`, from CUDA events recorded at the
+           stage boundaries inside moe_layer_forward during the timed steps;
+  * cpu_baseline: the reference's own CPU path (edge35b/cpu_experts.c built from
+           the reference sources into oracle/_ref, torch-CPU router / shared
+           expert / ordered combine) on a bounded sample of the same workload.
+L2 is flushed (256 MiB memset) between timed steps, outside each step's
+CUDA-event window.
+
+--impl reference times that CPU path alone as the reference arm.
+--gpus N (under torchrun) runs one replica of the layer per rank.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from lightreason_b200 import synthetic as S  # noqa: E402
+
+HIDDEN, INNER, EXPERTS, TOP_K = S.HIDDEN, S.INNER, S.EXPERTS, S.TOP_K
+GATE_UP_BYTES = 2 * INNER * HIDDEN * 2       # 4,194,304 B per expert
+DOWN_BYTES = HIDDEN * INNER * 2              # 2,097,152 B per expert
+EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES    # 6,291,456 B
+STAGES = ("router", "permute", "gather", "groups", "gate_up", "down", "combine")
+KERNEL_NAMES = {"router": "router_logits_kernel+router_select_kernel", "permute": "permute_kernel",
+                "gather": "stage_experts_kernel", "groups": "build_groups_kernel", "gate_up": "gate_up_kernel",
+                "down": "down_kernel", "combine": "combine_kernel"}
+
+CONFIGS = {
+    0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
+    1: dict(tokens=16, bias="normal",
+            workload="config1: one MoE layer, speculative-verify width T=16; experts in pinned host RAM (e2e)"),
+    3: dict(tokens=4096, bias="zipf", workload="config3: one MoE layer, prefill T=4096, Zipf(1.1) routing"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, ValueError):
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def dist_max(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def to_dev(bits: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+# ------------------------------------------------------------ our arm ---
+
+def build_layer(cfg, dev, seed):
+    from lightreason_b200 import native
+
+    w = S.layer_weights(seed, bias=cfg["bias"])
+    gu, dn = w.stacked()
+    d = lambda a: to_dev(a, dev)  # noqa: E731
+    sh = [d(w.sh_gate), d(w.sh_up), d(w.sh_down), d(w.sh_gate_w)]
+    bias = torch.from_numpy(w.bias).to(dev)
+    router = d(w.router)
+    hbm = native.Layer(router=router, gate_up=d(gu), down=d(dn), bias=bias, shared_gate=sh[0], shared_up=sh[1],
+                       shared_down=sh[2], shared_gate_w=sh[3])
+    host = None
+    if cfg.get("e2e_host_experts", True):
+        hg = torch.from_numpy(gu.view(np.int16)).view(torch.bfloat16).pin_memory()
+        hd = torch.from_numpy(dn.view(np.int16)).view(torch.bfloat16).pin_memory()
+        host = native.Layer(router=router, bias=bias, shared_gate=sh[0], shared_up=sh[1], shared_down=sh[2],
+                            shared_gate_w=sh[3], host_gate_up=hg, host_down=hd)
+    return w, gu, dn, hbm, host
+
+
+def timed_steps(run_step, steps, warmup, flush, world, stage_events=False):
+    """Per-step CUDA-event timing with an L2 flush outside each step window."""
+    for i in range(warmup):
+        flush.zero_()
+        run_step(i, None)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    stg = [[torch.cuda.Event(enable_timing=True) for _ in range(8)] for _ in range(steps)] if stage_events else None
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        flush.zero_()
+        ev[i][0].record()
+        run_step(warmup + i, stg[i] if stg else None)
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    wall = time.perf_counter() - t0
+    ms = [s.elapsed_time(e) for s, e in ev]
+    stage_ms = None
+    if stg:
+        stage_ms = {name: [row[j].elapsed_time(row[j + 1]) for row in stg] for j, name in enumerate(STAGES)}
+    return ms, stage_ms, wall
+
+
+def cpu_reference_layer(w, gu, dn, x_bits, threads):
+    """The reference's CPU implementation of one layer step on host cores:
+    torch-CPU router (modeling_qwen3_5_moe.py:762-770 + bias) and shared expert
+    (:698-711, :788), edge35b/cpu_experts.c expert_block_rows for T <= 16
+    (cpu_experts.c:74-105, as edge35b/block_experts.py:52-86 binds it) or the
+    eager expert loop (:727-751) beyond, and the ordered BF16 combine
+    (edge35b/cpu_route.py:66-68)."""
+    from oracle import oracle as O
+
+    F = torch.nn.functional
+    torch.set_num_threads(threads)
+    t_bf = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int16)).view(torch.bfloat16)  # noqa: E731
+    x = t_bf(x_bits)
+    router, sg, su, sd, sgw = (t_bf(a) for a in (w.router, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w))
+    bias = torch.from_numpy(w.bias)
+    with torch.no_grad():
+        logits = F.linear(x, router)
+        probs = F.softmax(logits.float() + bias, dim=-1)
+        top_v, top_i = torch.topk(probs, TOP_K, dim=-1)
+        scores = (top_v / top_v.sum(-1, keepdim=True)).to(torch.bfloat16)
+        shared = F.linear(F.silu(F.linear(x, sg)) * F.linear(x, su), sd)
+        gate = torch.sigmoid(F.linear(x, sgw.reshape(1, -1)))
+        result = torch.zeros_like(x)
+        tokens = x.shape[0]
+        ids = top_i.numpy()
+        pairs = [(int(ids[t, s]), s, t) for s in range(TOP_K) for t in range(tokens)]
+        pairs.sort(key=lambda p: p[0])
+        if tokens <= 16 and O.ref_experts_lib() is not None:
+            y = O.ref_expert_block_rows(x_bits, [gu[e] for e, _, _ in pairs], [dn[e] for e, _, _ in pairs],
+                                        np.array([t for _, _, t in pairs], dtype=np.int32), threads=threads)
+            yt = t_bf(y)
+            for i, (e, s, t) in enumerate(pairs):
+                result[t].add_(yt[i] * scores[t, s])
+        else:
+            for e in sorted(set(e for e, _, _ in pairs)):
+                sel = [(s, t) for ee, s, t in pairs if ee == e]
+                tok = torch.tensor([t for _, t in sel])
+                slot = torch.tensor([s for s, _ in sel])
+                g, u = F.linear(x[tok], t_bf(gu[e])).chunk(2, dim=-1)
+                cur = F.linear(F.silu(g) * u, t_bf(dn[e])) * scores[tok, slot, None]
+                result.index_add_(0, tok, cur.to(result.dtype))
+        out = result + gate * shared
+    return out
+
+
+def cpu_baseline(cfg, w, gu, dn, seed, budget_s=15.0):
+    from oracle import oracle as O
+
+    threads = len(os.sched_getaffinity(0))
+    tokens = cfg["tokens"]
+    sample_tokens = tokens if tokens <= 16 else 256
+    kind = "reference" if (sample_tokens <= 16 and O.ref_experts_lib() is not None) else "port"
+    xs = [S.hidden_states(seed + 1000 + i, sample_tokens) for i in range(4)]
+    cpu_reference_layer(w, gu, dn, xs[0], threads)          # warm-up
+    times, t_start, i = [], time.perf_counter(), 0
+    while (time.perf_counter() - t_start < budget_s and i < 50) or i < 2:
+        t = time.perf_counter()
+        cpu_reference_layer(w, gu, dn, xs[i % len(xs)], threads)
+        times.append(time.perf_counter() - t)
+        i += 1
+    step_s = statistics.median(times)
+    sample = (f"{len(times)} steps of {sample_tokens} tokens through the reference CPU layer "
+              f"(cpu_experts.c expert_block_rows + torch-CPU router/shared/combine)" if kind == "reference" else
+              f"{len(times)} steps of {sample_tokens} tokens through the eager torch-CPU expert loop")
+    return {"value": sample_tokens / step_s, "unit": "tokens/s", "cores": threads, "kind": kind, "sample": sample,
+            "ms_per_step": step_s * 1e3}
+
+
+def run_ours(args, cfg, world, rank, local):
+    from lightreason_b200 import native
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    native.device_check(local)
+    hbm_peak, tensor_peak, peak_src = peaks()
+    tokens = cfg["tokens"]
+    seed = 1 + rank
+    t_setup = time.perf_counter()
+    w, gu, dn, hbm, host = build_layer(cfg, dev, seed)
+    pool = 16
+    xs_np = [S.hidden_states(seed, tokens, step=i) for i in range(pool)]
+    xs = [to_dev(a, dev) for a in xs_np]
+    xs_host = [torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).pin_memory() for a in xs_np]
+    out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
+    out_host = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    idx_buf = [torch.empty((tokens, TOP_K), dtype=torch.int64, device=dev) for _ in range(pool)]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    log(f"[bench] setup {time.perf_counter() - t_setup:.1f}s, tokens={tokens}")
+
+    def hbm_step(i, stage):
+        hbm(xs[i % pool], out=out, idx_out=idx_buf[i % pool], stage_events=stage)
+
+    xin = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
+
+    def e2e_step(i, stage):
+        xin.copy_(xs_host[i % pool], non_blocking=True)
+        host(xin, out=out, stage_events=stage)
+        out_host.copy_(out, non_blocking=True)
+
+    sampler = ClockSampler(local)
+    with sampler:
+        ms, stage_ms, wall = timed_steps(hbm_step, args.steps, args.warmup, flush, world, stage_events=True)
+        e2e_ms = None
+        if host is not None:
+            e2e_ms, e2e_stage, _ = timed_steps(e2e_step, args.steps, args.warmup, flush, world, stage_events=True)
+    clocks = sampler.summary()
+
+    total_ms = dist_max(sum(ms), world)
+    value = world * tokens * args.steps / (total_ms / 1e3)
+    # routing actually realised in the timed steps
+    used = [(args.warmup + i) % pool for i in range(args.steps)]
+    u_per_step = [len(set(idx_buf[j].cpu().numpy().reshape(-1).tolist())) for j in used]
+    u_mean = float(np.mean(u_per_step))
+    routes = tokens * TOP_K
+    # algorithmic bytes per launch of each expert kernel (groups = U routed + shared)
+    algo = {
+        "gate_up": [(u + 1) * GATE_UP_BYTES + tokens * HIDDEN * 2 + (routes + tokens) * INNER * 2 for u in u_per_step],
+        "down": [(u + 1) * DOWN_BYTES + (routes + tokens) * INNER * 2 + (routes + tokens) * HIDDEN * 2
+                 for u in u_per_step],
+        "router": [EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 2 + tokens * EXPERTS * 2] * len(used),
+        "combine": [(routes + tokens) * HIDDEN * 2 + tokens * HIDDEN * 2] * len(used),
+    }
+    totals = {k: sum(v) for k, v in stage_ms.items()}
+    dominant = max(totals, key=totals.get)
+    dur_ms = statistics.mean(stage_ms[dominant])
+    bytes_per_launch = statistics.mean(algo.get(dominant, [0]))
+    achieved = bytes_per_launch / (dur_ms / 1e3) / 1e9
+    layer_bytes = [u * EXPERT_BYTES + EXPERT_BYTES + EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 4
+                   for u in u_per_step]
+    layer_gbs = statistics.mean(b / (m / 1e3) / 1e9 for b, m in zip(layer_bytes, ms))
+    launches_per_step = 7
+    result = {
+        "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "us_per_step": round(1e3 * total_ms / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, N(0,0.5) router bias)",
+        "config": {"workload": cfg["workload"], "tokens_per_step": tokens, "hidden": HIDDEN, "inner": INNER,
+                   "experts": EXPERTS, "top_k": TOP_K, "shared_expert": True,
+                   "distinct_experts_per_step": round(u_mean, 2),
+                   "parallelism": "single-gpu" if world == 1 else f"replicas{world}",
+                   "l2": "flushed (256 MiB memset) between timed steps, outside each step's event window"},
+        "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dominant], "achieved": round(achieved, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else
+                     "fallback 6650 GB/s", "traffic": None,
+                     "algorithmic_bytes_per_launch": int(bytes_per_launch),
+                     "launch_us": round(dur_ms * 1e3, 2),
+                     "layer_gbs": round(layer_gbs, 1), "layer_frac": round(layer_gbs / hbm_peak, 4),
+                     "stage_us": {k: round(1e3 * statistics.mean(v), 2) for k, v in stage_ms.items()}},
+        "gpu_launches": launches_per_step * args.steps + (8 * args.steps if e2e_ms else 0),
+        "clocks": clocks,
+        "wall_s_timed_loop": round(wall, 4),
+    }
+    if e2e_ms is not None:
+        e2e_total = dist_max(sum(e2e_ms), world)
+        gathered = statistics.mean(u * EXPERT_BYTES for u in u_per_step)
+        result["e2e"] = {
+            "value": round(world * tokens * args.steps / (e2e_total / 1e3), 2), "unit": "tokens/s",
+            "ms_per_step": round(e2e_total / args.steps, 4),
+            "h2d_bytes_per_step": int(tokens * HIDDEN * 2 + gathered),
+            "d2h_bytes_per_step": tokens * HIDDEN * 2,
+            "h2d_expert_bytes_per_step": int(gathered),
+            "gather_us": round(1e3 * statistics.mean(e2e_stage["gather"]), 2),
+            "gather_gbs": round(gathered / (statistics.mean(e2e_stage["gather"]) / 1e3) / 1e9, 2),
+            "path": "moe_layer_forward with host_gate_up/host_down (mapped pinned banks), x H2D + out D2H per step",
+        }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(cfg, w, gu, dn, seed)
+    return result
+
+
+def run_reference(args, cfg, world, rank):
+    """Reference arm: the reference's CPU implementation on the host cores."""
+    if rank != 0:
+        return None
+    tokens = cfg["tokens"]
+    seed = 1
+    w = S.layer_weights(seed, bias=cfg["bias"])
+    gu, dn = w.stacked()
+    threads = len(os.sched_getaffinity(0))
+    from oracle import oracle as O
+
+    sample_tokens = tokens if tokens <= 16 else 256
+    xs = [S.hidden_states(seed, sample_tokens, step=i) for i in range(8)]
+    for i in range(args.warmup):
+        cpu_reference_layer(w, gu, dn, xs[i % 8], threads)
+    times = []
+    for i in range(args.steps):
+        t = time.perf_counter()
+        cpu_reference_layer(w, gu, dn, xs[i % 8], threads)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = sample_tokens * args.steps / total
+    kind = "reference" if (sample_tokens <= 16 and O.ref_experts_lib() is not None) else "port"
+    return {
+        "impl": "reference", "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": cfg["workload"], "tokens_per_step": sample_tokens},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{args.steps} steps of {sample_tokens} tokens"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=1)
+    ap.add_argument("--tokens", type=int, default=None, help="override the config's tokens per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    cfg = dict(CONFIGS[args.config])
+    if args.tokens:
+        cfg["tokens"] = args.tokens
+        cfg["workload"] += f" (tokens overridden to {args.tokens})"
+    if args.impl == "reference":
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        res = run_reference(args, cfg, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+    world, rank, local = dist_setup()
+    try:
+        res = run_ours(args, cfg, world, rank, local)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

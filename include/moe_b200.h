@@ -1,0 +1,219 @@
+/*
+ * moe_b200.h -- C ABI of libmoe_b200.so, the B200 (sm_100a) MoE layer behind
+ * lightreason's edge35b expert-forward operator API.
+ *
+ * Conventions (all entry points):
+ *   - plain pointers and sizes; BF16 values travel as uint16_t bit patterns;
+ *   - every pointer to tensor data is a device pointer (or a CUDA-mapped pinned
+ *     host pointer where an entry point says so);
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     work is enqueued on it and the call returns without synchronising;
+ *   - the return value is a status: MOE_OK, or MOE_EINVAL for argument errors
+ *     (the Python layer raises ValueError, as the reference does for shape and
+ *     dtype violations: edge35b/fused_experts.py:41-50), MOE_ECUDA for a CUDA
+ *     failure (RuntimeError, as edge35b/native_bf16_gather.py:25-29 _checked),
+ *     MOE_EARCH when the device is not sm_100; moe_last_error() describes the
+ *     last failure on the calling thread;
+ *   - no entry point allocates device memory unless its comment says so.
+ *     Scratch lives in a caller-owned workspace sized by a *_workspace_bytes
+ *     query; entry points that read routing counts do so on the device, so a
+ *     call can be captured in a CUDA graph and replayed with new routes.
+ */
+#ifndef LIGHTREASON_B200_MOE_H
+#define LIGHTREASON_B200_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_OK 0
+#define MOE_EINVAL 1
+#define MOE_ECUDA 2
+#define MOE_EARCH 3
+
+/* Library version (major*10000 + minor*100 + patch). */
+int moe_version(void);
+
+/* Description of the last nonzero status returned on this thread. */
+const char *moe_last_error(void);
+
+/* MOE_OK when `device` is an sm_100 GPU this build can run on. */
+int moe_device_check(int device);
+
+/* Page-lock and map a host range for zero-copy device reads (the pinned host
+ * expert banks read by moe_gather_*).  Replaces the pinned staging set-up of
+ * edge35b/expert_stream.py:177-198 (_PackedBuffers) and FreeToken's
+ * device_ptr() mapping (edge35b/gpu_resident_experts.py:159,228).  Returns the
+ * device address of `ptr` in *device_ptr. */
+int moe_host_register(void *ptr, size_t bytes, uint64_t *device_ptr);
+int moe_host_unregister(void *ptr);
+
+/* ------------------------------------------------------------------------
+ * Router.  Replaces Qwen3_5MoeTopKRouter.forward (transformers
+ * models/qwen3_5_moe/modeling_qwen3_5_moe.py:762-770, the third-party router
+ * edge35b calls) and the shared_expert_gate Linear (same file :779, :788).
+ *
+ * logits[t][e] = bf16(x[t] . router[e]) (FP32 accumulation), then per token
+ * z = float(logits) + bias (bias may be NULL), softmax(z), top_k by z with
+ * exact ties to the lower expert id, weights w_k = p_k / sum_k p_k written as
+ * FP32 (scores_f32, may be NULL) and BF16 (scores_bf16, may be NULL).
+ * If shared_gate_w != NULL, sig[t] = bf16(sigmoid(bf16(x[t] . shared_gate_w))).
+ * x [T,H] row-major; router [E,H]; idx [T,top_k] int64; logits [T,E] is a
+ * required output (it is also the scratch between the two halves).
+ * hidden in {1024,2048,4096}, experts <= 1024, top_k <= 32.
+ * ------------------------------------------------------------------------ */
+int moe_router_topk(const uint16_t *x, const uint16_t *router, const float *bias,
+                    const uint16_t *shared_gate_w, int tokens, int hidden, int experts,
+                    int top_k, uint16_t *logits, int64_t *idx, float *scores_f32,
+                    uint16_t *scores_bf16, uint16_t *sig, void *stream);
+
+/* Selection only, from given BF16 logits [T,E] (the router's second half). */
+int moe_router_select(const uint16_t *logits, const float *bias, int tokens, int experts,
+                      int top_k, int64_t *idx, float *scores_f32, uint16_t *scores_bf16,
+                      void *stream);
+
+/* ------------------------------------------------------------------------
+ * Token permute.  Replaces the eager dispatch order of
+ * Qwen3_5MoeExperts.forward (modeling_qwen3_5_moe.py:730-744: ascending
+ * expert, then slot-major, then token) and edge35b/pipeline.py:59-76 _routes.
+ * Outputs: offsets[E+1] (exclusive scan of per-expert counts), perm_token[R],
+ * perm_slot[R] (route position -> token, slot), route_pos[T*top_k] ((token,
+ * slot) -> position), active[E] (experts with routes, ascending) and
+ * num_active[1].  R = tokens*top_k.  Ids outside [0,E) are dropped and counted
+ * in *bad_routes (may be NULL).  Requires experts <= 1024.
+ * ------------------------------------------------------------------------ */
+int moe_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets,
+                int32_t *perm_token, int32_t *perm_slot, int32_t *route_pos, int32_t *active,
+                int32_t *num_active, int32_t *bad_routes, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Expert rows by pointer table, the GPU counterpart of edge35b/cpu_experts.c.
+ *
+ * moe_expert_rows replaces expert_rows (cpu_experts.c:43-71, bound by
+ * edge35b/cpu_route.py:10-20): output[e] = the BF16 down projection of the one
+ * token `input` [H] through expert e, for e < experts (<= 128), with
+ * gate_up[e] -> [2I,H] and down[e] -> [H,I] device pointers (host arrays of
+ * device pointers).  H = 2048, I = 512 as in cpu_experts.c:7-9.
+ *
+ * moe_expert_block_rows replaces expert_block_rows (cpu_experts.c:74-105,
+ * bound by edge35b/block_experts.py:52-59): pair e reads token token_ids[e] of
+ * input [tokens,H]; tokens <= 16, experts <= 128 as in cpu_experts.c:77-78.
+ *
+ * gate_up, down and token_ids are HOST arrays (as the reference's ctypes
+ * arrays); input, output and the weights they point to are device memory.
+ * The reference keeps the [experts, 512] intermediate activations on its
+ * stack; on the GPU they live in a caller workspace of >= experts*512*2 bytes.
+ * ------------------------------------------------------------------------ */
+int moe_expert_rows(const uint16_t *const *gate_up, const uint16_t *const *down,
+                    const uint16_t *input, uint16_t *output, int experts, void *workspace,
+                    size_t workspace_bytes, void *stream);
+int moe_expert_block_rows(const uint16_t *const *gate_up, const uint16_t *const *down,
+                          const uint16_t *input, const int32_t *token_ids, uint16_t *output,
+                          int tokens, int experts, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
+/* ------------------------------------------------------------------------
+ * One MoE layer.  moe_layer_forward replaces Qwen3_5MoeSparseMoeBlock.forward
+ * (modeling_qwen3_5_moe.py:781-792: router + shared expert + experts + gate)
+ * and, with route_in != NULL, Qwen3_5MoeExperts.forward as patched by
+ * edge35b/expert_stream.py:457-526 (_Layer.forward :383-454; fused_forward,
+ * edge35b/fused_experts.py:40-70; grouped_block, edge35b/block_experts.py:89-139):
+ * the caller then supplies idx [T,top_k] and BF16 weights [T,top_k] and the
+ * router and shared expert are skipped.
+ * ------------------------------------------------------------------------ */
+typedef struct moe_layer_weights {
+    const uint16_t *router;        /* [E,H]                                   */
+    const float *router_bias;      /* [E] FP32 or NULL                        */
+    const uint16_t *gate_up;       /* expert e at gate_up + e*gate_up_stride: [2I,H] */
+    const uint16_t *down;          /* expert e at down + e*down_stride: [H,I]  */
+    int64_t gate_up_stride;        /* elements between experts (2I*H packed)  */
+    int64_t down_stride;           /* elements between experts (H*I packed)   */
+    const uint16_t *shared_gate;   /* [Is,H] or NULL: no shared expert        */
+    const uint16_t *shared_up;     /* [Is,H]                                  */
+    const uint16_t *shared_down;   /* [H,Is]                                  */
+    const uint16_t *shared_gate_w; /* [H]                                     */
+    int experts, hidden, inner, shared_inner, top_k;
+} moe_layer_weights;
+
+/* Optional inputs/outputs of moe_layer_forward (any pointer may be NULL). */
+typedef struct moe_layer_io {
+    const int64_t *route_in;       /* [T,top_k] given expert ids: skip router and shared expert */
+    const uint16_t *weights_in;    /* [T,top_k] BF16 router weights for route_in */
+    int64_t *idx_out;              /* [T,top_k] selected ids                   */
+    uint16_t *scores_out;          /* [T,top_k] BF16 router weights            */
+    uint16_t *logits_out;          /* [T,E] BF16 router logits                 */
+    /* Host-resident experts.  When host_gate_up != NULL the layer copies each
+     * active expert e (ascending id) from host_gate_up + e*gate_up_stride and
+     * host_down + e*down_stride -- device addresses of mapped pinned banks
+     * (moe_host_register) -- into slot g (the g-th active expert) of the HBM
+     * slot banks, and the expert kernels read the slots; w->gate_up/down are
+     * then unused.  Only the union of selected experts crosses the host link
+     * (edge35b/expert_stream.py:200-236 _PackedBuffers.gather moves the same
+     * rows through a pinned staging copy).  max_slots >= min(E, T*top_k). */
+    const uint16_t *host_gate_up;
+    const uint16_t *host_down;
+    uint16_t *gate_up_slots;       /* [max_slots,2I,H]                         */
+    uint16_t *down_slots;          /* [max_slots,H,I]                          */
+    int max_slots;
+    /* Optional cudaEvent_t handles recorded on `stream` at the stage
+     * boundaries: 0 start, 1 router done, 2 permute done, 3 host gather done,
+     * 4 groups resolved, 5 gate/up done, 6 down done, 7 combine done.  NULL
+     * entries (or num_stage_events <= i) are skipped.  For live per-kernel
+     * timing (the role of the NVTX ranges of edge35b/native_bench.py:30-69). */
+    void *const *stage_events;
+    int num_stage_events;
+} moe_layer_io;
+
+/* Scratch bytes moe_layer_forward needs for `tokens` tokens. */
+size_t moe_layer_workspace_bytes(int tokens, int experts, int top_k, int hidden, int inner,
+                                 int shared_inner);
+
+/* hidden in {1024,2048,4096}, inner in {256,512,1024}, experts <= 1024,
+ * top_k <= 32, shared_inner == inner.  x, out [T,H] BF16. */
+int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens, uint16_t *out,
+                      const moe_layer_io *io, void *workspace, size_t workspace_bytes,
+                      void *stream);
+
+/* ------------------------------------------------------------------------
+ * Descriptor-driven expert gathers.  Same tables and semantics as the kernels
+ * of edge35b/bf16_gather_ada.cu (ABI :105-107, bound through NVRTC +
+ * cuLaunchKernel by edge35b/native_bf16_gather.py:71-77 NativeBf16Gather.copy):
+ *   descriptors int64 [banks][experts][3], destinations int64 [banks]
+ *   (device addresses), sizes int64 [banks] (row bytes), source_ids /
+ *   destination_ids int32 [max_copies], count int64 [1] read on the device.
+ * Row r < *count copies expert source_ids[r] of every bank into slot
+ * destination_ids[r] of that bank's destination.
+ *   codec MOE_CODEC_ROW      (src, base, escapes): base < 0 copies raw bytes,
+ *                            else the row codec of edge35b/bf16_expert_codec.py
+ *                            (gather_bf16 / gather_bf16_l2, :36-115);
+ *   codec MOE_CODEC_TILES    (packed, bases, raw): bases == 0 copies raw, else
+ *                            256-value tiles of cpu_bf16_reads.h:16-52
+ *                            (gather_bf16_cpu_tiles, :117-189);
+ *   codec MOE_CODEC_RESIDENT as TILES, and raw == -1 marks a compact row with
+ *                            uint32 headers (gather_bf16_resident, :191-198;
+ *                            edge35b/gpu_resident_experts.py:22-42 encode).
+ * Sources may be device memory or mapped pinned host memory.  stripes splits a
+ * row across CTAs (geometry of native_bf16_gather.py:7-11); threads per CTA is
+ * a multiple of 32 in [32,1024].  Rows need row_bytes % 16 == 0 (raw/row codec)
+ * or % 512 == 0 (tile codecs); every 16-byte unit is written whatever the
+ * stripe count.
+ * ------------------------------------------------------------------------ */
+#define MOE_CODEC_ROW 0
+#define MOE_CODEC_TILES 1
+#define MOE_CODEC_RESIDENT 2
+#define MOE_CODEC_ROW_L2 3 /* MOE_CODEC_ROW with L2-only loads (gather_bf16_l2) */
+
+int moe_gather_rows(const int64_t *descriptors, const int64_t *destinations,
+                    const int64_t *sizes, const int32_t *source_ids,
+                    const int32_t *destination_ids, const int64_t *count, int experts,
+                    int banks, int max_copies, int codec, int stripes, int threads,
+                    void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LIGHTREASON_B200_MOE_H */

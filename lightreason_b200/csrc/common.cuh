@@ -1,0 +1,85 @@
+// Shared helpers for the sm_100a MoE kernels: BF16 bit handling, streaming
+// loads, warp reductions and the host-side status plumbing of the C ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "moe_b200.h"
+
+namespace lrb {
+
+// ---------------------------------------------------------------- BF16 ----
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ float bf2f(uint16_t v) { return __uint_as_float(static_cast<uint32_t>(v) << 16); }
+__device__ __forceinline__ uint16_t f2bf(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+// Round an FP32 value to the nearest BF16 and widen it back (one eager BF16 op).
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+}
+
+// 16-byte loads.  Weights are read once per layer step: keep them out of L1.
+__device__ __forceinline__ uint4 ld_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_cached(const void *p) {
+    return __ldg(reinterpret_cast<const uint4 *>(p));
+}
+
+// acc += dot(8 BF16 weights, 8 BF16 activations) in FP32 FMA.
+__device__ __forceinline__ float dot8(uint4 w, uint4 a, float acc) {
+    acc = fmaf(bf16_lo(w.x), bf16_lo(a.x), acc);
+    acc = fmaf(bf16_hi(w.x), bf16_hi(a.x), acc);
+    acc = fmaf(bf16_lo(w.y), bf16_lo(a.y), acc);
+    acc = fmaf(bf16_hi(w.y), bf16_hi(a.y), acc);
+    acc = fmaf(bf16_lo(w.z), bf16_lo(a.z), acc);
+    acc = fmaf(bf16_hi(w.z), bf16_hi(a.z), acc);
+    acc = fmaf(bf16_lo(w.w), bf16_lo(a.w), acc);
+    acc = fmaf(bf16_hi(w.w), bf16_hi(a.w), acc);
+    return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);
+    return v;
+}
+
+// eager SiLU on a BF16 tensor (torch computes x / (1 + exp(-x)) in FP32 and
+// rounds once), the arithmetic of edge35b/cpu_experts.c:61.
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+__device__ __forceinline__ float sigmoid_f32(float g) { return 1.0f / (1.0f + expf(-g)); }
+
+// -------------------------------------------------------- host status ----
+int set_error(int status, const char *fmt, ...);
+int cuda_error(cudaError_t err, const char *where);
+int check_launch(const char *where);
+int require_sm100();
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+}  // namespace lrb
+
+#define LRB_REQUIRE(cond, ...)                                         \
+    do {                                                               \
+        if (!(cond)) return ::lrb::set_error(MOE_EINVAL, __VA_ARGS__); \
+    } while (0)
+
+#define LRB_CUDA(call)                                                    \
+    do {                                                                  \
+        cudaError_t err_ = (call);                                        \
+        if (err_ != cudaSuccess) return ::lrb::cuda_error(err_, #call);   \
+    } while (0)
+
+#define LRB_LAUNCHED(where)                                  \
+    do {                                                     \
+        int rc_ = ::lrb::check_launch(where);                \
+        if (rc_ != MOE_OK) return rc_;                       \
+    } while (0)

@@ -1,0 +1,57 @@
+// Internal launchers shared between the translation units of libmoe_b200.so.
+#pragma once
+
+#include "common.cuh"
+
+namespace lrb {
+
+// Weights of one work group of the expert kernels: the routed expert whose
+// routes occupy positions [begin, begin + count), or the shared expert.
+struct Group {
+    const uint16_t *gate;  // [I, H]
+    const uint16_t *up;    // [I, H]
+    const uint16_t *down;  // [H, I]
+    int32_t begin;
+    int32_t count;
+};
+
+// Groups resolved on the device (layer path): groups[g] for g < *num_groups;
+// route_token[p] is the token of route position p.
+struct DeviceGroups {
+    const Group *groups;
+    const int32_t *num_groups;
+    const int32_t *route_token;
+    __device__ __forceinline__ int n() const { return *num_groups; }
+    __device__ __forceinline__ Group get(int g) const { return groups[g]; }
+    __device__ __forceinline__ int token(int p) const { return route_token[p]; }
+};
+
+// Groups passed by value (pointer-table entry points, one route per group).
+constexpr int kMaxParamGroups = 128;
+struct ParamGroups {
+    Group groups[kMaxParamGroups];
+    int32_t tokens[kMaxParamGroups];
+    int32_t count;
+    __device__ __forceinline__ int n() const { return count; }
+    __device__ __forceinline__ Group get(int g) const { return groups[g]; }
+    __device__ __forceinline__ int token(int p) const { return tokens[p]; }
+};
+
+int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
+                         int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);
+int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
+                         int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream);
+int check_router_args(int tokens, int hidden, int experts, int top_k);
+
+int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets, int32_t *perm_token,
+                   int32_t *perm_slot, int32_t *route_pos, int32_t *active, int32_t *num_active, int32_t *bad_routes,
+                   cudaStream_t stream);
+
+template <class Src>
+int launch_experts(const Src &src, int max_groups, const uint16_t *x, int hidden, int inner, uint16_t *act,
+                   uint16_t *y, cudaStream_t stream, cudaEvent_t between);
+
+int launch_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, int tokens, int top_k,
+                   int hidden, const uint16_t *shared_y, const uint16_t *sig, uint16_t *out, cudaStream_t stream);
+
+}  // namespace lrb

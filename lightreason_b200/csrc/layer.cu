@@ -1,0 +1,220 @@
+// One MoE layer on the device: router -> permute -> (host-resident gather) ->
+// grouped SwiGLU experts (+ shared expert) -> ordered combine.  Every step
+// reads its routing from device memory, so the whole call is one stream of
+// launches with no host synchronisation and can be captured in a CUDA graph.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace lrb {
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Byte offsets of the scratch arrays inside the caller's workspace.
+struct Layout {
+    size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, act, y,
+        total;
+};
+
+Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
+    const size_t T = tokens, E = experts, K = top_k, R = T * K;
+    Layout L{};
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes);
+        return at;
+    };
+    L.logits = take(T * E * 2);
+    L.sig = take(T * 2);
+    L.idx = take(R * 8);
+    L.scores = take(R * 2);
+    L.offsets = take((E + 1) * 4);
+    L.route_token = take((R + T) * 4);
+    L.perm_slot = take(R * 4);
+    L.route_pos = take(R * 4);
+    L.active = take(E * 4);
+    L.counters = take(4 * 4);  // num_active, bad_routes, num_groups, slot overflow
+    L.groups = take((E + 1) * sizeof(Group));
+    L.act = take((R + T) * inner * 2);
+    L.y = take((R + T) * hidden * 2);
+    L.total = o;
+    return L;
+}
+
+template <class T>
+T *at(void *base, size_t offset) {
+    return reinterpret_cast<T *>(static_cast<char *>(base) + offset);
+}
+
+}  // namespace
+
+// Resolve the weights of each active expert (ascending id) and append the
+// shared expert as the last group.
+__global__ void build_groups_kernel(const int32_t *__restrict__ active, const int32_t *__restrict__ num_active,
+                                    const int32_t *__restrict__ offsets, const uint16_t *gate_up,
+                                    const uint16_t *down, int64_t gate_up_stride, int64_t down_stride,
+                                    int use_slots, int hidden, int inner, const uint16_t *sh_gate,
+                                    const uint16_t *sh_up, const uint16_t *sh_down, int routes, int tokens,
+                                    Group *__restrict__ groups, int32_t *__restrict__ num_groups,
+                                    int32_t *__restrict__ route_token) {
+    const int n = *num_active;
+    for (int g = threadIdx.x; g < n; g += blockDim.x) {
+        const int e = active[g];
+        const int64_t w = use_slots ? g : e;
+        const uint16_t *gu = gate_up + w * gate_up_stride;
+        groups[g] = Group{gu, gu + static_cast<size_t>(inner) * hidden, down + w * down_stride, offsets[e],
+                          offsets[e + 1] - offsets[e]};
+    }
+    if (sh_gate) {
+        if (threadIdx.x == 0) groups[n] = Group{sh_gate, sh_up, sh_down, routes, tokens};
+        for (int t = threadIdx.x; t < tokens; t += blockDim.x) route_token[routes + t] = t;
+    }
+    if (threadIdx.x == 0) *num_groups = n + (sh_gate != nullptr);
+}
+
+// Copy every active expert's gate_up and down rows from the mapped host banks
+// into HBM slot g (g-th active expert).  Grid (stripes, 2 banks, max_slots);
+// 16-byte loads over the host link, four in flight per thread.
+__global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__restrict__ active,
+                                                            const int32_t *__restrict__ num_active,
+                                                            const uint16_t *host_gate_up, const uint16_t *host_down,
+                                                            int64_t gate_up_stride, int64_t down_stride,
+                                                            int64_t gate_up_bytes, int64_t down_bytes,
+                                                            uint16_t *gate_up_slots, uint16_t *down_slots,
+                                                            int32_t *overflow) {
+    const int g = blockIdx.z;
+    const int n = *num_active;
+    if (g == 0 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *overflow = n > static_cast<int>(gridDim.z);
+    if (g >= n) return;
+    const int64_t e = active[g];
+    const bool gu = blockIdx.y == 0;
+    const uint4 *src = reinterpret_cast<const uint4 *>(gu ? host_gate_up + e * gate_up_stride
+                                                          : host_down + e * down_stride);
+    const int64_t bytes = gu ? gate_up_bytes : down_bytes;
+    uint4 *dst = reinterpret_cast<uint4 *>(gu ? gate_up_slots + g * (gate_up_bytes / 2)
+                                              : down_slots + g * (down_bytes / 2));
+    const int64_t units = bytes / 16;
+    const int64_t begin = units * blockIdx.x / gridDim.x, end = units * (blockIdx.x + 1) / gridDim.x;
+    int64_t i = begin + threadIdx.x;
+    for (; i + 3 * blockDim.x < end; i += 4 * blockDim.x) {
+        uint4 v0 = ld_stream(src + i), v1 = ld_stream(src + i + blockDim.x);
+        uint4 v2 = ld_stream(src + i + 2 * blockDim.x), v3 = ld_stream(src + i + 3 * blockDim.x);
+        dst[i] = v0;
+        dst[i + blockDim.x] = v1;
+        dst[i + 2 * blockDim.x] = v2;
+        dst[i + 3 * blockDim.x] = v3;
+    }
+    for (; i < end; i += blockDim.x) dst[i] = ld_stream(src + i);
+}
+
+}  // namespace lrb
+
+extern "C" {
+
+size_t moe_layer_workspace_bytes(int tokens, int experts, int top_k, int hidden, int inner, int shared_inner) {
+    (void)shared_inner;
+    if (tokens < 0 || experts <= 0 || top_k <= 0 || hidden <= 0 || inner <= 0) return 0;
+    return lrb::layout(tokens, experts, top_k, hidden, inner).total;
+}
+
+int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens, uint16_t *out,
+                      const moe_layer_io *io, void *workspace, size_t workspace_bytes, void *stream) {
+    using namespace lrb;
+    LRB_REQUIRE(w && x && out, "moe_layer_forward: weights, x and out are required");
+    const moe_layer_io none{};
+    if (!io) io = &none;
+    const int E = w->experts, H = w->hidden, I = w->inner, K = w->top_k;
+    if (int rc = check_router_args(tokens, H, E, K)) return rc;
+    LRB_REQUIRE(I == 256 || I == 512 || I == 1024, "moe_layer_forward: inner %d not in {256, 512, 1024}", I);
+    const bool routed_in = io->route_in != nullptr;
+    const bool shared = !routed_in && w->shared_gate != nullptr;
+    LRB_REQUIRE(!routed_in || io->weights_in, "moe_layer_forward: route_in needs weights_in");
+    LRB_REQUIRE(routed_in || w->router, "moe_layer_forward: router weights required without route_in");
+    LRB_REQUIRE(!shared || (w->shared_up && w->shared_down && w->shared_gate_w && w->shared_inner == I),
+                "moe_layer_forward: shared expert needs gate/up/down/gate_w with shared_inner == inner");
+    const bool staged = io->host_gate_up != nullptr;
+    LRB_REQUIRE(!staged || (io->host_down && io->gate_up_slots && io->down_slots),
+                "moe_layer_forward: host banks need slot banks");
+    const int R = tokens * K;
+    const int max_groups = std::min(E, R);
+    LRB_REQUIRE(!staged || io->max_slots >= max_groups, "moe_layer_forward: max_slots %d < min(E, T*top_k) = %d",
+                staged ? io->max_slots : 0, max_groups);
+    LRB_REQUIRE(staged || (w->gate_up && w->down), "moe_layer_forward: expert banks required");
+    const int64_t gu_stride = w->gate_up_stride ? w->gate_up_stride : static_cast<int64_t>(2) * I * H;
+    const int64_t dn_stride = w->down_stride ? w->down_stride : static_cast<int64_t>(H) * I;
+    const Layout L = layout(tokens, E, K, H, I);
+    LRB_REQUIRE(workspace && workspace_bytes >= L.total, "moe_layer_forward: workspace %zu < %zu bytes",
+                workspace_bytes, L.total);
+    if (tokens == 0) return MOE_OK;
+    if (int rc = require_sm100()) return rc;
+    cudaStream_t s = as_stream(stream);
+    auto mark = [&](int i) -> int {
+        if (io->stage_events && i < io->num_stage_events && io->stage_events[i])
+            LRB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(io->stage_events[i]), s));
+        return MOE_OK;
+    };
+    if (int rc = mark(0)) return rc;
+
+    void *ws = workspace;
+    const int64_t *idx = io->route_in;
+    const uint16_t *scores = io->weights_in;
+    uint16_t *sig = at<uint16_t>(ws, L.sig);
+    if (!routed_in) {
+        uint16_t *logits = io->logits_out ? io->logits_out : at<uint16_t>(ws, L.logits);
+        int64_t *idx_w = io->idx_out ? io->idx_out : at<int64_t>(ws, L.idx);
+        uint16_t *scores_w = io->scores_out ? io->scores_out : at<uint16_t>(ws, L.scores);
+        if (int rc = launch_router_logits(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, logits,
+                                          sig, s))
+            return rc;
+        if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx_w, nullptr, scores_w, s))
+            return rc;
+        idx = idx_w;
+        scores = scores_w;
+    }
+    if (int rc = mark(1)) return rc;
+    int32_t *offsets = at<int32_t>(ws, L.offsets), *route_token = at<int32_t>(ws, L.route_token);
+    int32_t *route_pos = at<int32_t>(ws, L.route_pos), *active = at<int32_t>(ws, L.active);
+    int32_t *counters = at<int32_t>(ws, L.counters);
+    if (int rc = launch_permute(idx, tokens, K, E, offsets, route_token, at<int32_t>(ws, L.perm_slot), route_pos,
+                                active, counters + 0, counters + 1, s))
+        return rc;
+    if (int rc = mark(2)) return rc;
+    const uint16_t *gu_base = w->gate_up, *dn_base = w->down;
+    int64_t gu_str = gu_stride, dn_str = dn_stride;
+    if (staged) {
+        stage_experts_kernel<<<dim3(64, 2, max_groups), 256, 0, s>>>(
+            active, counters + 0, io->host_gate_up, io->host_down, gu_stride, dn_stride,
+            static_cast<int64_t>(2) * I * H * 2, static_cast<int64_t>(H) * I * 2, io->gate_up_slots,
+            io->down_slots, counters + 3);
+        LRB_LAUNCHED("stage_experts_kernel");
+        gu_base = io->gate_up_slots;
+        dn_base = io->down_slots;
+        gu_str = static_cast<int64_t>(2) * I * H;
+        dn_str = static_cast<int64_t>(H) * I;
+    }
+    if (int rc = mark(3)) return rc;
+    Group *groups = at<Group>(ws, L.groups);
+    build_groups_kernel<<<1, 256, 0, s>>>(active, counters + 0, offsets, gu_base, dn_base, gu_str, dn_str, staged,
+                                          H, I, shared ? w->shared_gate : nullptr, w->shared_up, w->shared_down, R,
+                                          tokens, groups, counters + 2, route_token);
+    LRB_LAUNCHED("build_groups_kernel");
+    if (int rc = mark(4)) return rc;
+    uint16_t *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
+    const DeviceGroups src{groups, counters + 2, route_token};
+    cudaEvent_t mid = io->stage_events && io->num_stage_events > 5
+                          ? static_cast<cudaEvent_t>(io->stage_events[5]) : nullptr;
+    if (int rc = launch_experts(src, max_groups + (shared ? 1 : 0), x, H, I, act, y, s, mid)) return rc;
+    if (int rc = mark(6)) return rc;
+    if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
+                                sig, out, s))
+        return rc;
+    return mark(7);
+}
+
+}  // extern "C"

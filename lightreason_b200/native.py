@@ -1,0 +1,319 @@
+"""ctypes binding of libmoe_b200.so and thin torch wrappers around its C ABI.
+
+This is the only route from Python to the device code.  There is no fallback:
+if the library is missing or the GPU is not sm_100, every call raises.
+Status codes map to exceptions the way the reference's APIs raise them:
+argument errors -> ValueError (edge35b/fused_experts.py:41-50), CUDA failures
+-> RuntimeError (edge35b/native_bf16_gather.py:25-29).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from functools import lru_cache
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_native" / "libmoe_b200.so"
+
+MOE_OK, MOE_EINVAL, MOE_ECUDA, MOE_EARCH = 0, 1, 2, 3
+CODEC_ROW, CODEC_TILES, CODEC_RESIDENT, CODEC_ROW_L2 = 0, 1, 2, 3
+
+_p = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+
+
+class LayerWeights(ctypes.Structure):
+    """moe_layer_weights of include/moe_b200.h."""
+
+    _fields_ = [("router", _p), ("router_bias", _p), ("gate_up", _p), ("down", _p),
+                ("gate_up_stride", ctypes.c_int64), ("down_stride", ctypes.c_int64),
+                ("shared_gate", _p), ("shared_up", _p), ("shared_down", _p), ("shared_gate_w", _p),
+                ("experts", _i), ("hidden", _i), ("inner", _i), ("shared_inner", _i), ("top_k", _i)]
+
+
+class LayerIO(ctypes.Structure):
+    """moe_layer_io of include/moe_b200.h."""
+
+    _fields_ = [("route_in", _p), ("weights_in", _p), ("idx_out", _p), ("scores_out", _p), ("logits_out", _p),
+                ("host_gate_up", _p), ("host_down", _p), ("gate_up_slots", _p), ("down_slots", _p),
+                ("max_slots", _i), ("stage_events", ctypes.POINTER(_p)), ("num_stage_events", _i)]
+
+
+_SIGNATURES = {
+    "moe_version": ([], _i),
+    "moe_last_error": ([], ctypes.c_char_p),
+    "moe_device_check": ([_i], _i),
+    "moe_host_register": ([_p, _sz, ctypes.POINTER(ctypes.c_uint64)], _i),
+    "moe_host_unregister": ([_p], _i),
+    "moe_router_topk": ([_p, _p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p], _i),
+    "moe_router_select": ([_p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
+    "moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
+    "moe_expert_rows": ([_p, _p, _p, _p, _i, _p, _sz, _p], _i),
+    "moe_expert_block_rows": ([_p, _p, _p, _p, _p, _i, _i, _p, _sz, _p], _i),
+    "moe_layer_workspace_bytes": ([_i, _i, _i, _i, _i, _i], _sz),
+    "moe_layer_forward": ([ctypes.POINTER(LayerWeights), _p, _i, _p, ctypes.POINTER(LayerIO), _p, _sz, _p], _i),
+    "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+}
+
+EXPORTED = tuple(_SIGNATURES)
+
+
+@lru_cache(maxsize=1)
+def lib() -> ctypes.CDLL:
+    """Load the in-tree library; raise if it was not built."""
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m lightreason_b200.build` "
+                           "(there is no CPU fallback)")
+    so = ctypes.CDLL(str(LIB_PATH))
+    for name, (args, res) in _SIGNATURES.items():
+        fn = getattr(so, name)
+        fn.argtypes = args
+        fn.restype = res
+    return so
+
+
+def check(status: int, what: str) -> None:
+    if status == MOE_OK:
+        return
+    msg = f"{what}: {lib().moe_last_error().decode(errors='replace')}"
+    if status == MOE_EINVAL:
+        raise ValueError(msg)
+    raise RuntimeError(msg)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _bits(t: torch.Tensor) -> torch.Tensor:
+    """A BF16 tensor seen as the int16 bit patterns the ABI takes."""
+    return t.view(torch.int16) if t.dtype == torch.bfloat16 else t
+
+
+def _require(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def device_check(device: torch.device | int | None = None) -> None:
+    index = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    check(lib().moe_device_check(index.index if index.index is not None else torch.cuda.current_device()),
+          "moe_device_check")
+
+
+def _cuda_bf16(t: torch.Tensor, name: str) -> None:
+    _require(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous(),
+             f"{name} must be a contiguous CUDA BF16 tensor")
+
+
+# ---------------------------------------------------------------- router ---
+
+def router_topk(x: torch.Tensor, router: torch.Tensor, bias: torch.Tensor | None = None,
+                shared_gate_w: torch.Tensor | None = None, top_k: int = 8):
+    """Router + top-k (+ sigmoid shared gate).  Returns idx int64 [T,K], scores
+    f32 [T,K], scores bf16 [T,K], logits bf16 [T,E], sig bf16 [T] or None."""
+    _cuda_bf16(x, "x")
+    _cuda_bf16(router, "router")
+    tokens, hidden = x.shape
+    experts = router.shape[0]
+    dev = x.device
+    logits = torch.empty((tokens, experts), dtype=torch.bfloat16, device=dev)
+    idx = torch.empty((tokens, top_k), dtype=torch.int64, device=dev)
+    sf = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
+    sb = torch.empty((tokens, top_k), dtype=torch.bfloat16, device=dev)
+    sig = torch.empty(tokens, dtype=torch.bfloat16, device=dev) if shared_gate_w is not None else None
+    if bias is not None:
+        _require(bias.is_cuda and bias.dtype == torch.float32 and bias.numel() == experts, "bias must be CUDA f32 [E]")
+    check(lib().moe_router_topk(_ptr(x), _ptr(router), _ptr(bias), _ptr(shared_gate_w), tokens, hidden, experts, top_k,
+                                _ptr(logits), _ptr(idx), _ptr(sf), _ptr(sb), _ptr(sig), _stream(dev)),
+          "moe_router_topk")
+    return idx, sf, sb, logits, sig
+
+
+def router_select(logits: torch.Tensor, bias: torch.Tensor | None = None, top_k: int = 8):
+    _cuda_bf16(logits, "logits")
+    tokens, experts = logits.shape
+    dev = logits.device
+    idx = torch.empty((tokens, top_k), dtype=torch.int64, device=dev)
+    sf = torch.empty((tokens, top_k), dtype=torch.float32, device=dev)
+    sb = torch.empty((tokens, top_k), dtype=torch.bfloat16, device=dev)
+    check(lib().moe_router_select(_ptr(logits), _ptr(bias), tokens, experts, top_k, _ptr(idx), _ptr(sf), _ptr(sb),
+                                  _stream(dev)), "moe_router_select")
+    return idx, sf, sb
+
+
+# --------------------------------------------------------------- permute ---
+
+def permute(idx: torch.Tensor, experts: int):
+    """Eager dispatch order.  Returns offsets [E+1], perm_token [R], perm_slot
+    [R], route_pos [T,K], active [E] (first num_active valid), num_active [1],
+    bad_routes [1] (int32, on the device)."""
+    _require(idx.is_cuda and idx.dtype == torch.int64 and idx.dim() == 2 and idx.is_contiguous(),
+             "idx must be a contiguous CUDA int64 [T, K] tensor")
+    tokens, top_k = idx.shape
+    dev = idx.device
+    i32 = dict(dtype=torch.int32, device=dev)
+    offsets = torch.empty(experts + 1, **i32)
+    ptok = torch.empty(max(tokens * top_k, 1), **i32)
+    pslot = torch.empty(max(tokens * top_k, 1), **i32)
+    rpos = torch.empty((tokens, top_k), **i32)
+    active = torch.empty(experts, **i32)
+    counters = torch.zeros(2, **i32)
+    check(lib().moe_permute(_ptr(idx), tokens, top_k, experts, _ptr(offsets), _ptr(ptok), _ptr(pslot), _ptr(rpos),
+                            _ptr(active), counters.data_ptr(), counters.data_ptr() + 4, _stream(dev)), "moe_permute")
+    return offsets, ptok[:tokens * top_k], pslot[:tokens * top_k], rpos, active, counters[:1], counters[1:]
+
+
+# ------------------------------------------------- pointer-table experts ---
+
+def expert_block_rows(gate_up: list, down: list, hidden: torch.Tensor, token_ids: list[int] | None = None):
+    """GPU counterpart of cpu_experts.c expert_rows / expert_block_rows: the
+    BF16 down projection of each (expert weights, token) pair.  gate_up[i] is a
+    [2I,H] and down[i] a [H,I] CUDA BF16 tensor; hidden [T,H]."""
+    _cuda_bf16(hidden, "hidden")
+    pairs = len(gate_up)
+    _require(len(down) == pairs, "gate_up and down need one entry per pair")
+    for g, d in zip(gate_up, down):
+        _cuda_bf16(g, "gate_up row")
+        _cuda_bf16(d, "down row")
+    out = torch.empty((pairs, hidden.shape[-1]), dtype=torch.bfloat16, device=hidden.device)
+    if pairs == 0:
+        return out
+    work = torch.empty(pairs * 512 * 2, dtype=torch.uint8, device=hidden.device)
+    gp = (ctypes.c_void_p * pairs)(*[t.data_ptr() for t in gate_up])
+    dp = (ctypes.c_void_p * pairs)(*[t.data_ptr() for t in down])
+    if token_ids is None:
+        check(lib().moe_expert_rows(ctypes.cast(gp, _p), ctypes.cast(dp, _p), _ptr(hidden), _ptr(out), pairs,
+                                    _ptr(work), work.numel(), _stream(hidden.device)), "moe_expert_rows")
+    else:
+        tid = (ctypes.c_int32 * pairs)(*token_ids)
+        check(lib().moe_expert_block_rows(ctypes.cast(gp, _p), ctypes.cast(dp, _p), _ptr(hidden),
+                                          ctypes.cast(tid, _p), _ptr(out), hidden.shape[0], pairs, _ptr(work),
+                                          work.numel(), _stream(hidden.device)), "moe_expert_block_rows")
+    return out
+
+
+# ----------------------------------------------------------------- layer ---
+
+def layer_workspace_bytes(tokens: int, experts: int, top_k: int, hidden: int, inner: int) -> int:
+    return int(lib().moe_layer_workspace_bytes(tokens, experts, top_k, hidden, inner, inner))
+
+
+class Layer:
+    """Device-resident weights of one MoE layer bound to the C ABI structure.
+
+    gate_up [E,2I,H] and down [E,H,I] may instead be host-resident: pass
+    host_gate_up/host_down as pinned CPU tensors (mapped with
+    moe_host_register) and the forward gathers the selected experts per call.
+    """
+
+    def __init__(self, *, router, gate_up=None, down=None, bias=None, shared_gate=None, shared_up=None,
+                 shared_down=None, shared_gate_w=None, top_k=8, host_gate_up=None, host_down=None):
+        _cuda_bf16(router, "router")
+        self.router, self.bias = router, bias
+        self.gate_up, self.down = gate_up, down
+        self.shared = (shared_gate, shared_up, shared_down, shared_gate_w)
+        self.experts, self.hidden = router.shape
+        self.top_k = top_k
+        self.host_gate_up, self.host_down = host_gate_up, host_down
+        bank = gate_up if gate_up is not None else host_gate_up
+        dbank = down if down is not None else host_down
+        _require(bank is not None and dbank is not None, "expert banks are required")
+        self.inner = bank.shape[1] // 2
+        _require(tuple(bank.shape) == (self.experts, 2 * self.inner, self.hidden), "gate_up must be [E, 2I, H]")
+        _require(tuple(dbank.shape) == (self.experts, self.hidden, self.inner), "down must be [E, H, I]")
+        self.device = router.device
+        self._mapped = []
+        self._host_dev = (None, None)
+        if host_gate_up is not None:
+            self._host_dev = (self._map(host_gate_up), self._map(host_down))
+        self.w = LayerWeights(
+            router=_ptr(router), router_bias=_ptr(bias), gate_up=_ptr(gate_up), down=_ptr(down),
+            gate_up_stride=2 * self.inner * self.hidden, down_stride=self.hidden * self.inner,
+            shared_gate=_ptr(shared_gate), shared_up=_ptr(shared_up), shared_down=_ptr(shared_down),
+            shared_gate_w=_ptr(shared_gate_w), experts=self.experts, hidden=self.hidden, inner=self.inner,
+            shared_inner=(shared_gate.shape[0] if shared_gate is not None else self.inner), top_k=top_k)
+        self._slots = None
+        self._ws = None
+
+    def _map(self, t: torch.Tensor) -> int:
+        _require(t.device.type == "cpu" and t.is_contiguous() and t.dtype == torch.bfloat16,
+                 "host banks must be contiguous CPU BF16 tensors")
+        dev = ctypes.c_uint64()
+        if t.is_pinned():
+            # Memory pinned by torch's allocator is already mapped (UVA).
+            return t.data_ptr()
+        check(lib().moe_host_register(ctypes.c_void_p(t.data_ptr()), t.numel() * 2, ctypes.byref(dev)),
+              "moe_host_register")
+        self._mapped.append(t)
+        return dev.value
+
+    def release(self) -> None:
+        for t in self._mapped:
+            lib().moe_host_unregister(ctypes.c_void_p(t.data_ptr()))
+        self._mapped.clear()
+
+    def workspace(self, tokens: int) -> torch.Tensor:
+        need = layer_workspace_bytes(tokens, self.experts, self.top_k, self.hidden, self.inner)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._ws
+
+    def slots(self, tokens: int):
+        n = min(self.experts, tokens * self.top_k)
+        if self._slots is None or self._slots[0].shape[0] < n:
+            self._slots = (torch.empty((n, 2 * self.inner, self.hidden), dtype=torch.bfloat16, device=self.device),
+                           torch.empty((n, self.hidden, self.inner), dtype=torch.bfloat16, device=self.device))
+        return self._slots
+
+    def forward(self, x: torch.Tensor, *, route_in=None, weights_in=None, out=None, idx_out=None, scores_out=None,
+                logits_out=None, stage_events=None) -> torch.Tensor:
+        """One layer step on the current stream.  stage_events: optional list of
+        8 torch.cuda.Event recorded at the stage boundaries (see moe_layer_io)."""
+        _cuda_bf16(x, "x")
+        tokens = x.shape[0]
+        _require(x.shape[1] == self.hidden, "x must be [T, H]")
+        if route_in is not None:
+            _require(route_in.dtype == torch.int64 and tuple(route_in.shape) == (tokens, self.top_k)
+                     and route_in.is_contiguous() and route_in.is_cuda, "route_in must be CUDA int64 [T, K]")
+            _require(weights_in is not None and weights_in.dtype == torch.bfloat16
+                     and tuple(weights_in.shape) == (tokens, self.top_k) and weights_in.is_contiguous(),
+                     "weights_in must be CUDA BF16 [T, K]")
+        out = torch.empty_like(x) if out is None else out
+        ws = self.workspace(tokens)
+        io = LayerIO(route_in=_ptr(route_in), weights_in=_ptr(weights_in), idx_out=_ptr(idx_out),
+                     scores_out=_ptr(scores_out), logits_out=_ptr(logits_out))
+        if stage_events is not None:
+            handles = (_p * len(stage_events))(*[e.cuda_event if e is not None else None for e in stage_events])
+            io.stage_events, io.num_stage_events = ctypes.cast(handles, ctypes.POINTER(_p)), len(stage_events)
+        if self.host_gate_up is not None:
+            gs, ds = self.slots(tokens)
+            io.host_gate_up, io.host_down = self._host_dev
+            io.gate_up_slots, io.down_slots, io.max_slots = gs.data_ptr(), ds.data_ptr(), gs.shape[0]
+        check(lib().moe_layer_forward(ctypes.byref(self.w), _ptr(x), tokens, _ptr(out), ctypes.byref(io), _ptr(ws),
+                                      ws.numel(), _stream(x.device)), "moe_layer_forward")
+        return out
+
+    __call__ = forward
+
+
+# ---------------------------------------------------------------- gather ---
+
+def gather_rows(descriptors, destinations, sizes, src, dst, count, *, max_copies, experts, codec, stripes,
+                threads):
+    """Launch the descriptor-driven copy on the current stream (tables are CUDA tensors)."""
+    for name, t, dt in (("descriptors", descriptors, torch.int64), ("destinations", destinations, torch.int64),
+                        ("sizes", sizes, torch.int64), ("src", src, torch.int32), ("dst", dst, torch.int32),
+                        ("count", count, torch.int64)):
+        _require(t.is_cuda and t.dtype == dt and t.is_contiguous(), f"{name} must be a contiguous CUDA {dt} tensor")
+    banks = destinations.numel()
+    check(lib().moe_gather_rows(_ptr(descriptors), _ptr(destinations), _ptr(sizes), _ptr(src), _ptr(dst), _ptr(count),
+                                experts, banks, max_copies, codec, stripes, threads, _stream(destinations.device)),
+          "moe_gather_rows")

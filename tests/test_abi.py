@@ -1,0 +1,62 @@
+"""The C-ABI library loads, exports every entry point include/moe_b200.h
+declares, and rejects bad arguments before touching a GPU (CPU only)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from lightreason_b200 import build, native
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "moe_b200.h"
+
+
+def declared() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(moe_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def so():
+    build.build()
+    return native.lib()
+
+
+def test_every_declared_symbol_is_exported(so):
+    names = declared()
+    assert len(names) >= 10
+    missing = [n for n in names if not hasattr(so, n)]
+    assert not missing, missing
+    assert set(names) == set(native.EXPORTED), "native.py binds a different symbol set than the header declares"
+
+
+def test_version_and_error_channel(so):
+    assert so.moe_version() >= 100
+    rc = so.moe_gather_rows(None, None, None, None, None, None, 1, 1, 1, 0, 1, 33, None)
+    assert rc == native.MOE_EINVAL
+    assert b"null table" in so.moe_last_error()
+    with pytest.raises(ValueError):
+        native.check(rc, "moe_gather_rows")
+
+
+def test_argument_checks_precede_device_use(so):
+    fake = ctypes.c_void_p(16)
+    # threads not a multiple of 32
+    assert so.moe_gather_rows(fake, fake, fake, fake, fake, fake, 1, 1, 1, 0, 1, 33, None) == native.MOE_EINVAL
+    # unknown codec is rejected only after the checks that need no GPU; bad experts first
+    assert so.moe_gather_rows(fake, fake, fake, fake, fake, fake, 0, 1, 1, 0, 1, 32, None) == native.MOE_EINVAL
+    assert so.moe_permute(fake, 4, 8, 2048, fake, fake, fake, fake, fake, fake, None, None) == native.MOE_EINVAL
+    assert so.moe_router_topk(fake, fake, None, None, 1, 3000, 256, 8, fake, fake, None, None, None,
+                              None) == native.MOE_EINVAL
+    assert so.moe_expert_rows(None, None, None, None, 129, None, 0, None) == native.MOE_EINVAL
+
+
+def test_workspace_query_is_host_only(so):
+    small = native.layer_workspace_bytes(1, 256, 8, 2048, 512)
+    big = native.layer_workspace_bytes(4096, 256, 8, 2048, 512)
+    assert 0 < small < big
+    # y for T*K + T routes of 2048 BF16 dominates
+    assert big >= (4096 * 9) * 2048 * 2

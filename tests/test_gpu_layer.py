@@ -1,0 +1,246 @@
+"""Parity of the CUDA layer path against the CPU oracle (GPU only).
+
+Ids and per-expert token orders are compared bit-exactly (tier 1: selection on
+the oracle's own logits; tier 2: end-to-end, where only a near tie may move),
+outputs within max-abs 2e-2 / rel-L2 1e-2 (helpers.assert_close).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from lightreason_b200 import build, native
+from lightreason_b200 import synthetic as S
+from oracle import oracle as O
+from tests.helpers import assert_close, compare_ids, golden_layers, load_golden
+
+pytestmark = pytest.mark.gpu
+
+
+def to_dev(bits: np.ndarray, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).to(dev).view(torch.bfloat16)
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.fixture(scope="module")
+def dev():
+    build.build()
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    native.device_check(0)
+    return torch.device("cuda", 0)
+
+
+class Case:
+    def __init__(self, seed: int, bias: str, dev, *, host_resident: bool = False):
+        self.w = S.layer_weights(seed, bias=bias)
+        self.gu, self.dn = self.w.stacked()
+        for e in range(256):
+            self.w.gate_up[e], self.w.down[e] = self.gu[e], self.dn[e]
+        self.seed = seed
+        d = lambda a: to_dev(a, dev)  # noqa: E731
+        self.router, self.sh = d(self.w.router), [d(self.w.sh_gate), d(self.w.sh_up), d(self.w.sh_down),
+                                                  d(self.w.sh_gate_w)]
+        self.bias = torch.from_numpy(self.w.bias).to(dev) if self.w.bias is not None else None
+        self.gu_dev, self.dn_dev = d(self.gu), d(self.dn)
+        self.layer = native.Layer(router=self.router, gate_up=self.gu_dev, down=self.dn_dev, bias=self.bias,
+                                  shared_gate=self.sh[0], shared_up=self.sh[1], shared_down=self.sh[2],
+                                  shared_gate_w=self.sh[3])
+        self.dev = dev
+
+    def host_layer(self):
+        hg = torch.from_numpy(self.gu.view(np.int16)).view(torch.bfloat16).pin_memory()
+        hd = torch.from_numpy(self.dn.view(np.int16)).view(torch.bfloat16).pin_memory()
+        return native.Layer(router=self.router, bias=self.bias, shared_gate=self.sh[0], shared_up=self.sh[1],
+                            shared_down=self.sh[2], shared_gate_w=self.sh[3], host_gate_up=hg, host_down=hd)
+
+    def run(self, x_bits, layer=None):
+        x = to_dev(x_bits, self.dev)
+        tokens = x.shape[0]
+        idx = torch.empty((tokens, 8), dtype=torch.int64, device=self.dev)
+        sc = torch.empty((tokens, 8), dtype=torch.bfloat16, device=self.dev)
+        lg = torch.empty((tokens, 256), dtype=torch.bfloat16, device=self.dev)
+        out = (layer or self.layer)(x, idx_out=idx, scores_out=sc, logits_out=lg)
+        torch.cuda.synchronize()
+        return bits(out), idx.cpu().numpy(), bits(sc), bits(lg)
+
+    def oracle(self, x_bits):
+        w = self.w
+        return O.moe_layer(x_bits, w.router, w.bias, w.gate_up, w.down, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w)
+
+
+@pytest.fixture(scope="module")
+def case13(dev):
+    return Case(13, "normal", dev)
+
+
+@pytest.fixture(scope="module")
+def case14(dev):
+    return Case(14, "zipf", dev)
+
+
+def test_router_select_tier1_exact(dev, case13):
+    x = S.hidden_states(101, 64)
+    logits = O.linear_bf16(x, case13.w.router)
+    want_idx, want_f32, want_bf16 = O.router_select(logits, case13.w.bias)
+    idx, sf, sb = native.router_select(to_dev(logits, dev), case13.bias)
+    assert np.array_equal(idx.cpu().numpy(), want_idx)
+    np.testing.assert_allclose(sf.cpu().numpy(), want_f32, rtol=2e-6, atol=1e-7)
+    assert_close(bits(sb), want_bf16, max_abs=1e-2, rel_l2=1e-3, what="scores")
+
+
+def test_router_select_exact_ties_take_lower_ids(dev):
+    logits = np.full((3, 256), 0x3F80, dtype=np.uint16)       # all equal
+    logits[1, [5, 9, 200]] = 0x4000                          # three winners, then ties
+    logits[2, ::2] = 0x4000                                  # every even id ties on top
+    idx, _, sb = native.router_select(to_dev(logits, dev), None)
+    got = idx.cpu().numpy()
+    want, _, want_sb = O.router_select(logits, None)
+    assert np.array_equal(got, want)
+    assert got[0].tolist() == list(range(8))
+    assert got[1].tolist() == [5, 9, 200, 0, 1, 2, 3, 4]
+    assert got[2].tolist() == [0, 2, 4, 6, 8, 10, 12, 14]
+
+
+@pytest.mark.parametrize("tokens,experts,top_k", [(1, 256, 8), (16, 256, 8), (333, 256, 8), (4096, 256, 8),
+                                                   (50, 1024, 4), (7, 64, 8)])
+def test_permute_bit_exact(dev, tokens, experts, top_k):
+    rng = np.random.default_rng(tokens * 7 + experts)
+    p = rng.zipf(1.1, size=experts * 4).astype(np.float64)
+    p = p[:experts] / p[:experts].sum()
+    idx = np.stack([rng.choice(experts, size=top_k, replace=False, p=p) for _ in range(tokens)]).astype(np.int64)
+    want = O.permute(idx, experts)
+    off, ptok, pslot, rpos, active, n_active, bad = native.permute(torch.from_numpy(idx).to(dev), experts)
+    torch.cuda.synchronize()
+    assert np.array_equal(off.cpu().numpy(), want[0])
+    assert np.array_equal(ptok.cpu().numpy(), want[1])
+    assert np.array_equal(pslot.cpu().numpy(), want[2])
+    assert np.array_equal(rpos.cpu().numpy(), want[3])
+    n = int(n_active.item())
+    assert active[:n].cpu().numpy().tolist() == sorted(set(idx.reshape(-1).tolist()))
+    assert int(bad.item()) == 0
+
+
+def test_permute_drops_out_of_range_ids(dev):
+    idx = np.array([[3, 1], [-1, 3], [7, 300]], dtype=np.int64)
+    off, ptok, pslot, rpos, active, n_active, bad = native.permute(torch.from_numpy(idx).to(dev), 8)
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 2
+    r = rpos.cpu().numpy()
+    assert r[1, 0] == -1 and r[2, 1] == -1
+    assert off.cpu().numpy().tolist() == [0, 0, 1, 1, 3, 3, 3, 3, 4]
+    # expert 3: (slot 0, token 0) then (slot 1, token 1)
+    assert ptok.cpu().numpy()[1:3].tolist() == [0, 1] and pslot.cpu().numpy()[1:3].tolist() == [0, 1]
+    assert active[:int(n_active.item())].cpu().numpy().tolist() == [1, 3, 7]
+
+
+@pytest.mark.parametrize("tokens", [1, 8, 16, 64])
+def test_layer_matches_oracle(dev, case13, tokens):
+    x = S.hidden_states(200 + tokens, tokens)
+    out, idx, sc, lg = case13.run(x)
+    w_out, w_idx, w_sc, w_lg = case13.oracle(x)
+    z = S.bf16_bits_to_f32(w_lg) + case13.w.bias
+    compare_ids(idx, w_idx, z, slack_ulps=1.0)
+    same = np.all(idx == w_idx, axis=1)
+    assert same.mean() > 0.9
+    assert_close(lg, w_lg, what="logits")
+    assert_close(sc[same], w_sc[same], what="scores")
+    assert_close(out[same], w_out[same], what="layer output")
+
+
+@pytest.mark.parametrize("name", golden_layers())
+def test_layer_matches_transformers_golden(dev, name):
+    g = load_golden(name)
+    case = Case(int(g["seed"]), str(g["bias_kind"]), dev)
+    x = S.hidden_states(int(g["seed"]), int(g["tokens"]))
+    out, idx, sc, lg = case.run(x)
+    z = S.bf16_bits_to_f32(g["logits"]) + case.w.bias
+    compare_ids(idx, g["idx"], z, slack_ulps=1.0)
+    same = np.all(idx == g["idx"], axis=1)
+    assert_close(out[same], g["out"][same], what="layer output vs transformers eager")
+
+
+def test_host_resident_experts_match_hbm_resident(dev, case13):
+    x = S.hidden_states(300, 16)
+    hbm = case13.run(x)
+    host = case13.run(x, layer=case13.host_layer())
+    for a, b in zip(hbm, host):
+        assert np.array_equal(a, b)
+
+
+def test_route_in_is_the_experts_forward(dev, case13):
+    """Qwen3_5MoeExperts.forward semantics: given ids and BF16 weights, no router
+    and no shared expert (edge35b _Layer.forward)."""
+    tokens = 12
+    rng = np.random.default_rng(4)
+    idx = np.stack([rng.choice(256, 8, replace=False) for _ in range(tokens)]).astype(np.int64)
+    wts = S.f32_to_bf16_bits(rng.dirichlet(np.ones(8), size=tokens).astype(np.float32))
+    x = S.hidden_states(301, tokens)
+    out = case13.layer(to_dev(x, dev), route_in=torch.from_numpy(idx).to(dev), weights_in=to_dev(wts, dev))
+    offsets, ptok, _, rpos = O.permute(idx, 256)
+    y = O.experts_by_route(x, case13.w.gate_up, case13.w.down, offsets, ptok, 256)
+    want = O.combine(y, rpos, wts)
+    assert_close(bits(out), want, what="experts forward")
+
+
+def test_layer_prefill_4096_sampled_tokens(dev, case14):
+    """T=4096 with Zipf(1.1) routing: ids and outputs of a token sample against
+    the oracle (a token's output depends on its own row only)."""
+    tokens = 4096
+    x = S.hidden_states(400, tokens)
+    out, idx, sc, lg = case14.run(x)
+    rng = np.random.default_rng(0)
+    sample = np.sort(rng.choice(tokens, 24, replace=False))
+    w_out, w_idx, w_sc, w_lg = case14.oracle(np.ascontiguousarray(x[sample]))
+    z = S.bf16_bits_to_f32(w_lg) + case14.w.bias
+    compare_ids(idx[sample], w_idx, z, slack_ulps=1.0)
+    same = np.all(idx[sample] == w_idx, axis=1)
+    assert_close(out[sample][same], w_out[same], what="prefill output")
+    # every token has 8 distinct ids in range, scores sum to ~1
+    assert (idx >= 0).all() and (idx < 256).all()
+    assert all(len(set(r)) == 8 for r in idx[:512].tolist())
+    np.testing.assert_allclose(S.bf16_bits_to_f32(sc).sum(1), 1.0, atol=3e-2)
+
+
+def test_graph_capture_replays_with_new_routes(dev, case13):
+    tokens = 16
+    x1, x2 = S.hidden_states(500, tokens), S.hidden_states(501, tokens)
+    want2 = case13.run(x2)[0]
+    xs = to_dev(x1, dev)
+    out = torch.empty_like(xs)
+    case13.layer(xs, out=out)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        case13.layer(xs, out=out)
+    xs.copy_(to_dev(x2, dev))
+    graph.replay()
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(out), want2)
+
+
+def test_expert_rows_against_cpu_experts(dev, case13):
+    """moe_expert_rows / moe_expert_block_rows vs edge35b/cpu_experts.c (built
+    from the reference) or, where that was not built, the oracle restatement."""
+    rng = np.random.default_rng(8)
+    experts = rng.choice(256, 8, replace=False)
+    x = S.hidden_states(600, 4)
+    gu = [case13.gu_dev[e] for e in experts]
+    dn = [case13.dn_dev[e] for e in experts]
+    got1 = bits(native.expert_block_rows(gu, dn, to_dev(x[:1], dev)))
+    tok = rng.integers(0, 4, size=8).tolist()
+    got4 = bits(native.expert_block_rows(gu, dn, to_dev(x, dev), token_ids=tok))
+    off = np.arange(9, dtype=np.int32)
+    table_g = {i: case13.gu[e] for i, e in enumerate(experts)}
+    table_d = {i: case13.dn[e] for i, e in enumerate(experts)}
+    want1 = O.experts_by_route(x[:1], table_g, table_d, off, np.zeros(8, np.int32), 8)
+    want4 = O.experts_by_route(x, table_g, table_d, off, np.array(tok, np.int32), 8)
+    if O.ref_experts_lib() is not None:
+        assert np.array_equal(want4, O.ref_expert_block_rows(x, [case13.gu[e] for e in experts],
+                                                             [case13.dn[e] for e in experts], tok))
+    assert_close(got1, want1, what="expert_rows")
+    assert_close(got4, want4, what="expert_block_rows")
