@@ -291,6 +291,9 @@ class Layer:
         io = LayerIO(route_in=_ptr(route_in), weights_in=_ptr(weights_in), idx_out=_ptr(idx_out),
                      scores_out=_ptr(scores_out), logits_out=_ptr(logits_out))
         if stage_events is not None:
+            for e in stage_events:
+                if e is not None and not e.cuda_event:
+                    e.record()  # torch creates the CUDA event lazily on first record
             handles = (_p * len(stage_events))(*[e.cuda_event if e is not None else None for e in stage_events])
             io.stage_events, io.num_stage_events = ctypes.cast(handles, ctypes.POINTER(_p)), len(stage_events)
         if self.host_gate_up is not None:
