@@ -115,6 +115,20 @@ int moe_expert_block_rows(const uint16_t *const *gate_up, const uint16_t *const 
                           int tokens, int experts, void *workspace, size_t workspace_bytes,
                           void *stream);
 
+/* Allocation-free variant of moe_expert_block_rows.  It has no counterpart in
+ * the reference.  It serves callers that hold only device pointers and cannot
+ * allocate device memory (a C/C++ worker in the place of the reference's
+ * cpu_experts.c call, or a server that forbids allocation once it runs): the
+ * [experts, 512] activations live in a 128 KiB array inside the library
+ * instead of a caller workspace.  At most 128 pairs (larger tables are
+ * rejected with MOE_EINVAL); token_ids == NULL means one token (expert_rows).
+ * The first call on each device looks up the array's device address; make it
+ * before any stream capture.  All calls on a device share the array: calls
+ * that can overlap on the GPU race and must be ordered on one stream. */
+int moe_expert_block_rows_noalloc(const uint16_t *const *gate_up, const uint16_t *const *down,
+                                  const uint16_t *input, const int32_t *token_ids,
+                                  uint16_t *output, int tokens, int experts, void *stream);
+
 /* ------------------------------------------------------------------------
  * One MoE layer.  moe_layer_forward replaces Qwen3_5MoeSparseMoeBlock.forward
  * (modeling_qwen3_5_moe.py:781-792: router + shared expert + experts + gate)

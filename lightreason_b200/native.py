@@ -53,6 +53,7 @@ _SIGNATURES = {
     "moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "moe_expert_rows": ([_p, _p, _p, _p, _i, _p, _sz, _p], _i),
     "moe_expert_block_rows": ([_p, _p, _p, _p, _p, _i, _i, _p, _sz, _p], _i),
+    "moe_expert_block_rows_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
     "moe_layer_workspace_bytes": ([_i, _i, _i, _i, _i, _i], _sz),
     "moe_layer_forward": ([ctypes.POINTER(LayerWeights), _p, _i, _p, ctypes.POINTER(LayerIO), _p, _sz, _p], _i),
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
