@@ -174,11 +174,15 @@ typedef struct moe_layer_io {
     int max_slots;
     /* Optional cudaEvent_t handles recorded on `stream` at the stage
      * boundaries: 0 start, 1 router done, 2 permute done, 3 host gather done,
-     * 4 groups resolved, 5 gate/up done, 6 down done, 7 combine done.  NULL
+     * 4 expert plan + token gather done, 5 experts (gate/up and down) done,
+     * 6 = 5, 7 combine done.  NULL
      * entries (or num_stage_events <= i) are skipped.  For live per-kernel
      * timing (the role of the NVTX ranges of edge35b/native_bench.py:30-69). */
     void *const *stage_events;
     int num_stage_events;
+    /* Optional device int32: 0, or nonzero when a bounded wait inside the
+     * expert kernel gave up (the results of that call are then invalid). */
+    int32_t *status;
 } moe_layer_io;
 
 /* Scratch bytes moe_layer_forward needs for `tokens` tokens. */

@@ -27,6 +27,18 @@ int check_launch(const char *where) {
     return err == cudaSuccess ? MOE_OK : cuda_error(err, where);
 }
 
+int sm_count() {
+    static int cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+    if (!cached[device]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        cached[device] = n > 0 ? n : 148;
+    }
+    return cached[device];
+}
+
 int require_sm100() {
     int device = 0;
     LRB_CUDA(cudaGetDevice(&device));

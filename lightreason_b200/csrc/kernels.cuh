@@ -37,6 +37,40 @@ struct ParamGroups {
     __device__ __forceinline__ int token(int p) const { return tokens[p]; }
 };
 
+// Grouped tensor-core experts (grouped.cu).
+struct GroupedGroup {
+    int32_t weight;  // index into the expert bank (expert id or HBM slot); -1 = shared expert
+    int32_t begin;   // first route position
+    int32_t count;   // routes
+    int32_t ntiles;  // token tiles of width BN
+};
+struct GroupedPlan {
+    int32_t num_groups, items1, items2, work, error, pad[3];
+};
+struct GroupedLaunch {
+    const uint16_t *gate_up, *down;  // banks: [bank_experts, 2I, H], [bank_experts, H, I]
+    int64_t gate_up_stride, down_stride;
+    int bank_experts;
+    const uint16_t *sh_gate, *sh_up, *sh_down;  // shared expert (may be null)
+    const uint16_t *xs;                          // [rows, H] tokens in route order
+    uint16_t *act, *y;                           // [rows, I], [rows, H]
+    int rows;
+    const GroupedGroup *groups;
+    GroupedPlan *plan;
+    const int32_t *off1, *off2;
+    int32_t *done1;
+    int hidden, inner, bn, ctas;
+};
+int grouped_bn_for(int tokens);
+int launch_grouped_plan(const int32_t *active, const int32_t *num_active, const int32_t *offsets, bool use_slots,
+                        bool shared, int routes, int tokens, int bn, int hidden, int inner, GroupedGroup *groups,
+                        GroupedPlan *plan, int32_t *off1, int32_t *off2, int32_t *done1, int32_t *route_token,
+                        cudaStream_t stream);
+int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
+                         int routes, int shared_rows, int hidden, uint16_t *xs, cudaStream_t stream);
+int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
+int sm_count();
+
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,

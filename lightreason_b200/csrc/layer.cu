@@ -17,8 +17,8 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 // Byte offsets of the scratch arrays inside the caller's workspace.
 struct Layout {
-    size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, act, y,
-        total;
+    size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, plan, off1,
+        off2, done1, xs, act, y, total;
 };
 
 Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
@@ -40,7 +40,12 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.route_pos = take(R * 4);
     L.active = take(E * 4);
     L.counters = take(4 * 4);  // num_active, bad_routes, num_groups, slot overflow
-    L.groups = take((E + 1) * sizeof(Group));
+    L.groups = take((E + 1) * sizeof(GroupedGroup));
+    L.plan = take(sizeof(GroupedPlan));
+    L.off1 = take((E + 2) * 4);
+    L.off2 = take((E + 2) * 4);
+    L.done1 = take((E + 1) * 4);
+    L.xs = take((R + T) * hidden * 2);
     L.act = take((R + T) * inner * 2);
     L.y = take((R + T) * hidden * 2);
     L.total = o;
@@ -53,30 +58,6 @@ T *at(void *base, size_t offset) {
 }
 
 }  // namespace
-
-// Resolve the weights of each active expert (ascending id) and append the
-// shared expert as the last group.
-__global__ void build_groups_kernel(const int32_t *__restrict__ active, const int32_t *__restrict__ num_active,
-                                    const int32_t *__restrict__ offsets, const uint16_t *gate_up,
-                                    const uint16_t *down, int64_t gate_up_stride, int64_t down_stride,
-                                    int use_slots, int hidden, int inner, const uint16_t *sh_gate,
-                                    const uint16_t *sh_up, const uint16_t *sh_down, int routes, int tokens,
-                                    Group *__restrict__ groups, int32_t *__restrict__ num_groups,
-                                    int32_t *__restrict__ route_token) {
-    const int n = *num_active;
-    for (int g = threadIdx.x; g < n; g += blockDim.x) {
-        const int e = active[g];
-        const int64_t w = use_slots ? g : e;
-        const uint16_t *gu = gate_up + w * gate_up_stride;
-        groups[g] = Group{gu, gu + static_cast<size_t>(inner) * hidden, down + w * down_stride, offsets[e],
-                          offsets[e + 1] - offsets[e]};
-    }
-    if (sh_gate) {
-        if (threadIdx.x == 0) groups[n] = Group{sh_gate, sh_up, sh_down, routes, tokens};
-        for (int t = threadIdx.x; t < tokens; t += blockDim.x) route_token[routes + t] = t;
-    }
-    if (threadIdx.x == 0) *num_groups = n + (sh_gate != nullptr);
-}
 
 // Copy every active expert's gate_up and down rows from the mapped host banks
 // into HBM slot g (g-th active expert).  Grid (stripes, 2 banks, max_slots);
@@ -154,9 +135,15 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     if (tokens == 0) return MOE_OK;
     if (int rc = require_sm100()) return rc;
     cudaStream_t s = as_stream(stream);
+    // Under stream capture an ordinary record is only a dependency node; an
+    // external record node keeps the event usable for timing each replay.
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (io->stage_events) LRB_CUDA(cudaStreamIsCapturing(s, &capturing));
     auto mark = [&](int i) -> int {
         if (io->stage_events && i < io->num_stage_events && io->stage_events[i])
-            LRB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(io->stage_events[i]), s));
+            LRB_CUDA(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(io->stage_events[i]), s,
+                                              capturing == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
+                                                                                         : cudaEventRecordDefault));
         return MOE_OK;
     };
     if (int rc = mark(0)) return rc;
@@ -199,17 +186,41 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         dn_str = static_cast<int64_t>(H) * I;
     }
     if (int rc = mark(3)) return rc;
-    Group *groups = at<Group>(ws, L.groups);
-    build_groups_kernel<<<1, 256, 0, s>>>(active, counters + 0, offsets, gu_base, dn_base, gu_str, dn_str, staged,
-                                          H, I, shared ? w->shared_gate : nullptr, w->shared_up, w->shared_down, R,
-                                          tokens, groups, counters + 2, route_token);
-    LRB_LAUNCHED("build_groups_kernel");
+    const int bn = grouped_bn_for(tokens);
+    GroupedGroup *groups = at<GroupedGroup>(ws, L.groups);
+    GroupedPlan *plan = at<GroupedPlan>(ws, L.plan);
+    if (int rc = launch_grouped_plan(active, counters + 0, offsets, staged, shared, R, tokens, bn, H, I, groups, plan,
+                                     at<int32_t>(ws, L.off1), at<int32_t>(ws, L.off2), at<int32_t>(ws, L.done1),
+                                     route_token, s))
+        return rc;
+    uint16_t *xs = at<uint16_t>(ws, L.xs), *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
+    if (int rc = launch_gather_tokens(x, route_token, offsets, E, R, shared ? tokens : 0, H, xs, s)) return rc;
     if (int rc = mark(4)) return rc;
-    uint16_t *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
-    const DeviceGroups src{groups, counters + 2, route_token};
-    cudaEvent_t mid = io->stage_events && io->num_stage_events > 5
-                          ? static_cast<cudaEvent_t>(io->stage_events[5]) : nullptr;
-    if (int rc = launch_experts(src, max_groups + (shared ? 1 : 0), x, H, I, act, y, s, mid)) return rc;
+    GroupedLaunch GL{};
+    GL.gate_up = gu_base;
+    GL.down = dn_base;
+    GL.gate_up_stride = gu_str;
+    GL.down_stride = dn_str;
+    GL.bank_experts = staged ? io->max_slots : E;
+    GL.sh_gate = shared ? w->shared_gate : nullptr;
+    GL.sh_up = shared ? w->shared_up : nullptr;
+    GL.sh_down = shared ? w->shared_down : nullptr;
+    GL.xs = xs;
+    GL.act = act;
+    GL.y = y;
+    GL.rows = R + (shared ? tokens : 0);
+    GL.groups = groups;
+    GL.plan = plan;
+    GL.off1 = at<int32_t>(ws, L.off1);
+    GL.off2 = at<int32_t>(ws, L.off2);
+    GL.done1 = at<int32_t>(ws, L.done1);
+    GL.hidden = H;
+    GL.inner = I;
+    GL.bn = bn;
+    GL.ctas = sm_count();
+    if (int rc = launch_grouped(GL, s)) return rc;
+    if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+    if (int rc = mark(5)) return rc;
     if (int rc = mark(6)) return rc;
     if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
                                 sig, out, s))

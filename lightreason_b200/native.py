@@ -39,7 +39,8 @@ class LayerIO(ctypes.Structure):
 
     _fields_ = [("route_in", _p), ("weights_in", _p), ("idx_out", _p), ("scores_out", _p), ("logits_out", _p),
                 ("host_gate_up", _p), ("host_down", _p), ("gate_up_slots", _p), ("down_slots", _p),
-                ("max_slots", _i), ("stage_events", ctypes.POINTER(_p)), ("num_stage_events", _i)]
+                ("max_slots", _i), ("stage_events", ctypes.POINTER(_p)), ("num_stage_events", _i),
+                ("status", _p)]
 
 
 _SIGNATURES = {
