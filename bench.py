@@ -19,8 +19,8 @@ activations.
   * cpu_baseline: the reference's own CPU path (edge35b/cpu_experts.c built from
            the reference sources into oracle/_ref, torch-CPU router / shared
            expert / ordered combine) on a bounded sample of the same workload.
-L2 is flushed (256 MiB memset) between timed steps, outside each step's
-CUDA-event window.
+L2 is flushed between timed steps by reading a 256 MiB buffer (twice the L2),
+outside each step's CUDA-event window.
 
 --impl reference times that CPU path alone as the reference arm.
 --gpus N (under torchrun) runs one replica of the layer per rank.
@@ -50,10 +50,11 @@ HIDDEN, INNER, EXPERTS, TOP_K = S.HIDDEN, S.INNER, S.EXPERTS, S.TOP_K
 GATE_UP_BYTES = 2 * INNER * HIDDEN * 2       # 4,194,304 B per expert
 DOWN_BYTES = HIDDEN * INNER * 2              # 2,097,152 B per expert
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES    # 6,291,456 B
-STAGES = ("router", "permute", "gather", "plan", "experts", "unused", "combine")
-KERNEL_NAMES = {"router": "router_logits_kernel+router_select_kernel", "permute": "permute_kernel",
-                "gather": "stage_experts_kernel", "plan": "grouped_plan_kernel+gather_tokens_kernel",
-                "experts": "swiglu_grouped_kernel (tcgen05)", "unused": "-", "combine": "combine_kernel"}
+STAGES = ("router", "route", "gather", "xs", "experts", "unused", "unused2")
+KERNEL_NAMES = {"router": "router_split_kernel | router_logits_kernel",
+                "route": "route_decode_kernel | router_select+permute+grouped_plan kernels",
+                "gather": "stage_experts_kernel", "xs": "gather_tokens_kernel",
+                "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down + combine)", "unused": "-", "unused2": "-"}
 
 CONFIGS = {
     0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
@@ -196,7 +197,7 @@ def timed_steps(run_step, steps, warmup, flush, world, stage_events=None):
     step and stage events inside the graph), so the window holds device work
     only; the flush is launched eagerly between replays."""
     for i in range(warmup):
-        flush.zero_()
+        flush()
         run_step(i, None)
     torch.cuda.synchronize()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
@@ -222,7 +223,7 @@ def timed_steps(run_step, steps, warmup, flush, world, stage_events=None):
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for i in range(steps):
-        flush.zero_()
+        flush()
         ev[i][0].record()
         graphs[i].replay()
         ev[i][1].record()
@@ -327,7 +328,14 @@ def run_ours(args, cfg, world, rank, local):
     out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
     out_host = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory()
     idx_buf = [torch.empty((tokens, TOP_K), dtype=torch.int64, device=dev) for _ in range(pool)]
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    # L2 flush between steps: read a 256 MiB buffer (twice the L2).  Reading
+    # evicts every line without leaving ~126 MB of dirty lines behind, whose
+    # write-back would otherwise land inside the next timed step.
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    flush_out = torch.empty((), dtype=torch.float32, device=dev)
+
+    def flush():
+        torch.sum(flush_buf, 0, out=flush_out)
     log(f"[bench] setup {time.perf_counter() - t_setup:.1f}s, tokens={tokens}")
 
     def hbm_step(i, stage):
@@ -367,10 +375,10 @@ def run_ours(args, cfg, world, rank, local):
     algo = {
         # grouped kernel: every selected expert's weights (+ shared) once, the
         # routed token rows in, activations out and back in, per-route outputs out
-        "experts": [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
-                    for u in u_per_step],
+        # + the combine: per-route outputs read back, the layer output written
+        "experts": [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + 2 * rows * HIDDEN * 2
+                    + tokens * HIDDEN * 2 for u in u_per_step],
         "router": [EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 2 + tokens * EXPERTS * 2] * len(used),
-        "combine": [(routes + tokens) * HIDDEN * 2 + tokens * HIDDEN * 2] * len(used),
     }
     totals = {k: sum(v) for k, v in stage_ms.items()}
     dominant = max(totals, key=totals.get)
@@ -383,7 +391,7 @@ def run_ours(args, cfg, world, rank, local):
     layer_bytes = [u * EXPERT_BYTES + EXPERT_BYTES + EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 4
                    for u in u_per_step]
     layer_gbs = statistics.mean(b / (m / 1e3) / 1e9 for b, m in zip(layer_bytes, ms))
-    launches_per_step = 7  # router x2, permute, plan, token gather, grouped experts, combine
+    launches_per_step = 4 if tokens <= 64 else 7  # decode: router_split, route_decode, gather, grouped
     result = {
         "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -394,7 +402,7 @@ def run_ours(args, cfg, world, rank, local):
                    "experts": EXPERTS, "top_k": TOP_K, "shared_expert": True,
                    "distinct_experts_per_step": round(u_mean, 2),
                    "parallelism": "single-gpu" if world == 1 else f"replicas{world}",
-                   "l2": "flushed (256 MiB memset) between timed steps, outside each step's event window"},
+                   "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window"},
         "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dominant], "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "moe_b200.h"
 
 namespace lrb {
@@ -57,6 +59,14 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 __device__ __forceinline__ float sigmoid_f32(float g) { return 1.0f / (1.0f + expf(-g)); }
 
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// while its predecessor in the stream still runs; it must call
+// grid_dependency_wait() before touching anything the predecessor writes.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependency_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // -------------------------------------------------------- host status ----
 int set_error(int status, const char *fmt, ...);
 int cuda_error(cudaError_t err, const char *where);
@@ -64,6 +74,24 @@ int check_launch(const char *where);
 int require_sm100();
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char *name,
+               Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (err != cudaSuccess) return cuda_error(err, name);
+    return MOE_OK;
+}
 
 }  // namespace lrb
 

@@ -1,26 +1,35 @@
-// Grouped SwiGLU experts on the 5th-generation tensor cores.
+// Grouped SwiGLU experts and the ordered combine on the 5th-generation tensor
+// cores, in one persistent launch.
 //
-// One persistent launch computes, for every active expert group g (routed
-// experts in ascending id, then the shared expert):
-//   phase 1  act[p, :]  = bf16(bf16(silu(bf16(x_p . Wg))) * bf16(x_p . Wu))
-//   phase 2  y[p, :]    = bf16(act_p . Wd)
-// for the routes p of the group (modeling_qwen3_5_moe.py:745-748 rounding
-// points).  The weights are the M = 128 operand (rows of gate/up/down), the
-// group's routed tokens the N operand ("swap AB"), so decode widths (a handful
-// of tokens per expert) and prefill widths (hundreds) use the same tiles.
+// For every active expert group g (routed experts in ascending id, then the
+// shared expert) and its routes p:
+//   phase 1  act[p, :] = bf16(bf16(silu(bf16(x_p . Wg))) * bf16(x_p . Wu))
+//   phase 2  y[p, :]   = bf16(act_p . Wd)
+// and for every token t (phase 3, the ordered combine):
+//   out[t] = bf16(acc + bf16(sig_t * y[shared row t])) after
+//   acc = bf16(acc + bf16(y_p * w_p)) over t's routes in ascending expert id
+// (modeling_qwen3_5_moe.py:745-750, :788-790; edge35b/fused_experts.py:27-37).
+// The weights are the M = 128 operand (rows of gate/up/down) and the group's
+// routed tokens the N operand ("swap AB"), so decode widths (a handful of
+// tokens per expert) and prefill widths (hundreds) share one tile shape.
 //
-// Work items: phase-1 (group, 128-row block of gate+up, token tile) and
-// phase-2 (group, 128-row block of down, token tile), handed out in that order
-// from a device counter.  A phase-2 item waits (bounded) until every phase-1
-// item of its group has published its activations; phase-1 items never wait,
-// so the queue cannot deadlock.
+// Work items, handed out in this order from a device counter:
+//   phase 1  (group, 128-row block of gate+up, token tile, K split)
+//   phase 2  (group, 128-row block of down, token tile)
+//   phase 3  (token, 1024-column half)
+// A phase-2 item waits until its group's activations are published, a phase-3
+// item until the outputs of all of its token's groups are; phase-1 items wait
+// on nothing, so the queue cannot deadlock.  When few experts are active
+// (small T) the K dimension of phase 1 is split so that every SM streams
+// weights; the last split of a tile sums the FP32 partials in split order, so
+// results do not depend on timing.
 //
 // Per CTA (192 threads, one CTA per SM): warp 0 issues TMA loads of 64-wide K
 // slices (128B swizzle) into a ring of stages; warp 1 allocates TMEM and issues
 // tcgen05.mma (M=128, N=BN, K=16) into a double-buffered FP32 accumulator;
-// warps 2-5 read the accumulator back with tcgen05.ld and write BF16 results.
-// Every wait is bounded (globaltimer); on timeout the CTA raises the plan's
-// error word, drains its own TMA and MMA work and returns.
+// warps 2-5 read the accumulator with tcgen05.ld, write BF16 results and run
+// the combine.  Every wait is bounded (globaltimer); on timeout the CTA raises
+// the plan's error word, drains its own TMA and MMA work and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -29,6 +38,7 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "plan.cuh"
 #include "sm100.cuh"
 
 namespace lrb {
@@ -40,12 +50,8 @@ constexpr int kBK = 64;                 // K per stage: one 128-byte swizzle ato
 constexpr int kATile = kBM * kBK * 2;   // 16 KiB
 constexpr int kThreads = 192;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any legal wait
-
-__device__ __forceinline__ uint64_t now_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
+constexpr int kCombineCols = 1024;       // columns per phase-3 item (128 threads x 8)
+constexpr int kSmemGroups = 257;         // plans up to this many groups are staged in shared memory
 
 }  // namespace
 
@@ -55,7 +61,8 @@ struct GroupedShape {
     static constexpr int kStage = 2 * kATile + kBTile;
     static constexpr int kStages = BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
     static constexpr int kTmemCols = 4 * BN < 32 ? 32 : 4 * BN;  // two buffers of (gate, up)
-    static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 512 /*barriers*/;
+    static constexpr int kPlanBytes = 2 * (kSmemGroups + 1) * 4 + kSmemGroups * 16;
+    static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 512 /*barriers*/ + kPlanBytes;
 };
 
 struct GroupedSmemTail {
@@ -68,13 +75,24 @@ struct GroupedSmemTail {
 struct GroupedParams {
     const GroupedGroup *groups;
     GroupedPlan *plan;
-    const int32_t *off1;  // [num_groups + 1] phase-1 item prefix
-    const int32_t *off2;  // [num_groups + 1] phase-2 item prefix
-    int32_t *done1;       // [num_groups] finished phase-1 items
-    uint16_t *act;        // [rows, inner]
-    uint16_t *y;          // [rows, hidden]
-    int hidden, inner;
+    const int32_t *off1, *off2;   // [num_groups + 1] item prefixes of phases 1 and 2
+    int32_t *done1, *done2;       // [num_groups] published epilogue-warp results
+    int32_t *split_cnt;           // [phase-1 tiles * 4] arrivals of K splits
+    float *part;                  // [phase-1 tiles, ks, 2, BN, 128] FP32 partials
+    uint16_t *act, *y, *out;      // [rows, I], [rows, H], [T, H]
+    const int32_t *route_pos;     // [T, K]
+    const int64_t *idx;           // [T, K]
+    const uint16_t *scores;       // [T, K] BF16
+    const uint16_t *sig;          // [T] BF16 or null (no shared expert)
+    const int32_t *group_of_expert;  // [E]
+    int tokens, top_k, hidden, inner, ks;
 };
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort) {
     if (sm100::mbar_try_wait(bar, parity)) return true;
@@ -89,6 +107,17 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     }
 }
 
+// Bounded wait until *counter >= need (acquire).  false on timeout/abort.
+__device__ __forceinline__ bool wait_count(const int32_t *counter, int need, volatile int *abort) {
+    if (sm100::ld_acquire(counter) >= need) return true;
+    const uint64_t t0 = now_ns();
+    while (sm100::ld_acquire(counter) < need) {
+        if (*abort || now_ns() - t0 > kWaitNs) return false;
+        __nanosleep(64);
+    }
+    return true;
+}
+
 __device__ __forceinline__ int find_group(const int32_t *off, int n, int item) {
     int lo = 0, hi = n;  // largest g with off[g] <= item
     while (hi - lo > 1) {
@@ -100,25 +129,38 @@ __device__ __forceinline__ int find_group(const int32_t *off, int n, int item) {
 }
 
 struct ItemPos {
-    int phase, g, mb, nt;
+    int phase, g, mb, nt, ks, tile;  // tile: phase-1 tile index (for split partials)
 };
 
-__device__ __forceinline__ ItemPos decode_item(const GroupedParams &P, int n_groups, int items1, int item, int mb1,
-                                               int mb2) {
-    ItemPos r;
+// off1/off2/groups point at the shared-memory copy of the plan (or at the
+// global one when it is too large to stage).
+struct PlanView {
+    const int32_t *off1, *off2;
+    const GroupedGroup *groups;
+};
+
+__device__ __forceinline__ ItemPos decode_item(const GroupedParams &P, const PlanView &V, int n_groups, int items1,
+                                               int items2, int item, int mb1, int mb2) {
+    ItemPos r{};
     if (item < items1) {
         r.phase = 1;
-        r.g = find_group(P.off1, n_groups, item);
-        const int local = item - P.off1[r.g];
-        r.mb = local % mb1;
-        r.nt = local / mb1;
-    } else {
+        r.g = find_group(V.off1, n_groups, item);
+        const int local = item - V.off1[r.g];
+        r.ks = local % P.ks;
+        const int rest = local / P.ks;
+        r.mb = rest % mb1;
+        r.nt = rest / mb1;
+        r.tile = V.off1[r.g] / P.ks + rest;
+    } else if (item < items1 + items2) {
         const int j = item - items1;
         r.phase = 2;
-        r.g = find_group(P.off2, n_groups, j);
-        const int local = j - P.off2[r.g];
+        r.g = find_group(V.off2, n_groups, j);
+        const int local = j - V.off2[r.g];
         r.mb = local % mb2;
         r.nt = local / mb2;
+    } else {
+        r.phase = 3;
+        r.g = item - items1 - items2;  // token * halves + half
     }
     return r;
 }
@@ -134,12 +176,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     GroupedSmemTail *tail = reinterpret_cast<GroupedSmemTail *>(smem + S::kStages * S::kStage);
     volatile int *abort = &tail->abort;
-
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_groups = P.plan->num_groups;
-    const int items1 = P.plan->items1, total = items1 + P.plan->items2;
-    const int mb1 = P.inner / kBM, mb2 = P.hidden / kBM;
 
+    // Prologue (overlaps the previous kernel under programmatic launch).
     if (threadIdx.x == 0) {
         for (int s = 0; s < S::kStages; ++s) {
             sm100::mbar_init(&tail->full[s], 1);
@@ -160,8 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0 && lane == 0) {
         sm100::tma_prefetch_map(&tm_gu);
         sm100::tma_prefetch_map(&tm_dn);
-        sm100::tma_prefetch_map(&tm_x);
-        sm100::tma_prefetch_map(&tm_act);
+        sm100::tma_prefetch_map(&tm_sg);
+        sm100::tma_prefetch_map(&tm_su);
+        sm100::tma_prefetch_map(&tm_sd);
     }
     if (warp == 1) {
         sm100::tmem_alloc(&tail->tmem_base, S::kTmemCols);
@@ -171,6 +211,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     sm100::tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
+    grid_dependency_wait();  // routing and token gather are complete from here on
+    grid_dependency_trigger();
+
+    const int n_groups = P.plan->num_groups;
+    const int items1 = P.plan->items1, items2 = P.plan->items2;
+    const int total = items1 + items2 + P.plan->items3;
+    const int mb1 = P.inner / kBM, mb2 = P.hidden / kBM;
+    // Stage the plan in shared memory: every item decode then costs a few
+    // shared loads instead of a chain of dependent global ones.
+    PlanView V{P.off1, P.off2, P.groups};
+    if (n_groups <= kSmemGroups) {
+        int32_t *s_off1 = reinterpret_cast<int32_t *>(reinterpret_cast<uint8_t *>(tail) + 512);
+        int32_t *s_off2 = s_off1 + kSmemGroups + 1;
+        GroupedGroup *s_groups = reinterpret_cast<GroupedGroup *>(s_off2 + kSmemGroups + 1);
+        for (int i = threadIdx.x; i <= n_groups; i += blockDim.x) {
+            s_off1[i] = P.off1[i];
+            s_off2[i] = P.off2[i];
+            if (i < n_groups) s_groups[i] = P.groups[i];
+        }
+        V = PlanView{s_off1, s_off2, s_groups};
+    }
+    __syncthreads();
 
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
@@ -178,41 +240,50 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, sphase = 0;
             uint32_t issued_parity[8];
             bool issued[8] = {false, false, false, false, false, false, false, false};
+            int next = atomicAdd(&P.plan->work, 1);
             for (int it = 0;; ++it) {
-                int item = atomicAdd(&P.plan->work, 1);
+                int item = next;
                 if (item >= total) item = -1;
+                else next = atomicAdd(&P.plan->work, 1);  // in flight while this item streams
                 const int slot = it & 3;
                 if (!wait_bar(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort)) break;
                 tail->item[slot] = item;
                 sm100::mbar_arrive(&tail->ifull[slot]);
                 if (item < 0) break;
-                const ItemPos ip = decode_item(P, n_groups, items1, item, mb1, mb2);
-                const GroupedGroup G = P.groups[ip.g];
-                if (ip.phase == 2) {
-                    // every phase-1 item of the group publishes once per epilogue warp
-                    const int need = 4 * mb1 * G.ntiles;
-                    const uint64_t t0 = now_ns();
-                    bool ok = true;
-                    while (sm100::ld_acquire(&P.done1[ip.g]) < need) {
-                        if (*abort || now_ns() - t0 > kWaitNs) {
-                            ok = false;
-                            break;
-                        }
-                        __nanosleep(100);
-                    }
-                    if (!ok) {
-                        *abort = 1;
-                        atomicExch(&P.plan->error, 2);
-                        break;
-                    }
-                    sm100::fence_proxy_async_global();
-                }
-                const int kblocks = (ip.phase == 1 ? P.hidden : P.inner) / kBK;
+                const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
+                if (ip.phase == 3) continue;  // combine: no operand loads
+                const GroupedGroup G = V.groups[ip.g];
+                const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
+                const int kb0 = ip.phase == 1 ? ip.ks * kspan : 0;
                 const uint32_t bytes = (ip.phase == 1 ? 2 * kATile : kATile) + BN * kBK * 2;
                 const int row0 = ip.mb * kBM;
                 const int tok0 = G.begin + ip.nt * BN;
+                // Phase 2 streams its down-weight tiles right away and issues the
+                // activation tiles only once the group's phase 1 has published
+                // them (every phase-1 tile once per epilogue warp).
+                bool dep_ok = ip.phase == 1;
+                const int need = 4 * mb1 * G.ntiles;
+                int pending[8];
+                int n_pending = 0;
                 bool ok = true;
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = kb0; kb < kb0 + kspan; ++kb) {
+                    if (!dep_ok && n_pending > 0 && !sm100::mbar_try_wait(&tail->empty[stage], sphase ^ 1)) {
+                        // out of free stages: the earlier stages need their activation tiles
+                        if (!wait_count(&P.done1[ip.g], need, abort)) {
+                            *abort = 1;
+                            atomicExch(&P.plan->error, 2);
+                            ok = false;
+                            break;
+                        }
+                        sm100::fence_proxy_async_global();
+                        dep_ok = true;
+                        for (int j = 0; j < n_pending; ++j) {
+                            const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
+                            sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps], pk * kBK,
+                                               tok0);
+                        }
+                        n_pending = 0;
+                    }
                     if (!wait_bar(&tail->empty[stage], sphase ^ 1, abort)) {
                         ok = false;
                         break;
@@ -233,13 +304,39 @@ __global__ void __launch_bounds__(kThreads, 1)
                     } else {
                         if (G.weight >= 0) sm100::tma_load_3d(st, &tm_dn, fb, k0, row0, G.weight);
                         else sm100::tma_load_2d(st, &tm_sd, fb, k0, row0);
-                        sm100::tma_load_2d(st + 2 * kATile, &tm_act, fb, k0, tok0);
+                        if (!dep_ok && sm100::ld_acquire(&P.done1[ip.g]) >= need) {
+                            sm100::fence_proxy_async_global();
+                            dep_ok = true;
+                            for (int j = 0; j < n_pending; ++j) {
+                                const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
+                                sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps],
+                                                   pk * kBK, tok0);
+                            }
+                            n_pending = 0;
+                        }
+                        if (dep_ok) sm100::tma_load_2d(st + 2 * kATile, &tm_act, fb, k0, tok0);
+                        else pending[n_pending++] = stage | (kb << 8);
                     }
                     issued[stage] = true;
                     issued_parity[stage] = sphase;
                     if (++stage == S::kStages) {
                         stage = 0;
                         sphase ^= 1;
+                    }
+                }
+                if (ok && n_pending > 0) {
+                    if (!wait_count(&P.done1[ip.g], need, abort)) {
+                        *abort = 1;
+                        atomicExch(&P.plan->error, 2);
+                        ok = false;
+                    } else {
+                        sm100::fence_proxy_async_global();
+                        for (int j = 0; j < n_pending; ++j) {
+                            const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
+                            sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps],
+                                               pk * kBK, tok0);
+                        }
+                        n_pending = 0;
                     }
                 }
                 if (!ok) break;
@@ -267,14 +364,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int item = tail->item[slot];
                 sm100::mbar_arrive(&tail->iempty[slot]);
                 if (item < 0) break;
-                const ItemPos ip = decode_item(P, n_groups, items1, item, mb1, mb2);
-                const int kblocks = (ip.phase == 1 ? P.hidden : P.inner) / kBK;
+                const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
+                if (ip.phase == 3) continue;
+                const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
                 const int buf = acc & 1;
                 if (!wait_bar(&tail->tempty[buf], ((acc >> 1) & 1) ^ 1, abort)) break;
                 sm100::tc_fence_after();
                 const uint32_t d_gate = tmem + buf * 2 * BN, d_up = d_gate + BN;
                 bool ok = true;
-                for (int kb = 0; kb < kblocks; ++kb) {
+                for (int kb = 0; kb < kspan; ++kb) {
                     if (!wait_bar(&tail->full[stage], sphase, abort)) {
                         ok = false;
                         break;
@@ -310,8 +408,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
         }
     } else {
-        // ----------------------------------------------------------- epilogue
-        const int q = warp & 3;  // TMEM lane quadrant this warp may read
+        // ------------------------------------------------- epilogue + combine
+        const int q = warp & 3;           // TMEM lane quadrant this warp may read
+        const int et = threadIdx.x - 64;  // 0..127
         int acc = 0;
         for (int it = 0;; ++it) {
             const int slot = it & 3;
@@ -320,8 +419,87 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive(&tail->iempty[slot]);
             if (item < 0) break;
-            const ItemPos ip = decode_item(P, n_groups, items1, item, mb1, mb2);
-            const GroupedGroup G = P.groups[ip.g];
+            const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
+
+            if (ip.phase == 3) {
+                const int halves = P.hidden / kCombineCols;
+                const int t = ip.g / halves, c = (ip.g % halves) * kCombineCols + et * 8;
+                int pos[32];
+                float wt[32];
+                bool ok = true;
+                for (int k = 0; k < P.top_k; ++k) {
+                    const size_t o = static_cast<size_t>(t) * P.top_k + k;
+                    pos[k] = P.route_pos[o];
+                    wt[k] = bf2f(P.scores[o]);
+                }
+                // Every route row and shared row exists once all phase-2 items
+                // (4 epilogue warps each) have published.
+                if (lane == 0) ok = wait_count(&P.plan->done2_total, 4 * items2, abort);
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) {
+                    *abort = 1;
+                    atomicExch(&P.plan->error, 3);
+                    break;
+                }
+                __threadfence();
+                for (int a = 1; a < P.top_k; ++a) {
+                    for (int b = a; b > 0 && pos[b] < pos[b - 1]; --b) {
+                        const int tp = pos[b];
+                        pos[b] = pos[b - 1];
+                        pos[b - 1] = tp;
+                        const float tw = wt[b];
+                        wt[b] = wt[b - 1];
+                        wt[b - 1] = tw;
+                    }
+                }
+                // Issue every row load first, then the ordered BF16 sums.
+                uint4 shv = make_uint4(0, 0, 0, 0);
+                if (P.sig) {
+                    const int prow = V.groups[n_groups - 1].begin + t;
+                    shv = __ldcg(reinterpret_cast<const uint4 *>(P.y + static_cast<size_t>(prow) * P.hidden + c));
+                }
+                float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (int k0 = 0; k0 < P.top_k; k0 += 8) {
+                    uint4 v[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int k = k0 + j;
+                        v[j] = make_uint4(0, 0, 0, 0);
+                        if (k < P.top_k && pos[k] >= 0)
+                            v[j] = __ldcg(
+                                reinterpret_cast<const uint4 *>(P.y + static_cast<size_t>(pos[k]) * P.hidden + c));
+                    }
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int k = k0 + j;
+                        if (k >= P.top_k || pos[k] < 0) continue;
+                        const uint32_t vw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            o8[2 * h] = rbf(o8[2 * h] + rbf(bf16_lo(vw[h]) * wt[k]));
+                            o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(bf16_hi(vw[h]) * wt[k]));
+                        }
+                    }
+                }
+                if (P.sig) {
+                    const float sg = bf2f(P.sig[t]);
+                    const uint32_t vw[4] = {shv.x, shv.y, shv.z, shv.w};
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        o8[2 * h] = rbf(o8[2 * h] + rbf(sg * bf16_lo(vw[h])));
+                        o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(sg * bf16_hi(vw[h])));
+                    }
+                }
+                uint4 o;
+                o.x = pack_bf16x2(o8[0], o8[1]);
+                o.y = pack_bf16x2(o8[2], o8[3]);
+                o.z = pack_bf16x2(o8[4], o8[5]);
+                o.w = pack_bf16x2(o8[6], o8[7]);
+                *reinterpret_cast<uint4 *>(P.out + static_cast<size_t>(t) * P.hidden + c) = o;
+                continue;
+            }
+
+            const GroupedGroup G = V.groups[ip.g];
             const int buf = acc & 1;
             if (!wait_bar(&tail->tfull[buf], (acc >> 1) & 1, abort)) break;
             __syncwarp();
@@ -330,7 +508,45 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int p0 = G.begin + ip.nt * BN;
             const int nvalid = min(BN, G.count - ip.nt * BN);
             const uint32_t t_gate = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 2 * BN;
-            if (ip.phase == 1) {
+            if (ip.phase == 1 && P.ks > 1) {
+                // Write this split's FP32 partials; the last split of the tile
+                // sums all of them in split order and writes the activations.
+                float *mine = P.part + (static_cast<size_t>(ip.tile) * P.ks + ip.ks) * 2 * BN * kBM;
+#pragma unroll
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float g[16], u[16];
+                    __syncwarp();
+                    sm100::tmem_ld16(t_gate + c0, g);
+                    sm100::tmem_ld16(t_gate + BN + c0, u);
+                    sm100::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        mine[(c0 + j) * kBM + q * 32 + lane] = g[j];
+                        mine[(BN + c0 + j) * kBM + q * 32 + lane] = u[j];
+                    }
+                }
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                ++acc;
+                __threadfence();
+                __syncwarp();
+                int arrived = 0;
+                if (lane == 0) arrived = atomicAdd(&P.split_cnt[ip.tile * 4 + q], 1);
+                arrived = __shfl_sync(0xffffffffu, arrived, 0);
+                if (arrived != P.ks - 1) continue;  // not the last split: nothing to publish yet
+                __threadfence();
+                const float *all = P.part + static_cast<size_t>(ip.tile) * P.ks * 2 * BN * kBM;
+                for (int j = 0; j < nvalid; ++j) {
+                    float gs = 0.f, us = 0.f;
+                    for (int s = 0; s < P.ks; ++s) {
+                        gs += __ldcg(all + (static_cast<size_t>(s) * 2 * BN + j) * kBM + q * 32 + lane);
+                        us += __ldcg(all + (static_cast<size_t>(s) * 2 * BN + BN + j) * kBM + q * 32 + lane);
+                    }
+                    const float gv = rbf(gs), uv = rbf(us);
+                    P.act[static_cast<size_t>(p0 + j) * P.inner + row] = f2bf(rbf(silu_f32(gv)) * uv);
+                }
+            } else if (ip.phase == 1) {
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float g[16], u[16];
@@ -346,6 +562,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                 }
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                ++acc;
             } else {
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
@@ -357,21 +577,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j)
                         if (c0 + j < nvalid) P.y[static_cast<size_t>(p0 + c0 + j) * P.hidden + row] = f2bf(v[j]);
                 }
-            }
-            sm100::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
-            ++acc;
-            if (ip.phase == 1) {
-                // Publish this warp's 32 activation rows: each lane fences its
-                // own stores, then one release per warp (no cross-warp barrier,
-                // so an aborting warp can never strand the others).
-                __threadfence();
+                sm100::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    sm100::fence_proxy_async_global();
-                    atomicAdd(&P.done1[ip.g], 1);
-                }
+                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                ++acc;
+            }
+            // Publish this warp's 32 rows: each lane fences its own stores, then
+            // one release per warp (no cross-warp barrier, so an aborting warp
+            // can never strand the others).
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                sm100::fence_proxy_async_global();
+                if (ip.phase == 1) atomicAdd(&P.done1[ip.g], 1);
+                else atomicAdd(&P.plan->done2_total, 1);
             }
         }
     }
@@ -386,50 +605,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0 && *abort) atomicCAS(&P.plan->error, 0, 1);
 }
 
-// One CTA: groups in ascending expert id (+ shared expert last), item prefix
-// sums, zeroed counters, and the route -> token map of the shared rows.
-__global__ void grouped_plan_kernel(const int32_t *__restrict__ active, const int32_t *__restrict__ num_active,
-                                    const int32_t *__restrict__ offsets, int use_slots, int shared, int routes,
-                                    int tokens, int bn, int mb1, int mb2, GroupedGroup *__restrict__ groups,
-                                    GroupedPlan *__restrict__ plan, int32_t *__restrict__ off1,
-                                    int32_t *__restrict__ off2, int32_t *__restrict__ done1,
-                                    int32_t *__restrict__ route_token) {
-    const int n = *num_active;
-    const int ng = n + (shared ? 1 : 0);
-    for (int g = threadIdx.x; g < ng; g += blockDim.x) {
-        GroupedGroup G;
-        if (g < n) {
-            const int e = active[g];
-            G.weight = use_slots ? g : e;
-            G.begin = offsets[e];
-            G.count = offsets[e + 1] - offsets[e];
-        } else {
-            G.weight = -1;
-            G.begin = routes;
-            G.count = tokens;
-        }
-        G.ntiles = (G.count + bn - 1) / bn;
-        groups[g] = G;
-        done1[g] = 0;
-    }
-    for (int t = threadIdx.x; shared && t < tokens; t += blockDim.x) route_token[routes + t] = t;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int a = 0, b = 0;
-        for (int g = 0; g < ng; ++g) {
-            off1[g] = a;
-            off2[g] = b;
-            a += mb1 * groups[g].ntiles;
-            b += mb2 * groups[g].ntiles;
-        }
-        off1[ng] = a;
-        off2[ng] = b;
-        plan->num_groups = ng;
-        plan->items1 = a;
-        plan->items2 = b;
-        plan->work = 0;
-        plan->error = 0;
-    }
+// Standalone plan for the general (prefill) path; the decode path runs the
+// same plan_block inside its fused routing kernel.
+__global__ void __launch_bounds__(1024) grouped_plan_kernel(PlanArgs a) {
+    __shared__ int scratch[33];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    plan_block(a, scratch);
 }
 
 // xs[p] = x[route_token[p]] for the placed routes (p < offsets[experts]) and,
@@ -439,6 +621,8 @@ __global__ void __launch_bounds__(256) gather_tokens_kernel(const uint16_t *__re
                                                             const int32_t *__restrict__ offsets, int experts,
                                                             int routes, int shared_rows, int hidden,
                                                             uint16_t *__restrict__ xs) {
+    grid_dependency_wait();
+    grid_dependency_trigger();
     const int units = hidden / 8;
     const int placed = offsets[experts];
     const int64_t total = static_cast<int64_t>(routes + shared_rows) * units;
@@ -518,33 +702,61 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
         const uint64_t dims[2] = {I, rows}, str[1] = {I * 2};
         if (int rc = make_map(&am, L.act, 2, dims, str, BN)) return rc;
     }
-    static std::once_flag once[4];
-    static cudaError_t attr_err[4];
-    const int which = BN == 16 ? 0 : BN == 32 ? 1 : BN == 64 ? 2 : 3;
-    std::call_once(once[which], [] {
-        attr_err[BN == 16 ? 0 : BN == 32 ? 1 : BN == 64 ? 2 : 3] = cudaFuncSetAttribute(
-            swiglu_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
+    static std::once_flag once;
+    static cudaError_t attr_err = cudaSuccess;
+    std::call_once(once, [] {
+        attr_err = cudaFuncSetAttribute(swiglu_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        S::kSmem);
     });
-    if (attr_err[which] != cudaSuccess) return cuda_error(attr_err[which], "cudaFuncSetAttribute(grouped)");
-    GroupedParams P{L.groups, L.plan, L.off1, L.off2, L.done1, L.act, L.y, L.hidden, L.inner};
-    swiglu_grouped_kernel<BN><<<L.ctas, kThreads, S::kSmem, stream>>>(gu, dn, sg, su, sd, xm, am, P);
-    LRB_LAUNCHED("swiglu_grouped_kernel");
-    return MOE_OK;
+    if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(grouped)");
+    GroupedParams P{};
+    P.groups = L.groups;
+    P.plan = L.plan;
+    P.off1 = L.off1;
+    P.off2 = L.off2;
+    P.done1 = L.done1;
+    P.done2 = L.done2;
+    P.split_cnt = L.split_cnt;
+    P.part = L.part;
+    P.act = L.act;
+    P.y = L.y;
+    P.out = L.out;
+    P.route_pos = L.route_pos;
+    P.idx = L.idx;
+    P.scores = L.scores;
+    P.sig = L.sig;
+    P.group_of_expert = L.group_of_expert;
+    P.tokens = L.tokens;
+    P.top_k = L.top_k;
+    P.hidden = L.hidden;
+    P.inner = L.inner;
+    P.ks = L.ks;
+    return launch_pdl(swiglu_grouped_kernel<BN>, dim3(L.ctas), dim3(kThreads), S::kSmem, stream,
+                      "swiglu_grouped_kernel", gu, dn, sg, su, sd, xm, am, P);
 }
 
 }  // namespace
 
 int grouped_bn_for(int tokens) { return tokens <= 16 ? 16 : tokens <= 64 ? 32 : tokens <= 512 ? 64 : 128; }
+int grouped_ks_for(int tokens) { return tokens <= 4 ? 4 : tokens <= 8 ? 2 : 1; }
 
-int launch_grouped_plan(const int32_t *active, const int32_t *num_active, const int32_t *offsets, bool use_slots,
-                        bool shared, int routes, int tokens, int bn, int hidden, int inner, GroupedGroup *groups,
-                        GroupedPlan *plan, int32_t *off1, int32_t *off2, int32_t *done1, int32_t *route_token,
-                        cudaStream_t stream) {
-    grouped_plan_kernel<<<1, 256, 0, stream>>>(active, num_active, offsets, use_slots, shared, routes, tokens, bn,
-                                                inner / kBM, hidden / kBM, groups, plan, off1, off2, done1,
-                                                route_token);
-    LRB_LAUNCHED("grouped_plan_kernel");
-    return MOE_OK;
+// Upper bound of phase-1 tiles times splits times 2 * BN * 128 floats.
+size_t grouped_part_floats(int tokens, int experts, int top_k, int inner) {
+    const int ks = grouped_ks_for(tokens);
+    if (ks == 1) return 0;
+    return static_cast<size_t>(grouped_tiles_max(tokens, experts, top_k, inner)) * ks * 2 * grouped_bn_for(tokens) *
+           kBM;
+}
+
+int grouped_tiles_max(int tokens, int experts, int top_k, int inner) {
+    const int bn = grouped_bn_for(tokens);
+    const int groups = std::min(experts, tokens * top_k) + 1;
+    const int rows = tokens * top_k + tokens;
+    return (inner / kBM) * (groups + rows / bn + 1);
+}
+
+int launch_grouped_plan(const PlanArgs &a, cudaStream_t stream) {
+    return launch_pdl(grouped_plan_kernel, dim3(1), dim3(1024), 0, stream, "grouped_plan_kernel", a);
 }
 
 int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
@@ -552,14 +764,15 @@ int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const in
     const int64_t units = static_cast<int64_t>(routes + shared_rows) * (hidden / 8);
     const int grid = static_cast<int>(std::min<int64_t>((units + 255) / 256, 148 * 16));
     if (grid == 0) return MOE_OK;
-    gather_tokens_kernel<<<grid, 256, 0, stream>>>(x, route_token, offsets, experts, routes, shared_rows, hidden,
-                                                    xs);
-    LRB_LAUNCHED("gather_tokens_kernel");
-    return MOE_OK;
+    return launch_pdl(gather_tokens_kernel, dim3(grid), dim3(256), 0, stream, "gather_tokens_kernel", x,
+                      route_token, offsets, experts, routes, shared_rows, hidden, xs);
 }
 
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream) {
-    LRB_REQUIRE(L.hidden % kBM == 0 && L.inner % kBM == 0, "grouped: hidden and inner must be multiples of 128");
+    LRB_REQUIRE(L.hidden % kBM == 0 && L.inner % kBM == 0 && L.hidden % kCombineCols == 0,
+                "grouped: hidden must be a multiple of 1024 and inner of 128");
+    LRB_REQUIRE(L.ks == 1 || L.ks == 2 || L.ks == 4, "grouped: K split %d not in {1, 2, 4}", L.ks);
+    LRB_REQUIRE(L.top_k <= 32, "grouped: top_k %d > 32", L.top_k);
     switch (L.bn) {
         case 16: return launch_bn<16>(L, stream);
         case 32: return launch_bn<32>(L, stream);

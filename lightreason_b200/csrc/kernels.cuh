@@ -45,7 +45,7 @@ struct GroupedGroup {
     int32_t ntiles;  // token tiles of width BN
 };
 struct GroupedPlan {
-    int32_t num_groups, items1, items2, work, error, pad[3];
+    int32_t num_groups, items1, items2, items3, work, error, done2_total, pad;
 };
 struct GroupedLaunch {
     const uint16_t *gate_up, *down;  // banks: [bank_experts, 2I, H], [bank_experts, H, I]
@@ -53,19 +53,25 @@ struct GroupedLaunch {
     int bank_experts;
     const uint16_t *sh_gate, *sh_up, *sh_down;  // shared expert (may be null)
     const uint16_t *xs;                          // [rows, H] tokens in route order
-    uint16_t *act, *y;                           // [rows, I], [rows, H]
+    uint16_t *act, *y, *out;                     // [rows, I], [rows, H], [T, H]
     int rows;
     const GroupedGroup *groups;
     GroupedPlan *plan;
     const int32_t *off1, *off2;
-    int32_t *done1;
-    int hidden, inner, bn, ctas;
+    int32_t *done1, *done2, *split_cnt;
+    float *part;
+    const int32_t *route_pos;
+    const int64_t *idx;
+    const uint16_t *scores, *sig;
+    const int32_t *group_of_expert;
+    int tokens, top_k, hidden, inner, bn, ks, ctas;
 };
+struct PlanArgs;
 int grouped_bn_for(int tokens);
-int launch_grouped_plan(const int32_t *active, const int32_t *num_active, const int32_t *offsets, bool use_slots,
-                        bool shared, int routes, int tokens, int bn, int hidden, int inner, GroupedGroup *groups,
-                        GroupedPlan *plan, int32_t *off1, int32_t *off2, int32_t *done1, int32_t *route_token,
-                        cudaStream_t stream);
+int grouped_ks_for(int tokens);
+int grouped_tiles_max(int tokens, int experts, int top_k, int inner);
+size_t grouped_part_floats(int tokens, int experts, int top_k, int inner);
+int launch_grouped_plan(const PlanArgs &a, cudaStream_t stream);
 int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
                          int routes, int shared_rows, int hidden, uint16_t *xs, cudaStream_t stream);
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
@@ -76,6 +82,23 @@ int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
                          int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream);
 int check_router_args(int tokens, int hidden, int experts, int top_k);
+
+// Decode routing (T <= kDecodeMaxTokens): split-K router partials, then one CTA
+// that sums them, selects, permutes and plans.
+constexpr int kDecodeMaxTokens = 64;
+constexpr int kRouterSplit = 4;
+int launch_router_split(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
+                        int experts, float *part, cudaStream_t stream);
+struct DecodeRouteArgs {
+    const float *part;            // [kRouterSplit][T][E+1] router partials (null with route_in)
+    const float *bias;
+    const int64_t *route_in;      // given ids (skip selection) or null
+    uint16_t *logits, *sig, *scores;
+    int64_t *idx;
+    int tokens, experts, top_k, has_gate;
+    int32_t *offsets, *perm_token, *perm_slot, *route_pos, *active, *num_active, *bad_routes;
+};
+int launch_route_decode(const DecodeRouteArgs &r, const PlanArgs &plan, cudaStream_t stream);
 
 int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets, int32_t *perm_token,
                    int32_t *perm_slot, int32_t *route_pos, int32_t *active, int32_t *num_active, int32_t *bad_routes,

@@ -1,11 +1,18 @@
 // One MoE layer on the device: router -> permute -> (host-resident gather) ->
-// grouped SwiGLU experts (+ shared expert) -> ordered combine.  Every step
-// reads its routing from device memory, so the whole call is one stream of
-// launches with no host synchronisation and can be captured in a CUDA graph.
+// grouped SwiGLU experts + shared expert + ordered combine.  Every step reads
+// its routing from device memory, so a call is a short chain of launches with
+// no host synchronisation and can be captured in a CUDA graph.  Consecutive
+// kernels use programmatic dependent launch, so each one's prologue overlaps
+// its predecessor.
+//
+// Decode widths (T <= 64): split-K router partials, then one CTA that sums
+// them, selects, permutes and plans, a token gather, and the grouped kernel.
+// Wider calls: router GEMV, selection, permute and plan as separate kernels.
 #include <algorithm>
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "plan.cuh"
 
 namespace lrb {
 
@@ -18,7 +25,8 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of the scratch arrays inside the caller's workspace.
 struct Layout {
     size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, plan, off1,
-        off2, done1, xs, act, y, total;
+        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, total;
+    int split_len;
 };
 
 Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
@@ -39,12 +47,18 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.perm_slot = take(R * 4);
     L.route_pos = take(R * 4);
     L.active = take(E * 4);
-    L.counters = take(4 * 4);  // num_active, bad_routes, num_groups, slot overflow
+    L.counters = take(4 * 4);  // num_active, bad_routes, spare, slot overflow
     L.groups = take((E + 1) * sizeof(GroupedGroup));
     L.plan = take(sizeof(GroupedPlan));
     L.off1 = take((E + 2) * 4);
     L.off2 = take((E + 2) * 4);
     L.done1 = take((E + 1) * 4);
+    L.done2 = take((E + 1) * 4);
+    L.split_len = grouped_tiles_max(tokens, experts, top_k, inner) * 4;
+    L.split_cnt = take(static_cast<size_t>(L.split_len) * 4);
+    L.gofe = take(E * 4);
+    L.rpart = take(tokens <= kDecodeMaxTokens ? static_cast<size_t>(kRouterSplit) * T * (E + 1) * 4 : 0);
+    L.part = take(grouped_part_floats(tokens, experts, top_k, inner) * 4);
     L.xs = take((R + T) * hidden * 2);
     L.act = take((R + T) * inner * 2);
     L.y = take((R + T) * hidden * 2);
@@ -69,6 +83,8 @@ __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__res
                                                             int64_t gate_up_bytes, int64_t down_bytes,
                                                             uint16_t *gate_up_slots, uint16_t *down_slots,
                                                             int32_t *overflow) {
+    grid_dependency_wait();
+    grid_dependency_trigger();
     const int g = blockIdx.z;
     const int n = *num_active;
     if (g == 0 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *overflow = n > static_cast<int>(gridDim.z);
@@ -113,6 +129,7 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     const int E = w->experts, H = w->hidden, I = w->inner, K = w->top_k;
     if (int rc = check_router_args(tokens, H, E, K)) return rc;
     LRB_REQUIRE(I == 256 || I == 512 || I == 1024, "moe_layer_forward: inner %d not in {256, 512, 1024}", I);
+    LRB_REQUIRE(H % 1024 == 0, "moe_layer_forward: hidden %d is not a multiple of 1024", H);
     const bool routed_in = io->route_in != nullptr;
     const bool shared = !routed_in && w->shared_gate != nullptr;
     LRB_REQUIRE(!routed_in || io->weights_in, "moe_layer_forward: route_in needs weights_in");
@@ -149,50 +166,103 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     if (int rc = mark(0)) return rc;
 
     void *ws = workspace;
-    const int64_t *idx = io->route_in;
-    const uint16_t *scores = io->weights_in;
+    const bool decode = tokens <= kDecodeMaxTokens && E <= 256;  // logits of the CTA fit in shared memory
+    const int bn = grouped_bn_for(tokens), ks = grouped_ks_for(tokens);
     uint16_t *sig = at<uint16_t>(ws, L.sig);
-    if (!routed_in) {
-        uint16_t *logits = io->logits_out ? io->logits_out : at<uint16_t>(ws, L.logits);
-        int64_t *idx_w = io->idx_out ? io->idx_out : at<int64_t>(ws, L.idx);
-        uint16_t *scores_w = io->scores_out ? io->scores_out : at<uint16_t>(ws, L.scores);
-        if (int rc = launch_router_logits(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, logits,
-                                          sig, s))
-            return rc;
-        if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx_w, nullptr, scores_w, s))
-            return rc;
-        idx = idx_w;
-        scores = scores_w;
-    }
-    if (int rc = mark(1)) return rc;
+    uint16_t *logits = io->logits_out ? io->logits_out : at<uint16_t>(ws, L.logits);
+    int64_t *idx = routed_in ? const_cast<int64_t *>(io->route_in)
+                             : io->idx_out ? io->idx_out : at<int64_t>(ws, L.idx);
+    uint16_t *scores = routed_in ? const_cast<uint16_t *>(io->weights_in)
+                                 : io->scores_out ? io->scores_out : at<uint16_t>(ws, L.scores);
     int32_t *offsets = at<int32_t>(ws, L.offsets), *route_token = at<int32_t>(ws, L.route_token);
     int32_t *route_pos = at<int32_t>(ws, L.route_pos), *active = at<int32_t>(ws, L.active);
     int32_t *counters = at<int32_t>(ws, L.counters);
-    if (int rc = launch_permute(idx, tokens, K, E, offsets, route_token, at<int32_t>(ws, L.perm_slot), route_pos,
-                                active, counters + 0, counters + 1, s))
-        return rc;
-    if (int rc = mark(2)) return rc;
+    GroupedGroup *groups = at<GroupedGroup>(ws, L.groups);
+    GroupedPlan *plan = at<GroupedPlan>(ws, L.plan);
+
+    PlanArgs pa{};
+    pa.active = active;
+    pa.num_active = counters + 0;
+    pa.offsets = offsets;
+    pa.use_slots = staged;
+    pa.shared = shared;
+    pa.routes = R;
+    pa.tokens = tokens;
+    pa.bn = bn;
+    pa.ks = ks;
+    pa.mb1 = I / 128;
+    pa.mb2 = H / 128;
+    pa.halves = H / 1024;
+    pa.groups = groups;
+    pa.plan = plan;
+    pa.off1 = at<int32_t>(ws, L.off1);
+    pa.off2 = at<int32_t>(ws, L.off2);
+    pa.done1 = at<int32_t>(ws, L.done1);
+    pa.done2 = at<int32_t>(ws, L.done2);
+    pa.split_cnt = at<int32_t>(ws, L.split_cnt);
+    pa.split_cnt_len = L.split_len;
+    pa.route_token = route_token;
+    pa.group_of_expert = at<int32_t>(ws, L.gofe);
+
+    if (decode) {
+        float *rpart = at<float>(ws, L.rpart);
+        if (!routed_in) {
+            if (int rc = launch_router_split(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, rpart,
+                                             s))
+                return rc;
+        }
+        if (int rc = mark(1)) return rc;
+        DecodeRouteArgs ra{};
+        ra.part = routed_in ? nullptr : rpart;
+        ra.bias = w->router_bias;
+        ra.route_in = routed_in ? io->route_in : nullptr;
+        ra.logits = logits;
+        ra.sig = sig;
+        ra.scores = scores;
+        ra.idx = idx;
+        ra.tokens = tokens;
+        ra.experts = E;
+        ra.top_k = K;
+        ra.has_gate = shared;
+        ra.offsets = offsets;
+        ra.perm_token = route_token;
+        ra.perm_slot = at<int32_t>(ws, L.perm_slot);
+        ra.route_pos = route_pos;
+        ra.active = active;
+        ra.num_active = counters + 0;
+        ra.bad_routes = counters + 1;
+        if (int rc = launch_route_decode(ra, pa, s)) return rc;
+        if (int rc = mark(2)) return rc;
+    } else {
+        if (!routed_in) {
+            if (int rc = launch_router_logits(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, logits,
+                                              sig, s))
+                return rc;
+            if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx, nullptr, scores, s))
+                return rc;
+        }
+        if (int rc = mark(1)) return rc;
+        if (int rc = launch_permute(idx, tokens, K, E, offsets, route_token, at<int32_t>(ws, L.perm_slot), route_pos,
+                                    active, counters + 0, counters + 1, s))
+            return rc;
+        if (int rc = launch_grouped_plan(pa, s)) return rc;
+        if (int rc = mark(2)) return rc;
+    }
+
     const uint16_t *gu_base = w->gate_up, *dn_base = w->down;
     int64_t gu_str = gu_stride, dn_str = dn_stride;
     if (staged) {
-        stage_experts_kernel<<<dim3(64, 2, max_groups), 256, 0, s>>>(
-            active, counters + 0, io->host_gate_up, io->host_down, gu_stride, dn_stride,
-            static_cast<int64_t>(2) * I * H * 2, static_cast<int64_t>(H) * I * 2, io->gate_up_slots,
-            io->down_slots, counters + 3);
-        LRB_LAUNCHED("stage_experts_kernel");
+        if (int rc = launch_pdl(stage_experts_kernel, dim3(64, 2, max_groups), dim3(256), 0, s,
+                                "stage_experts_kernel", active, counters + 0, io->host_gate_up, io->host_down,
+                                gu_stride, dn_stride, static_cast<int64_t>(2) * I * H * 2,
+                                static_cast<int64_t>(H) * I * 2, io->gate_up_slots, io->down_slots, counters + 3))
+            return rc;
         gu_base = io->gate_up_slots;
         dn_base = io->down_slots;
         gu_str = static_cast<int64_t>(2) * I * H;
         dn_str = static_cast<int64_t>(H) * I;
     }
     if (int rc = mark(3)) return rc;
-    const int bn = grouped_bn_for(tokens);
-    GroupedGroup *groups = at<GroupedGroup>(ws, L.groups);
-    GroupedPlan *plan = at<GroupedPlan>(ws, L.plan);
-    if (int rc = launch_grouped_plan(active, counters + 0, offsets, staged, shared, R, tokens, bn, H, I, groups, plan,
-                                     at<int32_t>(ws, L.off1), at<int32_t>(ws, L.off2), at<int32_t>(ws, L.done1),
-                                     route_token, s))
-        return rc;
     uint16_t *xs = at<uint16_t>(ws, L.xs), *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
     if (int rc = launch_gather_tokens(x, route_token, offsets, E, R, shared ? tokens : 0, H, xs, s)) return rc;
     if (int rc = mark(4)) return rc;
@@ -208,23 +278,32 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.xs = xs;
     GL.act = act;
     GL.y = y;
+    GL.out = out;
     GL.rows = R + (shared ? tokens : 0);
     GL.groups = groups;
     GL.plan = plan;
-    GL.off1 = at<int32_t>(ws, L.off1);
-    GL.off2 = at<int32_t>(ws, L.off2);
-    GL.done1 = at<int32_t>(ws, L.done1);
+    GL.off1 = pa.off1;
+    GL.off2 = pa.off2;
+    GL.done1 = pa.done1;
+    GL.done2 = pa.done2;
+    GL.split_cnt = pa.split_cnt;
+    GL.part = at<float>(ws, L.part);
+    GL.route_pos = route_pos;
+    GL.idx = idx;
+    GL.scores = scores;
+    GL.sig = shared ? sig : nullptr;
+    GL.group_of_expert = pa.group_of_expert;
+    GL.tokens = tokens;
+    GL.top_k = K;
     GL.hidden = H;
     GL.inner = I;
     GL.bn = bn;
+    GL.ks = ks;
     GL.ctas = sm_count();
     if (int rc = launch_grouped(GL, s)) return rc;
     if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     if (int rc = mark(5)) return rc;
     if (int rc = mark(6)) return rc;
-    if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
-                                sig, out, s))
-        return rc;
     return mark(7);
 }
 

@@ -4,6 +4,8 @@
 
 #include "common.cuh"
 #include "kernels.cuh"
+#include "plan.cuh"
+#include "routing.cuh"
 
 namespace lrb {
 
@@ -56,76 +58,124 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t *__re
     }
 }
 
-// One warp per token.  z = float(bf16 logit) + bias; softmax over z; top_k by z
-// descending with exact ties to the lower expert id (softmax is monotonic, so
-// this is torch.topk's selection on p); w_k = p_k / sum_k p_k summed in slot
-// order.  VPL = logits per lane (experts <= 32 * VPL).
+// One warp per token: softmax / top-k / renormalise of routing.cuh warp_topk.
 template <int VPL>
 __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__restrict__ logits,
                                                             const float *__restrict__ bias, int tokens,
                                                             int experts, int top_k, int64_t *__restrict__ idx,
                                                             float *__restrict__ scores_f32,
                                                             uint16_t *__restrict__ scores_bf16) {
+    grid_dependency_wait();
+    grid_dependency_trigger();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= tokens) return;
-    float z[VPL];
-    float m = -INFINITY;
-#pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-        const int e = lane + 32 * v;
-        z[v] = -INFINITY;
-        if (e < experts) {
-            z[v] = bf2f(logits[static_cast<size_t>(t) * experts + e]) + (bias ? bias[e] : 0.0f);
-            m = fmaxf(m, z[v]);
-        }
-    }
-#pragma unroll
-    for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
-    float denom = 0.0f;
-#pragma unroll
-    for (int v = 0; v < VPL; ++v)
-        if (lane + 32 * v < experts) denom += expf(z[v] - m);
-    denom = warp_sum(denom);
-
-    uint32_t taken = 0;
-    float my_p = 0.0f;
-    int my_e = 0;
-    for (int k = 0; k < top_k; ++k) {
-        float bz = -INFINITY;
-        int be = INT_MAX;
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-            const int e = lane + 32 * v;
-            if (e < experts && !(taken & (1u << v)) && (z[v] > bz || be == INT_MAX)) {
-                bz = z[v];
-                be = e;
-            }
-        }
-#pragma unroll
-        for (int s = 16; s; s >>= 1) {
-            const float oz = __shfl_xor_sync(0xffffffffu, bz, s);
-            const int oe = __shfl_xor_sync(0xffffffffu, be, s);
-            if (oz > bz || (oz == bz && oe < be)) {
-                bz = oz;
-                be = oe;
-            }
-        }
-        if ((be & 31) == lane) taken |= 1u << (be >> 5);
-        if (lane == k) {
-            my_p = expf(bz - m) / denom;
-            my_e = be;
-        }
-    }
-    float sum = 0.0f;
-    for (int k = 0; k < top_k; ++k) sum += __shfl_sync(0xffffffffu, my_p, k);
+    const uint16_t *row = logits + static_cast<size_t>(t) * experts;
+    int e;
+    float w;
+    warp_topk<VPL>([&](int j) { return bf2f(row[j]) + (bias ? bias[j] : 0.0f); }, experts, top_k, &e, &w);
     if (lane < top_k) {
-        const float w = my_p / sum;
         const size_t o = static_cast<size_t>(t) * top_k + lane;
-        idx[o] = my_e;
+        idx[o] = e;
         if (scores_f32) scores_f32[o] = w;
         if (scores_bf16) scores_bf16[o] = f2bf(w);
     }
+}
+
+// Decode widths: every (row, K quarter) pair is one warp over all tokens, so
+// ~130 CTAs share the 1 MiB router read.  FP32 partials go to
+// part[ks][t][row] (row E = shared-expert gate); the routing kernel sums the
+// quarters in a fixed order.
+template <int NW>
+__global__ void __launch_bounds__(256) router_split_kernel(const uint16_t *__restrict__ x,
+                                                           const uint16_t *__restrict__ router,
+                                                           const uint16_t *__restrict__ gate_w, int tokens,
+                                                           int experts, float *__restrict__ part) {
+    constexpr int H = NW * 256 * kRouterSplit;
+    const int lane = threadIdx.x & 31;
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int ks = blockIdx.y;
+    const int rows = experts + (gate_w != nullptr);
+    grid_dependency_trigger();
+    if (row >= rows) {
+        grid_dependency_wait();
+        return;
+    }
+    const uint16_t *wrow = (row < experts ? router + static_cast<size_t>(row) * H : gate_w) + ks * (H / kRouterSplit);
+    uint4 w[NW];
+#pragma unroll
+    for (int i = 0; i < NW; ++i) w[i] = ld_stream(wrow + (lane + 32 * i) * 8);
+    grid_dependency_wait();  // x may come from the previous kernel
+    for (int t0 = 0; t0 < tokens; t0 += 8) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (t0 + j < tokens) {
+                const uint16_t *xr = x + static_cast<size_t>(t0 + j) * H + ks * (H / kRouterSplit);
+#pragma unroll
+                for (int i = 0; i < NW; ++i) acc[j] = dot8(w[i], ld_cached(xr + (lane + 32 * i) * 8), acc[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = warp_sum(acc[j]);
+        if (lane < 8 && t0 + lane < tokens) {
+            float v = acc[0];
+#pragma unroll
+            for (int j = 1; j < 8; ++j)
+                if (lane == j) v = acc[j];
+            part[(static_cast<size_t>(ks) * tokens + t0 + lane) * (experts + 1) + row] = v;
+        }
+    }
+}
+
+// One CTA: logits (sum of the quarters, rounded once to BF16 -- F.linear),
+// shared-expert gate, per-token top-k, the eager-order permute and the grouped
+// kernel's plan.  With route_in the selection is skipped.
+template <int VPL>
+__global__ void __launch_bounds__(1024) route_decode_kernel(DecodeRouteArgs r, PlanArgs plan) {
+    extern __shared__ float dyn[];
+    __shared__ int scratch[33];
+    const int T = r.tokens, E = r.experts, K = r.top_k;
+    float *z = dyn;                                                   // [T][E]
+    int32_t *sidx = reinterpret_cast<int32_t *>(z + T * E);           // [T][K]
+    int32_t *cnt = sidx + T * K;                                      // permute scratch
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (!r.route_in) {
+        const int cols = E + 1;
+        for (int i = threadIdx.x; i < T * cols; i += blockDim.x) {
+            const int t = i / cols, e = i % cols;
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < kRouterSplit; ++k) s += r.part[(static_cast<size_t>(k) * T + t) * cols + e];
+            const uint16_t lg = f2bf(s);
+            if (e < E) {
+                r.logits[static_cast<size_t>(t) * E + e] = lg;
+                z[t * E + e] = bf2f(lg) + (r.bias ? r.bias[e] : 0.0f);
+            } else if (r.has_gate) {
+                r.sig[t] = f2bf(sigmoid_f32(bf2f(lg)));
+            }
+        }
+        __syncthreads();
+        for (int t = warp; t < T; t += blockDim.x >> 5) {
+            int e;
+            float w;
+            const float *zr = z + t * E;
+            warp_topk<VPL>([&](int j) { return zr[j]; }, E, K, &e, &w);
+            if (lane < K) {
+                sidx[t * K + lane] = e;
+                r.idx[static_cast<size_t>(t) * K + lane] = e;
+                r.scores[static_cast<size_t>(t) * K + lane] = f2bf(w);
+            }
+        }
+    } else {
+        for (int i = threadIdx.x; i < T * K; i += blockDim.x) sidx[i] = static_cast<int32_t>(r.route_in[i]);
+    }
+    __syncthreads();
+    permute_block([&](int t, int k) -> int64_t { return sidx[t * K + k]; }, T, K, E, r.offsets, r.perm_token,
+                  r.perm_slot, r.route_pos, r.active, r.num_active, r.bad_routes, cnt, scratch);
+    plan_block(plan, scratch);
 }
 
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens,
@@ -156,17 +206,53 @@ int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
                          int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream) {
     const int grid = (tokens + 7) / 8;
-    if (experts <= 256) {
-        router_select_kernel<8><<<grid, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, idx, scores_f32,
-                                                           scores_bf16);
-    } else if (experts <= 1024) {
-        router_select_kernel<32><<<grid, 256, 0, stream>>>(logits, bias, tokens, experts, top_k, idx, scores_f32,
-                                                            scores_bf16);
-    } else {
-        return set_error(MOE_EINVAL, "router: experts %d > 1024", experts);
+    if (experts <= 256)
+        return launch_pdl(router_select_kernel<8>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16);
+    if (experts <= 1024)
+        return launch_pdl(router_select_kernel<32>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16);
+    return set_error(MOE_EINVAL, "router: experts %d > 1024", experts);
+}
+
+int launch_router_split(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
+                        int experts, float *part, cudaStream_t stream) {
+    const int rows = experts + (gate_w != nullptr);
+    const dim3 grid((rows + 7) / 8, kRouterSplit);
+    switch (hidden) {
+        case 2048:
+            return launch_pdl(router_split_kernel<2>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
+                              gate_w, tokens, experts, part);
+        case 1024:
+            return launch_pdl(router_split_kernel<1>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
+                              gate_w, tokens, experts, part);
+        case 4096:
+            return launch_pdl(router_split_kernel<4>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
+                              gate_w, tokens, experts, part);
+        default:
+            return set_error(MOE_EINVAL, "router: hidden %d not in {1024, 2048, 4096}", hidden);
     }
-    LRB_LAUNCHED("router_select_kernel");
-    return MOE_OK;
+}
+
+int route_decode_smem(int tokens, int experts, int top_k) {
+    return static_cast<int>(sizeof(float) * tokens * experts + sizeof(int32_t) * tokens * top_k +
+                            sizeof(int32_t) * 33 * experts);
+}
+
+int launch_route_decode(const DecodeRouteArgs &r, const PlanArgs &plan, cudaStream_t stream) {
+    LRB_REQUIRE(r.tokens <= kDecodeMaxTokens, "route_decode: tokens %d > %d", r.tokens, kDecodeMaxTokens);
+    const int smem = route_decode_smem(r.tokens, r.experts, r.top_k);
+    static bool configured[2] = {false, false};
+    const int v = r.experts <= 256 ? 0 : 1;
+    if (!configured[v]) {
+        const int most = route_decode_smem(kDecodeMaxTokens, v ? 1024 : 256, 32);
+        if (v == 0) LRB_CUDA(cudaFuncSetAttribute(route_decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        else LRB_CUDA(cudaFuncSetAttribute(route_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+        configured[v] = true;
+    }
+    if (v == 0)
+        return launch_pdl(route_decode_kernel<8>, dim3(1), dim3(1024), smem, stream, "route_decode_kernel", r, plan);
+    return launch_pdl(route_decode_kernel<32>, dim3(1), dim3(1024), smem, stream, "route_decode_kernel", r, plan);
 }
 
 int check_router_args(int tokens, int hidden, int experts, int top_k) {

@@ -1,0 +1,194 @@
+// Device-side routing helpers shared by the permute kernel and the fused
+// decode routing kernel: a CTA-wide exclusive scan, the stable counting-sort
+// permute of the eager dispatch order, and per-token top-k selection.
+#pragma once
+
+#include "common.cuh"
+
+namespace lrb {
+
+// Exclusive scan of one int per thread over the CTA (blockDim.x <= 1024).
+// `scratch` holds >= 33 ints of shared memory.  Returns the exclusive prefix;
+// *total receives the CTA-wide sum.  Every thread of the CTA must call it.
+__device__ __forceinline__ int block_exclusive_scan(int v, int *scratch, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = (blockDim.x + 31) >> 5;
+    int incl = v;
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, s);
+        if (lane >= s) incl += o;
+    }
+    __syncthreads();
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        const int ws = lane < warps ? scratch[lane] : 0;
+        int wincl = ws;
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, wincl, s);
+            if (lane >= s) wincl += o;
+        }
+        scratch[lane] = wincl - ws;
+        if (lane == 31) scratch[32] = wincl;
+    }
+    __syncthreads();
+    const int r = scratch[warp] + incl - v;
+    *total = scratch[32];
+    __syncthreads();
+    return r;
+}
+
+// The whole permute, executed by every thread of one CTA (blockDim.x is a
+// multiple of 32, >= experts).  idx_of(t, k) yields the expert id of (token,
+// slot).  cnt: shared [warps * experts + experts] ints; scratch: 33 ints.
+template <class IdxOf>
+__device__ void permute_block(IdxOf idx_of, int tokens, int top_k, int experts, int32_t *offsets,
+                              int32_t *perm_token, int32_t *perm_slot, int32_t *route_pos, int32_t *active,
+                              int32_t *num_active, int32_t *bad_routes, int32_t *cnt, int *scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    int32_t *total = cnt + warps * experts;
+    const int routes = tokens * top_k;
+    const int chunk = ((routes + warps * 32 - 1) / (warps * 32)) * 32;
+    const int r_begin = warp * chunk, r_end = min(routes, r_begin + chunk);
+
+    for (int i = threadIdx.x; i < warps * experts; i += blockDim.x) cnt[i] = 0;
+    __syncthreads();
+    int bad = 0;
+    for (int r0 = r_begin; r0 < r_end; r0 += 32) {
+        const int r = r0 + lane;
+        int e = -1;
+        if (r < r_end) {
+            const int64_t v = idx_of(r % tokens, r / tokens);
+            if (v >= 0 && v < experts) e = static_cast<int>(v);
+            else bad++;
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * experts + e] += __popc(peers);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < experts; e += blockDim.x) {
+        int run = 0;
+        for (int w = 0; w < warps; ++w) {
+            const int c = cnt[w * experts + e];
+            cnt[w * experts + e] = run;
+            run += c;
+        }
+        total[e] = run;
+    }
+    __syncthreads();
+    const int my_total = threadIdx.x < experts ? total[threadIdx.x] : 0;
+    int all = 0;
+    const int excl = block_exclusive_scan(my_total, scratch, &all);
+    if (threadIdx.x < experts) {
+        offsets[threadIdx.x] = excl;
+        if (threadIdx.x == experts - 1) offsets[experts] = excl + my_total;
+        for (int w = 0; w < warps; ++w) cnt[w * experts + threadIdx.x] += excl;
+    }
+    int n_active = 0;
+    const int apos = block_exclusive_scan(my_total > 0 ? 1 : 0, scratch, &n_active);
+    if (my_total > 0) active[apos] = threadIdx.x;
+    if (threadIdx.x == 0) *num_active = n_active;
+    __syncthreads();
+    for (int r0 = r_begin; r0 < r_end; r0 += 32) {
+        const int r = r0 + lane;
+        int e = -1, t = 0, k = 0;
+        if (r < r_end) {
+            t = r % tokens;
+            k = r / tokens;
+            const int64_t v = idx_of(t, k);
+            if (v >= 0 && v < experts) e = static_cast<int>(v);
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        int p = -1;
+        if (e >= 0) p = cnt[warp * experts + e] + __popc(peers & ((1u << lane) - 1));
+        __syncwarp();
+        if (e >= 0 && lane == __ffs(peers) - 1) cnt[warp * experts + e] += __popc(peers);
+        __syncwarp();
+        if (r < r_end) {
+            route_pos[static_cast<size_t>(t) * top_k + k] = p;
+            if (p >= 0) {
+                perm_token[p] = t;
+                perm_slot[p] = k;
+            }
+        }
+    }
+    if (bad_routes) {
+        int n_bad = 0;
+        block_exclusive_scan(bad, scratch, &n_bad);
+        if (threadIdx.x == 0) *bad_routes = n_bad;
+    }
+    __syncthreads();
+}
+
+struct GlobalIdx {
+    const int64_t *idx;
+    int top_k;
+    __device__ __forceinline__ int64_t operator()(int t, int k) const {
+        return idx[static_cast<size_t>(t) * top_k + k];
+    }
+};
+
+
+// Top-k of one token by one warp (modeling_qwen3_5_moe.py:762-770 plus the
+// per-expert bias): z[e] = logit + bias is given through z_of(e) for e <
+// experts (<= 32 * VPL); softmax over z; selection by z descending with exact
+// ties to the lower expert id; w_k = p_k / sum_k p_k in slot order.  Lane k <
+// top_k returns slot k's expert in *e_out and its weight in *w_out.
+template <int VPL, class ZOf>
+__device__ __forceinline__ void warp_topk(ZOf z_of, int experts, int top_k, int *e_out, float *w_out) {
+    const int lane = threadIdx.x & 31;
+    float z[VPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+        const int e = lane + 32 * v;
+        z[v] = -INFINITY;
+        if (e < experts) {
+            z[v] = z_of(e);
+            m = fmaxf(m, z[v]);
+        }
+    }
+#pragma unroll
+    for (int s = 16; s; s >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+    float denom = 0.0f;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v)
+        if (lane + 32 * v < experts) denom += expf(z[v] - m);
+    denom = warp_sum(denom);
+    uint32_t taken = 0;
+    float my_p = 0.0f;
+    int my_e = 0;
+    for (int k = 0; k < top_k; ++k) {
+        float bz = -INFINITY;
+        int be = 0x7fffffff;
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            const int e = lane + 32 * v;
+            if (e < experts && !(taken & (1u << v)) && (z[v] > bz || be == 0x7fffffff)) {
+                bz = z[v];
+                be = e;
+            }
+        }
+#pragma unroll
+        for (int s = 16; s; s >>= 1) {
+            const float oz = __shfl_xor_sync(0xffffffffu, bz, s);
+            const int oe = __shfl_xor_sync(0xffffffffu, be, s);
+            if (oz > bz || (oz == bz && oe < be)) {
+                bz = oz;
+                be = oe;
+            }
+        }
+        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        if (lane == k) {
+            my_p = expf(bz - m) / denom;
+            my_e = be;
+        }
+    }
+    float sum = 0.0f;
+    for (int k = 0; k < top_k; ++k) sum += __shfl_sync(0xffffffffu, my_p, k);
+    *e_out = my_e;
+    *w_out = my_p / sum;
+}
+
+}  // namespace lrb
