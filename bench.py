@@ -183,10 +183,11 @@ def build_layer(cfg, dev, seed):
                        shared_down=sh[2], shared_gate_w=sh[3])
     host = None
     if cfg.get("e2e_host_experts", True):
-        hg = torch.from_numpy(gu.view(np.int16)).view(torch.bfloat16).pin_memory()
-        hd = torch.from_numpy(dn.view(np.int16)).view(torch.bfloat16).pin_memory()
+        # all experts in pinned host RAM in the packed BF16 layout
+        # (the lossless row codec the reference streams over PCIe)
+        banks = native.PackedHostBanks(gu, dn, dev)
         host = native.Layer(router=router, bias=bias, shared_gate=sh[0], shared_up=sh[1], shared_down=sh[2],
-                            shared_gate_w=sh[3], host_gate_up=hg, host_down=hd)
+                            shared_gate_w=sh[3], host_packed=banks)
     return w, gu, dn, hbm, host
 
 
@@ -418,7 +419,9 @@ def run_ours(args, cfg, world, rank, local):
     }
     if e2e_ms is not None:
         e2e_total = dist_max(sum(e2e_ms), world)
-        gathered = statistics.mean(u * EXPERT_BYTES for u in u_per_step)
+        banks = host.host_packed
+        gathered = statistics.mean(sum(banks.expert_bytes(e) for e in set(idx_buf[j].cpu().numpy().reshape(-1).tolist()))
+                                   for j in used)
         result["e2e"] = {
             "value": round(world * tokens * args.steps / (e2e_total / 1e3), 2), "unit": "tokens/s",
             "ms_per_step": round(e2e_total / args.steps, 4),
@@ -427,7 +430,8 @@ def run_ours(args, cfg, world, rank, local):
             "h2d_expert_bytes_per_step": int(gathered),
             "gather_us": round(1e3 * statistics.mean(e2e_stage["gather"]), 2),
             "gather_gbs": round(gathered / (statistics.mean(e2e_stage["gather"]) / 1e3) / 1e9, 2),
-            "path": "moe_layer_forward with host_gate_up/host_down (mapped pinned banks), x H2D + out D2H per step",
+            "path": "moe_layer_forward with host_descriptors (pinned banks in the lossless row codec, decoded "
+                    "in registers into HBM slots), x H2D + out D2H per step",
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(cfg, w, gu, dn, seed)

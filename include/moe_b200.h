@@ -172,6 +172,12 @@ typedef struct moe_layer_io {
     uint16_t *gate_up_slots;       /* [max_slots,2I,H]                         */
     uint16_t *down_slots;          /* [max_slots,H,I]                          */
     int max_slots;
+    /* Packed host banks.  When host_descriptors != NULL (device int64
+     * [2][E][3], bank 0 gate_up, bank 1 down) the host experts are in the
+     * lossless row codec of edge35b/bf16_expert_codec.py -- (packed row, base,
+     * escapes), base < 0 a raw row -- and are decoded in registers on their way
+     * into the slots; host_gate_up/host_down are then unused. */
+    const int64_t *host_descriptors;
     /* Optional cudaEvent_t handles recorded on `stream` at the stage
      * boundaries: 0 start, 1 router done, 2 permute done, 3 host gather done,
      * 4 expert plan + token gather done, 5 experts (gate/up and down) done,

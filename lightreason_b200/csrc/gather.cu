@@ -14,6 +14,7 @@
 // is a raw tile.  One warp decodes one tile, 16 output bytes per lane.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "sm100.cuh"
 
 namespace lrb {
 
@@ -100,30 +101,46 @@ __device__ __forceinline__ int first_not_below(const int32_t *v, int n, int64_t 
 
 }  // namespace
 
+// Decode (or copy, base < 0) this CTA's share of one row-codec row into dst:
+// 16-byte output units [units*stripe/stripes, units*(stripe+1)/stripes), then
+// repair the escapes that fall inside that share.
 template <bool L2Only>
-__global__ void __launch_bounds__(1024) gather_row_codec_kernel(const int64_t *__restrict__ descriptors,
-                                                                 const int64_t *__restrict__ destinations,
-                                                                 const int64_t *__restrict__ sizes,
-                                                                 const int32_t *__restrict__ source_ids,
-                                                                 const int32_t *__restrict__ destination_ids,
-                                                                 const int64_t *__restrict__ count, int experts) {
-    const int row = blockIdx.z;
-    if (row >= *count) return;
-    const int bank = blockIdx.y;
-    const int64_t *d = descriptors + (static_cast<int64_t>(bank) * experts + source_ids[row]) * 3;
-    const uint8_t *src = reinterpret_cast<const uint8_t *>(d[0]);
-    const int64_t base = d[1], escapes = d[2];
-    const int64_t row_bytes = sizes[bank];
-    uint4 *dst = reinterpret_cast<uint4 *>(destinations[bank] + static_cast<int64_t>(destination_ids[row]) * row_bytes);
+__device__ __forceinline__ void row_codec_share(const uint8_t *src, int64_t base, int64_t escapes, int64_t row_bytes,
+                                                uint4 *dst, int stripe, int stripes) {
     const int64_t units = row_bytes >> 4;
-    const int64_t begin = units * blockIdx.x / gridDim.x, end = units * (blockIdx.x + 1) / gridDim.x;
+    const int64_t begin = units * stripe / stripes, end = units * (stripe + 1) / stripes;
     if (base < 0) {
         copy_units<L2Only>(reinterpret_cast<const uint4 *>(src), dst, begin, end);
         return;
     }
     const uint8_t *deltas = src + row_bytes / 2;
-    for (int64_t i = begin + threadIdx.x; i < end; i += blockDim.x)
-        dst[i] = row_unit(load8<L2Only>(src + 8 * i), load4<L2Only>(deltas + 4 * i), static_cast<uint32_t>(base));
+    const uint32_t b32 = static_cast<uint32_t>(base);
+    // Pairs of units per thread: 16 sign/fraction bytes + 8 delta bytes per
+    // load pair, two pairs in flight -- wide requests over the host link.
+    int64_t i = begin;
+    if ((i & 1) && i < end) {
+        if (threadIdx.x == 0) dst[i] = row_unit(load8<L2Only>(src + 8 * i), load4<L2Only>(deltas + 4 * i), b32);
+        ++i;
+    }
+    const int64_t pairs_end = i + ((end - i) & ~int64_t(1));
+    const int64_t step = 2 * static_cast<int64_t>(blockDim.x);
+    int64_t j = i + 2 * threadIdx.x;
+    for (; j + step < pairs_end; j += 2 * step) {
+        const uint4 sa = load16<L2Only>(src + 8 * j), sb = load16<L2Only>(src + 8 * (j + step));
+        const uint2 da = load8<L2Only>(deltas + 4 * j), db = load8<L2Only>(deltas + 4 * (j + step));
+        dst[j] = row_unit(make_uint2(sa.x, sa.y), da.x, b32);
+        dst[j + 1] = row_unit(make_uint2(sa.z, sa.w), da.y, b32);
+        dst[j + step] = row_unit(make_uint2(sb.x, sb.y), db.x, b32);
+        dst[j + step + 1] = row_unit(make_uint2(sb.z, sb.w), db.y, b32);
+    }
+    for (; j < pairs_end; j += step) {
+        const uint4 sa = load16<L2Only>(src + 8 * j);
+        const uint2 da = load8<L2Only>(deltas + 4 * j);
+        dst[j] = row_unit(make_uint2(sa.x, sa.y), da.x, b32);
+        dst[j + 1] = row_unit(make_uint2(sa.z, sa.w), da.y, b32);
+    }
+    if (pairs_end < end && threadIdx.x == 0)
+        dst[pairs_end] = row_unit(load8<L2Only>(src + 8 * pairs_end), load4<L2Only>(deltas + 4 * pairs_end), b32);
     if (escapes > 0) {
         // The escape list is sorted, so this CTA repairs exactly its own values
         // after all of its decode stores are done.
@@ -138,6 +155,146 @@ __global__ void __launch_bounds__(1024) gather_row_codec_kernel(const int64_t *_
         uint16_t *out = reinterpret_cast<uint16_t *>(dst);
         for (int j = range[0] + threadIdx.x; j < range[1]; j += blockDim.x) out[where[j]] = value[j];
     }
+}
+
+template <bool L2Only>
+__global__ void __launch_bounds__(1024) gather_row_codec_kernel(const int64_t *__restrict__ descriptors,
+                                                                 const int64_t *__restrict__ destinations,
+                                                                 const int64_t *__restrict__ sizes,
+                                                                 const int32_t *__restrict__ source_ids,
+                                                                 const int32_t *__restrict__ destination_ids,
+                                                                 const int64_t *__restrict__ count, int experts) {
+    const int row = blockIdx.z;
+    if (row >= *count) return;
+    const int bank = blockIdx.y;
+    const int64_t *d = descriptors + (static_cast<int64_t>(bank) * experts + source_ids[row]) * 3;
+    const int64_t row_bytes = sizes[bank];
+    uint4 *dst = reinterpret_cast<uint4 *>(destinations[bank] + static_cast<int64_t>(destination_ids[row]) * row_bytes);
+    row_codec_share<L2Only>(reinterpret_cast<const uint8_t *>(d[0]), d[1], d[2], row_bytes, dst, blockIdx.x,
+                            gridDim.x);
+}
+
+// The layer's host-resident stage with packed banks: active expert g (g-th
+// ascending id) decodes from descriptors[bank][active[g]] into HBM slot g of
+// bank 0 (gate_up) or 1 (down).  Grid (stripes, 2, max_slots), 256 threads.
+//
+// The packed bytes cross the host link as large bulk copies: thread 0 streams
+// the CTA's share of the sign/fraction and exponent-delta regions into a ring
+// of shared-memory stages (mbarrier completion), and the CTA decodes each stage
+// into HBM while the next ones are in flight.  Shares start and end on 4-unit
+// boundaries so every bulk copy is 16-byte aligned.  Raw rows (base < 0) and
+// escape repair use plain loads.  Waits are bounded; a timeout raises *error.
+constexpr int kStageUnits = 1024;   // 16 KiB of output per ring stage
+constexpr int kStageRing = 3;
+
+__global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__restrict__ descriptors,
+                                                              const int32_t *__restrict__ active,
+                                                              const int32_t *__restrict__ num_active, int experts,
+                                                              uint16_t *gate_up_slots, uint16_t *down_slots,
+                                                              int64_t gate_up_bytes, int64_t down_bytes,
+                                                              int32_t *error) {
+    __shared__ __align__(128) uint8_t sf_buf[kStageRing][kStageUnits * 8];
+    __shared__ __align__(128) uint8_t dl_buf[kStageRing][kStageUnits * 4];
+    __shared__ __align__(8) uint64_t bars[kStageRing];
+    __shared__ int range[2];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    const int g = blockIdx.z;
+    if (g >= *num_active) return;
+    const int bank = blockIdx.y;
+    const int64_t *d = descriptors + (static_cast<int64_t>(bank) * experts + active[g]) * 3;
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(d[0]);
+    const int64_t base = d[1], escapes = d[2];
+    const int64_t row_bytes = bank == 0 ? gate_up_bytes : down_bytes;
+    uint4 *dst = reinterpret_cast<uint4 *>(bank == 0 ? gate_up_slots + g * (gate_up_bytes / 2)
+                                                     : down_slots + g * (down_bytes / 2));
+    const int64_t units = row_bytes >> 4;
+    if (base < 0 || (units & 3)) {
+        row_codec_share<false>(src, base, escapes, row_bytes, dst, blockIdx.x, gridDim.x);
+        return;
+    }
+    const int64_t quads = units >> 2;
+    const int64_t begin = 4 * (quads * blockIdx.x / gridDim.x), end = 4 * (quads * (blockIdx.x + 1) / gridDim.x);
+    const uint8_t *deltas = src + row_bytes / 2;
+    const uint32_t b32 = static_cast<uint32_t>(base);
+    const int chunks = static_cast<int>((end - begin + kStageUnits - 1) / kStageUnits);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStageRing; ++s) sm100::mbar_init(&bars[s], 1);
+        sm100::fence_barrier_init();
+    }
+    __syncthreads();
+    auto issue = [&](int c) {
+        const int s = c % kStageRing;
+        const int64_t u0 = begin + static_cast<int64_t>(c) * kStageUnits;
+        const uint32_t n = static_cast<uint32_t>(min(static_cast<int64_t>(kStageUnits), end - u0));
+        sm100::mbar_expect_tx(&bars[s], 12 * n);
+        sm100::bulk_load(sf_buf[s], src + 8 * u0, 8 * n, &bars[s]);
+        sm100::bulk_load(dl_buf[s], deltas + 4 * u0, 4 * n, &bars[s]);
+    };
+    if (threadIdx.x == 0)
+        for (int c = 0; c < min(chunks, kStageRing); ++c) issue(c);
+    bool ok = true;
+    for (int c = 0; c < chunks; ++c) {
+        const int s = c % kStageRing;
+        const uint32_t parity = (c / kStageRing) & 1;
+        if (!sm100::mbar_try_wait(&bars[s], parity)) {
+            uint64_t t0;
+            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t0));
+            while (!sm100::mbar_try_wait(&bars[s], parity)) {
+                uint64_t t;
+                asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+                if (t - t0 > 2000000000ull) {
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) break;
+        const int64_t u0 = begin + static_cast<int64_t>(c) * kStageUnits;
+        const int n = static_cast<int>(min(static_cast<int64_t>(kStageUnits), end - u0));
+        for (int i = threadIdx.x; i < n; i += blockDim.x) {
+            const uint2 sf = *reinterpret_cast<const uint2 *>(sf_buf[s] + 8 * i);
+            const uint32_t dl = *reinterpret_cast<const uint32_t *>(dl_buf[s] + 4 * i);
+            dst[u0 + i] = row_unit(sf, dl, b32);
+        }
+        __syncthreads();  // stage s is free again
+        if (threadIdx.x == 0 && c + kStageRing < chunks) issue(c + kStageRing);
+    }
+    if (!ok) {
+        // Let the copies this CTA issued land before it leaves; then report.
+        if (threadIdx.x == 0) {
+            atomicExch(error, 4);
+            for (int s = 0; s < kStageRing; ++s) {
+                uint64_t t0, t;
+                asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t0));
+                do {
+                    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+                } while (!sm100::mbar_try_wait(&bars[s], 0) && !sm100::mbar_try_wait(&bars[s], 1) &&
+                         t - t0 < 2000000000ull);
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    if (escapes > 0) {
+        const int32_t *where = reinterpret_cast<const int32_t *>(src + row_bytes / 2 + row_bytes / 4);
+        const uint16_t *value = reinterpret_cast<const uint16_t *>(where + escapes);
+        if (threadIdx.x == 0) {
+            range[0] = first_not_below(where, static_cast<int>(escapes), begin * 8);
+            range[1] = first_not_below(where, static_cast<int>(escapes), end * 8);
+        }
+        __syncthreads();
+        uint16_t *out = reinterpret_cast<uint16_t *>(dst);
+        for (int j = range[0] + threadIdx.x; j < range[1]; j += blockDim.x) out[where[j]] = value[j];
+    }
+}
+
+int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
+                           int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
+                           int64_t down_bytes, int32_t *error, cudaStream_t stream) {
+    return launch_pdl(stage_row_codec_kernel, dim3(64, 2, max_slots), dim3(256), 0, stream, "stage_row_codec_kernel",
+                      descriptors, active, num_active, experts, gate_up_slots, down_slots, gate_up_bytes, down_bytes,
+                      error);
 }
 
 template <bool AllowCompact>

@@ -77,6 +77,10 @@ int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const in
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
 int sm_count();
 
+int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
+                           int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
+                           int64_t down_bytes, int32_t *error, cudaStream_t stream);
+
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,

@@ -47,7 +47,7 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.perm_slot = take(R * 4);
     L.route_pos = take(R * 4);
     L.active = take(E * 4);
-    L.counters = take(4 * 4);  // num_active, bad_routes, spare, slot overflow
+    L.counters = take(4 * 4);  // num_active, bad_routes, host-stage error, slot overflow
     L.groups = take((E + 1) * sizeof(GroupedGroup));
     L.plan = take(sizeof(GroupedPlan));
     L.off1 = take((E + 2) * 4);
@@ -136,8 +136,9 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     LRB_REQUIRE(routed_in || w->router, "moe_layer_forward: router weights required without route_in");
     LRB_REQUIRE(!shared || (w->shared_up && w->shared_down && w->shared_gate_w && w->shared_inner == I),
                 "moe_layer_forward: shared expert needs gate/up/down/gate_w with shared_inner == inner");
-    const bool staged = io->host_gate_up != nullptr;
-    LRB_REQUIRE(!staged || (io->host_down && io->gate_up_slots && io->down_slots),
+    const bool packed_host = io->host_descriptors != nullptr;
+    const bool staged = io->host_gate_up != nullptr || packed_host;
+    LRB_REQUIRE(!staged || ((packed_host || io->host_down) && io->gate_up_slots && io->down_slots),
                 "moe_layer_forward: host banks need slot banks");
     const int R = tokens * K;
     const int max_groups = std::min(E, R);
@@ -251,12 +252,19 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
 
     const uint16_t *gu_base = w->gate_up, *dn_base = w->down;
     int64_t gu_str = gu_stride, dn_str = dn_stride;
-    if (staged) {
+    if (packed_host) {
+        if (int rc = launch_stage_row_codec(io->host_descriptors, active, counters + 0, E, max_groups,
+                                            io->gate_up_slots, io->down_slots, static_cast<int64_t>(2) * I * H * 2,
+                                            static_cast<int64_t>(H) * I * 2, counters + 2, s))
+            return rc;
+    } else if (staged) {
         if (int rc = launch_pdl(stage_experts_kernel, dim3(64, 2, max_groups), dim3(256), 0, s,
                                 "stage_experts_kernel", active, counters + 0, io->host_gate_up, io->host_down,
                                 gu_stride, dn_stride, static_cast<int64_t>(2) * I * H * 2,
                                 static_cast<int64_t>(H) * I * 2, io->gate_up_slots, io->down_slots, counters + 3))
             return rc;
+    }
+    if (staged) {
         gu_base = io->gate_up_slots;
         dn_base = io->down_slots;
         gu_str = static_cast<int64_t>(2) * I * H;

@@ -61,6 +61,15 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
+// Untiled bulk copy global -> shared (16-byte aligned, size % 16 == 0), with
+// completion counted on `bar` in bytes.  The source may be mapped host memory.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // Generic-proxy writes by one kernel thread made visible to async-proxy (TMA)
 // reads issued later by threads that synchronise with it.
 __device__ __forceinline__ void fence_proxy_async_global() {

@@ -39,8 +39,8 @@ class LayerIO(ctypes.Structure):
 
     _fields_ = [("route_in", _p), ("weights_in", _p), ("idx_out", _p), ("scores_out", _p), ("logits_out", _p),
                 ("host_gate_up", _p), ("host_down", _p), ("gate_up_slots", _p), ("down_slots", _p),
-                ("max_slots", _i), ("stage_events", ctypes.POINTER(_p)), ("num_stage_events", _i),
-                ("status", _p)]
+                ("max_slots", _i), ("host_descriptors", _p), ("stage_events", ctypes.POINTER(_p)),
+                ("num_stage_events", _i), ("status", _p)]
 
 
 _SIGNATURES = {
@@ -217,7 +217,8 @@ class Layer:
     """
 
     def __init__(self, *, router, gate_up=None, down=None, bias=None, shared_gate=None, shared_up=None,
-                 shared_down=None, shared_gate_w=None, top_k=8, host_gate_up=None, host_down=None):
+                 shared_down=None, shared_gate_w=None, top_k=8, host_gate_up=None, host_down=None,
+                 host_packed=None):
         _cuda_bf16(router, "router")
         self.router, self.bias = router, bias
         self.gate_up, self.down = gate_up, down
@@ -225,12 +226,18 @@ class Layer:
         self.experts, self.hidden = router.shape
         self.top_k = top_k
         self.host_gate_up, self.host_down = host_gate_up, host_down
-        bank = gate_up if gate_up is not None else host_gate_up
-        dbank = down if down is not None else host_down
-        _require(bank is not None and dbank is not None, "expert banks are required")
-        self.inner = bank.shape[1] // 2
-        _require(tuple(bank.shape) == (self.experts, 2 * self.inner, self.hidden), "gate_up must be [E, 2I, H]")
-        _require(tuple(dbank.shape) == (self.experts, self.hidden, self.inner), "down must be [E, H, I]")
+        self.host_packed = host_packed
+        if host_packed is not None:
+            _require(host_packed.experts == self.experts and host_packed.hidden == self.hidden,
+                     "packed host banks do not match the router")
+            self.inner = host_packed.inner
+        else:
+            bank = gate_up if gate_up is not None else host_gate_up
+            dbank = down if down is not None else host_down
+            _require(bank is not None and dbank is not None, "expert banks are required")
+            self.inner = bank.shape[1] // 2
+            _require(tuple(bank.shape) == (self.experts, 2 * self.inner, self.hidden), "gate_up must be [E, 2I, H]")
+            _require(tuple(dbank.shape) == (self.experts, self.hidden, self.inner), "down must be [E, H, I]")
         self.device = router.device
         self._mapped = []
         self._host_dev = (None, None)
@@ -298,9 +305,12 @@ class Layer:
                     e.record()  # torch creates the CUDA event lazily on first record
             handles = (_p * len(stage_events))(*[e.cuda_event if e is not None else None for e in stage_events])
             io.stage_events, io.num_stage_events = ctypes.cast(handles, ctypes.POINTER(_p)), len(stage_events)
-        if self.host_gate_up is not None:
+        if self.host_gate_up is not None or self.host_packed is not None:
             gs, ds = self.slots(tokens)
-            io.host_gate_up, io.host_down = self._host_dev
+            if self.host_packed is not None:
+                io.host_descriptors = self.host_packed.descriptors.data_ptr()
+            else:
+                io.host_gate_up, io.host_down = self._host_dev
             io.gate_up_slots, io.down_slots, io.max_slots = gs.data_ptr(), ds.data_ptr(), gs.shape[0]
         check(lib().moe_layer_forward(ctypes.byref(self.w), _ptr(x), tokens, _ptr(out), ctypes.byref(io), _ptr(ws),
                                       ws.numel(), _stream(x.device)), "moe_layer_forward")
@@ -322,3 +332,48 @@ def gather_rows(descriptors, destinations, sizes, src, dst, count, *, max_copies
     check(lib().moe_gather_rows(_ptr(descriptors), _ptr(destinations), _ptr(sizes), _ptr(src), _ptr(dst), _ptr(count),
                                 experts, banks, max_copies, codec, stripes, threads, _stream(destinations.device)),
           "moe_gather_rows")
+
+
+class PackedHostBanks:
+    """Expert banks kept in pinned host RAM in the lossless row codec of
+    bf16_expert_codec (edge35b/bf16_expert_codec.py), with the device
+    descriptor table [2][E][3] that moe_layer_forward decodes from:
+    (packed row, base, escapes), or (raw row, -1, 0) for a row that does not
+    pack.  gate_up [E, 2I, H] and down [E, H, I] are uint16 BF16 bit arrays."""
+
+    def __init__(self, gate_up, down, device):
+        import numpy as np
+
+        from lightreason_b200 import bf16_expert_codec as codec
+
+        self.experts, two_i, self.hidden = gate_up.shape
+        self.inner = two_i // 2
+        _require(tuple(down.shape) == (self.experts, self.hidden, self.inner), "down must be [E, H, I]")
+        table = np.zeros((2, self.experts, 3), dtype=np.int64)
+        self.buffers = []
+        self.packed_bytes = []
+        for b, bank in enumerate((gate_up, down)):
+            packed, rows = codec.pack_bank(bank)
+            row_bytes = bank[0].nbytes
+            raw_rows = [e for e, r in enumerate(rows) if r is None]
+            tail = (packed.size + 15) & ~15
+            total = tail + len(raw_rows) * row_bytes
+            host = torch.empty(max(total, 16), dtype=torch.uint8).pin_memory()
+            host_np = host.numpy()
+            host_np[:packed.size] = packed
+            base_ptr = host.data_ptr()
+            for e, r in enumerate(rows):
+                if r is not None:
+                    table[b, e] = (base_ptr + r[0], r[1], r[2])
+            for j, e in enumerate(raw_rows):
+                off = tail + j * row_bytes
+                host_np[off:off + row_bytes] = np.ascontiguousarray(bank[e]).view(np.uint8).reshape(-1)
+                table[b, e] = (base_ptr + off, -1, 0)
+            self.buffers.append(host)
+            self.packed_bytes.append([(bank[0].nbytes if r is None else codec.row_bytes(bank[0].size, r[2]))
+                                      for r in rows])
+        self.descriptors = torch.from_numpy(table).to(device)
+
+    def expert_bytes(self, e: int) -> int:
+        """Bytes that cross the host link to stage expert e."""
+        return self.packed_bytes[0][e] + self.packed_bytes[1][e]

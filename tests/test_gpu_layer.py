@@ -52,6 +52,11 @@ class Case:
                                   shared_gate_w=self.sh[3])
         self.dev = dev
 
+    def packed_layer(self):
+        banks = native.PackedHostBanks(self.gu, self.dn, self.dev)
+        return native.Layer(router=self.router, bias=self.bias, shared_gate=self.sh[0], shared_up=self.sh[1],
+                            shared_down=self.sh[2], shared_gate_w=self.sh[3], host_packed=banks)
+
     def host_layer(self):
         hg = torch.from_numpy(self.gu.view(np.int16)).view(torch.bfloat16).pin_memory()
         hd = torch.from_numpy(self.dn.view(np.int16)).view(torch.bfloat16).pin_memory()
@@ -169,6 +174,17 @@ def test_host_resident_experts_match_hbm_resident(dev, case13):
     hbm = case13.run(x)
     host = case13.run(x, layer=case13.host_layer())
     for a, b in zip(hbm, host):
+        assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("tokens", [1, 16])
+def test_packed_host_experts_match_hbm_resident(dev, case13, tokens):
+    """Experts kept in pinned host RAM in the lossless row codec decode on their
+    way into HBM: the layer output is bit-identical to the HBM-resident one."""
+    x = S.hidden_states(310 + tokens, tokens)
+    hbm = case13.run(x)
+    packed = case13.run(x, layer=case13.packed_layer())
+    for a, b in zip(hbm, packed):
         assert np.array_equal(a, b)
 
 
