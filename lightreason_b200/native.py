@@ -216,14 +216,25 @@ class Layer:
     moe_host_register) and the forward gathers the selected experts per call.
     """
 
-    def __init__(self, *, router, gate_up=None, down=None, bias=None, shared_gate=None, shared_up=None,
+    def __init__(self, *, router=None, gate_up=None, down=None, bias=None, shared_gate=None, shared_up=None,
                  shared_down=None, shared_gate_w=None, top_k=8, host_gate_up=None, host_down=None,
-                 host_packed=None):
-        _cuda_bf16(router, "router")
+                 host_packed=None, device=None):
+        """router may be None for a layer only called with route_in (the
+        Qwen3_5MoeExperts.forward form); experts and hidden then come from the
+        banks."""
+        if router is not None:
+            _cuda_bf16(router, "router")
         self.router, self.bias = router, bias
         self.gate_up, self.down = gate_up, down
         self.shared = (shared_gate, shared_up, shared_down, shared_gate_w)
-        self.experts, self.hidden = router.shape
+        ref = gate_up if gate_up is not None else host_gate_up
+        if router is not None:
+            self.experts, self.hidden = router.shape
+        elif host_packed is not None:
+            self.experts, self.hidden = host_packed.experts, host_packed.hidden
+        else:
+            _require(ref is not None, "a router or expert banks are required")
+            self.experts, self.hidden = ref.shape[0], ref.shape[2]
         self.top_k = top_k
         self.host_gate_up, self.host_down = host_gate_up, host_down
         self.host_packed = host_packed
@@ -238,7 +249,13 @@ class Layer:
             self.inner = bank.shape[1] // 2
             _require(tuple(bank.shape) == (self.experts, 2 * self.inner, self.hidden), "gate_up must be [E, 2I, H]")
             _require(tuple(dbank.shape) == (self.experts, self.hidden, self.inner), "down must be [E, H, I]")
-        self.device = router.device
+        if router is not None:
+            self.device = router.device
+        elif gate_up is not None:
+            self.device = gate_up.device
+        else:
+            self.device = torch.device(device) if device is not None else torch.device("cuda",
+                                                                                         torch.cuda.current_device())
         self._mapped = []
         self._host_dev = (None, None)
         if host_gate_up is not None:
@@ -268,6 +285,12 @@ class Layer:
         for t in self._mapped:
             lib().moe_host_unregister(ctypes.c_void_p(t.data_ptr()))
         self._mapped.clear()
+
+    def set_top_k(self, top_k: int) -> None:
+        """Route width of later calls (the workspace and slots are re-sized)."""
+        _require(0 < top_k <= self.experts, "top_k must be in [1, experts]")
+        self.top_k = self.w.top_k = top_k
+        self._ws = self._slots = None
 
     def workspace(self, tokens: int) -> torch.Tensor:
         need = layer_workspace_bytes(tokens, self.experts, self.top_k, self.hidden, self.inner)
