@@ -23,7 +23,10 @@ L2 is flushed between timed steps by reading a 256 MiB buffer (twice the L2),
 outside each step's CUDA-event window.
 
 --impl reference times that CPU path alone as the reference arm.
---gpus N (under torchrun) runs one replica of the layer per rank.
+--gpus N > 1 (under torchrun) runs BASELINE configs[4], the expert-parallel
+layer: 512 tokens per rank, 256/N experts per rank, NCCL all-to-all dispatch
+and combine, step time = max over ranks of the device-timed steps.  The same
+workload runs on one GPU with --config 4.
 """
 
 from __future__ import annotations
@@ -61,6 +64,8 @@ CONFIGS = {
     1: dict(tokens=16, bias="normal",
             workload="config1: one MoE layer, speculative-verify width T=16; experts in pinned host RAM (e2e)"),
     3: dict(tokens=4096, bias="zipf", workload="config3: one MoE layer, prefill T=4096, Zipf(1.1) routing"),
+    4: dict(tokens=512, bias="zipf", workload="config4: expert-parallel MoE layer, 512 tokens per GPU, experts "
+                                               "sharded evenly over the ranks, NCCL all-to-all dispatch/combine"),
 }
 
 
@@ -438,6 +443,132 @@ def run_ours(args, cfg, world, rank, local):
     return result
 
 
+def run_ep(args, cfg, world, rank, local):
+    """one expert-parallel step per timed step."""
+    import torch.distributed as dist
+
+    from lightreason_b200 import native
+    from lightreason_b200.expert_parallel import ExpertParallelLayer, TorchExchange, run_virtual_ranks, shard
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    native.device_check(local)
+    hbm_peak, tensor_peak, peak_src = peaks()
+    tokens = cfg["tokens"]
+    seed = 4                                   # one layer, the same on every rank
+    t_setup = time.perf_counter()
+    w = S.layer_weights(seed, bias=cfg["bias"])
+    mine = shard(EXPERTS, world, rank)
+    d = lambda a: to_dev(a, dev)  # noqa: E731
+    gu = torch.empty((len(mine), 2 * INNER, HIDDEN), dtype=torch.bfloat16, device=dev)
+    dn = torch.empty((len(mine), HIDDEN, INNER), dtype=torch.bfloat16, device=dev)
+    for j, e in enumerate(mine):
+        gu[j].copy_(d(S.expert_gate_up(seed, 0, e)))
+        dn[j].copy_(d(S.expert_down(seed, 0, e)))
+    layer = ExpertParallelLayer(router=d(w.router), gate_up=gu, down=dn, shared_gate=d(w.sh_gate),
+                                shared_up=d(w.sh_up), shared_down=d(w.sh_down), shared_gate_w=d(w.sh_gate_w),
+                                bias=torch.from_numpy(w.bias).to(dev), rank=rank, world=world, tokens=tokens,
+                                exchange=TorchExchange() if world > 1 else None)
+    del gu, dn
+    pool = 8
+    xs_np = [S.hidden_states(100 + 17 * rank, tokens, step=i) for i in range(pool)]
+    xs = [to_dev(a, dev) for a in xs_np]
+    xs_host = [torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).pin_memory() for a in xs_np]
+    out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
+    out_host = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory()
+    xin = torch.empty_like(out)
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    flush_out = torch.empty((), dtype=torch.float32, device=dev)
+    log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, experts {mine.start}..{mine.stop - 1}")
+
+    def step(x, o, stage=None):
+        if world > 1:
+            layer(x, out=o, stage_events=stage)
+        else:
+            run_virtual_ranks([layer], [x], outs=[o], stage_events=stage)
+
+    def loop(kind, stage_idx=None):
+        for i in range(args.warmup):
+            step(xs[i % pool], out)
+        torch.cuda.synchronize()
+        barrier(world)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        stg = [[torch.cuda.Event(enable_timing=True) if stage_idx and j in stage_idx else None for j in range(8)]
+               for _ in range(args.steps)]
+        splits = []
+        for i in range(args.steps):
+            torch.sum(flush_buf, 0, out=flush_out)
+            j = (args.warmup + i) % pool
+            ev[i][0].record()
+            if kind == "e2e":
+                xin.copy_(xs_host[j], non_blocking=True)
+                step(xin, out, stg[i] if stage_idx else None)
+                out_host.copy_(out, non_blocking=True)
+            else:
+                step(xs[j], out, stg[i] if stage_idx else None)
+            ev[i][1].record()
+            splits.append(layer.last_splits)
+        torch.cuda.synchronize()
+        barrier(world)
+        ms = [a.elapsed_time(b) for a, b in ev]
+        kern = [row[4].elapsed_time(row[5]) for row in stg] if stage_idx else None
+        return ms, kern, splits
+
+    sampler = ClockSampler(local)
+    with sampler:
+        ms, _, splits = loop("device")
+        _, kern_ms, _ = loop("device", stage_idx=(4, 5))
+        e2e_ms, _, _ = loop("e2e")
+    clocks = sampler.summary()
+    total_ms = dist_max(sum(ms), world)
+    e2e_total = dist_max(sum(e2e_ms), world)
+    value = world * tokens * args.steps / (total_ms / 1e3)
+    # this rank's work in the last timed step
+    m = splits[-1] if splits[-1] is not None else [[int(layer.send_counts.sum())]]
+    received = sum(m[s][rank] for s in range(world))
+    leaving = sum(m[rank][dd] for dd in range(world) if dd != rank)
+    local_ids = (layer.recv_meta[:received] >> 16).cpu().numpy()
+    u_local = len(set(local_ids.tolist()))
+    rows = tokens + received
+    kernel_bytes = ((u_local + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + 2 * rows * HIDDEN * 2
+                    + rows * HIDDEN * 2)
+    kernel_flops = rows * 2 * (2 * INNER * HIDDEN + HIDDEN * INNER)
+    dur_ms = statistics.mean(kern_ms)          # this rank's launches, with this rank's bytes
+    gbs = kernel_bytes / (dur_ms / 1e3) / 1e9
+    tfs = kernel_flops / (dur_ms / 1e3) / 1e12
+    t_hbm, t_tc = kernel_bytes / (hbm_peak * 1e9), kernel_flops / (tensor_peak * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+    achieved, peak, unit = (gbs, hbm_peak, "GB/s") if bound == "hbm" else (tfs, tensor_peak, "TFLOP/s")
+    launches = 10  # router logits+select, permute, dispatch, unpack, local permute+plan+gather+grouped, combine
+    return {
+        "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
+        "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total_ms / args.steps, 5), "us_per_step": round(1e3 * total_ms / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, Zipf(1.1) router bias)",
+        "config": {"workload": cfg["workload"], "tokens_per_gpu": tokens, "hidden": HIDDEN, "inner": INNER,
+                   "experts": EXPERTS, "experts_per_gpu": len(mine), "top_k": TOP_K, "shared_expert": True,
+                   "parallelism": f"ep{world}", "rank0_rows_received": received,
+                   "rank0_routes_leaving": leaving, "rank0_nvlink_bytes_per_step": 2 * leaving * HIDDEN * 2,
+                   "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window",
+                   "timing": "CUDA events around each whole step on the compute stream (includes the host read "
+                             "of the all-to-all split sizes), max over ranks of the summed step times"},
+        "roofline": {"bound": bound, "kernel": "swiglu_grouped_kernel (local experts + shared, rank 0 rows)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
+                     "traffic": None, "algorithmic_bytes_per_launch": int(kernel_bytes),
+                     "algorithmic_flops_per_launch": int(kernel_flops), "launch_us": round(dur_ms * 1e3, 2),
+                     "hbm_frac": round(gbs / hbm_peak, 4), "tensor_frac": round(tfs / tensor_peak, 4)},
+        "e2e": {"value": round(world * tokens * args.steps / (e2e_total / 1e3), 2), "unit": "tokens/s",
+                "ms_per_step": round(e2e_total / args.steps, 4), "h2d_bytes_per_step": tokens * HIDDEN * 2,
+                "d2h_bytes_per_step": tokens * HIDDEN * 2,
+                "path": "ExpertParallelLayer.forward per rank, x H2D from pinned memory + out D2H per step"},
+        "gpu_launches": launches * args.steps,
+        "clocks": clocks,
+    }
+
+
 def run_reference(args, cfg, world, rank):
     """Reference arm: the reference's CPU implementation on the host cores."""
     if rank != 0:
@@ -479,12 +610,16 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=1)
+    ap.add_argument("--config", type=int, choices=sorted(CONFIGS), default=None,
+                    help="BASELINE config: 1 by default on one GPU, 4 (expert parallel) on more")
     ap.add_argument("--tokens", type=int, default=None, help="override the config's tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    n = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    if args.config is None:
+        args.config = 1 if n == 1 else 4
     cfg = dict(CONFIGS[args.config])
     if args.tokens:
         cfg["tokens"] = args.tokens
@@ -497,7 +632,11 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        res = run_ours(args, cfg, world, rank, local)
+        res = run_ep(args, cfg, world, rank, local) if args.config == 4 else run_ours(args, cfg, world, rank, local)
+        if rank == 0 and world == 1 and args.config == 4 and not args.no_cpu_baseline:
+            w = S.layer_weights(4, bias=cfg["bias"])
+            gu, dn = w.stacked()
+            res["cpu_baseline"] = cpu_baseline(cfg, w, gu, dn, 4)
         if rank == 0:
             print(json.dumps(res), flush=True)
     finally:

@@ -236,6 +236,31 @@ int moe_gather_rows(const int64_t *descriptors, const int64_t *destinations,
                     int banks, int max_copies, int codec, int stripes, int threads,
                     void *stream);
 
+/* ------------------------------------------------------------------------
+ * Expert parallelism (no counterpart in the reference, which runs its MoE
+ * layer on one GPU).  Rank r of `world` owns experts [r*E/world, (r+1)*E/world);
+ * the exchange between these calls is NCCL all_to_all_single.
+ *
+ * moe_ep_dispatch: after moe_router_topk + moe_permute of the rank's own tokens,
+ *   send_rows[p] = x[perm_token[p]] (BF16 [T*top_k, hidden]) and
+ *   send_meta[p] = (local expert id << 16) | BF16 weight, for every valid route
+ *   position p (in the permuted order, which is grouped by destination rank);
+ *   send_counts[d] (int64 [world]) = routes owned by rank d.
+ * moe_ep_unpack: received metadata -> route_in (int64) and weights_in (BF16)
+ *   of a one-slot moe_layer_forward over the rank's local experts, whose
+ *   output row i is bf16(y_i * w_i).
+ * moe_ep_combine: out[t] = ordered BF16 fold of ret[route_pos[t][k]] over k by
+ *   ascending position, then + shared_rows[t] (already gated; may be NULL).
+ * ------------------------------------------------------------------------ */
+int moe_ep_dispatch(const uint16_t *x, const int64_t *idx, const uint16_t *scores,
+                    const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot,
+                    int tokens, int top_k, int experts, int hidden, int world,
+                    uint16_t *send_rows, int32_t *send_meta, int64_t *send_counts, void *stream);
+int moe_ep_unpack(const int32_t *meta, int rows, int64_t *route_in, uint16_t *weights_in,
+                  void *stream);
+int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t *shared_rows,
+                   int tokens, int top_k, int hidden, uint16_t *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,228 @@
+"""Expert-parallel MoE layer: one process per GPU, experts sharded by rank,
+token dispatch and combine through NCCL all-to-all.
+
+Rank r of `world` owns the global experts [r*El, (r+1)*El), El = E / world,
+and keeps replicas of the router and the shared expert.  One step on rank r:
+
+  1. moe_router_topk on its own T tokens (logits, top-k, BF16 weights, and
+     the sigmoid shared gate written straight into the local weights_in);
+  2. moe_permute over the E global experts (eager order: ascending expert,
+     slot-major, token), which also groups the routes by owning rank;
+  3. moe_ep_dispatch packs the rows and (local expert, weight) words in that
+     order and counts the routes per destination;
+  4. the counts are all-gathered (the one host read of a step: the split
+     sizes of the all-to-all), then all_to_all_single moves rows and words;
+  5. moe_ep_unpack + one moe_layer_forward over [own tokens ; received rows]
+     with top_k = 1 and El + 1 local experts -- the shared expert is local
+     expert El, weighted by the shared gate -- so that output row i is
+     bf16(y_i * w_i), the rounding point of the eager weighted product;
+  6. the weighted rows go back with the transposed splits;
+  7. moe_ep_combine folds each token's returned rows in ascending position
+     (= ascending global expert, the eager index_add order) with BF16 rounding
+     after every add, then adds the gated shared row.
+
+The result equals the single-GPU layer bit for bit: every product and every
+rounding point is the same, only the place it runs on changes.  The
+reference runs this layer on one GPU; there is no reference interface for
+the exchange.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from lightreason_b200 import native
+from lightreason_b200.native import _ptr, _require, check, lib
+
+
+def shard(experts: int, world: int, rank: int) -> range:
+    _require(world >= 1 and experts % world == 0, f"{experts} experts do not shard evenly over {world} ranks")
+    el = experts // world
+    return range(rank * el, (rank + 1) * el)
+
+
+class TorchExchange:
+    """The all-to-all steps over a torch.distributed process group (NCCL for
+    CUDA tensors, gloo for CPU ones).  Rows travel as int32 views (gloo has
+    no 16-bit types)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+
+    def splits(self, send_counts: torch.Tensor) -> list[list[int]]:
+        """All ranks' per-destination counts as a host matrix m[src][dst]."""
+        gathered = torch.empty(self.world * self.world, dtype=send_counts.dtype, device=send_counts.device)
+        self.dist.all_gather_into_tensor(gathered, send_counts.contiguous(), group=self.group)
+        return gathered.view(self.world, self.world).tolist()
+
+    def all_to_all(self, out: torch.Tensor, inp: torch.Tensor, out_splits: list[int], in_splits: list[int]):
+        """Rows of `inp` (dim 0) split by in_splits to the ranks; `out` receives
+        out_splits rows from each rank, in rank order."""
+        width = math.prod(inp.shape[1:]) * inp.element_size() // 4
+        o = out.view(torch.int32).reshape(out.shape[0], width)
+        i = inp.view(torch.int32).reshape(inp.shape[0], width)
+        self.dist.all_to_all_single(o, i, out_splits, in_splits, group=self.group)
+
+
+def exchange_step(state, ex, compute) -> list[list[int]]:
+    """The exchange of one rank's step around its local compute.  `state`
+    holds the rank's buffers (tokens, rank, world, send_counts, send_rows,
+    send_meta, xin, recv_meta, yin, ret) with dispatch already done; rows
+    received from rank s land in xin after the own tokens, in rank order, and
+    the weighted rows go back in the same order, so ret follows the sender's
+    permuted order.  Returns the split matrix m[src][dst]."""
+    m = ex.splits(state.send_counts)
+    r, t = state.rank, state.tokens
+    sends = m[r]
+    recvs = [m[src][r] for src in range(state.world)]
+    received, routes = sum(recvs), sum(sends)
+    ex.all_to_all(state.xin[t:t + received], state.send_rows[:routes], recvs, sends)
+    ex.all_to_all(state.recv_meta[:received], state.send_meta[:routes], recvs, sends)
+    compute(received)
+    ex.all_to_all(state.ret[:routes], state.yin[t:t + received], sends, recvs)
+    return m
+
+
+class ExpertParallelLayer:
+    """One rank's share of the expert-parallel layer (device BF16 tensors).
+
+    gate_up [El, 2I, H] and down [El, H, I]: this rank's experts; router
+    [E, H], bias (f32 [E] or None) and the shared expert are replicas.
+    `tokens` bounds the per-step token count (it sizes the buffers)."""
+
+    def __init__(self, *, router, gate_up, down, shared_gate, shared_up, shared_down, shared_gate_w, rank, world,
+                 tokens, bias=None, top_k=8, exchange=None):
+        native._cuda_bf16(router, "router")
+        self.experts, self.hidden = router.shape
+        self.rank, self.world, self.top_k = rank, world, top_k
+        self.local_experts = len(shard(self.experts, world, rank))
+        _require(tuple(gate_up.shape[:1]) == (self.local_experts,) and tuple(down.shape[:1]) == (self.local_experts,),
+                 "gate_up/down must hold this rank's experts")
+        _require(shared_gate.shape[0] == gate_up.shape[1] // 2,
+                 "the shared expert runs as a local expert: its inner width must equal the experts'")
+        self.router, self.bias, self.shared_gate_w = router, bias, shared_gate_w
+        self.dev = router.device
+        # Local banks: the rank's experts, then the shared expert as expert El.
+        self.gate_up = torch.cat([gate_up, torch.cat([shared_gate, shared_up], 0)[None]], 0).contiguous()
+        self.down = torch.cat([down, shared_down[None]], 0).contiguous()
+        self.local = native.Layer(gate_up=self.gate_up, down=self.down, top_k=1)
+        self.exchange = exchange
+        self.max_tokens = tokens
+        routes = tokens * top_k
+        recv_max = world * routes          # every rank may route everything here
+        d = self.dev
+        bf = dict(dtype=torch.bfloat16, device=d)
+        i32 = dict(dtype=torch.int32, device=d)
+        self.logits = torch.empty((tokens, self.experts), **bf)
+        self.idx = torch.empty((tokens, top_k), dtype=torch.int64, device=d)
+        self.scores = torch.empty((tokens, top_k), **bf)
+        self.offsets = torch.empty(self.experts + 1, **i32)
+        self.perm_token = torch.empty(max(routes, 1), **i32)
+        self.perm_slot = torch.empty(max(routes, 1), **i32)
+        self.route_pos = torch.empty((tokens, top_k), **i32)
+        self.active = torch.empty(self.experts, **i32)
+        self.counters = torch.zeros(2, **i32)
+        self.send_rows = torch.empty((max(routes, 1), self.hidden), **bf)
+        self.send_meta = torch.empty(max(routes, 1), **i32)
+        self.send_counts = torch.zeros(world, dtype=torch.int64, device=d)
+        # [own tokens ; received rows] and their one-slot routes.
+        self.xin = torch.empty((tokens + recv_max, self.hidden), **bf)
+        self.route_in = torch.full((tokens + recv_max, 1), self.local_experts, dtype=torch.int64, device=d)
+        self.weights_in = torch.empty((tokens + recv_max, 1), **bf)
+        self.recv_meta = torch.empty(max(recv_max, 1), **i32)
+        self.yin = torch.empty((tokens + recv_max, self.hidden), **bf)
+        self.ret = torch.empty((max(routes, 1), self.hidden), **bf)
+        self.last_splits = None
+        self._own_routes = tokens
+
+    # -- phases (split out so that one process can drive several virtual ranks)
+    def dispatch(self, x: torch.Tensor) -> None:
+        native._cuda_bf16(x, "x")
+        tokens = x.shape[0]
+        _require(tokens <= self.max_tokens and x.shape[1] == self.hidden, "x must be [T <= tokens, H]")
+        self.tokens = tokens
+        s = native._stream(self.dev)
+        if tokens > self._own_routes:
+            self.route_in[:tokens].fill_(self.local_experts)   # unpack reuses the rows past the own tokens
+        self._own_routes = tokens
+        self.xin[:tokens].copy_(x)
+        if self.bias is not None:
+            _require(self.bias.is_cuda and self.bias.dtype == torch.float32, "bias must be CUDA f32 [E]")
+        check(lib().moe_router_topk(_ptr(self.xin), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
+                                    tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits), _ptr(self.idx),
+                                    None, _ptr(self.scores), _ptr(self.weights_in), s), "moe_router_topk")
+        c = self.counters.data_ptr()
+        check(lib().moe_permute(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
+                                _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos), _ptr(self.active),
+                                c, c + 4, s), "moe_permute")
+        check(lib().moe_ep_dispatch(_ptr(self.xin), _ptr(self.idx), _ptr(self.scores), _ptr(self.offsets),
+                                    _ptr(self.perm_token), _ptr(self.perm_slot), tokens, self.top_k, self.experts,
+                                    self.hidden, self.world, _ptr(self.send_rows), _ptr(self.send_meta),
+                                    _ptr(self.send_counts), s), "moe_ep_dispatch")
+
+    def compute(self, received: int, stage_events=None) -> None:
+        """Local experts over [own tokens ; `received` rows already in xin/recv_meta]
+        (stage_events: as in native.Layer.forward, for the local layer)."""
+        t = self.tokens
+        s = native._stream(self.dev)
+        check(lib().moe_ep_unpack(_ptr(self.recv_meta), received, self.route_in[t:].data_ptr(),
+                                  self.weights_in[t:].data_ptr(), s), "moe_ep_unpack")
+        n = t + received
+        self.local(self.xin[:n], route_in=self.route_in[:n], weights_in=self.weights_in[:n], out=self.yin[:n],
+                   stage_events=stage_events)
+
+    def combine(self, out: torch.Tensor) -> torch.Tensor:
+        t = self.tokens
+        check(lib().moe_ep_combine(_ptr(self.ret), _ptr(self.route_pos), _ptr(self.yin), t, self.top_k, self.hidden,
+                                   _ptr(out), native._stream(self.dev)), "moe_ep_combine")
+        return out
+
+    # -- one distributed step
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stage_events=None) -> torch.Tensor:
+        _require(self.exchange is not None, "forward needs an exchange (use run_virtual_ranks for one process)")
+        self.dispatch(x)
+        self.last_splits = exchange_step(self, self.exchange,
+                                         lambda received: self.compute(received, stage_events))
+        return self.combine(torch.empty_like(x) if out is None else out)
+
+    __call__ = forward
+
+
+def run_virtual_ranks(layers: list[ExpertParallelLayer], xs: list[torch.Tensor], outs=None,
+                      stage_events=None) -> list[torch.Tensor]:
+    """One step of `len(layers)` ranks driven from one process on one device:
+    the all-to-all becomes device copies between the ranks' buffers.  Same
+    kernels and buffers as the distributed step (for parity tests and for
+    measuring the layer at a world size larger than the GPUs at hand)."""
+    world = len(layers)
+    for layer, x in zip(layers, xs):
+        layer.dispatch(x)
+    m = torch.stack([layer.send_counts for layer in layers]).tolist()
+    for dst, layer in enumerate(layers):
+        row = layer.tokens
+        for src in range(world):
+            lo = sum(m[src][:dst])
+            n = m[src][dst]
+            layer.xin[row:row + n].copy_(layers[src].send_rows[lo:lo + n])
+            layer.recv_meta[row - layer.tokens:row - layer.tokens + n].copy_(layers[src].send_meta[lo:lo + n])
+            row += n
+        layer.compute(row - layer.tokens, stage_events if dst == 0 else None)
+    for src, layer in enumerate(layers):
+        pos = 0
+        for dst in range(world):
+            n = m[src][dst]
+            start = layers[dst].tokens + sum(m[s][dst] for s in range(src))
+            layer.ret[pos:pos + n].copy_(layers[dst].yin[start:start + n])
+            pos += n
+    outs = outs or [torch.empty_like(x) for x in xs]
+    return [layer.combine(o) for layer, o in zip(layers, outs)]
+
+
+__all__ = ["ExpertParallelLayer", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]

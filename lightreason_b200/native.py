@@ -58,6 +58,9 @@ _SIGNATURES = {
     "moe_layer_workspace_bytes": ([_i, _i, _i, _i, _i, _i], _sz),
     "moe_layer_forward": ([ctypes.POINTER(LayerWeights), _p, _i, _p, ctypes.POINTER(LayerIO), _p, _sz, _p], _i),
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+    "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
+    "moe_ep_unpack": ([_p, _i, _p, _p, _p], _i),
+    "moe_ep_combine": ([_p, _p, _p, _i, _i, _i, _p, _p], _i),
 }
 
 EXPORTED = tuple(_SIGNATURES)
