@@ -53,11 +53,12 @@ HIDDEN, INNER, EXPERTS, TOP_K = S.HIDDEN, S.INNER, S.EXPERTS, S.TOP_K
 GATE_UP_BYTES = 2 * INNER * HIDDEN * 2       # 4,194,304 B per expert
 DOWN_BYTES = HIDDEN * INNER * 2              # 2,097,152 B per expert
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES    # 6,291,456 B
-STAGES = ("router", "route", "gather", "xs", "experts", "unused", "unused2")
+STAGES = ("router", "route", "gather", "xs", "experts", "combine", "unused")
 KERNEL_NAMES = {"router": "router_split_kernel | router_logits_kernel",
                 "route": "route_decode_kernel | router_select+permute+grouped_plan kernels",
                 "gather": "stage_experts_kernel", "xs": "gather_tokens_kernel",
-                "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down + combine)", "unused": "-", "unused2": "-"}
+                "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down; + combine at T <= 64)",
+                "combine": "combine_kernel (T > 64)", "unused": "-"}
 
 CONFIGS = {
     0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
@@ -378,12 +379,16 @@ def run_ours(args, cfg, world, rank, local):
     routes = tokens * TOP_K
     # algorithmic bytes per launch of each expert kernel (groups = U routed + shared)
     rows = routes + tokens
+    fused = tokens <= 64   # the expert kernel runs the combine itself at decode widths
+    combine_bytes = rows * HIDDEN * 2 + tokens * HIDDEN * 2 + routes * 6
     algo = {
         # grouped kernel: every selected expert's weights (+ shared) once, the
-        # routed token rows in, activations out and back in, per-route outputs out
-        # + the combine: per-route outputs read back, the layer output written
-        "experts": [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + 2 * rows * HIDDEN * 2
-                    + tokens * HIDDEN * 2 for u in u_per_step],
+        # routed token rows in, activations out and back in, per-route outputs
+        # out (+ the combine at decode widths: per-route outputs read back, the
+        # layer output written)
+        "experts": [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
+                    + (combine_bytes if fused else 0) for u in u_per_step],
+        "combine": [combine_bytes] * len(used),
         "router": [EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 2 + tokens * EXPERTS * 2] * len(used),
     }
     totals = {k: sum(v) for k, v in stage_ms.items()}
@@ -528,7 +533,7 @@ def run_ep(args, cfg, world, rank, local):
     m = splits[-1] if splits[-1] is not None else [[int(layer.send_counts.sum())]]
     received = sum(m[s][rank] for s in range(world))
     leaving = sum(m[rank][dd] for dd in range(world) if dd != rank)
-    local_ids = (layer.recv_meta[:received] >> 16).cpu().numpy()
+    local_ids = layer.recv_meta[:received].cpu().numpy()
     u_local = len(set(local_ids.tolist()))
     rows = tokens + received
     kernel_bytes = ((u_local + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + 2 * rows * HIDDEN * 2

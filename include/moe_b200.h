@@ -181,7 +181,8 @@ typedef struct moe_layer_io {
     /* Optional cudaEvent_t handles recorded on `stream` at the stage
      * boundaries: 0 start, 1 router done, 2 permute done, 3 host gather done,
      * 4 expert plan + token gather done, 5 experts (gate/up and down) done,
-     * 6 = 5, 7 combine done.  NULL
+     * 6 combine done (= 5 at T <= 64, where the expert kernel combines), 7 = 6.
+     * NULL
      * entries (or num_stage_events <= i) are skipped.  For live per-kernel
      * timing (the role of the NVTX ranges of edge35b/native_bench.py:30-69). */
     void *const *stage_events;
@@ -189,6 +190,11 @@ typedef struct moe_layer_io {
     /* Optional device int32: 0, or nonzero when a bounded wait inside the
      * expert kernel gave up (the results of that call are then invalid). */
     int32_t *status;
+    /* Expert rows instead of the combined output (expert parallelism): with
+     * route_in and top_k == 1, out[t] = token t's unweighted expert row
+     * bf16(act . Wd); weights_in may be NULL and no combine runs.  Rows of
+     * dropped routes (ids outside [0, E)) are left untouched. */
+    int rows_mode;
 } moe_layer_io;
 
 /* Scratch bytes moe_layer_forward needs for `tokens` tokens. */
@@ -196,7 +202,7 @@ size_t moe_layer_workspace_bytes(int tokens, int experts, int top_k, int hidden,
                                  int shared_inner);
 
 /* hidden in {1024,2048,4096}, inner in {256,512,1024}, experts <= 1024,
- * top_k <= 32, shared_inner == inner.  x, out [T,H] BF16. */
+ * top_k <= 16, shared_inner == inner.  x, out [T,H] BF16. */
 int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens, uint16_t *out,
                       const moe_layer_io *io, void *workspace, size_t workspace_bytes,
                       void *stream);
@@ -243,23 +249,25 @@ int moe_gather_rows(const int64_t *descriptors, const int64_t *destinations,
  *
  * moe_ep_dispatch: after moe_router_topk + moe_permute of the rank's own tokens,
  *   send_rows[p] = x[perm_token[p]] (BF16 [T*top_k, hidden]) and
- *   send_meta[p] = (local expert id << 16) | BF16 weight, for every valid route
- *   position p (in the permuted order, which is grouped by destination rank);
- *   send_counts[d] (int64 [world]) = routes owned by rank d.
- * moe_ep_unpack: received metadata -> route_in (int64) and weights_in (BF16)
- *   of a one-slot moe_layer_forward over the rank's local experts, whose
- *   output row i is bf16(y_i * w_i).
- * moe_ep_combine: out[t] = ordered BF16 fold of ret[route_pos[t][k]] over k by
- *   ascending position, then + shared_rows[t] (already gated; may be NULL).
+ *   send_meta[p] = the local expert id on the owning rank, for every valid
+ *   route position p (in the permuted order, which is grouped by destination
+ *   rank); send_counts[d] (int64 [world]) = routes owned by rank d.
+ * moe_ep_unpack: received ids -> route_in (int64 [rows, 1]) of a one-slot
+ *   moe_layer_forward in rows_mode over the rank's local experts, whose output
+ *   row i is the unweighted expert row y_i.
+ * moe_ep_combine: the layer's ordered combine over rows returned in the
+ *   permuted order: out[t] = bf16(acc + bf16(ret[p] * w)) over t's routes p =
+ *   route_pos[t][k] in ascending p, w = scores[t][k] (BF16), then
+ *   + bf16(sig[t] * shared_rows[t]) (shared_rows may be NULL).  top_k <= 16.
  * ------------------------------------------------------------------------ */
-int moe_ep_dispatch(const uint16_t *x, const int64_t *idx, const uint16_t *scores,
+int moe_ep_dispatch(const uint16_t *x, const int64_t *idx,
                     const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot,
                     int tokens, int top_k, int experts, int hidden, int world,
                     uint16_t *send_rows, int32_t *send_meta, int64_t *send_counts, void *stream);
-int moe_ep_unpack(const int32_t *meta, int rows, int64_t *route_in, uint16_t *weights_in,
-                  void *stream);
-int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t *shared_rows,
-                   int tokens, int top_k, int hidden, uint16_t *out, void *stream);
+int moe_ep_unpack(const int32_t *meta, int rows, int64_t *route_in, void *stream);
+int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t *scores,
+                   const uint16_t *shared_rows, const uint16_t *sig, int tokens, int top_k,
+                   int hidden, uint16_t *out, void *stream);
 
 #ifdef __cplusplus
 }

@@ -127,67 +127,87 @@ template int launch_experts<ParamGroups>(const ParamGroups &, int, const uint16_
 // expert id), acc = bf16(acc + bf16(y * w)) as index_add_ on BF16 does
 // (modeling_qwen3_5_moe.py:749-750; edge35b/fused_experts.py:27-37), then the
 // gated shared expert, acc = bf16(acc + bf16(sig * shared)) (:788-790).
-// One CTA per token; each thread owns 8 consecutive columns.
-__global__ void __launch_bounds__(256) combine_kernel(const uint16_t *__restrict__ y,
+// One thread per (token, 8 columns): a warp covers 256 columns of one token,
+// and every thread issues all of its row loads before the ordered sums.  KMAX
+// (8 or 16) bounds top_k; MINB CTAs stay resident on an SM without spills.
+template <int KMAX, int MINB>
+__global__ void __launch_bounds__(256, MINB) combine_kernel(const uint16_t *__restrict__ y,
                                                       const int32_t *__restrict__ route_pos,
-                                                      const uint16_t *__restrict__ scores, int top_k, int hidden,
-                                                      const uint16_t *__restrict__ shared_y,
-                                                      const uint16_t *__restrict__ sig,
-                                                      uint16_t *__restrict__ out) {
-    const int t = blockIdx.x;
-    int pos[32];
-    float wt[32];
-    for (int k = 0; k < top_k; ++k) {
-        pos[k] = route_pos[static_cast<size_t>(t) * top_k + k];
-        wt[k] = bf2f(scores[static_cast<size_t>(t) * top_k + k]);
-    }
-    for (int a = 1; a < top_k; ++a) {
-        for (int b = a; b > 0 && pos[b] < pos[b - 1]; --b) {
-            const int tp = pos[b];
-            pos[b] = pos[b - 1];
-            pos[b - 1] = tp;
-            const float tw = wt[b];
-            wt[b] = wt[b - 1];
-            wt[b - 1] = tw;
-        }
-    }
-    const float sg = shared_y ? bf2f(sig[t]) : 0.0f;
-    for (int c = threadIdx.x * 8; c < hidden; c += blockDim.x * 8) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int k = 0; k < top_k; ++k) {
-            if (pos[k] < 0) continue;
-            const uint4 v = ld_cached(y + static_cast<size_t>(pos[k]) * hidden + c);
-            const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+                                                      const uint16_t *__restrict__ scores, int tokens, int top_k,
+                                                      int hidden, const uint16_t *__restrict__ shared_y,
+                                                      const uint16_t *__restrict__ sig, uint16_t *__restrict__ out) {
+    grid_dependency_wait();
+    const int chunks = hidden / 8;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(tokens) * chunks) return;
+    const int t = static_cast<int>(i / chunks), c = static_cast<int>(i % chunks) * 8;
+    int pos[KMAX];
+    float wt[KMAX];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                acc[2 * q] = rbf(acc[2 * q] + rbf(bf16_lo(vw[q]) * wt[k]));
-                acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(bf16_hi(vw[q]) * wt[k]));
-            }
-        }
-        if (shared_y) {
-            const uint4 v = ld_cached(shared_y + static_cast<size_t>(t) * hidden + c);
-            const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                acc[2 * q] = rbf(acc[2 * q] + rbf(sg * bf16_lo(vw[q])));
-                acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(sg * bf16_hi(vw[q])));
-            }
-        }
-        uint4 o;
-        o.x = pack_bf16x2(acc[0], acc[1]);
-        o.y = pack_bf16x2(acc[2], acc[3]);
-        o.z = pack_bf16x2(acc[4], acc[5]);
-        o.w = pack_bf16x2(acc[6], acc[7]);
-        *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
+    for (int k = 0; k < KMAX; ++k) {
+        pos[k] = k < top_k ? __ldg(route_pos + static_cast<size_t>(t) * top_k + k) : -1;
+        wt[k] = k < top_k ? bf2f(__ldg(scores + static_cast<size_t>(t) * top_k + k)) : 0.f;
     }
+#pragma unroll
+    for (int a = 1; a < KMAX; ++a) {
+#pragma unroll
+        for (int b = a; b > 0; --b) {
+            // -1 (no route) sorts last
+            const bool swap = static_cast<unsigned>(pos[b]) < static_cast<unsigned>(pos[b - 1]);
+            const int p0 = pos[b - 1], p1 = pos[b];
+            const float w0 = wt[b - 1], w1 = wt[b];
+            pos[b - 1] = swap ? p1 : p0;
+            pos[b] = swap ? p0 : p1;
+            wt[b - 1] = swap ? w1 : w0;
+            wt[b] = swap ? w0 : w1;
+        }
+    }
+    uint4 v[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+        v[k] = pos[k] >= 0 ? __ldcg(reinterpret_cast<const uint4 *>(y + static_cast<size_t>(pos[k]) * hidden + c))
+                           : make_uint4(0, 0, 0, 0);
+    const uint4 sv = shared_y ? __ldcg(reinterpret_cast<const uint4 *>(shared_y + static_cast<size_t>(t) * hidden + c))
+                              : make_uint4(0, 0, 0, 0);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        if (pos[k] < 0) continue;
+        const uint32_t vw[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc[2 * q] = rbf(acc[2 * q] + rbf(bf16_lo(vw[q]) * wt[k]));
+            acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(bf16_hi(vw[q]) * wt[k]));
+        }
+    }
+    if (shared_y) {
+        const float sg = bf2f(sig[t]);
+        const uint32_t vw[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            acc[2 * q] = rbf(acc[2 * q] + rbf(sg * bf16_lo(vw[q])));
+            acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(sg * bf16_hi(vw[q])));
+        }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
 }
 
 int launch_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, int tokens, int top_k,
                    int hidden, const uint16_t *shared_y, const uint16_t *sig, uint16_t *out, cudaStream_t stream) {
     if (tokens == 0) return MOE_OK;
-    combine_kernel<<<tokens, 256, 0, stream>>>(y, route_pos, scores, top_k, hidden, shared_y, sig, out);
-    LRB_LAUNCHED("combine_kernel");
-    return MOE_OK;
+    if (top_k > 16 || hidden % 8) return set_error(MOE_EINVAL, "combine: top_k %d > 16", top_k);
+    const int64_t threads = static_cast<int64_t>(tokens) * (hidden / 8);
+    const dim3 grid(static_cast<unsigned>((threads + 255) / 256));
+    if (top_k <= 8)
+        return launch_pdl(combine_kernel<8, 3>, grid, dim3(256), 0, stream, "combine_kernel", y, route_pos, scores,
+                          tokens, top_k, hidden, shared_y, sig, out);
+    return launch_pdl(combine_kernel<16, 2>, grid, dim3(256), 0, stream, "combine_kernel", y, route_pos, scores, tokens,
+                      top_k, hidden, shared_y, sig, out);
 }
 
 namespace {

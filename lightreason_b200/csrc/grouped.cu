@@ -14,9 +14,12 @@
 // tokens per expert) and prefill widths (hundreds) share one tile shape.
 //
 // Work items, handed out in this order from a device counter:
-//   phase 1  (group, 128-row block of gate+up, token tile, K split)
-//   phase 2  (group, 128-row block of down, token tile)
-//   phase 3  (token, 1024-column half)
+//   phase 1  (group, 128-row block of gate and of up, token tile, K split)
+//   phase 2  (group, 256-row block of down, token tile)
+//   phase 3  (token, 1024-column half; decode widths only)
+// Both matrix phases issue two M = 128 products per K step on one shared token
+// tile (gate and up rows, or two halves of the down block), so every token
+// tile loaded from L2 feeds 256 weight rows.
 // A phase-2 item waits until its group's activations are published, a phase-3
 // item until the outputs of all of its token's groups are; phase-1 items wait
 // on nothing, so the queue cannot deadlock.  When few experts are active
@@ -85,6 +88,8 @@ struct GroupedParams {
     const uint16_t *scores;       // [T, K] BF16
     const uint16_t *sig;          // [T] BF16 or null (no shared expert)
     const int32_t *group_of_expert;  // [E]
+    const int32_t *route_token;      // [rows] route -> token
+    uint16_t *rows_out;              // [T, H] per-token y rows instead of y (top_k 1), or null
     int tokens, top_k, hidden, inner, ks;
 };
 
@@ -217,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_groups = P.plan->num_groups;
     const int items1 = P.plan->items1, items2 = P.plan->items2;
     const int total = items1 + items2 + P.plan->items3;
-    const int mb1 = P.inner / kBM, mb2 = P.hidden / kBM;
+    const int mb1 = P.inner / kBM, mb2 = P.hidden / (2 * kBM);
     // Stage the plan in shared memory: every item decode then costs a few
     // shared loads instead of a chain of dependent global ones.
     PlanView V{P.off1, P.off2, P.groups};
@@ -255,8 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const GroupedGroup G = V.groups[ip.g];
                 const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
                 const int kb0 = ip.phase == 1 ? ip.ks * kspan : 0;
-                const uint32_t bytes = (ip.phase == 1 ? 2 * kATile : kATile) + BN * kBK * 2;
-                const int row0 = ip.mb * kBM;
+                const uint32_t bytes = 2 * kATile + BN * kBK * 2;
+                const int row0 = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM);
                 const int tok0 = G.begin + ip.nt * BN;
                 // Phase 2 streams its down-weight tiles right away and issues the
                 // activation tiles only once the group's phase 1 has published
@@ -302,8 +307,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                         sm100::tma_load_2d(st + 2 * kATile, &tm_x, fb, k0, tok0);
                     } else {
-                        if (G.weight >= 0) sm100::tma_load_3d(st, &tm_dn, fb, k0, row0, G.weight);
-                        else sm100::tma_load_2d(st, &tm_sd, fb, k0, row0);
+                        if (G.weight >= 0) {
+                            sm100::tma_load_3d(st, &tm_dn, fb, k0, row0, G.weight);
+                            sm100::tma_load_3d(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight);
+                        } else {
+                            sm100::tma_load_2d(st, &tm_sd, fb, k0, row0);
+                            sm100::tma_load_2d(st + kATile, &tm_sd, fb, k0, row0 + kBM);
+                        }
                         if (!dep_ok && sm100::ld_acquire(&P.done1[ip.g]) >= need) {
                             sm100::fence_proxy_async_global();
                             dep_ok = true;
@@ -386,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int kk = 0; kk < kBK / 16; ++kk) {
                         const uint32_t accumulate = (kb | kk) != 0;
                         sm100::mma_bf16(d_gate, a0 + 2 * kk, b + 2 * kk, idesc, accumulate);
-                        if (ip.phase == 1) sm100::mma_bf16(d_up, a1 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                        sm100::mma_bf16(d_up, a1 + 2 * kk, b + 2 * kk, idesc, accumulate);
                     }
                     sm100::mma_commit(&tail->empty[stage]);
                     any = true;
@@ -504,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!wait_bar(&tail->tfull[buf], (acc >> 1) & 1, abort)) break;
             __syncwarp();
             sm100::tc_fence_after();
-            const int row = ip.mb * kBM + q * 32 + lane;
+            const int row = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM) + q * 32 + lane;
             const int p0 = G.begin + ip.nt * BN;
             const int nvalid = min(BN, G.count - ip.nt * BN);
             const uint32_t t_gate = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 2 * BN;
@@ -567,15 +577,38 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
                 ++acc;
             } else {
+                // rows_out: column c of the tile is route p0 + c, whose token the
+                // lanes hold (lane c % 32 of register c / 32) and broadcast.
+                constexpr int kTokRegs = BN < 32 ? 1 : BN / 32;
+                int tok[kTokRegs];
+                if (P.rows_out) {
+#pragma unroll
+                    for (int i = 0; i < kTokRegs; ++i) {
+                        const int c = i * 32 + lane;
+                        tok[i] = c < nvalid ? P.route_token[p0 + c] : 0;
+                    }
+                }
+                // accumulator 0 holds down rows `row`, accumulator 1 rows `row + 128`
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
-                    float v[16];
+                    float v[16], v2[16];
                     __syncwarp();
                     sm100::tmem_ld16(t_gate + c0, v);
+                    sm100::tmem_ld16(t_gate + BN + c0, v2);
                     sm100::tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (c0 + j < nvalid) P.y[static_cast<size_t>(p0 + c0 + j) * P.hidden + row] = f2bf(v[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        if (c0 + j >= nvalid) continue;  // warp-uniform
+                        uint16_t *dst;
+                        if (P.rows_out) {
+                            const int t = __shfl_sync(0xffffffffu, tok[(c0 + j) >> 5], (c0 + j) & 31);
+                            dst = P.rows_out + static_cast<size_t>(t) * P.hidden;
+                        } else {
+                            dst = P.y + static_cast<size_t>(p0 + c0 + j) * P.hidden;
+                        }
+                        dst[row] = f2bf(v[j]);
+                        dst[row + kBM] = f2bf(v2[j]);
+                    }
                 }
                 sm100::tc_fence_before();
                 __syncwarp();
@@ -726,6 +759,8 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.scores = L.scores;
     P.sig = L.sig;
     P.group_of_expert = L.group_of_expert;
+    P.route_token = L.route_token;
+    P.rows_out = L.rows_out;
     P.tokens = L.tokens;
     P.top_k = L.top_k;
     P.hidden = L.hidden;

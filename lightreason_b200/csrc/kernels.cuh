@@ -64,6 +64,8 @@ struct GroupedLaunch {
     const int64_t *idx;
     const uint16_t *scores, *sig;
     const int32_t *group_of_expert;
+    const int32_t *route_token;  // [rows] route -> token
+    uint16_t *rows_out;            // [T, H]: write y per token (top_k 1, no shared), or null
     int tokens, top_k, hidden, inner, bn, ks, ctas;
 };
 struct PlanArgs;

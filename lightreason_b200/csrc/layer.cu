@@ -132,7 +132,10 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     LRB_REQUIRE(H % 1024 == 0, "moe_layer_forward: hidden %d is not a multiple of 1024", H);
     const bool routed_in = io->route_in != nullptr;
     const bool shared = !routed_in && w->shared_gate != nullptr;
-    LRB_REQUIRE(!routed_in || io->weights_in, "moe_layer_forward: route_in needs weights_in");
+    const bool rows_mode = io->rows_mode != 0;
+    LRB_REQUIRE(!rows_mode || (routed_in && K == 1), "moe_layer_forward: rows_mode needs route_in and top_k == 1");
+    LRB_REQUIRE(!routed_in || rows_mode || io->weights_in, "moe_layer_forward: route_in needs weights_in");
+    LRB_REQUIRE(K <= 16, "moe_layer_forward: top_k %d > 16", K);
     LRB_REQUIRE(routed_in || w->router, "moe_layer_forward: router weights required without route_in");
     LRB_REQUIRE(!shared || (w->shared_up && w->shared_down && w->shared_gate_w && w->shared_inner == I),
                 "moe_layer_forward: shared expert needs gate/up/down/gate_w with shared_inner == inner");
@@ -192,7 +195,7 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     pa.bn = bn;
     pa.ks = ks;
     pa.mb1 = I / 128;
-    pa.mb2 = H / 128;
+    pa.mb2 = H / 256;  // phase-2 items cover 256 down rows
     pa.halves = H / 1024;
     pa.groups = groups;
     pa.plan = plan;
@@ -204,6 +207,11 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     pa.split_cnt_len = L.split_len;
     pa.route_token = route_token;
     pa.group_of_expert = at<int32_t>(ws, L.gofe);
+    // Decode widths combine inside the expert kernel (one launch less on the
+    // latency path); wider calls run the standalone combine after it, whose
+    // parallelism the persistent kernel's epilogue warps cannot match.
+    const bool fused_combine = decode && !rows_mode;
+    pa.combine = fused_combine ? 1 : 0;
 
     if (decode) {
         float *rpart = at<float>(ws, L.rpart);
@@ -301,6 +309,8 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.scores = scores;
     GL.sig = shared ? sig : nullptr;
     GL.group_of_expert = pa.group_of_expert;
+    GL.route_token = route_token;
+    GL.rows_out = rows_mode ? out : nullptr;
     GL.tokens = tokens;
     GL.top_k = K;
     GL.hidden = H;
@@ -309,8 +319,13 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.ks = ks;
     GL.ctas = sm_count();
     if (int rc = launch_grouped(GL, s)) return rc;
-    if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     if (int rc = mark(5)) return rc;
+    if (!fused_combine && !rows_mode) {
+        if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
+                                    shared ? sig : nullptr, out, s))
+            return rc;
+    }
+    if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
     if (int rc = mark(6)) return rc;
     return mark(7);
 }

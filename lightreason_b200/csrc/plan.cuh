@@ -13,6 +13,7 @@ namespace lrb {
 struct PlanArgs {
     const int32_t *active, *num_active, *offsets;
     int use_slots, shared, routes, tokens, bn, ks, mb1, mb2, halves;
+    int combine;  // 1: the grouped kernel runs the ordered combine (phase 3)
     GroupedGroup *groups;
     GroupedPlan *plan;
     int32_t *off1, *off2, *done1, *done2, *split_cnt;
@@ -72,7 +73,7 @@ __device__ __forceinline__ void plan_block(const PlanArgs &a, int *scratch) {
         a.plan->num_groups = ng;
         a.plan->items1 = carry1;
         a.plan->items2 = carry2;
-        a.plan->items3 = a.tokens * a.halves;
+        a.plan->items3 = a.combine ? a.tokens * a.halves : 0;
         a.plan->work = 0;
         a.plan->error = 0;
         a.plan->done2_total = 0;

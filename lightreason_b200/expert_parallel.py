@@ -4,22 +4,22 @@ token dispatch and combine through NCCL all-to-all.
 Rank r of `world` owns the global experts [r*El, (r+1)*El), El = E / world,
 and keeps replicas of the router and the shared expert.  One step on rank r:
 
-  1. moe_router_topk on its own T tokens (logits, top-k, BF16 weights, and
-     the sigmoid shared gate written straight into the local weights_in);
+  1. moe_router_topk on its own T tokens (logits, top-k, BF16 weights and
+     the sigmoid shared gate);
   2. moe_permute over the E global experts (eager order: ascending expert,
      slot-major, token), which also groups the routes by owning rank;
-  3. moe_ep_dispatch packs the rows and (local expert, weight) words in that
-     order and counts the routes per destination;
+  3. moe_ep_dispatch packs the rows and local expert ids in that order and
+     counts the routes per destination;
   4. the counts are all-gathered (the one host read of a step: the split
-     sizes of the all-to-all), then all_to_all_single moves rows and words;
-  5. moe_ep_unpack + one moe_layer_forward over [own tokens ; received rows]
-     with top_k = 1 and El + 1 local experts -- the shared expert is local
-     expert El, weighted by the shared gate -- so that output row i is
-     bf16(y_i * w_i), the rounding point of the eager weighted product;
-  6. the weighted rows go back with the transposed splits;
-  7. moe_ep_combine folds each token's returned rows in ascending position
-     (= ascending global expert, the eager index_add order) with BF16 rounding
-     after every add, then adds the gated shared row.
+     sizes of the all-to-all), then all_to_all_single moves rows and ids;
+  5. moe_ep_unpack + one moe_layer_forward in rows mode over [own tokens ;
+     received rows] with top_k = 1 and El + 1 local experts -- the shared
+     expert is local expert El -- giving the unweighted row y of every row;
+  6. the rows go back with the transposed splits, in the sender's permuted
+     order;
+  7. moe_ep_combine runs the layer's ordered combine on them: bf16(acc +
+     bf16(y * w)) in ascending position (= ascending global expert, the eager
+     index_add order), then + bf16(sig * shared row).
 
 The result equals the single-GPU layer bit for bit: every product and every
 rounding point is the same, only the place it runs on changes.  The
@@ -132,10 +132,10 @@ class ExpertParallelLayer:
         self.send_rows = torch.empty((max(routes, 1), self.hidden), **bf)
         self.send_meta = torch.empty(max(routes, 1), **i32)
         self.send_counts = torch.zeros(world, dtype=torch.int64, device=d)
+        self.sig = torch.empty(tokens, **bf)
         # [own tokens ; received rows] and their one-slot routes.
         self.xin = torch.empty((tokens + recv_max, self.hidden), **bf)
         self.route_in = torch.full((tokens + recv_max, 1), self.local_experts, dtype=torch.int64, device=d)
-        self.weights_in = torch.empty((tokens + recv_max, 1), **bf)
         self.recv_meta = torch.empty(max(recv_max, 1), **i32)
         self.yin = torch.empty((tokens + recv_max, self.hidden), **bf)
         self.ret = torch.empty((max(routes, 1), self.hidden), **bf)
@@ -157,12 +157,12 @@ class ExpertParallelLayer:
             _require(self.bias.is_cuda and self.bias.dtype == torch.float32, "bias must be CUDA f32 [E]")
         check(lib().moe_router_topk(_ptr(self.xin), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
                                     tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits), _ptr(self.idx),
-                                    None, _ptr(self.scores), _ptr(self.weights_in), s), "moe_router_topk")
+                                    None, _ptr(self.scores), _ptr(self.sig), s), "moe_router_topk")
         c = self.counters.data_ptr()
         check(lib().moe_permute(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
                                 _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos), _ptr(self.active),
                                 c, c + 4, s), "moe_permute")
-        check(lib().moe_ep_dispatch(_ptr(self.xin), _ptr(self.idx), _ptr(self.scores), _ptr(self.offsets),
+        check(lib().moe_ep_dispatch(_ptr(self.xin), _ptr(self.idx), _ptr(self.offsets),
                                     _ptr(self.perm_token), _ptr(self.perm_slot), tokens, self.top_k, self.experts,
                                     self.hidden, self.world, _ptr(self.send_rows), _ptr(self.send_meta),
                                     _ptr(self.send_counts), s), "moe_ep_dispatch")
@@ -172,16 +172,16 @@ class ExpertParallelLayer:
         (stage_events: as in native.Layer.forward, for the local layer)."""
         t = self.tokens
         s = native._stream(self.dev)
-        check(lib().moe_ep_unpack(_ptr(self.recv_meta), received, self.route_in[t:].data_ptr(),
-                                  self.weights_in[t:].data_ptr(), s), "moe_ep_unpack")
+        check(lib().moe_ep_unpack(_ptr(self.recv_meta), received, self.route_in[t:].data_ptr(), s), "moe_ep_unpack")
         n = t + received
-        self.local(self.xin[:n], route_in=self.route_in[:n], weights_in=self.weights_in[:n], out=self.yin[:n],
-                   stage_events=stage_events)
+        self.local(self.xin[:n], route_in=self.route_in[:n], out=self.yin[:n], stage_events=stage_events,
+                   rows_mode=True)
 
     def combine(self, out: torch.Tensor) -> torch.Tensor:
         t = self.tokens
-        check(lib().moe_ep_combine(_ptr(self.ret), _ptr(self.route_pos), _ptr(self.yin), t, self.top_k, self.hidden,
-                                   _ptr(out), native._stream(self.dev)), "moe_ep_combine")
+        check(lib().moe_ep_combine(_ptr(self.ret), _ptr(self.route_pos), _ptr(self.scores), _ptr(self.yin),
+                                   _ptr(self.sig), t, self.top_k, self.hidden, _ptr(out), native._stream(self.dev)),
+              "moe_ep_combine")
         return out
 
     # -- one distributed step

@@ -40,7 +40,7 @@ class LayerIO(ctypes.Structure):
     _fields_ = [("route_in", _p), ("weights_in", _p), ("idx_out", _p), ("scores_out", _p), ("logits_out", _p),
                 ("host_gate_up", _p), ("host_down", _p), ("gate_up_slots", _p), ("down_slots", _p),
                 ("max_slots", _i), ("host_descriptors", _p), ("stage_events", ctypes.POINTER(_p)),
-                ("num_stage_events", _i), ("status", _p)]
+                ("num_stage_events", _i), ("status", _p), ("rows_mode", _i)]
 
 
 _SIGNATURES = {
@@ -58,9 +58,9 @@ _SIGNATURES = {
     "moe_layer_workspace_bytes": ([_i, _i, _i, _i, _i, _i], _sz),
     "moe_layer_forward": ([ctypes.POINTER(LayerWeights), _p, _i, _p, ctypes.POINTER(LayerIO), _p, _sz, _p], _i),
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
-    "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
-    "moe_ep_unpack": ([_p, _i, _p, _p, _p], _i),
-    "moe_ep_combine": ([_p, _p, _p, _i, _i, _i, _p, _p], _i),
+    "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
+    "moe_ep_unpack": ([_p, _i, _p, _p], _i),
+    "moe_ep_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -309,22 +309,25 @@ class Layer:
         return self._slots
 
     def forward(self, x: torch.Tensor, *, route_in=None, weights_in=None, out=None, idx_out=None, scores_out=None,
-                logits_out=None, stage_events=None) -> torch.Tensor:
+                logits_out=None, stage_events=None, rows_mode=False) -> torch.Tensor:
         """One layer step on the current stream.  stage_events: optional list of
-        8 torch.cuda.Event recorded at the stage boundaries (see moe_layer_io)."""
+        8 torch.cuda.Event recorded at the stage boundaries (see moe_layer_io).
+        rows_mode (route_in with top_k 1): out[t] = token t's unweighted expert
+        row, no combine; weights_in may be None."""
         _cuda_bf16(x, "x")
         tokens = x.shape[0]
         _require(x.shape[1] == self.hidden, "x must be [T, H]")
         if route_in is not None:
             _require(route_in.dtype == torch.int64 and tuple(route_in.shape) == (tokens, self.top_k)
                      and route_in.is_contiguous() and route_in.is_cuda, "route_in must be CUDA int64 [T, K]")
-            _require(weights_in is not None and weights_in.dtype == torch.bfloat16
-                     and tuple(weights_in.shape) == (tokens, self.top_k) and weights_in.is_contiguous(),
+            _require(rows_mode or (weights_in is not None and weights_in.dtype == torch.bfloat16
+                                   and tuple(weights_in.shape) == (tokens, self.top_k) and weights_in.is_contiguous()),
                      "weights_in must be CUDA BF16 [T, K]")
+        _require(not rows_mode or (route_in is not None and self.top_k == 1), "rows_mode needs route_in and top_k 1")
         out = torch.empty_like(x) if out is None else out
         ws = self.workspace(tokens)
         io = LayerIO(route_in=_ptr(route_in), weights_in=_ptr(weights_in), idx_out=_ptr(idx_out),
-                     scores_out=_ptr(scores_out), logits_out=_ptr(logits_out))
+                     scores_out=_ptr(scores_out), logits_out=_ptr(logits_out), rows_mode=int(rows_mode))
         if stage_events is not None:
             for e in stage_events:
                 if e is not None and not e.cuda_event:

@@ -4,9 +4,9 @@ NCCL path runs) around the oracle's arithmetic, and each rank's output must
 equal the single-process oracle layer bit for bit.
 
 This pins the decomposition the GPU path relies on: dispatch in the permuted
-order, per-route weighted rows bf16(y * w) computed by the owning rank, the
-shared expert as one more weighted row, and the ordered BF16 fold on the home
-rank.
+order, unweighted expert rows computed by the owning rank (the shared expert
+as one more local expert of the home rank), and the layer's ordered BF16
+combine on the home rank over the returned rows.
 """
 
 from __future__ import annotations
@@ -23,7 +23,6 @@ import torch.multiprocessing as mp
 from lightreason_b200 import synthetic as S
 
 EXPERTS, TOKENS, HIDDEN, INNER = 16, 5, 256, 128
-ONE = 0x3F80  # BF16 1.0
 
 
 def _rows(a: np.ndarray) -> torch.Tensor:
@@ -60,7 +59,7 @@ def _rank_main(rank: int, world: int, port: int, failures) -> None:
         el = EXPERTS // world
         routes = int(offsets[EXPERTS])
         eid = idx[ptok, pslot]
-        meta = ((eid % el).astype(np.int64) << 16) | scores[ptok, pslot].astype(np.int64)
+        meta = eid % el
         counts = [int(offsets[min((d + 1) * el, EXPERTS)] - offsets[d * el]) for d in range(world)]
         st = SimpleNamespace(
             rank=rank, world=world, tokens=TOKENS,
@@ -72,25 +71,24 @@ def _rank_main(rank: int, world: int, port: int, failures) -> None:
             ret=torch.empty((routes, HIDDEN), dtype=torch.bfloat16))
         mine = shard(EXPERTS, world, rank)
 
+        sh, sig = O.shared_expert(x, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w)
+
         def compute(received: int) -> None:
-            sh, sig = O.shared_expert(x, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w)
-            own = np.arange(TOKENS, dtype=np.int32).reshape(-1, 1)
-            st.yin[:TOKENS] = _rows(O.combine(sh, own, sig.reshape(-1, 1)))          # bf16(sig * shared)
+            st.yin[:TOKENS] = _rows(sh)                       # the shared expert: local expert El
             if received == 0:
                 return
             rows = _bits(st.xin[TOKENS:TOKENS + received])
-            m = st.recv_meta[:received].numpy().astype(np.uint32)
-            local = (m >> 16).astype(np.int64).reshape(-1, 1)
-            wts = (m & 0xFFFF).astype(np.uint16).reshape(-1, 1)
+            local = st.recv_meta[:received].numpy().astype(np.int64).reshape(-1, 1)
             assert local.max() < el
-            loc_off, loc_tok, _, loc_pos = O.permute(local, el)
+            loc_off, loc_tok, _, _ = O.permute(local, el)
             y = O.experts_by_route(rows, gu[mine.start:mine.stop], dn[mine.start:mine.stop], loc_off, loc_tok, el)
-            st.yin[TOKENS:TOKENS + received] = _rows(O.combine(y, loc_pos, wts))   # bf16(y * w)
+            unweighted = np.empty_like(y)
+            unweighted[loc_tok] = y                           # back to the received order
+            st.yin[TOKENS:TOKENS + received] = _rows(unweighted)
 
         m = exchange_step(st, TorchExchange(), compute)
         assert sum(m[rank]) == routes
-        ones = np.full((TOKENS, 8), ONE, dtype=np.uint16)
-        got = O.combine(_bits(st.ret), rpos, ones, _bits(st.yin[:TOKENS]), np.full(TOKENS, ONE, dtype=np.uint16))
+        got = O.combine(_bits(st.ret), rpos, scores, _bits(st.yin[:TOKENS]), sig)
         if not np.array_equal(got, want):
             failures.put(f"rank {rank}: {int((got != want).sum())} values differ")
     except Exception as exc:  # noqa: BLE001 - reported to the parent
