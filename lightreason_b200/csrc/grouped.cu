@@ -90,6 +90,7 @@ struct GroupedParams {
     const int32_t *group_of_expert;  // [E]
     const int32_t *route_token;      // [rows] route -> token
     uint16_t *rows_out;              // [T, H] per-token y rows instead of y (top_k 1), or null
+    const int32_t *stage_error;      // host-staging error word, or null
     int tokens, top_k, hidden, inner, ks;
 };
 
@@ -175,7 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     swiglu_grouped_kernel(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dn,
                           const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_su,
                           const __grid_constant__ CUtensorMap tm_sd, const __grid_constant__ CUtensorMap tm_x,
-                          const __grid_constant__ CUtensorMap tm_act, const GroupedParams P) {
+                          const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_x16,
+                          const __grid_constant__ CUtensorMap tm_act16, const GroupedParams P) {
     using S = GroupedShape<BN>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -218,6 +220,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = tail->tmem_base;
     grid_dependency_wait();  // routing and token gather are complete from here on
     grid_dependency_trigger();
+    if (blockIdx.x == 0 && threadIdx.x == 0 && P.stage_error) {
+        const int e = *P.stage_error;
+        if (e) atomicCAS(&P.plan->error, 0, e);
+    }
 
     const int n_groups = P.plan->num_groups;
     const int items1 = P.plan->items1, items2 = P.plan->items2;
@@ -260,9 +266,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const GroupedGroup G = V.groups[ip.g];
                 const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
                 const int kb0 = ip.phase == 1 ? ip.ks * kspan : 0;
-                const uint32_t bytes = 2 * kATile + BN * kBK * 2;
                 const int row0 = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM);
                 const int tok0 = G.begin + ip.nt * BN;
+                // Token tiles are loaded (and multiplied) only as wide as their
+                // rows, rounded up to 16: a full tile in one box of BN rows, a
+                // partial one in boxes of 16.
+                const int n16 = (min(BN, G.count - ip.nt * BN) + 15) & ~15;
+                const uint32_t bytes = 2 * kATile + n16 * kBK * 2;
+                auto load_b = [&](const CUtensorMap *full_map, const CUtensorMap *map16, uint8_t *dst, uint64_t *bar,
+                                  int k0) {
+                    if (n16 == BN) {
+                        sm100::tma_load_2d(dst, full_map, bar, k0, tok0);
+                    } else {
+                        for (int r = 0; r < n16; r += 16) sm100::tma_load_2d(dst + r * kBK * 2, map16, bar, k0, tok0 + r);
+                    }
+                };
                 // Phase 2 streams its down-weight tiles right away and issues the
                 // activation tiles only once the group's phase 1 has published
                 // them (every phase-1 tile once per epilogue warp).
@@ -284,8 +302,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         dep_ok = true;
                         for (int j = 0; j < n_pending; ++j) {
                             const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                            sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps], pk * kBK,
-                                               tok0);
+                            load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps], pk * kBK);
                         }
                         n_pending = 0;
                     }
@@ -305,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             sm100::tma_load_2d(st, &tm_sg, fb, k0, row0);
                             sm100::tma_load_2d(st + kATile, &tm_su, fb, k0, row0);
                         }
-                        sm100::tma_load_2d(st + 2 * kATile, &tm_x, fb, k0, tok0);
+                        load_b(&tm_x, &tm_x16, st + 2 * kATile, fb, k0);
                     } else {
                         if (G.weight >= 0) {
                             sm100::tma_load_3d(st, &tm_dn, fb, k0, row0, G.weight);
@@ -319,12 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             dep_ok = true;
                             for (int j = 0; j < n_pending; ++j) {
                                 const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                                sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps],
-                                                   pk * kBK, tok0);
+                                load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps],
+                                       pk * kBK);
                             }
                             n_pending = 0;
                         }
-                        if (dep_ok) sm100::tma_load_2d(st + 2 * kATile, &tm_act, fb, k0, tok0);
+                        if (dep_ok) load_b(&tm_act, &tm_act16, st + 2 * kATile, fb, k0);
                         else pending[n_pending++] = stage | (kb << 8);
                     }
                     issued[stage] = true;
@@ -343,8 +360,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                         sm100::fence_proxy_async_global();
                         for (int j = 0; j < n_pending; ++j) {
                             const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                            sm100::tma_load_2d(smem + ps * S::kStage + 2 * kATile, &tm_act, &tail->full[ps],
-                                               pk * kBK, tok0);
+                            load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps],
+                                   pk * kBK);
                         }
                         n_pending = 0;
                     }
@@ -364,7 +381,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // --------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            constexpr uint32_t idesc = sm100::idesc_bf16_f32(kBM, BN);
             uint32_t stage = 0, sphase = 0;
             int acc = 0;
             bool any = false;
@@ -377,6 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
                 if (ip.phase == 3) continue;
                 const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
+                const GroupedGroup G = V.groups[ip.g];
+                const int n16 = (min(BN, G.count - ip.nt * BN) + 15) & ~15;
+                const uint32_t idesc = sm100::idesc_bf16_f32(kBM, n16);
                 const int buf = acc & 1;
                 if (!wait_bar(&tail->tempty[buf], ((acc >> 1) & 1) ^ 1, abort)) break;
                 sm100::tc_fence_after();
@@ -524,6 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float *mine = P.part + (static_cast<size_t>(ip.tile) * P.ks + ip.ks) * 2 * BN * kBM;
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= nvalid) break;  // warp-uniform: columns past the tile's rows
                     float g[16], u[16];
                     __syncwarp();
                     sm100::tmem_ld16(t_gate + c0, g);
@@ -559,6 +579,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             } else if (ip.phase == 1) {
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= nvalid) break;  // warp-uniform: columns past the tile's rows
                     float g[16], u[16];
                     __syncwarp();
                     sm100::tmem_ld16(t_gate + c0, g);
@@ -591,6 +612,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // accumulator 0 holds down rows `row`, accumulator 1 rows `row + 128`
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
+                    if (c0 >= nvalid) break;  // warp-uniform
                     float v[16], v2[16];
                     __syncwarp();
                     sm100::tmem_ld16(t_gate + c0, v);
@@ -685,8 +707,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+}  // namespace
+
 // BF16 tensor map: dims[0] innermost (K), 128-byte swizzle, box {64, box_rows(, 1)}.
-int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,
+int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,
              uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return set_error(MOE_ECUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
@@ -701,39 +725,43 @@ int make_map(CUtensorMap *map, const void *base, int rank, const uint64_t *dims,
     return MOE_OK;
 }
 
+namespace {
+
 template <int BN>
 int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     using S = GroupedShape<BN>;
-    CUtensorMap gu{}, dn{}, sg{}, su{}, sd{}, xm{}, am{};
+    CUtensorMap gu{}, dn{}, sg{}, su{}, sd{}, xm{}, am{}, xm16{}, am16{};
     const uint64_t H = L.hidden, I = L.inner, rows = static_cast<uint64_t>(L.rows);
     {
         const uint64_t dims[3] = {H, 2 * I, static_cast<uint64_t>(L.bank_experts)};
         const uint64_t str[2] = {H * 2, static_cast<uint64_t>(L.gate_up_stride) * 2};
-        if (int rc = make_map(&gu, L.gate_up, 3, dims, str, kBM)) return rc;
+        if (int rc = make_map_bf16(&gu, L.gate_up, 3, dims, str, kBM)) return rc;
     }
     {
         const uint64_t dims[3] = {I, H, static_cast<uint64_t>(L.bank_experts)};
         const uint64_t str[2] = {I * 2, static_cast<uint64_t>(L.down_stride) * 2};
-        if (int rc = make_map(&dn, L.down, 3, dims, str, kBM)) return rc;
+        if (int rc = make_map_bf16(&dn, L.down, 3, dims, str, kBM)) return rc;
     }
     const void *sgp = L.sh_gate ? L.sh_gate : L.gate_up, *sup = L.sh_up ? L.sh_up : L.gate_up;
     const void *sdp = L.sh_down ? L.sh_down : L.down;
     {
         const uint64_t dims[2] = {H, I}, str[1] = {H * 2};
-        if (int rc = make_map(&sg, sgp, 2, dims, str, kBM)) return rc;
-        if (int rc = make_map(&su, sup, 2, dims, str, kBM)) return rc;
+        if (int rc = make_map_bf16(&sg, sgp, 2, dims, str, kBM)) return rc;
+        if (int rc = make_map_bf16(&su, sup, 2, dims, str, kBM)) return rc;
     }
     {
         const uint64_t dims[2] = {I, H}, str[1] = {I * 2};
-        if (int rc = make_map(&sd, sdp, 2, dims, str, kBM)) return rc;
+        if (int rc = make_map_bf16(&sd, sdp, 2, dims, str, kBM)) return rc;
     }
     {
         const uint64_t dims[2] = {H, rows}, str[1] = {H * 2};
-        if (int rc = make_map(&xm, L.xs, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&xm, L.xs, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&xm16, L.xs, 2, dims, str, 16)) return rc;
     }
     {
         const uint64_t dims[2] = {I, rows}, str[1] = {I * 2};
-        if (int rc = make_map(&am, L.act, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&am, L.act, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&am16, L.act, 2, dims, str, 16)) return rc;
     }
     static std::once_flag once;
     static cudaError_t attr_err = cudaSuccess;
@@ -761,13 +789,14 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.group_of_expert = L.group_of_expert;
     P.route_token = L.route_token;
     P.rows_out = L.rows_out;
+    P.stage_error = L.stage_error;
     P.tokens = L.tokens;
     P.top_k = L.top_k;
     P.hidden = L.hidden;
     P.inner = L.inner;
     P.ks = L.ks;
     return launch_pdl(swiglu_grouped_kernel<BN>, dim3(L.ctas), dim3(kThreads), S::kSmem, stream,
-                      "swiglu_grouped_kernel", gu, dn, sg, su, sd, xm, am, P);
+                      "swiglu_grouped_kernel", gu, dn, sg, su, sd, xm, am, xm16, am16, P);
 }
 
 }  // namespace

@@ -1,6 +1,8 @@
 // Internal launchers shared between the translation units of libmoe_b200.so.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace lrb {
@@ -66,6 +68,7 @@ struct GroupedLaunch {
     const int32_t *group_of_expert;
     const int32_t *route_token;  // [rows] route -> token
     uint16_t *rows_out;            // [T, H]: write y per token (top_k 1, no shared), or null
+    const int32_t *stage_error;    // nonzero: the host staging gave up; folded into plan->error
     int tokens, top_k, hidden, inner, bn, ks, ctas;
 };
 struct PlanArgs;
@@ -77,6 +80,11 @@ int launch_grouped_plan(const PlanArgs &a, cudaStream_t stream);
 int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
                          int routes, int shared_rows, int hidden, uint16_t *xs, cudaStream_t stream);
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
+// BF16 tensor map: dims[0] innermost, 128-byte swizzle, box {64, box_rows(, 1)}.
+int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,
+                  uint32_t box_rows);
+int launch_router_tc(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
+                     uint16_t *logits, int32_t *error, cudaStream_t stream);
 int sm_count();
 
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
@@ -85,8 +93,11 @@ int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, co
 
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);
+// With gate_w, also sig[t] = bf16(sigmoid(bf16(x[t] . gate_w))) (one warp per token).
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
-                         int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream);
+                         int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream,
+                         const uint16_t *x = nullptr, const uint16_t *gate_w = nullptr, int hidden = 0,
+                         uint16_t *sig = nullptr);
 int check_router_args(int tokens, int hidden, int experts, int top_k);
 
 // Decode routing (T <= kDecodeMaxTokens): split-K router partials, then one CTA

@@ -47,7 +47,7 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.perm_slot = take(R * 4);
     L.route_pos = take(R * 4);
     L.active = take(E * 4);
-    L.counters = take(4 * 4);  // num_active, bad_routes, host-stage error, slot overflow
+    L.counters = take(8 * 4);  // num_active, bad_routes, host-stage error, slot overflow, router error
     L.groups = take((E + 1) * sizeof(GroupedGroup));
     L.plan = take(sizeof(GroupedPlan));
     L.off1 = take((E + 2) * 4);
@@ -207,6 +207,8 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     pa.split_cnt_len = L.split_len;
     pa.route_token = route_token;
     pa.group_of_expert = at<int32_t>(ws, L.gofe);
+    pa.stage_error = counters + 2;
+    pa.router_error = decode ? nullptr : counters + 4;
     // Decode widths combine inside the expert kernel (one launch less on the
     // latency path); wider calls run the standalone combine after it, whose
     // parallelism the persistent kernel's epilogue warps cannot match.
@@ -243,11 +245,12 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         if (int rc = launch_route_decode(ra, pa, s)) return rc;
         if (int rc = mark(2)) return rc;
     } else {
+        LRB_CUDA(cudaMemsetAsync(counters + 4, 0, sizeof(int32_t), s));
         if (!routed_in) {
-            if (int rc = launch_router_logits(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, logits,
-                                              sig, s))
-                return rc;
-            if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx, nullptr, scores, s))
+            // tensor-core logits, then selection and the shared-expert gate
+            if (int rc = launch_router_tc(x, w->router, tokens, H, E, logits, counters + 4, s)) return rc;
+            if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx, nullptr, scores, s, x,
+                                              shared ? w->shared_gate_w : nullptr, H, shared ? sig : nullptr))
                 return rc;
         }
         if (int rc = mark(1)) return rc;
@@ -311,6 +314,7 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.group_of_expert = pa.group_of_expert;
     GL.route_token = route_token;
     GL.rows_out = rows_mode ? out : nullptr;
+    GL.stage_error = counters + 2;
     GL.tokens = tokens;
     GL.top_k = K;
     GL.hidden = H;

@@ -19,6 +19,8 @@ struct PlanArgs {
     int32_t *off1, *off2, *done1, *done2, *split_cnt;
     int split_cnt_len;
     int32_t *route_token, *group_of_expert;
+    int32_t *stage_error;         // zeroed here: the host-staging kernels run after the plan
+    const int32_t *router_error;  // folded into plan->error when non-null (the router ran before)
 };
 
 // Executed by every thread of one CTA.
@@ -75,7 +77,8 @@ __device__ __forceinline__ void plan_block(const PlanArgs &a, int *scratch) {
         a.plan->items2 = carry2;
         a.plan->items3 = a.combine ? a.tokens * a.halves : 0;
         a.plan->work = 0;
-        a.plan->error = 0;
+        a.plan->error = a.router_error ? *a.router_error : 0;
+        if (a.stage_error) *a.stage_error = 0;
         a.plan->done2_total = 0;
     }
     __syncthreads();

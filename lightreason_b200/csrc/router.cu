@@ -58,18 +58,30 @@ __global__ void __launch_bounds__(256) router_logits_kernel(const uint16_t *__re
     }
 }
 
-// One warp per token: softmax / top-k / renormalise of routing.cuh warp_topk.
+// One warp per token: softmax / top-k / renormalise of routing.cuh warp_topk,
+// and (gate_w != null) the shared-expert gate sig = bf16(sigmoid(bf16(x . w)))
+// (modeling_qwen3_5_moe :779, :788), FP32 lane partials summed by warp_sum.
 template <int VPL>
 __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__restrict__ logits,
                                                             const float *__restrict__ bias, int tokens,
                                                             int experts, int top_k, int64_t *__restrict__ idx,
                                                             float *__restrict__ scores_f32,
-                                                            uint16_t *__restrict__ scores_bf16) {
+                                                            uint16_t *__restrict__ scores_bf16,
+                                                            const uint16_t *__restrict__ x,
+                                                            const uint16_t *__restrict__ gate_w, int hidden,
+                                                            uint16_t *__restrict__ sig) {
     grid_dependency_wait();
     grid_dependency_trigger();
     const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= tokens) return;
+    if (gate_w) {
+        const uint16_t *xr = x + static_cast<size_t>(t) * hidden;
+        float acc = 0.f;
+        for (int c = lane * 8; c < hidden; c += 256) acc = dot8(ld_cached(gate_w + c), ld_cached(xr + c), acc);
+        acc = warp_sum(acc);
+        if (lane == 0) sig[t] = f2bf(sigmoid_f32(rbf(acc)));
+    }
     const uint16_t *row = logits + static_cast<size_t>(t) * experts;
     int e;
     float w;
@@ -204,14 +216,16 @@ int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16
 }
 
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
-                         int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream) {
+                         int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream,
+                         const uint16_t *x, const uint16_t *gate_w, int hidden, uint16_t *sig) {
     const int grid = (tokens + 7) / 8;
+    if (gate_w && (!x || !sig || hidden % 256)) return set_error(MOE_EINVAL, "router: bad shared-gate arguments");
     if (experts <= 256)
         return launch_pdl(router_select_kernel<8>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
-                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16);
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig);
     if (experts <= 1024)
         return launch_pdl(router_select_kernel<32>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
-                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16);
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig);
     return set_error(MOE_EINVAL, "router: experts %d > 1024", experts);
 }
 
@@ -278,6 +292,12 @@ int moe_router_topk(const uint16_t *x, const uint16_t *router, const float *bias
     if (tokens == 0) return MOE_OK;
     if (int rc = lrb::require_sm100()) return rc;
     cudaStream_t s = lrb::as_stream(stream);
+    if (tokens > lrb::kDecodeMaxTokens) {
+        // prefill widths: tensor-core logits, then selection + shared gate
+        if (int rc = lrb::launch_router_tc(x, router, tokens, hidden, experts, logits, nullptr, s)) return rc;
+        return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, s, x,
+                                         shared_gate_w, hidden, sig);
+    }
     if (int rc = lrb::launch_router_logits(x, router, shared_gate_w, tokens, hidden, experts, logits, sig, s))
         return rc;
     return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, s);

@@ -1,0 +1,199 @@
+// Router logits at prefill widths on the tensor cores: logits[T, E] =
+// bf16(x[T, H] . W[E, H]^T) with FP32 accumulation (F.linear on BF16,
+// transformers qwen3_5_moe modeling :764).
+//
+// One CTA per (128 router rows, BN tokens): the router rows are the M = 128
+// operand and the token tile the N operand, both K-major with the 128-byte
+// swizzle, streamed by TMA through a 4-stage ring.  Thread 0 issues the loads
+// and the tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator; all four
+// warps then read their 32 TMEM lanes (= router rows) and write BF16 logits,
+// 32 consecutive experts of one token per warp store.  Every wait is bounded:
+// on timeout the CTA records an error in *error, drains its own copies and
+// products, and returns.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace lrb {
+
+namespace {
+
+constexpr int kRows = 128, kK = 64, kStagesTc = 4;
+constexpr uint64_t kRouterWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity) {
+    if (sm100::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (sm100::mbar_try_wait(bar, parity)) return true;
+        if ((i & 63) == 0 && now_ns() - t0 > kRouterWaitNs) return false;
+    }
+}
+
+}  // namespace
+
+template <int BN>
+__global__ void __launch_bounds__(128, 1)
+    router_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, int tokens,
+                     int experts, int hidden, uint16_t *__restrict__ logits, int32_t *__restrict__ error) {
+    constexpr int kA = kRows * kK * 2;
+    constexpr int kB = BN * kK * 2;
+    constexpr int kStage = kA + kB;
+    constexpr uint32_t kCols = BN < 32 ? 32 : BN;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ uint64_t full[kStagesTc], empty[kStagesTc], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int failed;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStagesTc; ++s) {
+            sm100::mbar_init(&full[s], 1);
+            sm100::mbar_init(&empty[s], 1);
+        }
+        sm100::mbar_init(&done, 1);
+        failed = 0;
+        sm100::fence_barrier_init();
+        sm100::tma_prefetch_map(&tm_w);
+        sm100::tma_prefetch_map(&tm_x);
+    }
+    if (warp == 0) {
+        sm100::tmem_alloc(&tmem_base, kCols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    grid_dependency_wait();  // x may come from the previous kernel
+    grid_dependency_trigger();
+
+    const int row0 = blockIdx.x * kRows, t0 = blockIdx.y * BN;
+    const int nk = hidden / kK;
+    if (threadIdx.x == 0) {
+        constexpr uint32_t idesc = sm100::idesc_bf16_f32(kRows, BN);
+        bool issued[kStagesTc] = {false, false, false, false};
+        uint32_t issued_parity[kStagesTc] = {0, 0, 0, 0};
+        auto load = [&](int kb) {
+            const int s = kb % kStagesTc;
+            uint8_t *st = smem + s * kStage;
+            sm100::mbar_expect_tx(&full[s], kStage);
+            sm100::tma_load_2d(st, &tm_w, &full[s], kb * kK, row0);
+            sm100::tma_load_2d(st + kA, &tm_x, &full[s], kb * kK, t0);
+            issued[s] = true;
+            issued_parity[s] = (kb / kStagesTc) & 1;
+        };
+        for (int kb = 0; kb < nk && kb < kStagesTc; ++kb) load(kb);
+        bool ok = true, any_mma = false;
+        for (int kb = 0; kb < nk; ++kb) {
+            const int s = kb % kStagesTc;
+            const uint32_t ph = (kb / kStagesTc) & 1;
+            if (!wait_bounded(&full[s], ph)) {
+                ok = false;
+                break;
+            }
+            sm100::tc_fence_after();
+            const uint32_t base = sm100::smem_u32(smem + s * kStage);
+            const uint64_t a = sm100::desc_kmajor_sw128(base), b = sm100::desc_kmajor_sw128(base + kA);
+#pragma unroll
+            for (int kk = 0; kk < kK / 16; ++kk)
+                sm100::mma_bf16(tmem, a + 2 * kk, b + 2 * kk, idesc, (kb | kk) != 0);
+            sm100::mma_commit(&empty[s]);
+            any_mma = true;
+            // Refill the previous stage once the products reading it are done,
+            // so that this step's products stay in flight meanwhile.
+            const int prev = kb - 1;
+            if (prev >= 0 && prev + kStagesTc < nk) {
+                if (!wait_bounded(&empty[prev % kStagesTc], (prev / kStagesTc) & 1)) {
+                    ok = false;
+                    break;
+                }
+                load(prev + kStagesTc);
+            }
+        }
+        if (!ok) {
+            failed = 1;
+            if (error) atomicExch(error, 6);
+            // drain: every issued copy lands before the CTA leaves
+            for (int s = 0; s < kStagesTc; ++s)
+                if (issued[s]) wait_bounded(&full[s], issued_parity[s]);
+        }
+        if (any_mma) sm100::mma_commit(&done);
+        else sm100::mbar_arrive(&done);
+    }
+    __syncwarp();
+    const bool ready = wait_bounded(&done, 0);
+    sm100::tc_fence_after();
+    if (ready && !failed) {
+        const int row = row0 + warp * 32 + lane;
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            __syncwarp();
+            sm100::tmem_ld16(taddr + c0, v);
+            sm100::tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int t = t0 + c0 + j;
+                if (t < tokens && row < experts) logits[static_cast<size_t>(t) * experts + row] = f2bf(v[j]);
+            }
+        }
+    } else if (!ready && lane == 0 && error) {
+        atomicExch(error, 6);
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 0 && ready) {
+        __syncwarp();
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem, kCols);
+    }
+}
+
+int router_tc_bn(int tokens) { return tokens >= 2048 ? 64 : 32; }
+
+template <int BN>
+int launch_router_tc_bn(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
+                        uint16_t *logits, int32_t *error, cudaStream_t stream) {
+    constexpr int kSmem = kStagesTc * (kRows * kK * 2 + BN * kK * 2) + 1024;
+    CUtensorMap tw{}, tx{};
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(experts)};
+        const uint64_t str[1] = {static_cast<uint64_t>(hidden) * 2};
+        if (int rc = make_map_bf16(&tw, router, 2, dims, str, kRows)) return rc;
+    }
+    {
+        const uint64_t dims[2] = {static_cast<uint64_t>(hidden), static_cast<uint64_t>(tokens)};
+        const uint64_t str[1] = {static_cast<uint64_t>(hidden) * 2};
+        if (int rc = make_map_bf16(&tx, x, 2, dims, str, BN)) return rc;
+    }
+    static bool configured = false;
+    if (!configured) {
+        LRB_CUDA(cudaFuncSetAttribute(router_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
+        configured = true;
+    }
+    const dim3 grid((experts + kRows - 1) / kRows, (tokens + BN - 1) / BN);
+    return launch_pdl(router_tc_kernel<BN>, grid, dim3(128), kSmem, stream, "router_tc_kernel", tw, tx, tokens,
+                      experts, hidden, logits, error);
+}
+
+int launch_router_tc(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
+                     uint16_t *logits, int32_t *error, cudaStream_t stream) {
+    LRB_REQUIRE(hidden % kK == 0, "router: hidden %d is not a multiple of %d", hidden, kK);
+    LRB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(router) % 16 == 0,
+                "router: x and router must be 16-byte aligned");
+    if (router_tc_bn(tokens) == 64)
+        return launch_router_tc_bn<64>(x, router, tokens, hidden, experts, logits, error, stream);
+    return launch_router_tc_bn<32>(x, router, tokens, hidden, experts, logits, error, stream);
+}
+
+}  // namespace lrb
