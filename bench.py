@@ -60,6 +60,13 @@ KERNEL_NAMES = {"router": "router_split_kernel | router_logits_kernel",
                 "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down; + combine at T <= 64)",
                 "combine": "combine_kernel (T > 64)", "unused": "-"}
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
+# the dominant kernel, from the ncu captures summarised under profiles/.
+PROFILED_TRAFFIC = {
+    1: (451_650_000, "profiles/swiglu_grouped_kernel_T16_config1.md"),
+    3: (2_004_844_000, "profiles/swiglu_grouped_kernel_T4096_config3.md"),
+}
+
 CONFIGS = {
     0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
     1: dict(tokens=16, bias="normal",
@@ -417,7 +424,9 @@ def run_ours(args, cfg, world, rank, local):
         "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dominant], "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else
-                     "fallback 6650 GB/s", "traffic": None,
+                     "fallback 6650 GB/s",
+                     "traffic": PROFILED_TRAFFIC.get(args.config, (None, None))[0] if dominant == "experts" else None,
+                     "traffic_source": PROFILED_TRAFFIC.get(args.config, (None, None))[1],
                      "algorithmic_bytes_per_launch": int(bytes_per_launch),
                      "launch_us": round(dur_ms * 1e3, 2),
                      "layer_gbs": round(layer_gbs, 1), "layer_frac": round(layer_gbs / hbm_peak, 4),
@@ -574,6 +583,24 @@ def run_ep(args, cfg, world, rank, local):
     }
 
 
+def run_profile(args, cfg):
+    """--profile N: N eager steps of the HBM-resident layer on one GPU, no CUDA
+    graphs and no timing, for a profiler's launch list or kernel capture."""
+    from lightreason_b200 import native
+
+    dev = torch.device("cuda", 0)
+    native.device_check(0)
+    cfg = dict(cfg, e2e_host_experts=False)
+    w, gu, dn, hbm, _ = build_layer(cfg, dev, 1)
+    xs = [to_dev(S.hidden_states(1, cfg["tokens"], step=i), dev) for i in range(min(args.profile, 4))]
+    flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
+    for i in range(args.profile):
+        flush_buf.sum()
+        hbm(xs[i % len(xs)])
+    torch.cuda.synchronize()
+    return {"profile_steps": args.profile, "workload": cfg["workload"], "tokens": cfg["tokens"]}
+
+
 def run_reference(args, cfg, world, rank):
     """Reference arm: the reference's CPU implementation on the host cores."""
     if rank != 0:
@@ -619,6 +646,8 @@ def main():
                     help="BASELINE config: 1 by default on one GPU, 4 (expert parallel) on more")
     ap.add_argument("--tokens", type=int, default=None, help="override the config's tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", type=int, default=0, metavar="N",
+                    help="run N eager layer steps of the config on one GPU (for ncu) and print a short status line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -634,6 +663,9 @@ def main():
         res = run_reference(args, cfg, world, rank)
         if res is not None:
             print(json.dumps(res), flush=True)
+        return
+    if args.profile:
+        print(json.dumps(run_profile(args, cfg)), flush=True)
         return
     world, rank, local = dist_setup()
     try:
