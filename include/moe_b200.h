@@ -243,6 +243,39 @@ int moe_gather_rows(const int64_t *descriptors, const int64_t *destinations,
                     void *stream);
 
 /* ------------------------------------------------------------------------
+ * Packed primary cache.  Replaces edge35b/bf16_gather_ada.cu stage_bf16_primary
+ * (:202-308, bound by native_bf16_gather.py:79-84 stage_primary) and
+ * gather_bf16_compact_tail (:312-381, native_bf16_gather.py:86-93).  Slots hold
+ * rows in the compact tile codec (tile t at t*384 + 128 * raw tiles before t);
+ * prefix_tables[bank] -> uint64 [E][tiles/32] = (raw tiles before the group
+ * << 32) | raw-tile bitmask.  Rows are multiples of 16384 bytes.
+ *
+ * moe_stage_primary: for row r < *count of plan (int32 [3][max_rows]: expert,
+ *   slot, miss) and every bank b, with layouts[b] = (packed slot base, raw slot
+ *   base, work rows base, packed slot stride, row bytes): a packed slot
+ *   (0 <= slot < packed_slots) is decoded into work row r+1 on a hit and, on a
+ *   miss, read from sources[b][expert] (tile codec: packed, bases, raw) or
+ *   miss_sources[b][expert] (a compact replica, raw == -1, or a raw replica,
+ *   bases == 0) into work row r+1 while its compact bytes refill the slot; a
+ *   raw slot (slot >= packed_slots) is filled on a miss and skipped on a hit;
+ *   slot < 0 stages into the work row only.
+ * moe_gather_compact_tail: row r writes the BF16 row of expert source_ids[r]
+ *   to destinations[b] + dest_ids[r] * sizes[b]; entries (int32 [2][max_rows]:
+ *   tail entry or -1, resident flag) select a tail entry at tail[b] = (base,
+ *   stride): a resident row is decoded from its entry, a miss with an entry
+ *   also writes the entry's compact bytes.
+ * ------------------------------------------------------------------------ */
+int moe_stage_primary(const int64_t *sources, const int64_t *miss_sources, const int64_t *layouts,
+                      const int64_t *prefix_tables, const int32_t *plan, const int32_t *count,
+                      int experts, int packed_slots, int max_rows, int banks, void *stream);
+int moe_gather_compact_tail(const int64_t *sources, const int64_t *destinations,
+                            const int64_t *sizes, const int64_t *prefix_tables,
+                            const int64_t *tail, const int32_t *source_ids,
+                            const int32_t *dest_ids, const int64_t *count,
+                            const int32_t *entries, const int64_t *resident, int experts,
+                            int max_rows, int banks, void *stream);
+
+/* ------------------------------------------------------------------------
  * Expert parallelism (no counterpart in the reference, which runs its MoE
  * layer on one GPU).  Rank r of `world` owns experts [r*E/world, (r+1)*E/world);
  * the exchange between these calls is NCCL all_to_all_single.

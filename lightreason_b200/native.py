@@ -58,6 +58,8 @@ _SIGNATURES = {
     "moe_layer_workspace_bytes": ([_i, _i, _i, _i, _i, _i], _sz),
     "moe_layer_forward": ([ctypes.POINTER(LayerWeights), _p, _i, _p, ctypes.POINTER(LayerIO), _p, _sz, _p], _i),
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
+    "moe_stage_primary": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
+    "moe_gather_compact_tail": ([_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
     "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_ep_unpack": ([_p, _i, _p, _p], _i),
     "moe_ep_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),
@@ -361,6 +363,59 @@ def gather_rows(descriptors, destinations, sizes, src, dst, count, *, max_copies
     check(lib().moe_gather_rows(_ptr(descriptors), _ptr(destinations), _ptr(sizes), _ptr(src), _ptr(dst), _ptr(count),
                                 experts, banks, max_copies, codec, stripes, threads, _stream(destinations.device)),
           "moe_gather_rows")
+
+
+def _table(name, t, dtype, dims=None):
+    _require(t.is_cuda and t.dtype == dtype and t.is_contiguous() and (dims is None or t.dim() == dims),
+             f"{name} must be a contiguous CUDA {dtype} tensor")
+
+
+def stage_primary(sources, miss_sources, layouts, prefix_tables, plan, count, *, experts, packed_slots):
+    """moe_stage_primary on the current stream (all tables CUDA tensors)."""
+    for name, t, dt in (("sources", sources, torch.int64), ("miss_sources", miss_sources, torch.int64),
+                        ("layouts", layouts, torch.int64), ("prefix_tables", prefix_tables, torch.int64),
+                        ("count", count, torch.int32)):
+        _table(name, t, dt)
+    _table("plan", plan, torch.int32, 2)
+    _require(plan.shape[0] == 3, "plan must be int32 [3, rows]")
+    banks = layouts.numel() // 5
+    _require(banks * 5 == layouts.numel() and sources.numel() == banks * experts * 3
+             and miss_sources.numel() == sources.numel(), "tables disagree with experts / banks")
+    check(lib().moe_stage_primary(_ptr(sources), _ptr(miss_sources), _ptr(layouts), _ptr(prefix_tables), _ptr(plan),
+                                  _ptr(count), experts, packed_slots, plan.shape[1], banks, _stream(plan.device)),
+          "moe_stage_primary")
+
+
+def gather_compact_tail(sources, destinations, sizes, prefix_tables, tail, src, dst, count, entries, resident, *,
+                        experts):
+    """moe_gather_compact_tail on the current stream (all tables CUDA tensors)."""
+    for name, t, dt in (("sources", sources, torch.int64), ("destinations", destinations, torch.int64),
+                        ("sizes", sizes, torch.int64), ("prefix_tables", prefix_tables, torch.int64),
+                        ("tail", tail, torch.int64), ("src", src, torch.int32), ("dst", dst, torch.int32),
+                        ("count", count, torch.int64), ("resident", resident, torch.int64)):
+        _table(name, t, dt)
+    _table("entries", entries, torch.int32, 2)
+    _require(entries.shape[0] == 2, "entries must be int32 [2, rows]")
+    banks = destinations.numel()
+    check(lib().moe_gather_compact_tail(_ptr(sources), _ptr(destinations), _ptr(sizes), _ptr(prefix_tables),
+                                        _ptr(tail), _ptr(src), _ptr(dst), _ptr(count), _ptr(entries), _ptr(resident),
+                                        experts, entries.shape[1], banks, _stream(src.device)),
+          "moe_gather_compact_tail")
+
+
+def prefix_table(bases) -> "torch.Tensor":
+    """Per (expert, 32 tiles): (raw tiles before the group << 32) | bitmask of
+    the group's raw tiles (base 255), from tile bases uint8 [E, tiles] (a
+    numpy array; tiles a multiple of 32).  Returns int64 [E, tiles / 32] (CPU)."""
+    import numpy as np
+
+    bases = np.asarray(bases, dtype=np.uint8)
+    _require(bases.ndim == 2 and bases.shape[1] % 32 == 0, "bases must be [E, tiles] with tiles % 32 == 0")
+    fallback = (bases == 255).reshape(bases.shape[0], -1, 32)
+    flags = np.packbits(fallback, axis=-1, bitorder="little").view(np.uint32).reshape(bases.shape[0], -1)
+    counts = fallback.sum(axis=-1, dtype=np.uint64)
+    before = counts.cumsum(axis=-1) - counts
+    return torch.from_numpy(((before << np.uint64(32)) | flags.astype(np.uint64)).view(np.int64))
 
 
 class PackedHostBanks:

@@ -52,3 +52,17 @@ class NativeBf16Gather:
             raise ValueError(f"Unknown gather policy {policy!r}")
         native.gather_rows(descriptors, destinations, sizes, src, dst, count, max_copies=max_copies,
                            experts=experts, codec=self.functions[policy], stripes=stripes, threads=threads)
+
+    def stage_primary(self, sources, miss_sources, layouts, prefix_tables, plan, count, *, experts, packed_slots):
+        """edge35b/native_bf16_gather.py:79-84: stage the plan's experts as BF16
+        rows (packed-slot hit, or miss from the source / replica with a slot
+        refill); plan int32 [3, rows] (expert, slot, miss), count int32 [1]."""
+        native.stage_primary(sources, miss_sources, layouts, prefix_tables, plan, count, experts=experts,
+                             packed_slots=packed_slots)
+
+    def copy_compact_tail(self, sources, destinations, sizes, prefixes, tail, src, dst, count, entries, resident,
+                          experts):
+        """edge35b/native_bf16_gather.py:86-93: BF16 rows into their slots; a
+        cacheable miss also writes its compact bytes into its tail entry."""
+        native.gather_compact_tail(sources, destinations, sizes, prefixes, tail, src, dst, count, entries, resident,
+                                   experts=experts)

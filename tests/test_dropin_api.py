@@ -106,3 +106,22 @@ def test_per_path_shape_errors(model):
     with pytest.raises(ValueError, match="contiguous"):
         h2 = torch.zeros((2048, 2), dtype=torch.bfloat16).t()
         block_experts.grouped_block(layer, h2, torch.zeros((2, 8), dtype=torch.long), w1.expand(2, 8))
+
+
+def test_prefix_table_counts_raw_tiles():
+    """native.prefix_table: per 32 tiles, (raw tiles before << 32) | raw bitmask,
+    the table stage_bf16_primary / gather_bf16_compact_tail index
+    (edge35b/packed_primary_cache.py:80-86 builds the same words)."""
+    from lightreason_b200 import native
+
+    bases = np.full((2, 96), 7, dtype=np.uint8)
+    bases[0, [0, 31, 32, 95]] = 255
+    bases[1, 40:72] = 255
+    got = native.prefix_table(bases).numpy().view(np.uint64)
+    assert got.shape == (2, 3)
+    assert got[0, 0] == (0 << 32) | (1 | (1 << 31))
+    assert got[0, 1] == (2 << 32) | 1
+    assert got[0, 2] == (3 << 32) | (1 << 31)
+    assert got[1, 0] == 0
+    assert got[1, 1] == (0 << 32) | (0xFFFFFFFF & ~0xFF)
+    assert got[1, 2] == (24 << 32) | 0xFF
