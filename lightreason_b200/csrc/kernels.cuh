@@ -117,9 +117,12 @@ struct DecodeRouteArgs {
 };
 int launch_route_decode(const DecodeRouteArgs &r, const PlanArgs &plan, cudaStream_t stream);
 
+// Scratch ints the wide (multi-CTA) permute needs in `hist` (0: one CTA suffices).
+int permute_hist_ints(int tokens, int top_k, int experts);
 int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets, int32_t *perm_token,
                    int32_t *perm_slot, int32_t *route_pos, int32_t *active, int32_t *num_active, int32_t *bad_routes,
-                   cudaStream_t stream);
+                   cudaStream_t stream,
+                   int32_t *hist = nullptr);
 
 template <class Src>
 int launch_experts(const Src &src, int max_groups, const uint16_t *x, int hidden, int inner, uint16_t *act,

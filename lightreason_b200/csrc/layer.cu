@@ -25,7 +25,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of the scratch arrays inside the caller's workspace.
 struct Layout {
     size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, plan, off1,
-        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, total;
+        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, perm_hist, total;
     int split_len;
 };
 
@@ -57,6 +57,7 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.split_len = grouped_tiles_max(tokens, experts, top_k, inner) * 4;
     L.split_cnt = take(static_cast<size_t>(L.split_len) * 4);
     L.gofe = take(E * 4);
+    L.perm_hist = take(static_cast<size_t>(permute_hist_ints(tokens, top_k, experts)) * 4);
     L.rpart = take(tokens <= kDecodeMaxTokens ? static_cast<size_t>(kRouterSplit) * T * (E + 1) * 4 : 0);
     L.part = take(grouped_part_floats(tokens, experts, top_k, inner) * 4);
     L.xs = take((R + T) * hidden * 2);
@@ -255,7 +256,7 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         }
         if (int rc = mark(1)) return rc;
         if (int rc = launch_permute(idx, tokens, K, E, offsets, route_token, at<int32_t>(ws, L.perm_slot), route_pos,
-                                    active, counters + 0, counters + 1, s))
+                                    active, counters + 0, counters + 1, s, at<int32_t>(ws, L.perm_hist)))
             return rc;
         if (int rc = launch_grouped_plan(pa, s)) return rc;
         if (int rc = mark(2)) return rc;

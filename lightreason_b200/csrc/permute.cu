@@ -1,6 +1,7 @@
 // Token permute: the eager expert dispatch order of Qwen3_5MoeExperts.forward
 // (transformers qwen3_5_moe modeling :730-744) -- ascending expert, then
-// slot-major, then token -- as a stable counting sort inside one CTA.
+// slot-major, then token -- as a stable counting sort: inside one CTA for up
+// to kOneCtaRoutes routes, else across the GPU in three launches (below).
 //
 // Routes are numbered r = slot * T + token (slot-major).  Warp w owns the
 // contiguous r-range [w*chunk, (w+1)*chunk).  Pass 1 counts, per warp and
@@ -16,6 +17,8 @@
 
 namespace lrb {
 
+constexpr int64_t kOneCtaRoutes = 2048;  // at most this many routes: the one-CTA sort
+
 __global__ void __launch_bounds__(1024) permute_kernel(const int64_t *__restrict__ idx, int tokens, int top_k,
                                                        int experts, int32_t *__restrict__ offsets,
                                                        int32_t *__restrict__ perm_token,
@@ -30,13 +33,174 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int64_t *__restrict
                   num_active, bad_routes, smem, scratch);
 }
 
+// Wide permute: the route order r is cut into chunks of kChunk routes, one per
+// warp.  count: each warp writes its chunk's per-expert counts to hist[c][e];
+// scan (one CTA): hist[c][e] becomes the first position of chunk c's routes of
+// expert e (expert offsets + the counts of earlier chunks), plus offsets,
+// active experts and the dropped-route count; place: each warp re-walks its
+// chunk and puts every route at its chunk base plus its rank among the equal
+// experts before it.  The scattered position writes spread over many SMs.
+constexpr int kChunk = 128;
+constexpr int kWarpsPerCta = 8;
+
+__global__ void __launch_bounds__(256) permute_count_kernel(const int64_t *__restrict__ idx, int tokens, int top_k,
+                                                            int experts, int chunks, int32_t *__restrict__ hist) {
+    extern __shared__ int32_t cnt_smem[];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * kWarpsPerCta + warp;
+    if (c >= chunks) return;
+    int32_t *cnt = cnt_smem + warp * experts;
+    for (int e = lane; e < experts; e += 32) cnt[e] = 0;
+    __syncwarp();
+    const int routes = tokens * top_k;
+    int64_t v[kChunk / 32];
+#pragma unroll
+    for (int j = 0; j < kChunk / 32; ++j) {
+        const int r = c * kChunk + 32 * j + lane;
+        v[j] = r < routes ? idx[static_cast<size_t>(r % tokens) * top_k + r / tokens] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kChunk / 32; ++j) {
+        const int e = v[j] >= 0 && v[j] < experts ? static_cast<int>(v[j]) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        if (e >= 0 && lane == __ffs(peers) - 1) cnt[e] += __popc(peers);
+        __syncwarp();
+    }
+    for (int e = lane; e < experts; e += 32) hist[static_cast<size_t>(c) * experts + e] = cnt[e];
+}
+
+__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t *__restrict__ hist, int chunks, int experts,
+                                                            int routes, int32_t *__restrict__ offsets,
+                                                            int32_t *__restrict__ active,
+                                                            int32_t *__restrict__ num_active,
+                                                            int32_t *__restrict__ bad_routes) {
+    __shared__ int32_t part[1024];
+    __shared__ int scratch[33];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    const int S = blockDim.x / experts;  // threads per expert, each over a contiguous run of chunks
+    const int q = threadIdx.x / experts, e = threadIdx.x % experts;
+    const bool mine = q < S;
+    const int c_begin = mine ? chunks * q / S : 0, c_end = mine ? chunks * (q + 1) / S : 0;
+    int sum = 0;
+    for (int c = c_begin; c < c_end; ++c) sum += hist[static_cast<size_t>(c) * experts + e];
+    part[threadIdx.x] = sum;
+    __syncthreads();
+    int total = 0, before = 0;
+    if (mine)
+        for (int j = 0; j < S; ++j) {
+            const int v = part[j * experts + e];
+            if (j < q) before += v;
+            total += v;
+        }
+    const bool lead = mine && q == 0;
+    int all = 0;
+    const int excl = block_exclusive_scan(lead ? total : 0, scratch, &all);
+    if (lead) {
+        offsets[e] = excl;
+        if (e == experts - 1) offsets[experts] = excl + total;
+    }
+    int n_active = 0;
+    const int apos = block_exclusive_scan(lead && total > 0 ? 1 : 0, scratch, &n_active);
+    if (lead && total > 0) active[apos] = e;
+    if (threadIdx.x == 0) {
+        *num_active = n_active;
+        if (bad_routes) *bad_routes = routes - all;
+    }
+    if (lead) part[e] = excl;
+    __syncthreads();
+    if (mine) {
+        int base = part[e] + before;
+        for (int c = c_begin; c < c_end; ++c) {
+            const size_t o = static_cast<size_t>(c) * experts + e;
+            const int v = hist[o];
+            hist[o] = base;
+            base += v;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) permute_place_kernel(const int64_t *__restrict__ idx, int tokens, int top_k,
+                                                            int experts, int chunks,
+                                                            const int32_t *__restrict__ hist,
+                                                            int32_t *__restrict__ perm_token,
+                                                            int32_t *__restrict__ perm_slot,
+                                                            int32_t *__restrict__ route_pos) {
+    extern __shared__ int32_t base_smem[];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x * kWarpsPerCta + warp;
+    if (c >= chunks) return;
+    int32_t *base = base_smem + warp * experts;
+    for (int e = lane; e < experts; e += 32) base[e] = hist[static_cast<size_t>(c) * experts + e];
+    __syncwarp();
+    const int routes = tokens * top_k;
+    int64_t v[kChunk / 32];
+#pragma unroll
+    for (int j = 0; j < kChunk / 32; ++j) {
+        const int r = c * kChunk + 32 * j + lane;
+        v[j] = r < routes ? idx[static_cast<size_t>(r % tokens) * top_k + r / tokens] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < kChunk / 32; ++j) {
+        const int r = c * kChunk + 32 * j + lane;
+        const int e = v[j] >= 0 && v[j] < experts ? static_cast<int>(v[j]) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        int p = -1;
+        if (e >= 0) p = base[e] + __popc(peers & ((1u << lane) - 1));
+        __syncwarp();
+        if (e >= 0 && lane == __ffs(peers) - 1) base[e] += __popc(peers);
+        __syncwarp();
+        if (r < routes) {
+            const int t = r % tokens, k = r / tokens;
+            route_pos[static_cast<size_t>(t) * top_k + k] = p;
+            if (p >= 0) {
+                perm_token[p] = t;
+                perm_slot[p] = k;
+            }
+        }
+    }
+}
+
+int permute_hist_ints(int tokens, int top_k, int experts) {
+    const int64_t routes = static_cast<int64_t>(tokens) * top_k;
+    return routes <= kOneCtaRoutes ? 0 : static_cast<int>((routes + kChunk - 1) / kChunk) * experts;
+}
+
 int permute_smem_bytes(int warps, int experts) {
     return static_cast<int>(sizeof(int32_t) * static_cast<size_t>(warps + 1) * experts);
 }
 
 int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets, int32_t *perm_token,
                    int32_t *perm_slot, int32_t *route_pos, int32_t *active, int32_t *num_active, int32_t *bad_routes,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int32_t *hist) {
+    const int64_t routes = static_cast<int64_t>(tokens) * top_k;
+    if (hist && routes > kOneCtaRoutes && experts <= 1024) {
+        const int chunks = static_cast<int>((routes + kChunk - 1) / kChunk);
+        const int ctas = (chunks + kWarpsPerCta - 1) / kWarpsPerCta;
+        const size_t smem = sizeof(int32_t) * kWarpsPerCta * experts;
+        if (smem > 48 * 1024) {
+            static bool wide = false;
+            if (!wide) {
+                LRB_CUDA(cudaFuncSetAttribute(permute_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(sizeof(int32_t) * kWarpsPerCta * 1024)));
+                LRB_CUDA(cudaFuncSetAttribute(permute_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              static_cast<int>(sizeof(int32_t) * kWarpsPerCta * 1024)));
+                wide = true;
+            }
+        }
+        if (int rc = launch_pdl(permute_count_kernel, dim3(ctas), dim3(256), smem, stream, "permute_count_kernel", idx,
+                                tokens, top_k, experts, chunks, hist))
+            return rc;
+        if (int rc = launch_pdl(permute_scan_kernel, dim3(1), dim3(1024), 0, stream, "permute_scan_kernel", hist,
+                                chunks, experts, static_cast<int>(routes), offsets, active, num_active, bad_routes))
+            return rc;
+        return launch_pdl(permute_place_kernel, dim3(ctas), dim3(256), smem, stream, "permute_place_kernel", idx,
+                          tokens, top_k, experts, chunks, hist, perm_token, perm_slot, route_pos);
+    }
     const int smem = permute_smem_bytes(32, experts);
     static bool configured = false;
     if (!configured) {
@@ -69,4 +233,27 @@ extern "C" int moe_permute(const int64_t *idx, int tokens, int top_k, int expert
     }
     return lrb::launch_permute(idx, tokens, top_k, experts, offsets, perm_token, perm_slot, route_pos, active,
                                num_active, bad_routes, lrb::as_stream(stream));
+}
+
+extern "C" int moe_permute_hist_ints(int tokens, int top_k, int experts) {
+    if (tokens <= 0 || top_k <= 0 || experts <= 0) return 0;
+    return lrb::permute_hist_ints(tokens, top_k, experts);
+}
+
+extern "C" int moe_permute_wide(const int64_t *idx, int tokens, int top_k, int experts, int32_t *offsets,
+                                int32_t *perm_token, int32_t *perm_slot, int32_t *route_pos, int32_t *active,
+                                int32_t *num_active, int32_t *bad_routes, int32_t *hist, void *stream) {
+    LRB_REQUIRE(experts >= 1 && experts <= 1024, "moe_permute_wide: experts %d outside [1, 1024]", experts);
+    LRB_REQUIRE(top_k >= 1 && tokens >= 0, "moe_permute_wide: bad tokens %d / top_k %d", tokens, top_k);
+    LRB_REQUIRE(static_cast<int64_t>(tokens) * top_k < (1 << 30), "moe_permute_wide: too many routes");
+    LRB_REQUIRE(!lrb::permute_hist_ints(tokens, top_k, experts) || hist,
+                "moe_permute_wide: hist (moe_permute_hist_ints ints) is required at this size");
+    if (tokens == 0 || !lrb::permute_hist_ints(tokens, top_k, experts))
+        return moe_permute(idx, tokens, top_k, experts, offsets, perm_token, perm_slot, route_pos, active, num_active,
+                           bad_routes, stream);
+    LRB_REQUIRE(idx && offsets && perm_token && perm_slot && route_pos && active && num_active,
+                "moe_permute_wide: null output");
+    if (int rc = lrb::require_sm100()) return rc;
+    return lrb::launch_permute(idx, tokens, top_k, experts, offsets, perm_token, perm_slot, route_pos, active,
+                               num_active, bad_routes, lrb::as_stream(stream), hist);
 }

@@ -1,5 +1,6 @@
 // Router: BF16 logits GEMV/GEMM + softmax/top-k/renormalise, and the sigmoid
 // shared-expert gate (transformers qwen3_5_moe modeling :762-770, :779, :788).
+#include <algorithm>
 #include <climits>
 
 #include "common.cuh"
@@ -155,18 +156,33 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(DecodeRouteArgs r, P
     grid_dependency_trigger();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (!r.route_in) {
-        const int cols = E + 1;
-        for (int i = threadIdx.x; i < T * cols; i += blockDim.x) {
-            const int t = i / cols, e = i % cols;
-            float s = 0.f;
+        const int cols = E + 1, n = T * cols;
+        // four elements per thread per round, all their partial loads in flight
+        constexpr int kU = 4;
+        for (int i0 = threadIdx.x; i0 < n; i0 += kU * blockDim.x) {
+            float s[kU];
 #pragma unroll
-            for (int k = 0; k < kRouterSplit; ++k) s += r.part[(static_cast<size_t>(k) * T + t) * cols + e];
-            const uint16_t lg = f2bf(s);
-            if (e < E) {
-                r.logits[static_cast<size_t>(t) * E + e] = lg;
-                z[t * E + e] = bf2f(lg) + (r.bias ? r.bias[e] : 0.0f);
-            } else if (r.has_gate) {
-                r.sig[t] = f2bf(sigmoid_f32(bf2f(lg)));
+            for (int u = 0; u < kU; ++u) {
+                const int i = i0 + u * blockDim.x;
+                s[u] = 0.f;
+                if (i < n) {
+                    const int t = i / cols, e = i % cols;
+#pragma unroll
+                    for (int k = 0; k < kRouterSplit; ++k) s[u] += r.part[(static_cast<size_t>(k) * T + t) * cols + e];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int i = i0 + u * blockDim.x;
+                if (i >= n) break;
+                const int t = i / cols, e = i % cols;
+                const uint16_t lg = f2bf(s[u]);
+                if (e < E) {
+                    r.logits[static_cast<size_t>(t) * E + e] = lg;
+                    z[t * E + e] = bf2f(lg) + (r.bias ? r.bias[e] : 0.0f);
+                } else if (r.has_gate) {
+                    r.sig[t] = f2bf(sigmoid_f32(bf2f(lg)));
+                }
             }
         }
         __syncthreads();
@@ -250,7 +266,7 @@ int launch_router_split(const uint16_t *x, const uint16_t *router, const uint16_
 
 int route_decode_smem(int tokens, int experts, int top_k) {
     return static_cast<int>(sizeof(float) * tokens * experts + sizeof(int32_t) * tokens * top_k +
-                            sizeof(int32_t) * 33 * experts);
+                            sizeof(int32_t) * std::max(33 * experts, 1024));
 }
 
 int launch_route_decode(const DecodeRouteArgs &r, const PlanArgs &plan, cudaStream_t stream) {

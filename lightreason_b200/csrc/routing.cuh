@@ -42,15 +42,19 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *scratch, int *to
 // The whole permute, executed by every thread of one CTA (blockDim.x is a
 // multiple of 32, >= experts).  idx_of(t, k) yields the expert id of (token,
 // slot).  cnt: shared [warps * experts + experts] ints; scratch: 33 ints.
+// Only the first ceil(routes / 32) warps own routes (and counting tables), so
+// few routes cost few table columns.
 template <class IdxOf>
 __device__ void permute_block(IdxOf idx_of, int tokens, int top_k, int experts, int32_t *offsets,
                               int32_t *perm_token, int32_t *perm_slot, int32_t *route_pos, int32_t *active,
                               int32_t *num_active, int32_t *bad_routes, int32_t *cnt, int *scratch) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
-    int32_t *total = cnt + warps * experts;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int routes = tokens * top_k;
+    const int warps = max(1, min(static_cast<int>(blockDim.x >> 5), (routes + 31) / 32));
+    int32_t *total = cnt + warps * experts;
     const int chunk = ((routes + warps * 32 - 1) / (warps * 32)) * 32;
-    const int r_begin = warp * chunk, r_end = min(routes, r_begin + chunk);
+    const int r_begin = warp < warps ? warp * chunk : routes;
+    const int r_end = warp < warps ? min(routes, r_begin + chunk) : routes;
 
     for (int i = threadIdx.x; i < warps * experts; i += blockDim.x) cnt[i] = 0;
     __syncthreads();

@@ -52,6 +52,8 @@ _SIGNATURES = {
     "moe_router_topk": ([_p, _p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p], _i),
     "moe_router_select": ([_p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
+    "moe_permute_hist_ints": ([_i, _i, _i], _i),
+    "moe_permute_wide": ([_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "moe_expert_rows": ([_p, _p, _p, _p, _i, _p, _sz, _p], _i),
     "moe_expert_block_rows": ([_p, _p, _p, _p, _p, _i, _i, _p, _sz, _p], _i),
     "moe_expert_block_rows_noalloc": ([_p, _p, _p, _p, _p, _i, _i, _p], _i),
@@ -158,7 +160,7 @@ def router_select(logits: torch.Tensor, bias: torch.Tensor | None = None, top_k:
 
 # --------------------------------------------------------------- permute ---
 
-def permute(idx: torch.Tensor, experts: int):
+def permute(idx: torch.Tensor, experts: int, *, wide: bool = False):
     """Eager dispatch order.  Returns offsets [E+1], perm_token [R], perm_slot
     [R], route_pos [T,K], active [E] (first num_active valid), num_active [1],
     bad_routes [1] (int32, on the device)."""
@@ -173,8 +175,15 @@ def permute(idx: torch.Tensor, experts: int):
     rpos = torch.empty((tokens, top_k), **i32)
     active = torch.empty(experts, **i32)
     counters = torch.zeros(2, **i32)
-    check(lib().moe_permute(_ptr(idx), tokens, top_k, experts, _ptr(offsets), _ptr(ptok), _ptr(pslot), _ptr(rpos),
-                            _ptr(active), counters.data_ptr(), counters.data_ptr() + 4, _stream(dev)), "moe_permute")
+    if wide:
+        hist = torch.empty(max(lib().moe_permute_hist_ints(tokens, top_k, experts), 1), **i32)
+        check(lib().moe_permute_wide(_ptr(idx), tokens, top_k, experts, _ptr(offsets), _ptr(ptok), _ptr(pslot),
+                                     _ptr(rpos), _ptr(active), counters.data_ptr(), counters.data_ptr() + 4,
+                                     hist.data_ptr(), _stream(dev)), "moe_permute_wide")
+    else:
+        check(lib().moe_permute(_ptr(idx), tokens, top_k, experts, _ptr(offsets), _ptr(ptok), _ptr(pslot),
+                                _ptr(rpos), _ptr(active), counters.data_ptr(), counters.data_ptr() + 4,
+                                _stream(dev)), "moe_permute")
     return offsets, ptok[:tokens * top_k], pslot[:tokens * top_k], rpos, active, counters[:1], counters[1:]
 
 

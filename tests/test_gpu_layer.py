@@ -111,15 +111,17 @@ def test_router_select_exact_ties_take_lower_ids(dev):
     assert got[2].tolist() == [0, 2, 4, 6, 8, 10, 12, 14]
 
 
+@pytest.mark.parametrize("wide", [False, True])
 @pytest.mark.parametrize("tokens,experts,top_k", [(1, 256, 8), (16, 256, 8), (333, 256, 8), (4096, 256, 8),
-                                                   (50, 1024, 4), (7, 64, 8)])
-def test_permute_bit_exact(dev, tokens, experts, top_k):
+                                                   (50, 1024, 4), (7, 64, 8), (8192, 256, 8), (3000, 1024, 1),
+                                                   (2000, 16, 2)])
+def test_permute_bit_exact(dev, tokens, experts, top_k, wide):
     rng = np.random.default_rng(tokens * 7 + experts)
     p = rng.zipf(1.1, size=experts * 4).astype(np.float64)
     p = p[:experts] / p[:experts].sum()
     idx = np.stack([rng.choice(experts, size=top_k, replace=False, p=p) for _ in range(tokens)]).astype(np.int64)
     want = O.permute(idx, experts)
-    off, ptok, pslot, rpos, active, n_active, bad = native.permute(torch.from_numpy(idx).to(dev), experts)
+    off, ptok, pslot, rpos, active, n_active, bad = native.permute(torch.from_numpy(idx).to(dev), experts, wide=wide)
     torch.cuda.synchronize()
     assert np.array_equal(off.cpu().numpy(), want[0])
     assert np.array_equal(ptok.cpu().numpy(), want[1])
@@ -128,6 +130,30 @@ def test_permute_bit_exact(dev, tokens, experts, top_k):
     n = int(n_active.item())
     assert active[:n].cpu().numpy().tolist() == sorted(set(idx.reshape(-1).tolist()))
     assert int(bad.item()) == 0
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_permute_drops_out_of_range_ids_at_width(dev, wide):
+    """Dropped ids at 4096 routes (the wide path's size): the valid routes keep
+    the eager order (ascending expert, slot-major, token) and no position."""
+    experts, tokens, top_k = 64, 1024, 4
+    rng = np.random.default_rng(5)
+    idx = rng.integers(0, experts, size=(tokens, top_k)).astype(np.int64)
+    idx[3, 1], idx[100, 0], idx[777, 3], idx[1023, 0] = -1, experts, 1000, -5
+    r_t, r_k = np.tile(np.arange(tokens), top_k), np.repeat(np.arange(top_k), tokens)
+    e = idx[r_t, r_k]
+    valid = (e >= 0) & (e < experts)
+    order = np.argsort(np.where(valid, e, experts), kind="stable")[:int(valid.sum())]
+    want_pos = np.full((tokens, top_k), -1, dtype=np.int32)
+    want_pos[r_t[order], r_k[order]] = np.arange(order.size)
+    want_off = np.concatenate(([0], np.cumsum(np.bincount(e[valid], minlength=experts))))
+    off, ptok, pslot, rpos, active, n_active, bad = native.permute(torch.from_numpy(idx).to(dev), experts, wide=wide)
+    torch.cuda.synchronize()
+    assert int(bad.item()) == 4
+    assert np.array_equal(off.cpu().numpy(), want_off)
+    assert np.array_equal(ptok.cpu().numpy()[:order.size], r_t[order])
+    assert np.array_equal(pslot.cpu().numpy()[:order.size], r_k[order])
+    assert np.array_equal(rpos.cpu().numpy(), want_pos)
 
 
 def test_permute_drops_out_of_range_ids(dev):
