@@ -458,17 +458,22 @@ def run_ours(args, cfg, world, rank, local):
 
 
 def run_ep(args, cfg, world, rank, local):
-    """one expert-parallel step per timed step."""
-    import torch.distributed as dist
+    """one expert-parallel step per timed step.
 
+    transport "p2p" (default on N > 1 GPUs): the NVLink peer-memory exchange,
+    no host synchronisation, every timed step one CUDA-graph replay; "nccl":
+    the all_to_all_single exchange, eager steps (the split sizes are read on
+    the host every step).  On one GPU the exchange is a device copy."""
     from lightreason_b200 import native
-    from lightreason_b200.expert_parallel import ExpertParallelLayer, TorchExchange, run_virtual_ranks, shard
+    from lightreason_b200.expert_parallel import (ExpertParallelLayer, PeerExchange, TorchExchange,
+                                                  run_virtual_ranks, shard)
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     native.device_check(local)
     hbm_peak, tensor_peak, peak_src = peaks()
     tokens = cfg["tokens"]
+    transport = args.transport if world > 1 else "local"
     seed = 4                                   # one layer, the same on every rank
     t_setup = time.perf_counter()
     w = S.layer_weights(seed, bias=cfg["bias"])
@@ -479,10 +484,17 @@ def run_ep(args, cfg, world, rank, local):
     for j, e in enumerate(mine):
         gu[j].copy_(d(S.expert_gate_up(seed, 0, e)))
         dn[j].copy_(d(S.expert_down(seed, 0, e)))
+    peer = None
+    if transport == "p2p":
+        peer = PeerExchange(world=world, rank=rank, tokens=tokens, top_k=TOP_K, hidden=HIDDEN, experts=EXPERTS,
+                            device=dev)
+        exchange = peer
+    else:
+        exchange = TorchExchange() if world > 1 else None
     layer = ExpertParallelLayer(router=d(w.router), gate_up=gu, down=dn, shared_gate=d(w.sh_gate),
                                 shared_up=d(w.sh_up), shared_down=d(w.sh_down), shared_gate_w=d(w.sh_gate_w),
                                 bias=torch.from_numpy(w.bias).to(dev), rank=rank, world=world, tokens=tokens,
-                                exchange=TorchExchange() if world > 1 else None)
+                                exchange=exchange)
     del gu, dn
     pool = 8
     xs_np = [S.hidden_states(100 + 17 * rank, tokens, step=i) for i in range(pool)]
@@ -493,7 +505,11 @@ def run_ep(args, cfg, world, rank, local):
     xin = torch.empty_like(out)
     flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
     flush_out = torch.empty((), dtype=torch.float32, device=dev)
-    log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, experts {mine.start}..{mine.stop - 1}")
+
+    def flush():
+        torch.sum(flush_buf, 0, out=flush_out)
+    log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, experts "
+        f"{mine.start}..{mine.stop - 1}, transport {transport}")
 
     def step(x, o, stage=None):
         if world > 1:
@@ -502,6 +518,7 @@ def run_ep(args, cfg, world, rank, local):
             run_virtual_ranks([layer], [x], outs=[o], stage_events=stage)
 
     def loop(kind, stage_idx=None):
+        """Eager steps (the NCCL exchange reads its split sizes on the host)."""
         for i in range(args.warmup):
             step(xs[i % pool], out)
         torch.cuda.synchronize()
@@ -510,9 +527,8 @@ def run_ep(args, cfg, world, rank, local):
               for _ in range(args.steps)]
         stg = [[torch.cuda.Event(enable_timing=True) if stage_idx and j in stage_idx else None for j in range(8)]
                for _ in range(args.steps)]
-        splits = []
         for i in range(args.steps):
-            torch.sum(flush_buf, 0, out=flush_out)
+            flush()
             j = (args.warmup + i) % pool
             ev[i][0].record()
             if kind == "e2e":
@@ -522,27 +538,50 @@ def run_ep(args, cfg, world, rank, local):
             else:
                 step(xs[j], out, stg[i] if stage_idx else None)
             ev[i][1].record()
-            splits.append(layer.last_splits)
         torch.cuda.synchronize()
         barrier(world)
         ms = [a.elapsed_time(b) for a, b in ev]
         kern = [row[4].elapsed_time(row[5]) for row in stg] if stage_idx else None
-        return ms, kern, splits
+        return ms, kern
 
     sampler = ClockSampler(local)
     with sampler:
-        ms, _, splits = loop("device")
-        _, kern_ms, _ = loop("device", stage_idx=(4, 5))
-        e2e_ms, _, _ = loop("e2e")
+        if transport == "p2p":
+            def dev_step(i, stage):
+                layer(xs[i % pool], out=out, stage_events=stage)
+
+            def e2e_step(i, stage):
+                xin.copy_(xs_host[i % pool], non_blocking=True)
+                layer(xin, out=out, stage_events=stage)
+                out_host.copy_(out, non_blocking=True)
+            for i in range(args.warmup):          # buffers and workspaces exist before capture
+                dev_step(i, None)
+            torch.cuda.synchronize()
+            ms, _, _ = timed_steps(dev_step, args.steps, args.warmup, flush, world)
+            _, stage_ms, _ = timed_steps(dev_step, args.steps, args.warmup, flush, world, stage_events=(4, 5))
+            kern_ms = stage_ms["experts"]
+            e2e_ms, _, _ = timed_steps(e2e_step, args.steps, args.warmup, flush, world)
+            peer.check()
+        else:
+            ms, _ = loop("device")
+            _, kern_ms = loop("device", stage_idx=(4, 5))
+            e2e_ms, _ = loop("e2e")
     clocks = sampler.summary()
     total_ms = dist_max(sum(ms), world)
     e2e_total = dist_max(sum(e2e_ms), world)
     value = world * tokens * args.steps / (total_ms / 1e3)
     # this rank's work in the last timed step
-    m = splits[-1] if splits[-1] is not None else [[int(layer.send_counts.sum())]]
-    received = sum(m[s][rank] for s in range(world))
-    leaving = sum(m[rank][dd] for dd in range(world) if dd != rank)
-    local_ids = layer.recv_meta[:received].cpu().numpy()
+    if transport == "p2p":
+        received = int(peer.recv_total.item())
+        local_ids = layer.p_route_in[tokens:tokens + received, 0].cpu().numpy()
+        sent = layer.offsets.cpu().numpy()
+        el = EXPERTS // world
+        leaving = int(sent[EXPERTS] - (sent[(rank + 1) * el] - sent[rank * el]))
+    else:
+        m = layer.last_splits if layer.last_splits is not None else [[int(layer.send_counts.sum())]]
+        received = sum(m[s][rank] for s in range(world))
+        leaving = sum(m[rank][dd] for dd in range(world) if dd != rank)
+        local_ids = layer.recv_meta[:received].cpu().numpy()
     u_local = len(set(local_ids.tolist()))
     rows = tokens + received
     kernel_bytes = ((u_local + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + 2 * rows * HIDDEN * 2
@@ -554,7 +593,15 @@ def run_ep(args, cfg, world, rank, local):
     t_hbm, t_tc = kernel_bytes / (hbm_peak * 1e9), kernel_flops / (tensor_peak * 1e12)
     bound = "hbm" if t_hbm >= t_tc else "tensor"
     achieved, peak, unit = (gbs, hbm_peak, "GB/s") if bound == "hbm" else (tfs, tensor_peak, "TFLOP/s")
-    launches = 10  # router logits+select, permute, dispatch, unpack, local permute+plan+gather+grouped, combine
+    # router tc + select, permute (3 when wide), dispatch, collect, local permute/plan/gather/grouped, return,
+    # finish, combine  (NCCL: dispatch, unpack instead of collect/return/finish)
+    launches = 14 if transport == "p2p" else 12
+    if peer is not None:
+        peer.close()
+    timing = ("each timed step one CUDA-graph replay of the whole rank step (no host synchronisation), CUDA "
+              "events around it, max over ranks of the summed step times" if transport == "p2p" else
+              "CUDA events around each whole step on the compute stream (includes the host read of the "
+              "all-to-all split sizes), max over ranks of the summed step times")
     return {
         "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -563,11 +610,10 @@ def run_ep(args, cfg, world, rank, local):
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, Zipf(1.1) router bias)",
         "config": {"workload": cfg["workload"], "tokens_per_gpu": tokens, "hidden": HIDDEN, "inner": INNER,
                    "experts": EXPERTS, "experts_per_gpu": len(mine), "top_k": TOP_K, "shared_expert": True,
-                   "parallelism": f"ep{world}", "rank0_rows_received": received,
+                   "parallelism": f"ep{world}", "transport": transport, "rank0_rows_received": received,
                    "rank0_routes_leaving": leaving, "rank0_nvlink_bytes_per_step": 2 * leaving * HIDDEN * 2,
                    "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window",
-                   "timing": "CUDA events around each whole step on the compute stream (includes the host read "
-                             "of the all-to-all split sizes), max over ranks of the summed step times"},
+                   "timing": timing},
         "roofline": {"bound": bound, "kernel": "swiglu_grouped_kernel (local experts + shared, rank 0 rows)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": unit, "frac": round(achieved / peak, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
@@ -637,6 +683,11 @@ def run_reference(args, cfg, world, rank):
 
 
 def main():
+    # The one JSON line goes to the real stdout; anything libraries print there
+    # (NCCL's version banner, for one) is sent to stderr instead.
+    json_out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -646,6 +697,8 @@ def main():
                     help="BASELINE config: 1 by default on one GPU, 4 (expert parallel) on more")
     ap.add_argument("--tokens", type=int, default=None, help="override the config's tokens per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
+                    help="expert-parallel exchange on N > 1 GPUs: NVLink peer memory (default) or NCCL all_to_all")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="run N eager layer steps of the config on one GPU (for ncu) and print a short status line")
     args = ap.parse_args()
@@ -662,10 +715,10 @@ def main():
         world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
         res = run_reference(args, cfg, world, rank)
         if res is not None:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=json_out, flush=True)
         return
     if args.profile:
-        print(json.dumps(run_profile(args, cfg)), flush=True)
+        print(json.dumps(run_profile(args, cfg)), file=json_out, flush=True)
         return
     world, rank, local = dist_setup()
     try:
@@ -675,7 +728,7 @@ def main():
             gu, dn = w.stacked()
             res["cpu_baseline"] = cpu_baseline(cfg, w, gu, dn, 4)
         if rank == 0:
-            print(json.dumps(res), flush=True)
+            print(json.dumps(res), file=json_out, flush=True)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -311,6 +311,54 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
                    const uint16_t *shared_rows, const uint16_t *sig, int tokens, int top_k,
                    int hidden, uint16_t *out, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Expert-parallel exchange over NVLink peer memory (no host synchronisation;
+ * no counterpart in the reference).  Every rank allocates one symmetric
+ * buffer with moe_ipc_alloc (zero-filled; the 64-byte handle goes to the
+ * peers, which map it with moe_ipc_open) holding, at the byte offsets below:
+ * flags_dispatch uint32[world], flags_return uint32[world], count int32[world],
+ * meta int32[world][capacity][2], rx BF16[world][capacity][hidden] and ret
+ * BF16[capacity][hidden]; capacity >= tokens * top_k.  `peers` lists every
+ * rank's buffer as mapped in this process (its own included); step (uint32,
+ * start at 1), sync (int32[2], zero), error and recv_total are this rank's
+ * device words.  One step:
+ *   moe_router_topk, moe_permute(_wide) of the rank's own tokens;
+ *   moe_ep_p2p_dispatch   rows and (local expert, position) into the owners'
+ *                         rx / meta, then releases their flags_dispatch;
+ *   moe_ep_p2p_collect    waits for every sender, writes xin [own tokens ;
+ *                         received rows], route_in (own tokens -> the shared
+ *                         expert, local id local_experts; unused rows -1) and
+ *                         each received row's return address;
+ *   moe_layer_forward     rows_mode over tokens + recv_cap rows, local experts
+ *                         plus the shared expert appended as local expert El;
+ *   moe_ep_p2p_return     rows back to their senders' ret, releases
+ *                         flags_return;
+ *   moe_ep_p2p_finish     waits for every return, advances *step;
+ *   moe_ep_combine        over ret (in the permuted order), scores, the shared
+ *                         rows and sig.
+ * Waits give up after 1 s with *error = 1 (dispatch), 2 (return) or 3
+ * (received rows above recv_cap); the GPU is never left waiting. */
+typedef struct moe_ep_p2p {
+    const int64_t *peers;
+    int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
+    int world, rank, capacity, hidden, top_k, experts, local_experts;
+    uint32_t *step;
+    int32_t *sync, *error, *recv_total;
+} moe_ep_p2p;
+
+int moe_ipc_alloc(size_t bytes, void **ptr, void *handle64);
+int moe_ipc_free(void *ptr);
+int moe_ipc_open(const void *handle64, void **ptr);
+int moe_ipc_close(void *ptr);
+int moe_ep_p2p_dispatch(const moe_ep_p2p *p, const uint16_t *x, const int64_t *idx,
+                        const int32_t *offsets, const int32_t *perm_token,
+                        const int32_t *perm_slot, void *stream);
+int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int recv_cap,
+                       uint16_t *xin, int64_t *route_in, int64_t *ret_addr, void *stream);
+int moe_ep_p2p_return(const moe_ep_p2p *p, const uint16_t *rows, const int64_t *ret_addr,
+                      void *stream);
+int moe_ep_p2p_finish(const moe_ep_p2p *p, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

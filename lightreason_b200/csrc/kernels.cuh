@@ -80,6 +80,15 @@ int launch_grouped_plan(const PlanArgs &a, cudaStream_t stream);
 int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
                          int routes, int shared_rows, int hidden, uint16_t *xs, cudaStream_t stream);
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
+
+// Expert-parallel exchange over peer memory (ep_p2p.cu); fields as moe_ep_p2p.
+struct EpP2PArgs {
+    const int64_t *peers;
+    int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
+    int world, rank, capacity, hidden, top_k, experts, local_experts;
+    uint32_t *step;
+    int32_t *sync, *error, *recv_total;
+};
 // BF16 tensor map: dims[0] innermost, 128-byte swizzle, box {64, box_rows(, 1)}.
 int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,
                   uint32_t box_rows);

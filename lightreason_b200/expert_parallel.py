@@ -29,6 +29,7 @@ the exchange.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -187,12 +188,145 @@ class ExpertParallelLayer:
     # -- one distributed step
     def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stage_events=None) -> torch.Tensor:
         _require(self.exchange is not None, "forward needs an exchange (use run_virtual_ranks for one process)")
+        if isinstance(self.exchange, PeerExchange):
+            return self._forward_peer(x, torch.empty_like(x) if out is None else out, stage_events)
         self.dispatch(x)
         self.last_splits = exchange_step(self, self.exchange,
                                          lambda received: self.compute(received, stage_events))
         return self.combine(torch.empty_like(x) if out is None else out)
 
     __call__ = forward
+
+    # -- the peer-memory step: no host synchronisation, graph-capturable
+    def _peer_buffers(self):
+        ex = self.exchange
+        if getattr(self, "_peer_ready", False):
+            return
+        _require(ex.capacity >= self.max_tokens * self.top_k, "peer exchange capacity below tokens * top_k")
+        d = self.dev
+        self.recv_cap = ex.recv_cap
+        n = self.max_tokens + self.recv_cap
+        self.p_xin = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=d)
+        self.p_route_in = torch.empty((n, 1), dtype=torch.int64, device=d)
+        self.p_yin = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=d)
+        self.p_ret_addr = torch.zeros(max(self.recv_cap, 1), dtype=torch.int64, device=d)
+        hist = lib().moe_permute_hist_ints(self.max_tokens, self.top_k, self.experts)
+        self.p_hist = torch.empty(max(hist, 1), dtype=torch.int32, device=d)
+        self._peer_ready = True
+
+    def _forward_peer(self, x, out, stage_events):
+        ex = self.exchange
+        self._peer_buffers()
+        native._cuda_bf16(x, "x")
+        tokens = x.shape[0]
+        _require(tokens <= self.max_tokens and x.shape[1] == self.hidden, "x must be [T <= tokens, H]")
+        self.tokens = tokens
+        s = native._stream(self.dev)
+        a = ctypes.byref(ex.args)
+        check(lib().moe_router_topk(_ptr(x), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w), tokens,
+                                    self.hidden, self.experts, self.top_k, _ptr(self.logits), _ptr(self.idx), None,
+                                    _ptr(self.scores), _ptr(self.sig), s), "moe_router_topk")
+        c = self.counters.data_ptr()
+        check(lib().moe_permute_wide(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
+                                     _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos),
+                                     _ptr(self.active), c, c + 4, _ptr(self.p_hist), s), "moe_permute_wide")
+        check(lib().moe_ep_p2p_dispatch(a, _ptr(x), _ptr(self.idx), _ptr(self.offsets), _ptr(self.perm_token),
+                                        _ptr(self.perm_slot), s), "moe_ep_p2p_dispatch")
+        check(lib().moe_ep_p2p_collect(a, _ptr(x), tokens, self.recv_cap, _ptr(self.p_xin), _ptr(self.p_route_in),
+                                       _ptr(self.p_ret_addr), s), "moe_ep_p2p_collect")
+        n = tokens + self.recv_cap
+        self.local(self.p_xin[:n], route_in=self.p_route_in[:n], out=self.p_yin[:n], stage_events=stage_events,
+                   rows_mode=True)
+        check(lib().moe_ep_p2p_return(a, self.p_yin[tokens:].data_ptr(), _ptr(self.p_ret_addr), s),
+              "moe_ep_p2p_return")
+        check(lib().moe_ep_p2p_finish(a, s), "moe_ep_p2p_finish")
+        check(lib().moe_ep_combine(ctypes.c_void_p(ex.ret_ptr), _ptr(self.route_pos), _ptr(self.scores),
+                                   _ptr(self.p_yin), _ptr(self.sig), tokens, self.top_k, self.hidden, _ptr(out), s),
+              "moe_ep_combine")
+        return out
+
+
+class PeerExchange:
+    """Symmetric buffers over NVLink for ExpertParallelLayer: one CUDA-IPC
+    buffer per rank (moe_ipc_alloc), mapped by every peer, laid out as
+    moe_ep_p2p describes.  capacity = rows one rank may send to one peer
+    (>= tokens * top_k); recv_cap = rows a rank may receive in a step (default
+    world * capacity, the bound that never drops a route).  Construct it on
+    every rank of the process group together; close() before the group ends."""
+
+    def __init__(self, *, world, rank, tokens, top_k, hidden, experts, device, recv_cap=None, group=None):
+        import torch.distributed as dist
+
+        self.dist, self.group = dist, group
+        self.world, self.rank = world, rank
+        self.capacity = tokens * top_k
+        self.recv_cap = world * self.capacity if recv_cap is None else recv_cap
+        cap, h = self.capacity, hidden
+        align = lambda v, a: (v + a - 1) // a * a  # noqa: E731
+        off_fd, off_fr, off_count, off_meta = 0, 256, 512, 1024
+        off_rx = align(off_meta + world * cap * 8, 4096)
+        off_ret = align(off_rx + world * cap * h * 2, 4096)
+        total = off_ret + cap * h * 2
+        _require(world <= 64, "at most 64 ranks")
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_uint8 * 64)()
+        check(lib().moe_ipc_alloc(total, ctypes.byref(base), handle), "moe_ipc_alloc")
+        self._base = base
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=device)
+        if world > 1:
+            every = torch.empty(world * 64, dtype=torch.uint8, device=device)
+            dist.all_gather_into_tensor(every, mine, group=group)
+            handles = every.view(world, 64).cpu().numpy()
+        else:
+            handles = mine.view(1, 64).cpu().numpy()
+        self._opened = []
+        peers = []
+        for q in range(world):
+            if q == rank:
+                peers.append(base.value)
+                continue
+            h_q = (ctypes.c_uint8 * 64)(*handles[q].tolist())
+            p = ctypes.c_void_p()
+            check(lib().moe_ipc_open(h_q, ctypes.byref(p)), "moe_ipc_open")
+            self._opened.append(p)
+            peers.append(p.value)
+        i32 = dict(dtype=torch.int32, device=device)
+        self.peers = torch.tensor(peers, dtype=torch.int64, device=device)
+        self.step = torch.ones(1, **i32)
+        self.sync = torch.zeros(2, **i32)
+        self.error = torch.zeros(1, **i32)
+        self.recv_total = torch.zeros(1, **i32)
+        self.ret_ptr = base.value + off_ret
+        self.args = native.EpP2P(peers=self.peers.data_ptr(), off_flags_dispatch=off_fd, off_flags_return=off_fr,
+                                 off_count=off_count, off_meta=off_meta, off_rx=off_rx, off_ret=off_ret, world=world,
+                                 rank=rank, capacity=cap, hidden=hidden, top_k=top_k, experts=experts,
+                                 local_experts=experts // world, step=self.step.data_ptr(),
+                                 sync=self.sync.data_ptr(), error=self.error.data_ptr(),
+                                 recv_total=self.recv_total.data_ptr())
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier(group=group)  # every mapping exists before any rank's first step
+
+    def check(self) -> None:
+        """Raise if a bounded wait of an earlier step gave up (syncs the device)."""
+        code = int(self.error.item())
+        if code:
+            what = {1: "a sender never released its rows", 2: "a receiver never returned its rows",
+                    3: "received rows exceed recv_cap"}.get(code, "unknown")
+            raise RuntimeError(f"expert-parallel exchange failed ({code}): {what}")
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        if self.world > 1:
+            self.dist.barrier(group=self.group)
+        for p in self._opened:
+            lib().moe_ipc_close(p)
+        self._opened.clear()
+        if self.world > 1:
+            self.dist.barrier(group=self.group)
+        if self._base:
+            lib().moe_ipc_free(self._base)
+            self._base = None
 
 
 def run_virtual_ranks(layers: list[ExpertParallelLayer], xs: list[torch.Tensor], outs=None,
@@ -225,4 +359,4 @@ def run_virtual_ranks(layers: list[ExpertParallelLayer], xs: list[torch.Tensor],
     return [layer.combine(o) for layer, o in zip(layers, outs)]
 
 
-__all__ = ["ExpertParallelLayer", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]
+__all__ = ["ExpertParallelLayer", "PeerExchange", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]

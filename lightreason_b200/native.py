@@ -34,6 +34,15 @@ class LayerWeights(ctypes.Structure):
                 ("experts", _i), ("hidden", _i), ("inner", _i), ("shared_inner", _i), ("top_k", _i)]
 
 
+class EpP2P(ctypes.Structure):
+    """moe_ep_p2p: the peer-memory exchange of one expert-parallel rank."""
+    _fields_ = [("peers", _p), ("off_flags_dispatch", ctypes.c_int64), ("off_flags_return", ctypes.c_int64),
+                ("off_count", ctypes.c_int64), ("off_meta", ctypes.c_int64), ("off_rx", ctypes.c_int64),
+                ("off_ret", ctypes.c_int64), ("world", _i), ("rank", _i), ("capacity", _i), ("hidden", _i),
+                ("top_k", _i), ("experts", _i), ("local_experts", _i), ("step", _p), ("sync", _p), ("error", _p),
+                ("recv_total", _p)]
+
+
 class LayerIO(ctypes.Structure):
     """moe_layer_io of include/moe_b200.h."""
 
@@ -62,6 +71,14 @@ _SIGNATURES = {
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "moe_stage_primary": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "moe_gather_compact_tail": ([_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
+    "moe_ipc_alloc": ([_sz, ctypes.POINTER(_p), _p], _i),
+    "moe_ipc_free": ([_p], _i),
+    "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
+    "moe_ipc_close": ([_p], _i),
+    "moe_ep_p2p_dispatch": ([ctypes.POINTER(EpP2P), _p, _p, _p, _p, _p, _p], _i),
+    "moe_ep_p2p_collect": ([ctypes.POINTER(EpP2P), _p, _i, _i, _p, _p, _p, _p], _i),
+    "moe_ep_p2p_return": ([ctypes.POINTER(EpP2P), _p, _p, _p], _i),
+    "moe_ep_p2p_finish": ([ctypes.POINTER(EpP2P), _p], _i),
     "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_ep_unpack": ([_p, _i, _p, _p], _i),
     "moe_ep_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),

@@ -145,3 +145,84 @@ def test_nccl_ranks_equal_single_gpu_layer():
     while not failures.empty():
         errs.append(failures.get())
     assert not errs, errs
+
+
+def test_peer_exchange_one_rank_equals_single_gpu_layer(dev, weights):
+    """The peer-memory step at world 1 (its own buffer as the only peer; every
+    wait is on a kernel that already finished earlier in the stream): kernels
+    and buffer layout, bit-exact against the single-GPU layer, twice in a row,
+    and replayed from a CUDA graph."""
+    from lightreason_b200.expert_parallel import PeerExchange
+
+    tokens = 96
+    ex = PeerExchange(world=1, rank=0, tokens=tokens, top_k=8, hidden=2048, experts=256, device=dev)
+    try:
+        layer = weights.rank_layer(0, 1, tokens, exchange=ex)
+        for step in range(2):
+            x = to_dev(S.hidden_states(5000 + step, tokens - 7 * step), dev)
+            out = layer(x)
+            ex.check()
+            assert np.array_equal(bits(out), bits(weights.single(x))), step
+        x = to_dev(S.hidden_states(5100, tokens), dev)
+        out = torch.empty_like(x)
+        layer(x, out=out)                                    # warm every buffer before capture
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            layer(x, out=out)
+        for seed in (5200, 5300):
+            x.copy_(to_dev(S.hidden_states(seed, tokens), dev))
+            g.replay()
+            torch.cuda.synchronize()
+            ex.check()
+            assert np.array_equal(bits(out), bits(weights.single(x))), seed
+        del g
+    finally:
+        ex.close()
+
+
+def _peer_rank(rank: int, world: int, port: int, tokens: int, failures) -> None:
+    import torch.distributed as dist
+
+    from lightreason_b200.expert_parallel import PeerExchange
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=60))
+    ex = None
+    try:
+        w = Weights(41, dev)
+        ex = PeerExchange(world=world, rank=rank, tokens=tokens, top_k=8, hidden=2048, experts=256, device=dev)
+        layer = w.rank_layer(rank, world, tokens, exchange=ex)
+        for step in range(3):
+            x = to_dev(S.hidden_states(6000 + 10 * step + rank, tokens - step), dev)
+            out = layer(x)
+            want = w.single(x)
+            torch.cuda.synchronize()
+            ex.check()
+            if not np.array_equal(bits(out), bits(want)):
+                failures.put(f"rank {rank} step {step}: peer-exchange output differs from the single-GPU layer")
+        dist.barrier()
+    except Exception as exc:  # noqa: BLE001 - reported to the parent
+        failures.put(f"rank {rank}: {exc!r}")
+        raise
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_peer_exchange_ranks_equal_single_gpu_layer():
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    failures = ctx.SimpleQueue()
+    mp.start_processes(_peer_rank, args=(world, _free_port(), 128, failures), nprocs=world, start_method="spawn")
+    errs = []
+    while not failures.empty():
+        errs.append(failures.get())
+    assert not errs, errs
