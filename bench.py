@@ -572,8 +572,9 @@ def run_ep(args, cfg, world, rank, local):
     value = world * tokens * args.steps / (total_ms / 1e3)
     # this rank's work in the last timed step
     if transport == "p2p":
-        received = int(peer.recv_total.item())
-        local_ids = layer.p_route_in[tokens:tokens + received, 0].cpu().numpy()
+        ids = layer.p_route_in[peer.own_rows:, 0].cpu().numpy()
+        local_ids = ids[ids >= 0]
+        received = int(local_ids.size)
         sent = layer.offsets.cpu().numpy()
         el = EXPERTS // world
         leaving = int(sent[EXPERTS] - (sent[(rank + 1) * el] - sent[rank * el]))

@@ -70,6 +70,20 @@ int moe_router_topk(const uint16_t *x, const uint16_t *router, const float *bias
                     int top_k, uint16_t *logits, int64_t *idx, float *scores_f32,
                     uint16_t *scores_bf16, uint16_t *sig, void *stream);
 
+/* moe_router_topk with a scratch for FP32 K-split partials of the router GEMM
+ * at prefill widths (more CTAs when few tokens), summed in split order before
+ * the one BF16 rounding: the router moe_layer_forward runs, bit for bit.
+ * moe_router_topk itself accumulates K in one pass, so where this call splits
+ * a logit may differ from it by the rounding of the FP32 sum.
+ * moe_router_workspace_bytes: the scratch it uses (0: none, and the call is
+ * moe_router_topk). */
+size_t moe_router_workspace_bytes(int tokens, int experts);
+int moe_router_topk_ws(const uint16_t *x, const uint16_t *router, const float *bias,
+                       const uint16_t *shared_gate_w, int tokens, int hidden, int experts,
+                       int top_k, uint16_t *logits, int64_t *idx, float *scores_f32,
+                       uint16_t *scores_bf16, uint16_t *sig, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
 /* Selection only, from given BF16 logits [T,E] (the router's second half). */
 int moe_router_select(const uint16_t *logits, const float *bias, int tokens, int experts,
                       int top_k, int64_t *idx, float *scores_f32, uint16_t *scores_bf16,
@@ -317,33 +331,36 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
  * buffer with moe_ipc_alloc (zero-filled; the 64-byte handle goes to the
  * peers, which map it with moe_ipc_open) holding, at the byte offsets below:
  * flags_dispatch uint32[world], flags_return uint32[world], count int32[world],
- * meta int32[world][capacity][2], rx BF16[world][capacity][hidden] and ret
- * BF16[capacity][hidden]; capacity >= tokens * top_k.  `peers` lists every
- * rank's buffer as mapped in this process (its own included); step (uint32,
- * start at 1), sync (int32[2], zero), error and recv_total are this rank's
- * device words.  One step:
- *   moe_router_topk, moe_permute(_wide) of the rank's own tokens;
+ * meta int32[world][capacity][2], rows BF16[own_rows + world*capacity][hidden]
+ * (at off_rx: the rank's own tokens, then sender s's rows at own_rows +
+ * s*capacity) and ret BF16[capacity][hidden]; capacity >= tokens * top_k,
+ * own_rows >= tokens.  `peers` lists every rank's buffer as mapped in this
+ * process (its own included); step (uint32, start at 1), sync (int32[2],
+ * zero) and error are this rank's device words.  One step:
+ *   moe_router_topk(_ws), moe_permute(_wide) of the rank's own tokens;
  *   moe_ep_p2p_dispatch   rows and (local expert, position) into the owners'
- *                         rx / meta, then releases their flags_dispatch;
- *   moe_ep_p2p_collect    waits for every sender, writes xin [own tokens ;
- *                         received rows], route_in (own tokens -> the shared
- *                         expert, local id local_experts; unused rows -1) and
- *                         each received row's return address;
- *   moe_layer_forward     rows_mode over tokens + recv_cap rows, local experts
+ *                         rows / meta, then releases their flags_dispatch;
+ *   moe_ep_p2p_collect    copies the own tokens into rows, waits for every
+ *                         sender, writes route_in [own_rows + world*capacity]
+ *                         (own tokens -> the shared expert, local id
+ *                         local_experts; slots no sender filled -> -1) and each
+ *                         received row's return address;
+ *   moe_layer_forward     rows_mode over the rows region (x = buffer + off_rx,
+ *                         own_rows + world*capacity tokens), local experts
  *                         plus the shared expert appended as local expert El;
  *   moe_ep_p2p_return     rows back to their senders' ret, releases
  *                         flags_return;
  *   moe_ep_p2p_finish     waits for every return, advances *step;
  *   moe_ep_combine        over ret (in the permuted order), scores, the shared
  *                         rows and sig.
- * Waits give up after 1 s with *error = 1 (dispatch), 2 (return) or 3
- * (received rows above recv_cap); the GPU is never left waiting. */
+ * Waits give up after 1 s with *error = 1 (dispatch) or 2 (return); the GPU
+ * is never left waiting. */
 typedef struct moe_ep_p2p {
     const int64_t *peers;
     int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
-    int world, rank, capacity, hidden, top_k, experts, local_experts;
+    int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
-    int32_t *sync, *error, *recv_total;
+    int32_t *sync, *error;
 } moe_ep_p2p;
 
 int moe_ipc_alloc(size_t bytes, void **ptr, void *handle64);
@@ -353,8 +370,8 @@ int moe_ipc_close(void *ptr);
 int moe_ep_p2p_dispatch(const moe_ep_p2p *p, const uint16_t *x, const int64_t *idx,
                         const int32_t *offsets, const int32_t *perm_token,
                         const int32_t *perm_slot, void *stream);
-int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int recv_cap,
-                       uint16_t *xin, int64_t *route_in, int64_t *ret_addr, void *stream);
+int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int64_t *route_in,
+                       int64_t *ret_addr, void *stream);
 int moe_ep_p2p_return(const moe_ep_p2p *p, const uint16_t *rows, const int64_t *ret_addr,
                       void *stream);
 int moe_ep_p2p_finish(const moe_ep_p2p *p, void *stream);

@@ -3,12 +3,14 @@
 // ranks, mapped into every peer by CUDA IPC), and the ranks' kernels meet
 // through release/acquire flags in those buffers.
 //
-// Symmetric buffer of rank q (W ranks, C = capacity rows per source):
+// Symmetric buffer of rank q (W ranks, C = capacity rows per source, T0 own
+// token rows):
 //   flags_dispatch uint32 [W]   step at which rank s finished writing into q
 //   flags_return   uint32 [W]   step at which rank d finished returning q's rows
 //   count          int32  [W]   rows rank s wrote into q this step
 //   meta           int32  [W][C][2]  (local expert on q, position on s)
-//   rx             bf16   [W][C][H]  rows rank s sent to q
+//   rows           bf16   [T0 + W*C][H]  q's own tokens, then rank s's rows at
+//                                        T0 + s*C: the local layer's input
 //   ret            bf16   [C][H]     q's own routes' expert rows, by position
 //
 // One step on rank r (the step number lives in device memory and advances at
@@ -17,10 +19,11 @@
 //             j = p - offsets[d * El]: row x[perm_token[p]] -> d.rx[r][j],
 //             (e % El, p) -> d.meta[r][j]; the last CTA writes d.count[r] and
 //             releases d.flags_dispatch[r] = step.
-//   collect   wait for every flags_dispatch[s] == step, then compact: xin =
-//             [own tokens ; rows from rank 0 ; rank 1 ; ...], route_in = local
-//             expert (own tokens: the shared expert, El; unused rows: -1), and
-//             the peer address each received row returns to.
+//   collect   copy the own tokens into rows[0, T); wait for every
+//             flags_dispatch[s] == step; route_in of every row = its local
+//             expert (own tokens: the shared expert, El; rows no sender wrote:
+//             -1, dropped by the layer, whose token gather is the one
+//             compaction) and the peer address each received row returns to.
 //   return    after the local layer (rows mode): each received row -> its
 //             sender's ret[p]; the last CTA releases s.flags_return[r] = step.
 //   finish    wait for every flags_return[d] == step, advance the step; the
@@ -71,11 +74,21 @@ __device__ __forceinline__ uint8_t *peer_base(const EpP2PArgs &a, int q) {
     return reinterpret_cast<uint8_t *>(a.peers[q]);
 }
 
-// One 4-KB-class row copy by a warp (16-byte units).
+// One row copy by a warp in 16-byte units, eight loads per lane in flight
+// before their stores.
 __device__ __forceinline__ void warp_copy_row(const uint16_t *src, uint16_t *dst, int hidden, int lane) {
     const uint4 *s = reinterpret_cast<const uint4 *>(src);
     uint4 *d = reinterpret_cast<uint4 *>(dst);
-    for (int v = lane; v < hidden / 8; v += 32) d[v] = __ldg(s + v);
+    const int n = hidden / 8;
+    int v = lane;
+    for (; v + 7 * 32 < n; v += 8 * 32) {
+        uint4 r[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) r[i] = __ldg(s + v + 32 * i);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[v + 32 * i] = r[i];
+    }
+    for (; v < n; v += 32) d[v] = __ldg(s + v);
 }
 
 // Last-CTA election: every CTA fences its (peer) stores, then counts itself in.
@@ -109,7 +122,7 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a, const
         uint8_t *dst = peer_base(a, d);
         const size_t slot = static_cast<size_t>(a.rank) * a.capacity + j;
         warp_copy_row(x + static_cast<size_t>(t) * a.hidden,
-                      reinterpret_cast<uint16_t *>(dst + a.off_rx) + slot * a.hidden, a.hidden, lane);
+                      reinterpret_cast<uint16_t *>(dst + a.off_rx) + (a.own_rows + slot) * a.hidden, a.hidden, lane);
         if (lane == 0) {
             int32_t *meta = reinterpret_cast<int32_t *>(dst + a.off_meta) + slot * 2;
             meta[0] = e % El;
@@ -129,74 +142,63 @@ __global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a, const
     }
 }
 
-// xin [tokens + recv_cap, H], route_in [tokens + recv_cap] int64, ret_addr
-// [recv_cap] int64 (peer address of each received row's home slot).
+// route_in [own_rows + W*C] int64 and ret_addr [W*C] int64, both indexed like
+// the rows region (the layer's input and output rows).
 __global__ void __launch_bounds__(256) ep_p2p_collect_kernel(EpP2PArgs a, const uint16_t *__restrict__ x,
-                                                             int tokens, int recv_cap, uint16_t *__restrict__ xin,
-                                                             int64_t *__restrict__ route_in,
+                                                             int tokens, int64_t *__restrict__ route_in,
                                                              int64_t *__restrict__ ret_addr) {
     grid_dependency_wait();
     __shared__ int ok;
-    __shared__ int base[65];
     const uint32_t step = *a.step;
     uint8_t *self = peer_base(a, a.rank);
+    uint16_t *rows = reinterpret_cast<uint16_t *>(self + a.off_rx);
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    // own tokens first: the shared expert's rows (no wait needed)
+    for (int t = gw; t < a.own_rows; t += warps) {
+        if (t < tokens) warp_copy_row(x + static_cast<size_t>(t) * a.hidden, rows + static_cast<size_t>(t) * a.hidden,
+                                      a.hidden, lane);
+        if (lane == 0) route_in[t] = t < tokens ? a.local_experts : -1;
+    }
     if (threadIdx.x == 0) {
         ok = wait_flags(reinterpret_cast<const uint32_t *>(self + a.off_flags_dispatch), a.world, step);
         if (!ok) atomicExch(a.error, 1);
     }
     __syncthreads();
     if (!ok) return;
-    if (threadIdx.x == 0) {
-        const int32_t *count = reinterpret_cast<const int32_t *>(self + a.off_count);
-        int run = 0;
-        for (int q = 0; q < a.world; ++q) {
-            base[q] = run;
-            run += count[q];
-        }
-        base[a.world] = run;
-        if (blockIdx.x == 0) *a.recv_total = run;
-        if (run > recv_cap) atomicExch(a.error, 3);
-    }
-    __syncthreads();
-    const int received = min(base[a.world], recv_cap);
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    // own tokens first: the shared expert's rows
-    for (int t = gw; t < tokens; t += warps) {
-        warp_copy_row(x + static_cast<size_t>(t) * a.hidden, xin + static_cast<size_t>(t) * a.hidden, a.hidden, lane);
-        if (lane == 0) route_in[t] = a.local_experts;
-    }
-    const uint16_t *rx = reinterpret_cast<const uint16_t *>(self + a.off_rx);
+    const int32_t *count = reinterpret_cast<const int32_t *>(self + a.off_count);
     const int32_t *meta = reinterpret_cast<const int32_t *>(self + a.off_meta);
-    for (int i = gw; i < recv_cap; i += warps) {
-        if (i >= received) {
-            if (lane == 0) route_in[tokens + i] = -1;  // no row: dropped by the layer
-            continue;
-        }
-        int q = 0;
-        while (q + 1 < a.world && base[q + 1] <= i) ++q;
-        const size_t slot = static_cast<size_t>(q) * a.capacity + (i - base[q]);
-        warp_copy_row(rx + slot * a.hidden, xin + static_cast<size_t>(tokens + i) * a.hidden, a.hidden, lane);
-        if (lane == 0) {
-            route_in[tokens + i] = meta[slot * 2];
-            ret_addr[i] = a.peers[q] + a.off_ret + static_cast<int64_t>(meta[slot * 2 + 1]) * a.hidden * 2;
+    const int slots = a.world * a.capacity;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slots; i += gridDim.x * blockDim.x) {
+        const int q = i / a.capacity, j = i - q * a.capacity;
+        if (j < count[q]) {
+            route_in[a.own_rows + i] = meta[static_cast<size_t>(i) * 2];
+            ret_addr[i] = a.peers[q] + a.off_ret + static_cast<int64_t>(meta[static_cast<size_t>(i) * 2 + 1]) *
+                                                       a.hidden * 2;
+        } else {
+            route_in[a.own_rows + i] = -1;
         }
     }
 }
 
-// rows [recv_cap, H]: the local layer's unweighted rows of the received routes.
+// rows [W*C, H]: the local layer's unweighted rows of the received slots
+// (the layer's output rows past the own tokens).
 __global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a, const uint16_t *__restrict__ rows,
                                                             const int64_t *__restrict__ ret_addr) {
     grid_dependency_wait();
     const uint32_t step = *a.step;
-    const int received = *a.recv_total;
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
+    const int32_t *count = reinterpret_cast<const int32_t *>(peer_base(a, a.rank) + a.off_count);
     if (*a.error == 0) {
-        for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < received; i += warps)
-            warp_copy_row(rows + static_cast<size_t>(i) * a.hidden, reinterpret_cast<uint16_t *>(ret_addr[i]),
-                          a.hidden, lane);
+        const int slots = a.world * a.capacity;
+        for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < slots; i += warps) {
+            const int q = i / a.capacity, j = i - q * a.capacity;
+            if (j < count[q])
+                warp_copy_row(rows + static_cast<size_t>(i) * a.hidden, reinterpret_cast<uint16_t *>(ret_addr[i]),
+                              a.hidden, lane);
+        }
     }
     if (last_cta(a.sync + 1)) {
         if (threadIdx.x < a.world) {
@@ -223,7 +225,7 @@ __global__ void ep_p2p_finish_kernel(EpP2PArgs a) {
 namespace {
 
 int check_p2p(const moe_ep_p2p *p) {
-    LRB_REQUIRE(p && p->peers && p->step && p->sync && p->error && p->recv_total, "ep_p2p: null argument");
+    LRB_REQUIRE(p && p->peers && p->step && p->sync && p->error, "ep_p2p: null argument");
     LRB_REQUIRE(p->world >= 1 && p->world <= 64 && p->rank >= 0 && p->rank < p->world,
                 "ep_p2p: rank %d / world %d out of range", p->rank, p->world);
     LRB_REQUIRE(p->experts % p->world == 0 && p->local_experts == p->experts / p->world,
@@ -248,10 +250,11 @@ lrb::EpP2PArgs args_of(const moe_ep_p2p *p) {
     a.top_k = p->top_k;
     a.experts = p->experts;
     a.local_experts = p->local_experts;
+    a.own_rows = p->own_rows;
     a.step = p->step;
     a.sync = p->sync;
     a.error = p->error;
-    a.recv_total = p->recv_total;
+
     return a;
 }
 
@@ -302,13 +305,14 @@ int moe_ep_p2p_dispatch(const moe_ep_p2p *p, const uint16_t *x, const int64_t *i
                            perm_token, perm_slot);
 }
 
-int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int recv_cap, uint16_t *xin,
-                       int64_t *route_in, int64_t *ret_addr, void *stream) {
+int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int64_t *route_in, int64_t *ret_addr,
+                       void *stream) {
     if (int rc = check_p2p(p)) return rc;
-    LRB_REQUIRE(x && xin && route_in && ret_addr && tokens >= 0 && recv_cap >= 0, "moe_ep_p2p_collect: bad input");
+    LRB_REQUIRE(x && route_in && ret_addr && tokens >= 0 && tokens <= p->own_rows,
+                "moe_ep_p2p_collect: bad input (tokens %d, own rows %d)", tokens, p->own_rows);
     return lrb::launch_pdl(lrb::ep_p2p_collect_kernel, dim3(copy_grid()), dim3(256), 0,
-                           static_cast<cudaStream_t>(stream), "ep_p2p_collect_kernel", args_of(p), x, tokens, recv_cap,
-                           xin, route_in, ret_addr);
+                           static_cast<cudaStream_t>(stream), "ep_p2p_collect_kernel", args_of(p), x, tokens,
+                           route_in, ret_addr);
 }
 
 int moe_ep_p2p_return(const moe_ep_p2p *p, const uint16_t *rows, const int64_t *ret_addr, void *stream) {

@@ -680,13 +680,16 @@ __global__ void __launch_bounds__(256) gather_tokens_kernel(const uint16_t *__re
     grid_dependency_trigger();
     const int units = hidden / 8;
     const int placed = offsets[experts];
-    const int64_t total = static_cast<int64_t>(routes + shared_rows) * units;
+    // rows to fill: the placed routes, then the shared rows (routes past the
+    // placed ones were dropped and own no row)
+    const int64_t total = static_cast<int64_t>(placed + shared_rows) * units;
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int p = static_cast<int>(i / units), c = static_cast<int>(i % units);
-        if (p < routes && p >= placed) continue;
+        const int q = static_cast<int>(i / units), c = static_cast<int>(i % units);
+        const int p = q < placed ? q : routes + (q - placed);
         const int t = p < routes ? route_token[p] : p - routes;
-        reinterpret_cast<uint4 *>(xs)[i] = ld_cached(x + static_cast<size_t>(t) * hidden + c * 8);
+        reinterpret_cast<uint4 *>(xs)[static_cast<int64_t>(p) * units + c] =
+            ld_cached(x + static_cast<size_t>(t) * hidden + c * 8);
     }
 }
 

@@ -85,15 +85,17 @@ int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
 struct EpP2PArgs {
     const int64_t *peers;
     int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
-    int world, rank, capacity, hidden, top_k, experts, local_experts;
+    int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
-    int32_t *sync, *error, *recv_total;
+    int32_t *sync, *error;
 };
 // BF16 tensor map: dims[0] innermost, 128-byte swizzle, box {64, box_rows(, 1)}.
 int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,
                   uint32_t box_rows);
+// part != null: FP32 partials [ks][T][E] (router_select sums them); else BF16 logits.
 int launch_router_tc(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
-                     uint16_t *logits, int32_t *error, cudaStream_t stream);
+                     uint16_t *logits, float *part, int ks, int32_t *error, cudaStream_t stream);
+int router_tc_splits(int tokens, int experts);
 int sm_count();
 
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
@@ -103,10 +105,12 @@ int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, co
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);
 // With gate_w, also sig[t] = bf16(sigmoid(bf16(x[t] . gate_w))) (one warp per token).
+// part != null: logits = bf16(sum over ks splits of part[k][t][e]) are formed
+// (and stored to `logits`) before the selection.
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
                          int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream,
                          const uint16_t *x = nullptr, const uint16_t *gate_w = nullptr, int hidden = 0,
-                         uint16_t *sig = nullptr);
+                         uint16_t *sig = nullptr, const float *part = nullptr, int ks = 1);
 int check_router_args(int tokens, int hidden, int experts, int top_k);
 
 // Decode routing (T <= kDecodeMaxTokens): split-K router partials, then one CTA

@@ -25,7 +25,8 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of the scratch arrays inside the caller's workspace.
 struct Layout {
     size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, plan, off1,
-        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, perm_hist, total;
+        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, perm_hist, rsplit, total;
+    int router_ks;
     int split_len;
 };
 
@@ -58,6 +59,8 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.split_cnt = take(static_cast<size_t>(L.split_len) * 4);
     L.gofe = take(E * 4);
     L.perm_hist = take(static_cast<size_t>(permute_hist_ints(tokens, top_k, experts)) * 4);
+    L.router_ks = tokens > kDecodeMaxTokens ? router_tc_splits(tokens, experts) : 1;
+    L.rsplit = take(L.router_ks > 1 ? static_cast<size_t>(L.router_ks) * T * E * 4 : 0);
     L.rpart = take(tokens <= kDecodeMaxTokens ? static_cast<size_t>(kRouterSplit) * T * (E + 1) * 4 : 0);
     L.part = take(grouped_part_floats(tokens, experts, top_k, inner) * 4);
     L.xs = take((R + T) * hidden * 2);
@@ -249,9 +252,12 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         LRB_CUDA(cudaMemsetAsync(counters + 4, 0, sizeof(int32_t), s));
         if (!routed_in) {
             // tensor-core logits, then selection and the shared-expert gate
-            if (int rc = launch_router_tc(x, w->router, tokens, H, E, logits, counters + 4, s)) return rc;
+            float *rsplit = L.router_ks > 1 ? at<float>(ws, L.rsplit) : nullptr;
+            if (int rc = launch_router_tc(x, w->router, tokens, H, E, logits, rsplit, L.router_ks, counters + 4, s))
+                return rc;
             if (int rc = launch_router_select(logits, w->router_bias, tokens, E, K, idx, nullptr, scores, s, x,
-                                              shared ? w->shared_gate_w : nullptr, H, shared ? sig : nullptr))
+                                              shared ? w->shared_gate_w : nullptr, H, shared ? sig : nullptr, rsplit,
+                                              L.router_ks))
                 return rc;
         }
         if (int rc = mark(1)) return rc;

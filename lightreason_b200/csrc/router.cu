@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__re
                                                             uint16_t *__restrict__ scores_bf16,
                                                             const uint16_t *__restrict__ x,
                                                             const uint16_t *__restrict__ gate_w, int hidden,
-                                                            uint16_t *__restrict__ sig) {
+                                                            uint16_t *__restrict__ sig,
+                                                            const float *__restrict__ part, int ks) {
     grid_dependency_wait();
     grid_dependency_trigger();
     const int lane = threadIdx.x & 31;
@@ -83,10 +84,23 @@ __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__re
         acc = warp_sum(acc);
         if (lane == 0) sig[t] = f2bf(sigmoid_f32(rbf(acc)));
     }
-    const uint16_t *row = logits + static_cast<size_t>(t) * experts;
+    uint16_t *row = const_cast<uint16_t *>(logits) + static_cast<size_t>(t) * experts;
     int e;
     float w;
-    warp_topk<VPL>([&](int j) { return bf2f(row[j]) + (bias ? bias[j] : 0.0f); }, experts, top_k, &e, &w);
+    if (part) {
+        // one BF16 rounding of the FP32 sum of the K splits, in split order (F.linear)
+        warp_topk<VPL>(
+            [&](int j) {
+                float s = 0.f;
+                for (int k = 0; k < ks; ++k) s += part[(static_cast<size_t>(k) * tokens + t) * experts + j];
+                const uint16_t lg = f2bf(s);
+                row[j] = lg;
+                return bf2f(lg) + (bias ? bias[j] : 0.0f);
+            },
+            experts, top_k, &e, &w);
+    } else {
+        warp_topk<VPL>([&](int j) { return bf2f(row[j]) + (bias ? bias[j] : 0.0f); }, experts, top_k, &e, &w);
+    }
     if (lane < top_k) {
         const size_t o = static_cast<size_t>(t) * top_k + lane;
         idx[o] = e;
@@ -233,15 +247,18 @@ int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16
 
 int launch_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k,
                          int64_t *idx, float *scores_f32, uint16_t *scores_bf16, cudaStream_t stream,
-                         const uint16_t *x, const uint16_t *gate_w, int hidden, uint16_t *sig) {
+                         const uint16_t *x, const uint16_t *gate_w, int hidden, uint16_t *sig, const float *part,
+                         int ks) {
     const int grid = (tokens + 7) / 8;
     if (gate_w && (!x || !sig || hidden % 256)) return set_error(MOE_EINVAL, "router: bad shared-gate arguments");
     if (experts <= 256)
         return launch_pdl(router_select_kernel<8>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
-                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig);
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig, part,
+                          ks);
     if (experts <= 1024)
         return launch_pdl(router_select_kernel<32>, dim3(grid), dim3(256), 0, stream, "router_select_kernel", logits,
-                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig);
+                          bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig, part,
+                          ks);
     return set_error(MOE_EINVAL, "router: experts %d > 1024", experts);
 }
 
@@ -310,13 +327,40 @@ int moe_router_topk(const uint16_t *x, const uint16_t *router, const float *bias
     cudaStream_t s = lrb::as_stream(stream);
     if (tokens > lrb::kDecodeMaxTokens) {
         // prefill widths: tensor-core logits, then selection + shared gate
-        if (int rc = lrb::launch_router_tc(x, router, tokens, hidden, experts, logits, nullptr, s)) return rc;
+        if (int rc = lrb::launch_router_tc(x, router, tokens, hidden, experts, logits, nullptr, 1, nullptr, s))
+            return rc;
         return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, s, x,
                                          shared_gate_w, hidden, sig);
     }
     if (int rc = lrb::launch_router_logits(x, router, shared_gate_w, tokens, hidden, experts, logits, sig, s))
         return rc;
     return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, s);
+}
+
+size_t moe_router_workspace_bytes(int tokens, int experts) {
+    if (tokens <= lrb::kDecodeMaxTokens || experts <= 0) return 0;
+    const int ks = lrb::router_tc_splits(tokens, experts);
+    return ks > 1 ? static_cast<size_t>(ks) * tokens * experts * sizeof(float) : 0;
+}
+
+int moe_router_topk_ws(const uint16_t *x, const uint16_t *router, const float *bias, const uint16_t *shared_gate_w,
+                       int tokens, int hidden, int experts, int top_k, uint16_t *logits, int64_t *idx,
+                       float *scores_f32, uint16_t *scores_bf16, uint16_t *sig, void *workspace,
+                       size_t workspace_bytes, void *stream) {
+    const size_t need = moe_router_workspace_bytes(tokens, experts);
+    if (need == 0 || !workspace || workspace_bytes < need)
+        return moe_router_topk(x, router, bias, shared_gate_w, tokens, hidden, experts, top_k, logits, idx,
+                               scores_f32, scores_bf16, sig, stream);
+    if (int rc = lrb::check_router_args(tokens, hidden, experts, top_k)) return rc;
+    LRB_REQUIRE(x && router && logits && idx, "moe_router_topk_ws: x, router, logits and idx are required");
+    LRB_REQUIRE(!shared_gate_w || sig, "moe_router_topk_ws: shared_gate_w needs a sig output");
+    if (int rc = lrb::require_sm100()) return rc;
+    cudaStream_t s = lrb::as_stream(stream);
+    const int ks = lrb::router_tc_splits(tokens, experts);
+    float *part = static_cast<float *>(workspace);
+    if (int rc = lrb::launch_router_tc(x, router, tokens, hidden, experts, logits, part, ks, nullptr, s)) return rc;
+    return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, s, x,
+                                     shared_gate_w, hidden, sig, part, ks);
 }
 
 int moe_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k, int64_t *idx,

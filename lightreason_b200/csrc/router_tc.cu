@@ -2,9 +2,12 @@
 // bf16(x[T, H] . W[E, H]^T) with FP32 accumulation (F.linear on BF16,
 // transformers qwen3_5_moe modeling :764).
 //
-// One CTA per (128 router rows, BN tokens): the router rows are the M = 128
-// operand and the token tile the N operand, both K-major with the 128-byte
-// swizzle, streamed by TMA through a 4-stage ring.  Thread 0 issues the loads
+// One CTA per (128 router rows, BN tokens, K split): the router rows are the
+// M = 128 operand and the token tile the N operand, both K-major with the
+// 128-byte swizzle, streamed by TMA through a 4-stage ring.  With ks > 1 K
+// splits (few tokens: more CTAs than row blocks x token tiles) each CTA writes
+// FP32 partials part[split][t][e], which the selection kernel sums in split
+// order before the one BF16 rounding.  Thread 0 issues the loads
 // and the tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator; all four
 // warps then read their 32 TMEM lanes (= router rows) and write BF16 logits,
 // 32 consecutive experts of one token per warp store.  Every wait is bounded:
@@ -43,7 +46,8 @@ __device__ __forceinline__ bool wait_bounded(uint64_t *bar, uint32_t parity) {
 template <int BN>
 __global__ void __launch_bounds__(128, 1)
     router_tc_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x, int tokens,
-                     int experts, int hidden, uint16_t *__restrict__ logits, int32_t *__restrict__ error) {
+                     int experts, int hidden, uint16_t *__restrict__ logits, float *__restrict__ part,
+                     int32_t *__restrict__ error) {
     constexpr int kA = kRows * kK * 2;
     constexpr int kB = BN * kK * 2;
     constexpr int kStage = kA + kB;
@@ -77,7 +81,7 @@ __global__ void __launch_bounds__(128, 1)
     grid_dependency_trigger();
 
     const int row0 = blockIdx.x * kRows, t0 = blockIdx.y * BN;
-    const int nk = hidden / kK;
+    const int nk = hidden / kK / gridDim.z, kb_first = blockIdx.z * nk;
     if (threadIdx.x == 0) {
         constexpr uint32_t idesc = sm100::idesc_bf16_f32(kRows, BN);
         bool issued[kStagesTc] = {false, false, false, false};
@@ -86,8 +90,8 @@ __global__ void __launch_bounds__(128, 1)
             const int s = kb % kStagesTc;
             uint8_t *st = smem + s * kStage;
             sm100::mbar_expect_tx(&full[s], kStage);
-            sm100::tma_load_2d(st, &tm_w, &full[s], kb * kK, row0);
-            sm100::tma_load_2d(st + kA, &tm_x, &full[s], kb * kK, t0);
+            sm100::tma_load_2d(st, &tm_w, &full[s], (kb_first + kb) * kK, row0);
+            sm100::tma_load_2d(st + kA, &tm_x, &full[s], (kb_first + kb) * kK, t0);
             issued[s] = true;
             issued_parity[s] = (kb / kStagesTc) & 1;
         };
@@ -144,7 +148,10 @@ __global__ void __launch_bounds__(128, 1)
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
                 const int t = t0 + c0 + j;
-                if (t < tokens && row < experts) logits[static_cast<size_t>(t) * experts + row] = f2bf(v[j]);
+                if (t < tokens && row < experts) {
+                    if (part) part[(static_cast<size_t>(blockIdx.z) * tokens + t) * experts + row] = v[j];
+                    else logits[static_cast<size_t>(t) * experts + row] = f2bf(v[j]);
+                }
             }
         }
     } else if (!ready && lane == 0 && error) {
@@ -161,9 +168,14 @@ __global__ void __launch_bounds__(128, 1)
 
 int router_tc_bn(int tokens) { return tokens >= 2048 ? 64 : 32; }
 
+int router_tc_splits(int tokens, int experts) {
+    const int ctas = ((experts + kRows - 1) / kRows) * ((tokens + router_tc_bn(tokens) - 1) / router_tc_bn(tokens));
+    return ctas * 4 <= sm_count() ? 4 : ctas * 2 <= sm_count() ? 2 : 1;
+}
+
 template <int BN>
 int launch_router_tc_bn(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
-                        uint16_t *logits, int32_t *error, cudaStream_t stream) {
+                        uint16_t *logits, float *part, int ks, int32_t *error, cudaStream_t stream) {
     constexpr int kSmem = kStagesTc * (kRows * kK * 2 + BN * kK * 2) + 1024;
     CUtensorMap tw{}, tx{};
     {
@@ -181,19 +193,19 @@ int launch_router_tc_bn(const uint16_t *x, const uint16_t *router, int tokens, i
         LRB_CUDA(cudaFuncSetAttribute(router_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
         configured = true;
     }
-    const dim3 grid((experts + kRows - 1) / kRows, (tokens + BN - 1) / BN);
+    const dim3 grid((experts + kRows - 1) / kRows, (tokens + BN - 1) / BN, part ? ks : 1);
     return launch_pdl(router_tc_kernel<BN>, grid, dim3(128), kSmem, stream, "router_tc_kernel", tw, tx, tokens,
-                      experts, hidden, logits, error);
+                      experts, hidden, logits, part, error);
 }
 
 int launch_router_tc(const uint16_t *x, const uint16_t *router, int tokens, int hidden, int experts,
-                     uint16_t *logits, int32_t *error, cudaStream_t stream) {
-    LRB_REQUIRE(hidden % kK == 0, "router: hidden %d is not a multiple of %d", hidden, kK);
+                     uint16_t *logits, float *part, int ks, int32_t *error, cudaStream_t stream) {
+    LRB_REQUIRE(hidden % (kK * (part ? ks : 1)) == 0, "router: hidden %d does not split into %d K splits", hidden, ks);
     LRB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(router) % 16 == 0,
                 "router: x and router must be 16-byte aligned");
     if (router_tc_bn(tokens) == 64)
-        return launch_router_tc_bn<64>(x, router, tokens, hidden, experts, logits, error, stream);
-    return launch_router_tc_bn<32>(x, router, tokens, hidden, experts, logits, error, stream);
+        return launch_router_tc_bn<64>(x, router, tokens, hidden, experts, logits, part, ks, error, stream);
+    return launch_router_tc_bn<32>(x, router, tokens, hidden, experts, logits, part, ks, error, stream);
 }
 
 }  // namespace lrb

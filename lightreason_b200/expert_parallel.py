@@ -142,6 +142,8 @@ class ExpertParallelLayer:
         self.ret = torch.empty((max(routes, 1), self.hidden), **bf)
         self.last_splits = None
         self._own_routes = tokens
+        # K-split router partials: at most 4 splits of [T, E] FP32 for any T <= tokens
+        self.rsplit = torch.empty(16 * tokens * self.experts + 16, dtype=torch.uint8, device=d)
 
     # -- phases (split out so that one process can drive several virtual ranks)
     def dispatch(self, x: torch.Tensor) -> None:
@@ -156,9 +158,11 @@ class ExpertParallelLayer:
         self.xin[:tokens].copy_(x)
         if self.bias is not None:
             _require(self.bias.is_cuda and self.bias.dtype == torch.float32, "bias must be CUDA f32 [E]")
-        check(lib().moe_router_topk(_ptr(self.xin), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
-                                    tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits), _ptr(self.idx),
-                                    None, _ptr(self.scores), _ptr(self.sig), s), "moe_router_topk")
+        # the layer's own router (same K splits as moe_layer_forward at this width)
+        check(lib().moe_router_topk_ws(_ptr(self.xin), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
+                                       tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits),
+                                       _ptr(self.idx), None, _ptr(self.scores), _ptr(self.sig), _ptr(self.rsplit),
+                                       self.rsplit.numel(), s), "moe_router_topk_ws")
         c = self.counters.data_ptr()
         check(lib().moe_permute(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
                                 _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos), _ptr(self.active),
@@ -202,16 +206,16 @@ class ExpertParallelLayer:
         ex = self.exchange
         if getattr(self, "_peer_ready", False):
             return
-        _require(ex.capacity >= self.max_tokens * self.top_k, "peer exchange capacity below tokens * top_k")
+        _require(ex.capacity >= self.max_tokens * self.top_k and ex.own_rows >= self.max_tokens,
+                 "peer exchange sized below tokens * top_k")
         d = self.dev
-        self.recv_cap = ex.recv_cap
-        n = self.max_tokens + self.recv_cap
-        self.p_xin = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=d)
+        n = ex.rows
         self.p_route_in = torch.empty((n, 1), dtype=torch.int64, device=d)
         self.p_yin = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=d)
-        self.p_ret_addr = torch.zeros(max(self.recv_cap, 1), dtype=torch.int64, device=d)
+        self.p_ret_addr = torch.zeros(max(n - ex.own_rows, 1), dtype=torch.int64, device=d)
         hist = lib().moe_permute_hist_ints(self.max_tokens, self.top_k, self.experts)
         self.p_hist = torch.empty(max(hist, 1), dtype=torch.int32, device=d)
+        self.p_rsplit = self.rsplit
         self._peer_ready = True
 
     def _forward_peer(self, x, out, stage_events):
@@ -223,21 +227,20 @@ class ExpertParallelLayer:
         self.tokens = tokens
         s = native._stream(self.dev)
         a = ctypes.byref(ex.args)
-        check(lib().moe_router_topk(_ptr(x), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w), tokens,
-                                    self.hidden, self.experts, self.top_k, _ptr(self.logits), _ptr(self.idx), None,
-                                    _ptr(self.scores), _ptr(self.sig), s), "moe_router_topk")
+        check(lib().moe_router_topk_ws(_ptr(x), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
+                                       tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits),
+                                       _ptr(self.idx), None, _ptr(self.scores), _ptr(self.sig),
+                                       _ptr(self.p_rsplit), self.p_rsplit.numel(), s), "moe_router_topk_ws")
         c = self.counters.data_ptr()
         check(lib().moe_permute_wide(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
                                      _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos),
                                      _ptr(self.active), c, c + 4, _ptr(self.p_hist), s), "moe_permute_wide")
         check(lib().moe_ep_p2p_dispatch(a, _ptr(x), _ptr(self.idx), _ptr(self.offsets), _ptr(self.perm_token),
                                         _ptr(self.perm_slot), s), "moe_ep_p2p_dispatch")
-        check(lib().moe_ep_p2p_collect(a, _ptr(x), tokens, self.recv_cap, _ptr(self.p_xin), _ptr(self.p_route_in),
-                                       _ptr(self.p_ret_addr), s), "moe_ep_p2p_collect")
-        n = tokens + self.recv_cap
-        self.local(self.p_xin[:n], route_in=self.p_route_in[:n], out=self.p_yin[:n], stage_events=stage_events,
-                   rows_mode=True)
-        check(lib().moe_ep_p2p_return(a, self.p_yin[tokens:].data_ptr(), _ptr(self.p_ret_addr), s),
+        check(lib().moe_ep_p2p_collect(a, _ptr(x), tokens, _ptr(self.p_route_in), _ptr(self.p_ret_addr), s),
+              "moe_ep_p2p_collect")
+        self.local.forward_rows_raw(ex.rows_ptr, ex.rows, self.p_route_in, self.p_yin, stage_events=stage_events)
+        check(lib().moe_ep_p2p_return(a, self.p_yin[ex.own_rows:].data_ptr(), _ptr(self.p_ret_addr), s),
               "moe_ep_p2p_return")
         check(lib().moe_ep_p2p_finish(a, s), "moe_ep_p2p_finish")
         check(lib().moe_ep_combine(ctypes.c_void_p(ex.ret_ptr), _ptr(self.route_pos), _ptr(self.scores),
@@ -250,22 +253,23 @@ class PeerExchange:
     """Symmetric buffers over NVLink for ExpertParallelLayer: one CUDA-IPC
     buffer per rank (moe_ipc_alloc), mapped by every peer, laid out as
     moe_ep_p2p describes.  capacity = rows one rank may send to one peer
-    (>= tokens * top_k); recv_cap = rows a rank may receive in a step (default
-    world * capacity, the bound that never drops a route).  Construct it on
+    (tokens * top_k: no route is ever dropped); the rows region [tokens +
+    world * capacity, H] is also the local layer's input.  Construct it on
     every rank of the process group together; close() before the group ends."""
 
-    def __init__(self, *, world, rank, tokens, top_k, hidden, experts, device, recv_cap=None, group=None):
+    def __init__(self, *, world, rank, tokens, top_k, hidden, experts, device, group=None):
         import torch.distributed as dist
 
         self.dist, self.group = dist, group
         self.world, self.rank = world, rank
         self.capacity = tokens * top_k
-        self.recv_cap = world * self.capacity if recv_cap is None else recv_cap
+        self.own_rows = tokens
+        self.rows = tokens + world * self.capacity
         cap, h = self.capacity, hidden
         align = lambda v, a: (v + a - 1) // a * a  # noqa: E731
         off_fd, off_fr, off_count, off_meta = 0, 256, 512, 1024
         off_rx = align(off_meta + world * cap * 8, 4096)
-        off_ret = align(off_rx + world * cap * h * 2, 4096)
+        off_ret = align(off_rx + self.rows * h * 2, 4096)
         total = off_ret + cap * h * 2
         _require(world <= 64, "at most 64 ranks")
         base = ctypes.c_void_p()
@@ -295,14 +299,13 @@ class PeerExchange:
         self.step = torch.ones(1, **i32)
         self.sync = torch.zeros(2, **i32)
         self.error = torch.zeros(1, **i32)
-        self.recv_total = torch.zeros(1, **i32)
         self.ret_ptr = base.value + off_ret
+        self.rows_ptr = base.value + off_rx
         self.args = native.EpP2P(peers=self.peers.data_ptr(), off_flags_dispatch=off_fd, off_flags_return=off_fr,
                                  off_count=off_count, off_meta=off_meta, off_rx=off_rx, off_ret=off_ret, world=world,
                                  rank=rank, capacity=cap, hidden=hidden, top_k=top_k, experts=experts,
-                                 local_experts=experts // world, step=self.step.data_ptr(),
-                                 sync=self.sync.data_ptr(), error=self.error.data_ptr(),
-                                 recv_total=self.recv_total.data_ptr())
+                                 local_experts=experts // world, own_rows=tokens, step=self.step.data_ptr(),
+                                 sync=self.sync.data_ptr(), error=self.error.data_ptr())
         torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier(group=group)  # every mapping exists before any rank's first step
@@ -311,8 +314,7 @@ class PeerExchange:
         """Raise if a bounded wait of an earlier step gave up (syncs the device)."""
         code = int(self.error.item())
         if code:
-            what = {1: "a sender never released its rows", 2: "a receiver never returned its rows",
-                    3: "received rows exceed recv_cap"}.get(code, "unknown")
+            what = {1: "a sender never released its rows", 2: "a receiver never returned its rows"}.get(code, "unknown")
             raise RuntimeError(f"expert-parallel exchange failed ({code}): {what}")
 
     def close(self) -> None:

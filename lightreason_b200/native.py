@@ -39,8 +39,8 @@ class EpP2P(ctypes.Structure):
     _fields_ = [("peers", _p), ("off_flags_dispatch", ctypes.c_int64), ("off_flags_return", ctypes.c_int64),
                 ("off_count", ctypes.c_int64), ("off_meta", ctypes.c_int64), ("off_rx", ctypes.c_int64),
                 ("off_ret", ctypes.c_int64), ("world", _i), ("rank", _i), ("capacity", _i), ("hidden", _i),
-                ("top_k", _i), ("experts", _i), ("local_experts", _i), ("step", _p), ("sync", _p), ("error", _p),
-                ("recv_total", _p)]
+                ("top_k", _i), ("experts", _i), ("local_experts", _i), ("own_rows", _i), ("step", _p),
+                ("sync", _p), ("error", _p)]
 
 
 class LayerIO(ctypes.Structure):
@@ -59,6 +59,8 @@ _SIGNATURES = {
     "moe_host_register": ([_p, _sz, ctypes.POINTER(ctypes.c_uint64)], _i),
     "moe_host_unregister": ([_p], _i),
     "moe_router_topk": ([_p, _p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p], _i),
+    "moe_router_workspace_bytes": ([_i, _i], _sz),
+    "moe_router_topk_ws": ([_p, _p, _p, _p, _i, _i, _i, _i, _p, _p, _p, _p, _p, _p, _sz, _p], _i),
     "moe_router_select": ([_p, _p, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_permute": ([_p, _i, _i, _i, _p, _p, _p, _p, _p, _p, _p, _p], _i),
     "moe_permute_hist_ints": ([_i, _i, _i], _i),
@@ -76,7 +78,7 @@ _SIGNATURES = {
     "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
     "moe_ipc_close": ([_p], _i),
     "moe_ep_p2p_dispatch": ([ctypes.POINTER(EpP2P), _p, _p, _p, _p, _p, _p], _i),
-    "moe_ep_p2p_collect": ([ctypes.POINTER(EpP2P), _p, _i, _i, _p, _p, _p, _p], _i),
+    "moe_ep_p2p_collect": ([ctypes.POINTER(EpP2P), _p, _i, _p, _p, _p], _i),
     "moe_ep_p2p_return": ([ctypes.POINTER(EpP2P), _p, _p, _p], _i),
     "moe_ep_p2p_finish": ([ctypes.POINTER(EpP2P), _p], _i),
     "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
@@ -335,6 +337,29 @@ class Layer:
             self._slots = (torch.empty((n, 2 * self.inner, self.hidden), dtype=torch.bfloat16, device=self.device),
                            torch.empty((n, self.hidden, self.inner), dtype=torch.bfloat16, device=self.device))
         return self._slots
+
+    def forward_rows_raw(self, x_ptr: int, tokens: int, route_in: torch.Tensor, out: torch.Tensor,
+                         stage_events=None) -> torch.Tensor:
+        """Rows-mode forward whose input rows live at a raw device address (a
+        symmetric buffer): x [tokens, H] BF16 at x_ptr, route_in CUDA int64
+        [tokens, 1], out [tokens, H]."""
+        _require(self.top_k == 1, "rows mode needs top_k 1")
+        _require(route_in.dtype == torch.int64 and tuple(route_in.shape) == (tokens, 1) and route_in.is_contiguous()
+                 and route_in.is_cuda, "route_in must be CUDA int64 [T, 1]")
+        _cuda_bf16(out, "out")
+        _require(tuple(out.shape) == (tokens, self.hidden), "out must be [T, H]")
+        ws = self.workspace(tokens)
+        io = LayerIO(route_in=_ptr(route_in), rows_mode=1)
+        if stage_events is not None:
+            for e in stage_events:
+                if e is not None and not e.cuda_event:
+                    e.record()
+            handles = (_p * len(stage_events))(*[e.cuda_event if e is not None else None for e in stage_events])
+            io.stage_events, io.num_stage_events = ctypes.cast(handles, ctypes.POINTER(_p)), len(stage_events)
+        check(lib().moe_layer_forward(ctypes.byref(self.w), ctypes.c_void_p(x_ptr), tokens, _ptr(out),
+                                      ctypes.byref(io), _ptr(ws), ws.numel(), _stream(out.device)),
+              "moe_layer_forward")
+        return out
 
     def forward(self, x: torch.Tensor, *, route_in=None, weights_in=None, out=None, idx_out=None, scores_out=None,
                 logits_out=None, stage_events=None, rows_mode=False) -> torch.Tensor:
