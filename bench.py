@@ -69,6 +69,8 @@ PROFILED_TRAFFIC = {
 
 CONFIGS = {
     0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
+    2: dict(tokens=64, bias="zipf", layers=40,
+            workload="config2: 40-layer MoE stack, decode B=64 tokens per step, all experts HBM-resident"),
     1: dict(tokens=16, bias="normal",
             workload="config1: one MoE layer, speculative-verify width T=16; experts in pinned host RAM (e2e)"),
     3: dict(tokens=4096, bias="zipf", workload="config3: one MoE layer, prefill T=4096, Zipf(1.1) routing"),
@@ -630,6 +632,76 @@ def run_ep(args, cfg, world, rank, local):
     }
 
 
+def run_stack(args, cfg, world, rank, local):
+    """the 40-layer stack at decode width, every step one
+    CUDA-graph replay of all layers.  Each layer reads its own N(0,1) token
+    activations -- the normalised residual stream a MoE block sees; the mixer
+    layers between them are out of scope, and feeding one MoE output straight
+    into the next would collapse the activations and the routing.  Weights
+    are drawn on the GPU from seeded generators (~61 GiB; one layer's parity is
+    what the tests check)."""
+    from lightreason_b200 import native
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    native.device_check(local)
+    hbm_peak, _, peak_src = peaks()
+    tokens, n_layers = cfg["tokens"], cfg["layers"]
+    t_setup = time.perf_counter()
+    layers, u_all = [], []
+    for li in range(n_layers):
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + li)
+        rnd = lambda *shape: (torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * 0.02).to(  # noqa: E731
+            torch.bfloat16)
+        gate_up = rnd(EXPERTS, 2 * INNER, HIDDEN)
+        down = rnd(EXPERTS, HIDDEN, INNER)
+        bias = torch.from_numpy(S.router_bias(7, li, cfg["bias"])).to(dev)
+        layers.append(native.Layer(router=rnd(EXPERTS, HIDDEN), gate_up=gate_up, down=down, bias=bias,
+                                   shared_gate=rnd(INNER, HIDDEN), shared_up=rnd(INNER, HIDDEN),
+                                   shared_down=rnd(HIDDEN, INNER), shared_gate_w=rnd(HIDDEN)))
+    xs = [to_dev(S.hidden_states(7 + li, tokens), dev) for li in range(n_layers)]
+    acts = [torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev) for _ in range(n_layers)]
+    idx = [torch.empty((tokens, TOP_K), dtype=torch.int64, device=dev) for _ in range(n_layers)]
+    log(f"[bench] stack setup {time.perf_counter() - t_setup:.1f}s, {n_layers} layers, "
+        f"{torch.cuda.memory_allocated(dev) / 2**30:.1f} GiB allocated")
+
+    def stack_step(i, stage):
+        for li, layer in enumerate(layers):
+            layer(xs[li], out=acts[li], idx_out=idx[li])
+
+    def no_flush():
+        pass  # every step streams ~55 GB of weights: far larger than L2
+    sampler = ClockSampler(local)
+    with sampler:
+        ms, _, _ = timed_steps(stack_step, args.steps, args.warmup, no_flush, world)
+    clocks = sampler.summary()
+    total_ms = dist_max(sum(ms), world)
+    u = [len(set(t.cpu().numpy().reshape(-1).tolist())) for t in idx]
+    layer_bytes = [(ui + 1) * EXPERT_BYTES + EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 4 for ui in u]
+    step_ms = total_ms / args.steps
+    gbs = sum(layer_bytes) / (step_ms / 1e3) / 1e9
+    return {
+        "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
+        "value": round(world * tokens * args.steps / (total_ms / 1e3), 2), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 5),
+        "us_per_step": round(step_ms * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded GPU-drawn N(0,0.02) weights, N(0,1) activations, Zipf(1.1) router bias)",
+        "config": {"workload": cfg["workload"], "layers": n_layers, "tokens_per_step": tokens, "hidden": HIDDEN,
+                   "inner": INNER, "experts": EXPERTS, "top_k": TOP_K, "shared_expert": True,
+                   "distinct_experts_per_layer": round(float(np.mean(u)), 1),
+                   "l2": "not flushed: every step streams the selected experts of 40 layers (far above L2)",
+                   "parallelism": "single-gpu"},
+        "roofline": {"bound": "hbm", "kernel": "whole 40-layer step (all kernels)", "achieved": round(gbs, 1),
+                     "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
+                     "traffic": None, "algorithmic_bytes_per_step": int(sum(layer_bytes))},
+        "gpu_launches": 4 * n_layers * args.steps,
+        "clocks": clocks,
+    }
+
+
 def run_profile(args, cfg):
     """--profile N: N eager steps of the HBM-resident layer on one GPU, no CUDA
     graphs and no timing, for a profiler's launch list or kernel capture."""
@@ -723,7 +795,12 @@ def main():
         return
     world, rank, local = dist_setup()
     try:
-        res = run_ep(args, cfg, world, rank, local) if args.config == 4 else run_ours(args, cfg, world, rank, local)
+        if args.config == 4:
+            res = run_ep(args, cfg, world, rank, local)
+        elif args.config == 2:
+            res = run_stack(args, cfg, world, rank, local)
+        else:
+            res = run_ours(args, cfg, world, rank, local)
         if rank == 0 and world == 1 and args.config == 4 and not args.no_cpu_baseline:
             w = S.layer_weights(4, bias=cfg["bias"])
             gu, dn = w.stacked()
