@@ -67,6 +67,8 @@ PROFILED_TRAFFIC = {
     3: (2_004_844_000, "profiles/swiglu_grouped_kernel_T4096_config3.md"),
 }
 
+CACHE_SLOTS = 128  # experts the e2e_cached variant keeps in HBM (half of the bank, ~0.8 GB)
+
 CONFIGS = {
     0: dict(tokens=1, bias="normal", workload="config0: one MoE layer, decode T=1"),
     2: dict(tokens=64, bias="zipf", layers=40,
@@ -196,14 +198,18 @@ def build_layer(cfg, dev, seed):
     router = d(w.router)
     hbm = native.Layer(router=router, gate_up=d(gu), down=d(dn), bias=bias, shared_gate=sh[0], shared_up=sh[1],
                        shared_down=sh[2], shared_gate_w=sh[3])
-    host = None
+    host = cached = None
     if cfg.get("e2e_host_experts", True):
         # all experts in pinned host RAM in the packed BF16 layout
         # (the lossless row codec the reference streams over PCIe)
         banks = native.PackedHostBanks(gu, dn, dev)
         host = native.Layer(router=router, bias=bias, shared_gate=sh[0], shared_up=sh[1], shared_down=sh[2],
                             shared_gate_w=sh[3], host_packed=banks)
-    return w, gu, dn, hbm, host
+        # the same banks behind a device expert cache of CACHE_SLOTS experts
+        cached = native.Layer(router=router, bias=bias, shared_gate=sh[0], shared_up=sh[1], shared_down=sh[2],
+                              shared_gate_w=sh[3], host_packed=banks,
+                              cache_slots=max(CACHE_SLOTS, min(EXPERTS, cfg["tokens"] * TOP_K)))
+    return w, gu, dn, hbm, host, cached
 
 
 def timed_steps(run_step, steps, warmup, flush, world, stage_events=None):
@@ -336,7 +342,7 @@ def run_ours(args, cfg, world, rank, local):
     tokens = cfg["tokens"]
     seed = 1 + rank
     t_setup = time.perf_counter()
-    w, gu, dn, hbm, host = build_layer(cfg, dev, seed)
+    w, gu, dn, hbm, host, cached = build_layer(cfg, dev, seed)
     pool = 16
     xs_np = [S.hidden_states(seed, tokens, step=i) for i in range(pool)]
     xs = [to_dev(a, dev) for a in xs_np]
@@ -364,6 +370,11 @@ def run_ours(args, cfg, world, rank, local):
         host(xin, out=out, stage_events=stage)
         out_host.copy_(out, non_blocking=True)
 
+    def e2e_cached_step(i, stage):
+        xin.copy_(xs_host[i % pool], non_blocking=True)
+        cached(xin, out=out, stage_events=stage)
+        out_host.copy_(out, non_blocking=True)
+
     sampler = ClockSampler(local)
     with sampler:
         # step time: no stage events inside the steps
@@ -377,6 +388,9 @@ def run_ours(args, cfg, world, rank, local):
         if host is not None:
             e2e_ms, _, _ = timed_steps(e2e_step, args.steps, args.warmup, flush, world)
             _, e2e_stage, _ = timed_steps(e2e_step, args.steps, args.warmup, flush, world, stage_events=(2, 3))
+            cache_before = cached.cache_stats()
+            e2e_cached_ms, _, _ = timed_steps(e2e_cached_step, args.steps, args.warmup, flush, world)
+            cache_after = cached.cache_stats()
     clocks = sampler.summary()
 
     total_ms = dist_max(sum(ms), world)
@@ -453,6 +467,16 @@ def run_ours(args, cfg, world, rank, local):
             "gather_gbs": round(gathered / (statistics.mean(e2e_stage["gather"]) / 1e3) / 1e9, 2),
             "path": "moe_layer_forward with host_descriptors (pinned banks in the lossless row codec, decoded "
                     "in registers into HBM slots), x H2D + out D2H per step",
+        }
+        uses = cache_after["uses"] - cache_before["uses"]
+        misses = cache_after["misses"] - cache_before["misses"]
+        e2e_cached_total = dist_max(sum(e2e_cached_ms), world)
+        result["e2e_cached"] = {
+            "value": round(world * tokens * args.steps / (e2e_cached_total / 1e3), 2), "unit": "tokens/s",
+            "ms_per_step": round(e2e_cached_total / args.steps, 4), "cache_slots": cached.cache_slots,
+            "hit_rate": round((uses - misses) / uses, 4) if uses else None,
+            "path": f"as e2e, with a device expert cache (LRU over {cached.cache_slots} HBM slots, the B200 form "
+                    "of the reference's cached ExpertPool mode): only missing experts cross the host link",
         }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(cfg, w, gu, dn, seed)
@@ -710,7 +734,7 @@ def run_profile(args, cfg):
     dev = torch.device("cuda", 0)
     native.device_check(0)
     cfg = dict(cfg, e2e_host_experts=False)
-    w, gu, dn, hbm, _ = build_layer(cfg, dev, 1)
+    w, gu, dn, hbm, _, _ = build_layer(cfg, dev, 1)
     xs = [to_dev(S.hidden_states(1, cfg["tokens"], step=i), dev) for i in range(min(args.profile, 4))]
     flush_buf = torch.ones(64 << 20, dtype=torch.float32, device=dev)
     for i in range(args.profile):

@@ -218,6 +218,16 @@ typedef struct moe_layer_io {
      * bf16(act . Wd); weights_in may be NULL and no combine runs.  Rows of
      * dropped routes (ids outside [0, E)) are left untouched. */
     int rows_mode;
+    /* Expert cache over the host banks (the B200 form of edge35b/
+     * expert_stream.py:132-174 ExpertPool._expert's device-row LRU): with
+     * expert_cache != NULL the max_slots slot banks keep experts across calls
+     * and only the missing experts cross the host link.  expert_cache is
+     * device int32 [E + 2*max_slots + 3], zero-filled except slot_of[0..E) and
+     * expert_of[E..E+max_slots) = -1 before the first call, then owned by the
+     * layer (one cache per layer and stream); the last three words count the
+     * calls, the routed-expert uses and the misses.  Misses take the least
+     * recently used slots; max_slots <= 1024. */
+    int32_t *expert_cache;
 } moe_layer_io;
 
 /* Scratch bytes moe_layer_forward needs for `tokens` tokens. */

@@ -187,9 +187,12 @@ __global__ void __launch_bounds__(1024) gather_row_codec_kernel(const int64_t *_
 constexpr int kStageUnits = 1024;   // 16 KiB of output per ring stage
 constexpr int kStageRing = 3;
 
+// Entry g < *num_active stages expert active[g] into slot slot_of_entry[g]
+// (or slot g when slot_of_entry is null).
 __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__restrict__ descriptors,
                                                               const int32_t *__restrict__ active,
                                                               const int32_t *__restrict__ num_active, int experts,
+                                                              const int32_t *__restrict__ slot_of_entry,
                                                               uint16_t *gate_up_slots, uint16_t *down_slots,
                                                               int64_t gate_up_bytes, int64_t down_bytes,
                                                               int32_t *error) {
@@ -206,8 +209,9 @@ __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__r
     const uint8_t *src = reinterpret_cast<const uint8_t *>(d[0]);
     const int64_t base = d[1], escapes = d[2];
     const int64_t row_bytes = bank == 0 ? gate_up_bytes : down_bytes;
-    uint4 *dst = reinterpret_cast<uint4 *>(bank == 0 ? gate_up_slots + g * (gate_up_bytes / 2)
-                                                     : down_slots + g * (down_bytes / 2));
+    const int64_t slot = slot_of_entry ? slot_of_entry[g] : g;
+    uint4 *dst = reinterpret_cast<uint4 *>(bank == 0 ? gate_up_slots + slot * (gate_up_bytes / 2)
+                                                     : down_slots + slot * (down_bytes / 2));
     const int64_t units = row_bytes >> 4;
     if (base < 0 || (units & 3)) {
         row_codec_share<false>(src, base, escapes, row_bytes, dst, blockIdx.x, gridDim.x);
@@ -291,10 +295,10 @@ __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__r
 
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
                            int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
-                           int64_t down_bytes, int32_t *error, cudaStream_t stream) {
+                           int64_t down_bytes, int32_t *error, cudaStream_t stream, const int32_t *slot_of_entry) {
     return launch_pdl(stage_row_codec_kernel, dim3(64, 2, max_slots), dim3(256), 0, stream, "stage_row_codec_kernel",
-                      descriptors, active, num_active, experts, gate_up_slots, down_slots, gate_up_bytes, down_bytes,
-                      error);
+                      descriptors, active, num_active, experts, slot_of_entry, gate_up_slots, down_slots,
+                      gate_up_bytes, down_bytes, error);
 }
 
 template <bool AllowCompact>

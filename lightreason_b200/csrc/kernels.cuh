@@ -100,7 +100,8 @@ int sm_count();
 
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
                            int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
-                           int64_t down_bytes, int32_t *error, cudaStream_t stream);
+                           int64_t down_bytes, int32_t *error, cudaStream_t stream,
+                           const int32_t *slot_of_entry = nullptr);
 
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);

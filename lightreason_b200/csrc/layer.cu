@@ -25,7 +25,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of the scratch arrays inside the caller's workspace.
 struct Layout {
     size_t logits, sig, idx, scores, offsets, route_token, perm_slot, route_pos, active, counters, groups, plan, off1,
-        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, perm_hist, rsplit, total;
+        off2, done1, done2, split_cnt, gofe, rpart, part, xs, act, y, perm_hist, rsplit, stage_e, stage_s, total;
     int router_ks;
     int split_len;
 };
@@ -55,7 +55,9 @@ Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     L.perm_slot = take(R * 4);
     L.route_pos = take(R * 4);
     L.active = take(E * 4);
-    L.counters = take(8 * 4);  // num_active, bad_routes, host-stage error, slot overflow, router error
+    L.counters = take(8 * 4);  // num_active, bad_routes, host-stage error, slot overflow, router error, misses
+    L.stage_e = take(E * 4);
+    L.stage_s = take(E * 4);
     L.groups = take((E + 1) * sizeof(GroupedGroup));
     L.plan = take(sizeof(GroupedPlan));
     L.off1 = take((E + 2) * 4);
@@ -87,8 +89,11 @@ T *at(void *base, size_t offset) {
 // Copy every active expert's gate_up and down rows from the mapped host banks
 // into HBM slot g (g-th active expert).  Grid (stripes, 2 banks, max_slots);
 // 16-byte loads over the host link, four in flight per thread.
+// Entry g < *num_active copies expert active[g] into slot slot_of_entry[g]
+// (or slot g when slot_of_entry is null).
 __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__restrict__ active,
                                                             const int32_t *__restrict__ num_active,
+                                                            const int32_t *__restrict__ slot_of_entry,
                                                             const uint16_t *host_gate_up, const uint16_t *host_down,
                                                             int64_t gate_up_stride, int64_t down_stride,
                                                             int64_t gate_up_bytes, int64_t down_bytes,
@@ -105,8 +110,9 @@ __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__res
     const uint4 *src = reinterpret_cast<const uint4 *>(gu ? host_gate_up + e * gate_up_stride
                                                           : host_down + e * down_stride);
     const int64_t bytes = gu ? gate_up_bytes : down_bytes;
-    uint4 *dst = reinterpret_cast<uint4 *>(gu ? gate_up_slots + g * (gate_up_bytes / 2)
-                                              : down_slots + g * (down_bytes / 2));
+    const int64_t slot = slot_of_entry ? slot_of_entry[g] : g;
+    uint4 *dst = reinterpret_cast<uint4 *>(gu ? gate_up_slots + slot * (gate_up_bytes / 2)
+                                              : down_slots + slot * (down_bytes / 2));
     const int64_t units = bytes / 16;
     const int64_t begin = units * blockIdx.x / gridDim.x, end = units * (blockIdx.x + 1) / gridDim.x;
     int64_t i = begin + threadIdx.x;
@@ -119,6 +125,90 @@ __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__res
         dst[i + 3 * blockDim.x] = v3;
     }
     for (; i < end; i += blockDim.x) dst[i] = ld_stream(src + i);
+}
+
+// Expert cache (moe_layer_io.expert_cache): the slot banks keep experts across
+// calls.  State: slot_of[E] (-1: not cached), expert_of[S] (-1: empty),
+// stamp[S] (the call that last used the slot), then step, total routed-expert
+// uses and total misses.  One CTA, after the plan: hits stamp their slots;
+// misses take, in ascending expert order, the least recently used slots not
+// used by this call (ties to the lower slot), and become the stage list; every
+// routed group's weight index becomes its slot.  Needs S >= the routed groups
+// of the call and S <= 1024.
+__global__ void __launch_bounds__(1024) cache_plan_kernel(const int32_t *__restrict__ active,
+                                                          const int32_t *__restrict__ num_active,
+                                                          GroupedGroup *__restrict__ groups, int32_t *__restrict__ cache,
+                                                          int experts, int slots, int32_t *__restrict__ stage_e,
+                                                          int32_t *__restrict__ stage_s, int32_t *__restrict__ stage_n) {
+    __shared__ unsigned long long keys[1024];
+    __shared__ int miss_e[1024];
+    __shared__ int scratch[33];
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    int32_t *slot_of = cache, *expert_of = cache + experts, *stamp = cache + experts + slots;
+    int32_t *meta = cache + experts + 2 * slots;
+    const int step = meta[0] + 1;
+    const int n = *num_active;
+    const int g = threadIdx.x;
+    int e = -1;
+    bool miss = false;
+    if (g < n) {
+        e = active[g];
+        const int s = slot_of[e];
+        if (s >= 0) stamp[s] = step;
+        else miss = true;
+    }
+    __syncthreads();
+    int n_miss = 0;
+    const int m = block_exclusive_scan(miss ? 1 : 0, scratch, &n_miss);
+    if (miss) miss_e[m] = e;
+    int P = 1;
+    while (P < slots) P <<= 1;
+    for (int s = threadIdx.x; s < P; s += blockDim.x) {
+        unsigned long long k = ~0ull;
+        if (s < slots) {
+            const unsigned used = stamp[s] == step ? 0x7fffffffu : static_cast<unsigned>(stamp[s]);
+            k = (static_cast<unsigned long long>(used) << 32) | static_cast<unsigned>(s);
+        }
+        keys[s] = k;
+    }
+    __syncthreads();
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const int i = threadIdx.x;
+            if (i < P) {
+                const int o = i ^ j;
+                if (o > i) {
+                    const bool up = (i & k) == 0;
+                    const unsigned long long a = keys[i], b = keys[o];
+                    if ((a > b) == up) {
+                        keys[i] = b;
+                        keys[o] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    if (threadIdx.x < n_miss) {
+        const int v = static_cast<int>(keys[threadIdx.x] & 0xffffffffull);
+        const int ne = miss_e[threadIdx.x];
+        const int old = expert_of[v];
+        if (old >= 0) slot_of[old] = -1;
+        slot_of[ne] = v;
+        expert_of[v] = ne;
+        stamp[v] = step;
+        stage_e[threadIdx.x] = ne;
+        stage_s[threadIdx.x] = v;
+    }
+    __syncthreads();
+    if (g < n) groups[g].weight = slot_of[e];
+    if (threadIdx.x == 0) {
+        *stage_n = n_miss;
+        meta[0] = step;
+        meta[1] += n;
+        meta[2] += n_miss;
+    }
 }
 
 }  // namespace lrb
@@ -158,6 +248,9 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     const int max_groups = std::min(E, R);
     LRB_REQUIRE(!staged || io->max_slots >= max_groups, "moe_layer_forward: max_slots %d < min(E, T*top_k) = %d",
                 staged ? io->max_slots : 0, max_groups);
+    const bool cached = io->expert_cache != nullptr;
+    LRB_REQUIRE(!cached || (staged && io->max_slots <= 1024),
+                "moe_layer_forward: expert_cache needs host banks and at most 1024 slots");
     LRB_REQUIRE(staged || (w->gate_up && w->down), "moe_layer_forward: expert banks required");
     const int64_t gu_stride = w->gate_up_stride ? w->gate_up_stride : static_cast<int64_t>(2) * I * H;
     const int64_t dn_stride = w->down_stride ? w->down_stride : static_cast<int64_t>(H) * I;
@@ -277,15 +370,26 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
 
     const uint16_t *gu_base = w->gate_up, *dn_base = w->down;
     int64_t gu_str = gu_stride, dn_str = dn_stride;
+    // stage list: every active expert into slot g, or with the cache only the misses into their slots
+    const int32_t *stage_list = active, *stage_count = counters + 0, *stage_slot = nullptr;
+    if (cached) {
+        int32_t *se = at<int32_t>(ws, L.stage_e), *ss = at<int32_t>(ws, L.stage_s);
+        if (int rc = launch_pdl(cache_plan_kernel, dim3(1), dim3(1024), 0, s, "cache_plan_kernel", active,
+                                counters + 0, groups, io->expert_cache, E, io->max_slots, se, ss, counters + 5))
+            return rc;
+        stage_list = se;
+        stage_slot = ss;
+        stage_count = counters + 5;
+    }
     if (packed_host) {
-        if (int rc = launch_stage_row_codec(io->host_descriptors, active, counters + 0, E, max_groups,
+        if (int rc = launch_stage_row_codec(io->host_descriptors, stage_list, stage_count, E, max_groups,
                                             io->gate_up_slots, io->down_slots, static_cast<int64_t>(2) * I * H * 2,
-                                            static_cast<int64_t>(H) * I * 2, counters + 2, s))
+                                            static_cast<int64_t>(H) * I * 2, counters + 2, s, stage_slot))
             return rc;
     } else if (staged) {
         if (int rc = launch_pdl(stage_experts_kernel, dim3(64, 2, max_groups), dim3(256), 0, s,
-                                "stage_experts_kernel", active, counters + 0, io->host_gate_up, io->host_down,
-                                gu_stride, dn_stride, static_cast<int64_t>(2) * I * H * 2,
+                                "stage_experts_kernel", stage_list, stage_count, stage_slot, io->host_gate_up,
+                                io->host_down, gu_stride, dn_stride, static_cast<int64_t>(2) * I * H * 2,
                                 static_cast<int64_t>(H) * I * 2, io->gate_up_slots, io->down_slots, counters + 3))
             return rc;
     }

@@ -49,7 +49,7 @@ class LayerIO(ctypes.Structure):
     _fields_ = [("route_in", _p), ("weights_in", _p), ("idx_out", _p), ("scores_out", _p), ("logits_out", _p),
                 ("host_gate_up", _p), ("host_down", _p), ("gate_up_slots", _p), ("down_slots", _p),
                 ("max_slots", _i), ("host_descriptors", _p), ("stage_events", ctypes.POINTER(_p)),
-                ("num_stage_events", _i), ("status", _p), ("rows_mode", _i)]
+                ("num_stage_events", _i), ("status", _p), ("rows_mode", _i), ("expert_cache", _p)]
 
 
 _SIGNATURES = {
@@ -251,7 +251,7 @@ class Layer:
 
     def __init__(self, *, router=None, gate_up=None, down=None, bias=None, shared_gate=None, shared_up=None,
                  shared_down=None, shared_gate_w=None, top_k=8, host_gate_up=None, host_down=None,
-                 host_packed=None, device=None):
+                 host_packed=None, device=None, cache_slots=None):
         """router may be None for a layer only called with route_in (the
         Qwen3_5MoeExperts.forward form); experts and hidden then come from the
         banks."""
@@ -301,6 +301,21 @@ class Layer:
             shared_inner=(shared_gate.shape[0] if shared_gate is not None else self.inner), top_k=top_k)
         self._slots = None
         self._ws = None
+        # expert cache over the host banks: cache_slots slot rows kept across calls
+        self.cache_slots = cache_slots
+        self.cache = None
+        if cache_slots is not None:
+            _require(host_gate_up is not None or host_packed is not None, "cache_slots needs host banks")
+            _require(0 < cache_slots <= 1024, "cache_slots must be in [1, 1024]")
+            self.cache = torch.zeros(self.experts + 2 * cache_slots + 3, dtype=torch.int32, device=self.device)
+            self.cache[:self.experts + cache_slots] = -1
+
+    def cache_stats(self) -> dict:
+        """Calls, routed-expert uses and misses counted by the expert cache."""
+        _require(self.cache is not None, "no expert cache")
+        calls, uses, misses = self.cache[-3:].tolist()
+        return {"calls": calls, "uses": uses, "misses": misses,
+                "hit_rate": (uses - misses) / uses if uses else 0.0}
 
     def _map(self, t: torch.Tensor) -> int:
         _require(t.device.type == "cpu" and t.is_contiguous() and t.dtype == torch.bfloat16,
@@ -333,6 +348,9 @@ class Layer:
 
     def slots(self, tokens: int):
         n = min(self.experts, tokens * self.top_k)
+        if self.cache_slots is not None:
+            _require(self.cache_slots >= n, f"cache_slots {self.cache_slots} < min(E, T*top_k) = {n}")
+            n = self.cache_slots
         if self._slots is None or self._slots[0].shape[0] < n:
             self._slots = (torch.empty((n, 2 * self.inner, self.hidden), dtype=torch.bfloat16, device=self.device),
                            torch.empty((n, self.hidden, self.inner), dtype=torch.bfloat16, device=self.device))
@@ -394,6 +412,8 @@ class Layer:
             else:
                 io.host_gate_up, io.host_down = self._host_dev
             io.gate_up_slots, io.down_slots, io.max_slots = gs.data_ptr(), ds.data_ptr(), gs.shape[0]
+            if self.cache is not None:
+                io.expert_cache = self.cache.data_ptr()
         check(lib().moe_layer_forward(ctypes.byref(self.w), _ptr(x), tokens, _ptr(out), ctypes.byref(io), _ptr(ws),
                                       ws.numel(), _stream(x.device)), "moe_layer_forward")
         return out

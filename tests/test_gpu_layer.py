@@ -214,6 +214,40 @@ def test_packed_host_experts_match_hbm_resident(dev, case13, tokens):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("packed,slots,tokens", [(True, 128, 16), (False, 128, 16), (True, 200, 4), (True, 64, 8)])
+def test_expert_cache_matches_hbm_resident(dev, case13, packed, slots, tokens):
+    """The expert cache over host banks: over a run of calls (hits, misses and
+    evictions; slots == min(E, T*top_k) evicts on nearly every call) every
+    output is bit-identical to the HBM-resident layer, and the counters add up."""
+    kw = dict(router=case13.router, bias=case13.bias, shared_gate=case13.sh[0], shared_up=case13.sh[1],
+              shared_down=case13.sh[2], shared_gate_w=case13.sh[3], cache_slots=slots)
+    if packed:
+        cached = native.Layer(host_packed=native.PackedHostBanks(case13.gu, case13.dn, dev), **kw)
+    else:
+        hg = torch.from_numpy(case13.gu.view(np.int16)).view(torch.bfloat16).pin_memory()
+        hd = torch.from_numpy(case13.dn.view(np.int16)).view(torch.bfloat16).pin_memory()
+        cached = native.Layer(host_gate_up=hg, host_down=hd, **kw)
+    uses = 0
+    for call in range(6):
+        x = S.hidden_states(400 + call % 4, tokens)  # repeats: calls 4 and 5 reuse the inputs of 0 and 1
+        want = case13.run(x)
+        got = case13.run(x, layer=cached)
+        for a, b in zip(want, got):
+            assert np.array_equal(a, b), call
+        uses += len(set(got[1].reshape(-1).tolist()))
+    st = cached.cache_stats()
+    assert st["calls"] == 6 and st["uses"] == uses and 0 < st["misses"] <= uses
+    if slots >= 128:
+        assert st["misses"] < uses
+    cache = cached.cache.cpu().numpy()
+    slot_of, expert_of = cache[:256], cache[256:256 + slots]
+    held = expert_of[expert_of >= 0]
+    assert len(set(held.tolist())) == held.size                      # an expert holds at most one slot
+    assert all(slot_of[e] == s for s, e in enumerate(expert_of) if e >= 0)
+    assert (slot_of >= 0).sum() == held.size
+    cached.release()
+
+
 def test_route_in_is_the_experts_forward(dev, case13):
     """Qwen3_5MoeExperts.forward semantics: given ids and BF16 weights, no router
     and no shared expert (edge35b _Layer.forward)."""
