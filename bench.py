@@ -744,6 +744,106 @@ def run_profile(args, cfg):
     return {"profile_steps": args.profile, "workload": cfg["workload"], "tokens": cfg["tokens"]}
 
 
+def run_encode(args):
+    """--encode: the device codec encoders over one 35B layer's expert banks
+    (gate_up [256, 1024, 2048] + down [256, 2048, 512] BF16, N(0, 0.02) drawn
+    on the GPU, 1.5 GiB): row codec plan + pack and tile codec pack per step,
+    CUDA events per encoder, inputs far above L2.  Reported as GB/s of BF16
+    input; the roofline counts the algorithmic bytes of each encoder (row
+    codec: the bank read twice + packed bytes written; tile codec: the bank
+    read once + 3/4 of it written + one base byte per tile)."""
+
+    from lightreason_b200 import bf16_expert_codec as codec
+    from lightreason_b200 import native
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    native.device_check(0)
+    hbm_peak, _, peak_src = peaks()
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    banks = [(torch.randn(shape, generator=g, device=dev, dtype=torch.float32) * 0.02).to(torch.bfloat16)
+             .view(torch.int16) for shape in ((EXPERTS, 2 * INNER, HIDDEN), (EXPERTS, HIDDEN, INNER))]
+    L = native.lib()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    row = []
+    for bank in banks:
+        rows, n = bank.shape[0], bank[0].numel()
+        ws = torch.empty(L.moe_rowcodec_workspace_bytes(rows, n), dtype=torch.uint8, device=dev)
+        meta = torch.empty((rows, 3), dtype=torch.int64, device=dev)
+        total = torch.empty(1, dtype=torch.int64, device=dev)
+        native.check(L.moe_rowcodec_plan(bank.data_ptr(), rows, n, meta.data_ptr(), total.data_ptr(), ws.data_ptr(),
+                                         ws.numel(), stream), "moe_rowcodec_plan")
+        packed = torch.zeros(max(int(total.item()), 16), dtype=torch.uint8, device=dev)
+        row.append((bank, rows, n, ws, meta, total, packed))
+    tiles = [(bank, bank.numel() // 256, torch.empty((bank.numel() // 256, 384), dtype=torch.uint8, device=dev),
+              torch.empty(bank.numel() // 256, dtype=torch.uint8, device=dev)) for bank in banks]
+    encoded = torch.zeros(1, dtype=torch.int64, device=dev)
+
+    def row_step():
+        for bank, rows, n, ws, meta, total, packed in row:
+            native.check(L.moe_rowcodec_plan(bank.data_ptr(), rows, n, meta.data_ptr(), total.data_ptr(),
+                                             ws.data_ptr(), ws.numel(), stream), "moe_rowcodec_plan")
+            native.check(L.moe_rowcodec_pack(bank.data_ptr(), rows, n, meta.data_ptr(), packed.data_ptr(),
+                                             ws.data_ptr(), ws.numel(), stream), "moe_rowcodec_pack")
+
+    def tile_step():
+        for bank, nt, packed, bases in tiles:
+            native.check(L.moe_tilecodec_pack(bank.data_ptr(), nt, packed.data_ptr(), bases.data_ptr(),
+                                              encoded.data_ptr(), stream), "moe_tilecodec_pack")
+
+    def timed(step):
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        ms = []
+        for _ in range(args.steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            step()
+            b.record()
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+        return statistics.median(ms)
+
+    with ClockSampler(0) as clk:
+        row_ms = timed(row_step)
+        tile_ms = timed(tile_step)
+    in_bytes = sum(b.numel() * 2 for b in banks)
+    packed_bytes = sum(int(r[5].item()) for r in row)
+    row_alg = 2 * in_bytes + packed_bytes
+    n_tiles = sum(t[1] for t in tiles)
+    tile_alg = in_bytes + n_tiles * 384 + n_tiles
+    # the host encoder (numpy, all host threads) on 8 experts of the gate_up bank
+    host_bank = banks[0][:8].cpu().numpy().view(np.uint16)
+    t = time.perf_counter()
+    codec.pack_bank(host_bank)
+    host_s = time.perf_counter() - t
+    threads = min(32, os.cpu_count() or 1)
+    plans = [r[4].cpu().tolist() for r in row]
+    raw_rows = sum(1 for p in plans for o, _, _ in p if o < 0)
+    return {
+        "metric": "expert-bank encode throughput (GB/s of BF16 input), row codec",
+        "value": round(in_bytes / row_ms / 1e6, 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(row_ms, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u16", "data": "synthetic",
+        "config": {"workload": "one 35B layer's gate_up + down banks (1.5 GiB BF16), device encoders",
+                   "l2": "inputs 1.5 GiB, far above L2"},
+        "roofline": {"bound": "hbm", "achieved": round(row_alg / row_ms / 1e6, 1), "peak": hbm_peak,
+                     "unit": "GB/s", "frac": round(row_alg / row_ms / 1e6 / hbm_peak, 4), "traffic": None,
+                     "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else
+                     "fallback"},
+        "tile_codec": {"value": round(in_bytes / tile_ms / 1e6, 2), "unit": "GB/s", "ms_per_step": round(tile_ms, 4),
+                       "achieved": round(tile_alg / tile_ms / 1e6, 1),
+                       "frac": round(tile_alg / tile_ms / 1e6 / hbm_peak, 4),
+                       "encoded_tiles": int(encoded.item()) // (args.warmup + args.steps)},
+        "packed_bytes": packed_bytes, "raw_rows": raw_rows,
+        "cpu_baseline": {"value": round(host_bank.nbytes / host_s / 1e9, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": "bf16_expert_codec.pack_bank (numpy) on 8 gate_up experts"},
+        "gpu_launches": args.steps * (2 * 4 + 2), "clocks": clk.summary(),
+    }
+
+
 def run_reference(args, cfg, world, rank):
     """Reference arm: the reference's CPU implementation on the host cores."""
     if rank != 0:
@@ -796,6 +896,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
                     help="expert-parallel exchange on N > 1 GPUs: NVLink peer memory (default) or NCCL all_to_all")
+    ap.add_argument("--encode", action="store_true",
+                    help="time the device codec encoders on one layer's expert banks instead of the layer")
     ap.add_argument("--profile", type=int, default=0, metavar="N",
                     help="run N eager layer steps of the config on one GPU (for ncu) and print a short status line")
     args = ap.parse_args()
@@ -816,6 +918,9 @@ def main():
         return
     if args.profile:
         print(json.dumps(run_profile(args, cfg)), file=json_out, flush=True)
+        return
+    if args.encode:
+        print(json.dumps(run_encode(args)), file=json_out, flush=True)
         return
     world, rank, local = dist_setup()
     try:

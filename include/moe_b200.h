@@ -309,6 +309,36 @@ int moe_gather_compact_tail(const int64_t *sources, const int64_t *destinations,
                             int max_rows, int banks, void *stream);
 
 /* ------------------------------------------------------------------------
+ * Lossless codec encoders on the device.  The same bytes as the host encoders
+ * the gather kernels decode:
+ *
+ * moe_rowcodec_plan replaces edge35b/bf16_expert_codec.py:26-33
+ *   exponent_window + :66-78 plan_bank for a bank of `rows` rows of n BF16
+ *   values (n a multiple of 8, bank 16-byte aligned): meta (int64 [rows][3])
+ *   = (packed offset, or -1 for a row kept raw because its escapes exceed 1%
+ *   of n; window base; escapes), *total = packed bytes (offsets and sizes
+ *   rounded up to 16 bytes).
+ * moe_rowcodec_pack replaces :40-51 pack_row over every packed row of that
+ *   plan: [n sign|fraction bytes][n/2 exponent-delta nibbles][int32 escape
+ *   indices, ascending][uint16 escape values] at packed + offset.
+ * Both take a device workspace of moe_rowcodec_workspace_bytes(rows, n)
+ *   bytes, the same one: pack reads the per-chunk exponent histograms that
+ *   plan left there, so the bank is read twice in all (histograms, pack).
+ * moe_tilecodec_pack replaces edge35b/cpu_bf16_reads.h:16-52
+ *   pack_cpu_read_tiles: per 256-value tile, bases[t] = the smallest 7-bit
+ *   exponent when the tile's exponents span at most 8 (else 255, raw, its 384
+ *   packed bytes zeroed); packed + 384 t = 256 low bytes + 128 bytes of 4-bit
+ *   codes.  *encoded (device uint64, not cleared) += tiles encoded.
+ * ------------------------------------------------------------------------ */
+size_t moe_rowcodec_workspace_bytes(int rows, int64_t n);
+int moe_rowcodec_plan(const uint16_t *bank, int rows, int64_t n, int64_t *meta, int64_t *total, void *workspace,
+                      size_t workspace_bytes, void *stream);
+int moe_rowcodec_pack(const uint16_t *bank, int rows, int64_t n, const int64_t *meta, uint8_t *packed,
+                      void *workspace, size_t workspace_bytes, void *stream);
+int moe_tilecodec_pack(const uint16_t *raw, int64_t tiles, uint8_t *packed, uint8_t *bases,
+                       unsigned long long *encoded, void *stream);
+
+/* ------------------------------------------------------------------------
  * Expert parallelism (no counterpart in the reference, which runs its MoE
  * layer on one GPU).  Rank r of `world` owns experts [r*E/world, (r+1)*E/world);
  * the exchange between these calls is NCCL all_to_all_single.

@@ -19,7 +19,8 @@ CSRC = PKG / "csrc"
 OUT_DIR = PKG / "_native"
 LIB = OUT_DIR / "libmoe_b200.so"
 SOURCES = ["host.cu", "router.cu", "permute.cu", "experts.cu", "layer.cu", "gather.cu", "grouped.cu",
-           "expert_rows_noalloc.cu", "expert_parallel.cu", "router_tc.cu", "primary.cu", "ep_p2p.cu"]
+           "expert_rows_noalloc.cu", "expert_parallel.cu", "router_tc.cu", "primary.cu", "ep_p2p.cu",
+           "codec.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

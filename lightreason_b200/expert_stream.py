@@ -26,6 +26,11 @@ three residencies:
   "b200-packed"  as b200-host with the rows kept in the lossless row codec
                  (bf16_expert_codec), 25% fewer bytes over the host link --
                  also "packed".
+With capacity_bytes > 0 the host residencies keep up to capacity_bytes of
+experts per layer in HBM slots across calls (a device-side LRU, the role of
+the reference pool's byte-bounded row cache, expert_stream.py:132-174): only
+the missing experts cross the host link.  Calls that route to more experts
+than the cache holds take the uncached path.
 """
 
 from __future__ import annotations
@@ -106,11 +111,20 @@ class ExpertPool:
         elif owner != self._owner:
             raise RuntimeError("Use the pool on its original CUDA thread and stream")
 
-    def _native_layer(self, layer: "_Layer", top_k: int, owner=None, extra=None) -> native.Layer:
+    def cache_slots(self, layer: "_Layer", routed: int) -> int:
+        """Expert-cache slots for a host-resident layer (0: none), if a call
+        routing to `routed` distinct experts at most fits in them."""
+        if layer.residency == "b200" or not self._capacity_bytes:
+            return 0
+        slots = min(self._capacity_bytes // layer.row_bytes, layer.module.num_experts, 1024)
+        return slots if slots >= routed else 0
+
+    def _native_layer(self, layer: "_Layer", top_k: int, owner=None, extra=None, cache: int = 0) -> native.Layer:
         """The native layer of one patched module, built on first use: the
         expert banks in the layer's residency plus `extra` device tensors
-        (router and shared expert, for a whole-block patch)."""
-        key = (id(owner if owner is not None else layer.module), layer.residency)
+        (router and shared expert, for a whole-block patch), behind an
+        expert cache of `cache` slots when nonzero."""
+        key = (id(owner if owner is not None else layer.module), layer.residency, cache)
         cached = self._layers.get(key)
         if cached is not None:
             if cached.top_k != top_k:
@@ -125,14 +139,24 @@ class ExpertPool:
                 self.stats.resident_bytes += gu.numel() * 2 + dn.numel() * 2
             built = native.Layer(gate_up=gu.contiguous(), down=dn.contiguous(), top_k=top_k, **extra)
         elif layer.residency == "b200-host":
-            built = native.Layer(host_gate_up=gu.detach().contiguous(), host_down=dn.detach().contiguous(),
-                                 top_k=top_k, device=self.device, **extra)
-            self.stats.pinned_bytes += gu.numel() * 2 + dn.numel() * 2
+            shared = self._layers.get((key[0], layer.residency, 0))
+            if shared is not None and shared._host_dev[0] is not None:
+                host = dict(host_gate_up=shared.host_gate_up, host_down=shared.host_down)
+            else:
+                host = dict(host_gate_up=gu.detach().contiguous(), host_down=dn.detach().contiguous())
+                self.stats.pinned_bytes += gu.numel() * 2 + dn.numel() * 2
+            built = native.Layer(top_k=top_k, device=self.device, cache_slots=cache or None, **host, **extra)
         else:
-            bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
-            banks = native.PackedHostBanks(bits(gu), bits(dn), self.device)
-            built = native.Layer(host_packed=banks, top_k=top_k, device=self.device, **extra)
-            self.stats.pinned_bytes += sum(b.numel() for b in banks.buffers)
+            shared = self._layers.get((key[0], layer.residency, 0)) or next(
+                (v for k, v in self._layers.items() if k[:2] == key[:2]), None)
+            if shared is not None:
+                banks = shared.host_packed
+            else:
+                bits = lambda t: t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+                banks = native.PackedHostBanks(bits(gu), bits(dn), self.device)
+                self.stats.pinned_bytes += sum(b.numel() for b in banks.buffers)
+            built = native.Layer(host_packed=banks, top_k=top_k, device=self.device, cache_slots=cache or None,
+                                 **extra)
         self.stats.resident_bytes += sum(t.numel() * t.element_size() for t in extra.values())
         self._layers[key] = built
         return built
@@ -202,7 +226,8 @@ class _Layer:
         """The device chain itself, shared by the per-path entry points."""
         if hidden_states.shape[0] == 0:
             return torch.zeros_like(hidden_states)
-        layer = self.pool._native_layer(self, top_k_index.shape[1])
+        routed = min(self.module.num_experts, top_k_index.numel())
+        layer = self.pool._native_layer(self, top_k_index.shape[1], cache=self.pool.cache_slots(self, routed))
         return layer(hidden_states.contiguous(), route_in=top_k_index.contiguous(),
                      weights_in=top_k_weights.contiguous())
 

@@ -55,7 +55,9 @@ class _Block:
         pool.stats.tokens += x.shape[0]
         if x.shape[0] == 0:
             return torch.zeros_like(hidden_states)
-        layer = pool._native_layer(self.experts, self.top_k, owner=self.block, extra=self._extra())
+        routed = min(self.block.experts.num_experts, x.shape[0] * self.top_k)
+        layer = pool._native_layer(self.experts, self.top_k, owner=self.block, extra=self._extra(),
+                                   cache=pool.cache_slots(self.experts, routed))
         return layer(x).reshape(shape)
 
 

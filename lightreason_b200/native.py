@@ -73,6 +73,10 @@ _SIGNATURES = {
     "moe_gather_rows": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _i, _p], _i),
     "moe_stage_primary": ([_p, _p, _p, _p, _p, _p, _i, _i, _i, _i, _p], _i),
     "moe_gather_compact_tail": ([_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i, _i, _i, _p], _i),
+    "moe_rowcodec_workspace_bytes": ([_i, ctypes.c_int64], _sz),
+    "moe_rowcodec_plan": ([_p, _i, ctypes.c_int64, _p, _p, _p, _sz, _p], _i),
+    "moe_rowcodec_pack": ([_p, _i, ctypes.c_int64, _p, _p, _p, _sz, _p], _i),
+    "moe_tilecodec_pack": ([_p, ctypes.c_int64, _p, _p, _p, _p], _i),
     "moe_ipc_alloc": ([_sz, ctypes.POINTER(_p), _p], _i),
     "moe_ipc_free": ([_p], _i),
     "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
@@ -474,6 +478,75 @@ def gather_compact_tail(sources, destinations, sizes, prefix_tables, tail, src, 
           "moe_gather_compact_tail")
 
 
+# ---------------------------------------------------------------- codecs ---
+
+def _bits_view(t: "torch.Tensor", name: str) -> "torch.Tensor":
+    _require(t.is_cuda and t.is_contiguous() and t.element_size() == 2,
+             f"{name} must be a contiguous CUDA tensor of 16-bit values (BF16 bits)")
+    return t.view(torch.int16)
+
+
+def rowcodec_plan(bank: "torch.Tensor"):
+    """moe_rowcodec_plan on the current stream: the device version of
+    bf16_expert_codec.plan_bank for a CUDA bank [E, ...].  Returns (meta int64
+    [E, 3] CUDA tensor of (offset or -1, base, escapes), packed bytes,
+    workspace).  Synchronises once to read the packed size."""
+    bank = _bits_view(bank, "bank")
+    rows = bank.shape[0]
+    n = bank.numel() // max(rows, 1)
+    ws_bytes = lib().moe_rowcodec_workspace_bytes(rows, n)
+    ws = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=bank.device)
+    meta = torch.empty((rows, 3), dtype=torch.int64, device=bank.device)
+    total = torch.empty(1, dtype=torch.int64, device=bank.device)
+    check(lib().moe_rowcodec_plan(_ptr(bank), rows, n, _ptr(meta), _ptr(total), _ptr(ws), ws.numel(),
+                                  _stream(bank.device)), "moe_rowcodec_plan")
+    return meta, int(total.item()), ws
+
+
+def rowcodec_pack(bank: "torch.Tensor", meta=None):
+    """Device row-codec encoder of a CUDA bank [E, ...] (16-bit BF16 bits):
+    the bytes of bf16_expert_codec.pack_bank.  Returns (packed uint8 CUDA
+    tensor of max(size, 16) bytes, plan rows as plan_bank: (offset, base,
+    escapes) or None).  `meta` (int64 [E, 3] CUDA) overrides the plan, e.g. to
+    pack a row that the 1% rule keeps raw."""
+    bank = _bits_view(bank, "bank")
+    rows = bank.shape[0]
+    n = bank.numel() // max(rows, 1)
+    planned, size, ws = rowcodec_plan(bank)
+    if meta is None:
+        meta = planned
+    else:
+        _table("meta", meta, torch.int64, 2)
+        m = meta.cpu()
+        size = max([int(o) + row_bytes(n, int(e)) for o, _, e in m.tolist() if o >= 0] + [0])
+    packed = torch.zeros(max(size, 16), dtype=torch.uint8, device=bank.device)
+    check(lib().moe_rowcodec_pack(_ptr(bank), rows, n, _ptr(meta), _ptr(packed), _ptr(ws), ws.numel(),
+                                  _stream(bank.device)), "moe_rowcodec_pack")
+    plan = [None if o < 0 else (int(o), int(b), int(e)) for o, b, e in meta.cpu().tolist()]
+    return packed, plan
+
+
+def row_bytes(n: int, escapes: int) -> int:
+    """Packed bytes of a row of n values with `escapes` escapes (unaligned)."""
+    return 3 * n // 2 + 6 * escapes
+
+
+def tilecodec_pack(raw: "torch.Tensor"):
+    """Device tile-codec encoder (cpu_bf16_reads.h:16-52 pack_cpu_read_tiles)
+    of a CUDA array of 256-value tiles.  Returns (packed uint8 [tiles, 384],
+    bases uint8 [tiles] with 255 = raw, encoded tiles); raw tiles pack to 384
+    zero bytes."""
+    raw = _bits_view(raw, "raw")
+    _require(raw.numel() % 256 == 0, "raw must hold whole 256-value tiles")
+    tiles = raw.numel() // 256
+    packed = torch.empty((tiles, 384), dtype=torch.uint8, device=raw.device)
+    bases = torch.empty(tiles, dtype=torch.uint8, device=raw.device)
+    encoded = torch.zeros(1, dtype=torch.int64, device=raw.device)
+    check(lib().moe_tilecodec_pack(_ptr(raw), tiles, _ptr(packed), _ptr(bases), _ptr(encoded),
+                                   _stream(raw.device)), "moe_tilecodec_pack")
+    return packed, bases, int(encoded.item())
+
+
 def prefix_table(bases) -> "torch.Tensor":
     """Per (expert, 32 tiles): (raw tiles before the group << 32) | bitmask of
     the group's raw tiles (base 255), from tile bases uint8 [E, tiles] (a
@@ -494,12 +567,17 @@ class PackedHostBanks:
     bf16_expert_codec (edge35b/bf16_expert_codec.py), with the device
     descriptor table [2][E][3] that moe_layer_forward decodes from:
     (packed row, base, escapes), or (raw row, -1, 0) for a row that does not
-    pack.  gate_up [E, 2I, H] and down [E, H, I] are uint16 BF16 bit arrays."""
+    pack.  gate_up [E, 2I, H] and down [E, H, I] are uint16 BF16 bit arrays.
+    encoder "device" packs each bank with the device encoders
+    (moe_rowcodec_plan / moe_rowcodec_pack) and "host" with the numpy
+    encoder; both give the same bytes."""
 
-    def __init__(self, gate_up, down, device):
+    def __init__(self, gate_up, down, device, encoder: str = "device"):
         import numpy as np
 
         from lightreason_b200 import bf16_expert_codec as codec
+
+        _require(encoder in ("device", "host"), f"unknown encoder {encoder!r}")
 
         self.experts, two_i, self.hidden = gate_up.shape
         self.inner = two_i // 2
@@ -508,14 +586,19 @@ class PackedHostBanks:
         self.buffers = []
         self.packed_bytes = []
         for b, bank in enumerate((gate_up, down)):
-            packed, rows = codec.pack_bank(bank)
+            if encoder == "device":
+                packed, rows = rowcodec_pack(torch.from_numpy(np.ascontiguousarray(bank).view(np.int16)).to(device))
+            else:
+                packed, rows = codec.pack_bank(bank)
+                packed = torch.from_numpy(packed)
             row_bytes = bank[0].nbytes
             raw_rows = [e for e, r in enumerate(rows) if r is None]
-            tail = (packed.size + 15) & ~15
+            tail = (packed.numel() + 15) & ~15
             total = tail + len(raw_rows) * row_bytes
             host = torch.empty(max(total, 16), dtype=torch.uint8).pin_memory()
+            host[:packed.numel()].copy_(packed)
+            del packed
             host_np = host.numpy()
-            host_np[:packed.size] = packed
             base_ptr = host.data_ptr()
             for e, r in enumerate(rows):
                 if r is not None:

@@ -80,6 +80,28 @@ def test_patched_experts_every_residency(dev, model, tokens):
         assert_close(outs["b200"][layer], oracle_experts(w, x, idx, wts), what=f"patched layer {layer}")
 
 
+def test_capacity_bytes_caches_experts(dev, model):
+    """ExpertPool(capacity_bytes=...) on the host residencies: a device expert
+    cache per layer; repeated calls hit it and stay bit-identical to HBM."""
+    net, _ = model
+    want = {}
+    pool = expert_stream.ExpertPool(dev)
+    with torch.no_grad(), expert_stream.patch_experts(net, mode="b200", pool=pool):
+        for seed in (800, 801, 800):
+            want[seed] = bits(net.layers[0].experts(*routes(3, seed, dev)[3]))
+    pool.clear()
+    for mode in ("cached", "b200-packed"):
+        pool = expert_stream.ExpertPool(dev, capacity_bytes=24 * 6291456)   # 24 of the 32 experts
+        with torch.no_grad(), expert_stream.patch_experts(net, mode=mode, pool=pool):
+            for seed in (800, 801, 800):
+                got = bits(net.layers[0].experts(*routes(3, seed, dev)[3]))
+                assert np.array_equal(got, want[seed]), (mode, seed)
+        layer = next(v for k, v in pool._layers.items() if k[2])
+        st = layer.cache_stats()
+        assert st["calls"] == 3 and st["misses"] < st["uses"], st
+        pool.clear()
+
+
 def test_per_path_entry_points_are_the_patched_forward(dev, model):
     net, _ = model
     pool = expert_stream.ExpertPool(dev)
