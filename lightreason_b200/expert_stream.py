@@ -87,6 +87,7 @@ class ExpertPool:
         self._non_blocking = non_blocking
         self._owner = None
         self._attached = False
+        self._cache_layers = 1   # layers sharing capacity_bytes, set when a patch is installed
         self._layers = {}
         self.stats = TransferStats()
 
@@ -113,10 +114,14 @@ class ExpertPool:
 
     def cache_slots(self, layer: "_Layer", routed: int) -> int:
         """Expert-cache slots for a host-resident layer (0: none), if a call
-        routing to `routed` distinct experts at most fits in them."""
+        routing to `routed` distinct experts at most fits in them.  The
+        reference keeps one LRU of device rows under capacity_bytes for all
+        layers (expert_stream.py:147-174); here each patched layer gets an even
+        share of the budget as its own device-planned slot bank."""
         if layer.residency == "b200" or not self._capacity_bytes:
             return 0
-        slots = min(self._capacity_bytes // layer.row_bytes, layer.module.num_experts, 1024)
+        share = self._capacity_bytes // max(1, self._cache_layers)
+        slots = min(share // layer.row_bytes, layer.module.num_experts, 1024)
         return slots if slots >= routed else 0
 
     def _native_layer(self, layer: "_Layer", top_k: int, owner=None, extra=None, cache: int = 0) -> native.Layer:
@@ -252,6 +257,7 @@ def patch_experts(model, *, mode, pool):
         if len(layouts) != 1:
             raise ValueError("Host-resident expert layers must share one gate/down layout")
     pool._attached = True
+    pool._cache_layers = len(layers)
     installed = []
     try:
         for layer in layers:

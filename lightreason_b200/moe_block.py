@@ -77,6 +77,7 @@ def patch_moe_blocks(model, *, mode="b200", pool):
         raise ValueError("No Transformers Qwen3_5MoeSparseMoeBlock modules found")
     pool._check_context()
     pool._attached = True
+    pool._cache_layers = len(blocks)
     installed = []
     try:
         for b in blocks:

@@ -91,12 +91,14 @@ def test_capacity_bytes_caches_experts(dev, model):
             want[seed] = bits(net.layers[0].experts(*routes(3, seed, dev)[3]))
     pool.clear()
     for mode in ("cached", "b200-packed"):
-        pool = expert_stream.ExpertPool(dev, capacity_bytes=24 * 6291456)   # 24 of the 32 experts
+        # 24 of the 32 experts per layer: the budget is shared by the 2 layers
+        pool = expert_stream.ExpertPool(dev, capacity_bytes=2 * 24 * 6291456)
         with torch.no_grad(), expert_stream.patch_experts(net, mode=mode, pool=pool):
             for seed in (800, 801, 800):
                 got = bits(net.layers[0].experts(*routes(3, seed, dev)[3]))
                 assert np.array_equal(got, want[seed]), (mode, seed)
         layer = next(v for k, v in pool._layers.items() if k[2])
+        assert layer.cache_slots == 24
         st = layer.cache_stats()
         assert st["calls"] == 3 and st["misses"] < st["uses"], st
         pool.clear()
