@@ -110,7 +110,10 @@ __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__re
 }
 
 // Decode widths: every (row, K quarter) pair is one warp over all tokens, so
-// ~130 CTAs share the 1 MiB router read.  FP32 partials go to
+// ~130 CTAs share the 1 MiB router read.  Each CTA stages its K quarter of up
+// to 16 token rows in shared memory with all loads in flight at once (one L2
+// round trip instead of one per token), the warps' router rows having been
+// requested before the wait on the previous kernel.  FP32 partials go to
 // part[ks][t][row] (row E = shared-expert gate); the routing kernel sums the
 // quarters in a fixed order.
 template <int NW>
@@ -119,39 +122,55 @@ __global__ void __launch_bounds__(256) router_split_kernel(const uint16_t *__res
                                                            const uint16_t *__restrict__ gate_w, int tokens,
                                                            int experts, float *__restrict__ part) {
     constexpr int H = NW * 256 * kRouterSplit;
+    constexpr int kUnits = NW * 32;                 // 16-byte units of one token's K quarter
+    constexpr int kTB = 16;                         // tokens staged per round
+    constexpr int kPer = kTB * kUnits / 256;        // staging loads per thread
+    __shared__ uint4 xs[kTB][kUnits];
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int ks = blockIdx.y;
     const int rows = experts + (gate_w != nullptr);
+    const bool active = row < rows;
     grid_dependency_trigger();
-    if (row >= rows) {
-        grid_dependency_wait();
-        return;
-    }
-    const uint16_t *wrow = (row < experts ? router + static_cast<size_t>(row) * H : gate_w) + ks * (H / kRouterSplit);
     uint4 w[NW];
+    if (active) {
+        const uint16_t *wrow =
+            (row < experts ? router + static_cast<size_t>(row) * H : gate_w) + ks * (H / kRouterSplit);
 #pragma unroll
-    for (int i = 0; i < NW; ++i) w[i] = ld_stream(wrow + (lane + 32 * i) * 8);
+        for (int i = 0; i < NW; ++i) w[i] = ld_stream(wrow + (lane + 32 * i) * 8);
+    }
     grid_dependency_wait();  // x may come from the previous kernel
-    for (int t0 = 0; t0 < tokens; t0 += 8) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int t0 = 0; t0 < tokens; t0 += kTB) {
+        const int nt = min(kTB, tokens - t0);
+        uint4 v[kPer];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            if (t0 + j < tokens) {
-                const uint16_t *xr = x + static_cast<size_t>(t0 + j) * H + ks * (H / kRouterSplit);
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * 256, t = min(i / kUnits, nt - 1);
+            v[u] = ld_cached(x + static_cast<size_t>(t0 + t) * H + ks * (H / kRouterSplit) + (i % kUnits) * 8);
+        }
 #pragma unroll
-                for (int i = 0; i < NW; ++i) acc[j] = dot8(w[i], ld_cached(xr + (lane + 32 * i) * 8), acc[j]);
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * 256;
+            xs[i / kUnits][i % kUnits] = v[u];
+        }
+        __syncthreads();
+        if (active) {
+            float acc[kTB];
+#pragma unroll
+            for (int j = 0; j < kTB; ++j) {
+                acc[j] = 0.f;
+#pragma unroll
+                for (int i = 0; i < NW; ++i) acc[j] = dot8(w[i], xs[j][lane + 32 * i], acc[j]);
             }
-        }
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = warp_sum(acc[j]);
-        if (lane < 8 && t0 + lane < tokens) {
-            float v = acc[0];
+            for (int j = 0; j < kTB; ++j) acc[j] = warp_sum(acc[j]);
+            float out = acc[0];
 #pragma unroll
-            for (int j = 1; j < 8; ++j)
-                if (lane == j) v = acc[j];
-            part[(static_cast<size_t>(ks) * tokens + t0 + lane) * (experts + 1) + row] = v;
+            for (int j = 1; j < kTB; ++j)
+                if (lane == j) out = acc[j];
+            if (lane < nt) part[(static_cast<size_t>(ks) * tokens + t0 + lane) * (experts + 1) + row] = out;
         }
+        __syncthreads();
     }
 }
 
@@ -161,7 +180,7 @@ __global__ void __launch_bounds__(256) router_split_kernel(const uint16_t *__res
 template <int VPL>
 __global__ void __launch_bounds__(1024) route_decode_kernel(DecodeRouteArgs r, PlanArgs plan) {
     extern __shared__ float dyn[];
-    __shared__ int scratch[33];
+    __shared__ int scratch[100];
     const int T = r.tokens, E = r.experts, K = r.top_k;
     float *z = dyn;                                                   // [T][E]
     int32_t *sidx = reinterpret_cast<int32_t *>(z + T * E);           // [T][K]
@@ -170,34 +189,47 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(DecodeRouteArgs r, P
     grid_dependency_trigger();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (!r.route_in) {
-        const int cols = E + 1, n = T * cols;
-        // four elements per thread per round, all their partial loads in flight
-        constexpr int kU = 4;
-        for (int i0 = threadIdx.x; i0 < n; i0 += kU * blockDim.x) {
-            float s[kU];
+        // Thread (g, e): column e < E of tokens g, g + G, ...; four tokens per
+        // round with all their partial loads in flight (no division: the
+        // column width CW is a power of two).  Threads t < T also sum the
+        // shared-expert gate column E of token t.
+        constexpr int CW = 32 * VPL;
+        const int cols = E + 1, G = blockDim.x / CW;
+        const int e = threadIdx.x % CW, g = threadIdx.x / CW;
+        const bool gate_thread = r.has_gate && static_cast<int>(threadIdx.x) < T;
+        float gp[kRouterSplit];
+        if (gate_thread) {
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int i = i0 + u * blockDim.x;
-                s[u] = 0.f;
-                if (i < n) {
-                    const int t = i / cols, e = i % cols;
+            for (int k = 0; k < kRouterSplit; ++k) gp[k] = r.part[(static_cast<size_t>(k) * T + threadIdx.x) * cols + E];
+        }
+        if (e < E) {
+            const float be = r.bias ? r.bias[e] : 0.0f;
+            for (int t0 = g; t0 < T; t0 += 4 * G) {
+                float p[4][kRouterSplit];
 #pragma unroll
-                    for (int k = 0; k < kRouterSplit; ++k) s[u] += r.part[(static_cast<size_t>(k) * T + t) * cols + e];
+                for (int u = 0; u < 4; ++u) {
+                    const int t = min(t0 + u * G, T - 1);
+#pragma unroll
+                    for (int k = 0; k < kRouterSplit; ++k) p[u][k] = r.part[(static_cast<size_t>(k) * T + t) * cols + e];
                 }
-            }
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const int i = i0 + u * blockDim.x;
-                if (i >= n) break;
-                const int t = i / cols, e = i % cols;
-                const uint16_t lg = f2bf(s[u]);
-                if (e < E) {
+                for (int u = 0; u < 4; ++u) {
+                    const int t = t0 + u * G;
+                    if (t >= T) break;
+                    float sum = 0.f;
+#pragma unroll
+                    for (int k = 0; k < kRouterSplit; ++k) sum += p[u][k];
+                    const uint16_t lg = f2bf(sum);
                     r.logits[static_cast<size_t>(t) * E + e] = lg;
-                    z[t * E + e] = bf2f(lg) + (r.bias ? r.bias[e] : 0.0f);
-                } else if (r.has_gate) {
-                    r.sig[t] = f2bf(sigmoid_f32(bf2f(lg)));
+                    z[t * E + e] = bf2f(lg) + be;
                 }
             }
+        }
+        if (gate_thread) {
+            float sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < kRouterSplit; ++k) sum += gp[k];
+            r.sig[threadIdx.x] = f2bf(sigmoid_f32(bf2f(f2bf(sum))));
         }
         __syncthreads();
         for (int t = warp; t < T; t += blockDim.x >> 5) {
@@ -215,9 +247,8 @@ __global__ void __launch_bounds__(1024) route_decode_kernel(DecodeRouteArgs r, P
         for (int i = threadIdx.x; i < T * K; i += blockDim.x) sidx[i] = static_cast<int32_t>(r.route_in[i]);
     }
     __syncthreads();
-    permute_block([&](int t, int k) -> int64_t { return sidx[t * K + k]; }, T, K, E, r.offsets, r.perm_token,
-                  r.perm_slot, r.route_pos, r.active, r.num_active, r.bad_routes, cnt, scratch);
-    plan_block(plan, scratch);
+    route_plan_block([&](int t, int k) -> int64_t { return sidx[t * K + k]; }, T, K, E, r.offsets, r.perm_token,
+                     r.perm_slot, r.route_pos, r.active, r.num_active, r.bad_routes, plan, cnt, scratch);
 }
 
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens,

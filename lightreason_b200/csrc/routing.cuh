@@ -39,6 +39,61 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int *scratch, int *to
     return r;
 }
 
+// Exclusive scan of three ints per thread over the CTA in one pass (the three
+// shuffle chains interleave, so it costs about one scan).  `scratch` holds
+// >= 99 ints of shared memory; *total receives the CTA-wide sums.
+__device__ __forceinline__ int3 block_exclusive_scan3(int3 v, int *scratch, int3 *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = (blockDim.x + 31) >> 5;
+    int a = v.x, b = v.y, c = v.z;
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+        const int oa = __shfl_up_sync(0xffffffffu, a, s);
+        const int ob = __shfl_up_sync(0xffffffffu, b, s);
+        const int oc = __shfl_up_sync(0xffffffffu, c, s);
+        if (lane >= s) {
+            a += oa;
+            b += ob;
+            c += oc;
+        }
+    }
+    __syncthreads();
+    if (lane == 31) {
+        scratch[warp] = a;
+        scratch[33 + warp] = b;
+        scratch[66 + warp] = c;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int wa = lane < warps ? scratch[lane] : 0, wb = lane < warps ? scratch[33 + lane] : 0,
+                  wc = lane < warps ? scratch[66 + lane] : 0;
+        int ia = wa, ib = wb, ic = wc;
+#pragma unroll
+        for (int s = 1; s < 32; s <<= 1) {
+            const int oa = __shfl_up_sync(0xffffffffu, ia, s);
+            const int ob = __shfl_up_sync(0xffffffffu, ib, s);
+            const int oc = __shfl_up_sync(0xffffffffu, ic, s);
+            if (lane >= s) {
+                ia += oa;
+                ib += ob;
+                ic += oc;
+            }
+        }
+        scratch[lane] = ia - wa;
+        scratch[33 + lane] = ib - wb;
+        scratch[66 + lane] = ic - wc;
+        if (lane == 31) {
+            scratch[32] = ia;
+            scratch[65] = ib;
+            scratch[98] = ic;
+        }
+    }
+    __syncthreads();
+    const int3 r = make_int3(scratch[warp] + a - v.x, scratch[33 + warp] + b - v.y, scratch[66 + warp] + c - v.z);
+    *total = make_int3(scratch[32], scratch[65], scratch[98]);
+    __syncthreads();
+    return r;
+}
+
 // The whole permute, executed by every thread of one CTA (blockDim.x is a
 // multiple of 32, >= experts).  idx_of(t, k) yields the expert id of (token,
 // slot).  cnt: shared [warps * experts + experts] ints; scratch: 33 ints.
@@ -139,18 +194,32 @@ struct GlobalIdx {
 // experts (<= 32 * VPL); softmax over z; selection by z descending with exact
 // ties to the lower expert id; w_k = p_k / sum_k p_k in slot order.  Lane k <
 // top_k returns slot k's expert in *e_out and its weight in *w_out.
+// Order-preserving unsigned key of a float (larger float, larger key), with
+// -0 ranked as +0 so that the two compare equal as floats do.
+__device__ __forceinline__ uint32_t topk_key(float f) {
+    uint32_t b = __float_as_uint(f);
+    if (b == 0x80000000u) b = 0;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float topk_value(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <int VPL, class ZOf>
 __device__ __forceinline__ void warp_topk(ZOf z_of, int experts, int top_k, int *e_out, float *w_out) {
     const int lane = threadIdx.x & 31;
     float z[VPL];
+    uint32_t key[VPL];
     float m = -INFINITY;
 #pragma unroll
     for (int v = 0; v < VPL; ++v) {
         const int e = lane + 32 * v;
         z[v] = -INFINITY;
+        key[v] = 0;
         if (e < experts) {
             z[v] = z_of(e);
             m = fmaxf(m, z[v]);
+            key[v] = topk_key(z[v]);
         }
     }
 #pragma unroll
@@ -160,35 +229,31 @@ __device__ __forceinline__ void warp_topk(ZOf z_of, int experts, int top_k, int 
     for (int v = 0; v < VPL; ++v)
         if (lane + 32 * v < experts) denom += expf(z[v] - m);
     denom = warp_sum(denom);
-    uint32_t taken = 0;
-    float my_p = 0.0f;
+    // Selection rounds: each lane's best untaken key (its lowest expert on a
+    // tie), the warp's largest key by one redux, and the lowest expert holding
+    // it by a second.
+    uint32_t taken = 0, my_key = 0;
     int my_e = 0;
     for (int k = 0; k < top_k; ++k) {
-        float bz = -INFINITY;
+        uint32_t bk = 0;
         int be = 0x7fffffff;
 #pragma unroll
         for (int v = 0; v < VPL; ++v) {
-            const int e = lane + 32 * v;
-            if (e < experts && !(taken & (1u << v)) && (z[v] > bz || be == 0x7fffffff)) {
-                bz = z[v];
-                be = e;
+            if (!(taken & (1u << v)) && key[v] > bk) {
+                bk = key[v];
+                be = lane + 32 * v;
             }
         }
-#pragma unroll
-        for (int s = 16; s; s >>= 1) {
-            const float oz = __shfl_xor_sync(0xffffffffu, bz, s);
-            const int oe = __shfl_xor_sync(0xffffffffu, be, s);
-            if (oz > bz || (oz == bz && oe < be)) {
-                bz = oz;
-                be = oe;
-            }
-        }
-        if ((be & 31) == lane) taken |= 1u << (be >> 5);
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+        const int we = __reduce_min_sync(0xffffffffu, bk == wk ? be : 0x7fffffff);
+        if ((we & 31) == lane) taken |= 1u << (we >> 5);
         if (lane == k) {
-            my_p = expf(bz - m) / denom;
-            my_e = be;
+            my_key = wk;
+            my_e = we;
         }
     }
+    // slot probabilities, every lane at once (lanes >= top_k unused)
+    const float my_p = lane < top_k ? expf(topk_value(my_key) - m) / denom : 0.0f;
     float sum = 0.0f;
     for (int k = 0; k < top_k; ++k) sum += __shfl_sync(0xffffffffu, my_p, k);
     *e_out = my_e;
