@@ -39,6 +39,8 @@
 #include <algorithm>
 #include <mutex>
 
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "plan.cuh"
@@ -91,6 +93,9 @@ struct GroupedParams {
     const int32_t *route_token;      // [rows] route -> token
     uint16_t *rows_out;              // [T, H] per-token y rows instead of y (top_k 1), or null
     const int32_t *stage_error;      // host-staging error word, or null
+    const uint16_t *x;               // gather_x: token rows [T, H]
+    uint16_t *xs;                    // gather_x: route-ordered rows the kernel fills
+    int gather_x, gather_need;       // gather in the kernel; epilogue warps that must publish it
     int tokens, top_k, hidden, inner, ks;
 };
 
@@ -171,6 +176,116 @@ __device__ __forceinline__ ItemPos decode_item(const GroupedParams &P, const Pla
     return r;
 }
 
+// The ordered combine of 8 columns [c, c + 8) of token t (phase 3): the sum
+// over the token's routes in ascending route position of bf16(y[pos] * w),
+// rounded to BF16 after every add, then + bf16(sig[t] * shared row).  KMAX >=
+// top_k fixes every index at compile time, so the routes live in registers
+// and every load of a stage is in flight at once.  The route positions and
+// weights are read before waiting for `done` to reach `need` (lane 0 polls,
+// bounded).  Out of line on purpose: the epilogue warps run it once at kernel
+// start on token 0 with store = false, so its code is cached when the real
+// combine runs after the weight stream.  Returns false when the wait gave up.
+template <int KMAX>
+__device__ __noinline__ bool combine_cols(const int32_t *__restrict__ route_pos, const uint16_t *__restrict__ scores,
+                                          const uint16_t *y, const uint16_t *__restrict__ sig, uint16_t *out,
+                                          int hidden, int top_k, int shared_row, int t, int c, const int32_t *done,
+                                          int need, volatile int *abort, bool store) {
+    const int lane = threadIdx.x & 31;
+    int pos[KMAX];
+    uint16_t wb[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        pos[k] = INT_MAX;  // past top_k: sorts last, never summed
+        wb[k] = 0;
+        if (k < top_k) {
+            const size_t o = static_cast<size_t>(t) * top_k + k;
+            pos[k] = route_pos[o];
+            wb[k] = scores[o];
+        }
+    }
+    bool ok = true;
+    if (lane == 0) ok = wait_count(done, need, abort);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) return false;
+    __threadfence();
+    // ascending route position (insertion sort without early exit: a pair
+    // already in order is never swapped)
+#pragma unroll
+    for (int a = 1; a < KMAX; ++a) {
+#pragma unroll
+        for (int b = a; b > 0; --b) {
+            if (pos[b] < pos[b - 1]) {
+                const int tp = pos[b];
+                pos[b] = pos[b - 1];
+                pos[b - 1] = tp;
+                const uint16_t tw = wb[b];
+                wb[b] = wb[b - 1];
+                wb[b - 1] = tw;
+            }
+        }
+    }
+    uint4 shv = make_uint4(0, 0, 0, 0);
+    if (sig) shv = __ldcg(reinterpret_cast<const uint4 *>(y + static_cast<size_t>(shared_row) * hidden + c));
+    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k0 = 0; k0 < KMAX; k0 += 8) {
+        if (k0 >= top_k) break;
+        uint4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int k = k0 + j;
+            v[j] = make_uint4(0, 0, 0, 0);
+            if (pos[k] >= 0 && pos[k] != INT_MAX)
+                v[j] = __ldcg(reinterpret_cast<const uint4 *>(y + static_cast<size_t>(pos[k]) * hidden + c));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int k = k0 + j;
+            if (pos[k] < 0 || pos[k] == INT_MAX) continue;
+            const float w = bf2f(wb[k]);
+            const uint32_t vw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                o8[2 * h] = rbf(o8[2 * h] + rbf(bf16_lo(vw[h]) * w));
+                o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(bf16_hi(vw[h]) * w));
+            }
+        }
+    }
+    if (sig) {
+        const float sg = bf2f(sig[t]);
+        const uint32_t vw[4] = {shv.x, shv.y, shv.z, shv.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            o8[2 * h] = rbf(o8[2 * h] + rbf(sg * bf16_lo(vw[h])));
+            o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(sg * bf16_hi(vw[h])));
+        }
+    }
+    if (store) {
+        uint4 o;
+        o.x = pack_bf16x2(o8[0], o8[1]);
+        o.y = pack_bf16x2(o8[2], o8[3]);
+        o.z = pack_bf16x2(o8[4], o8[5]);
+        o.w = pack_bf16x2(o8[6], o8[7]);
+        *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
+    }
+    return true;
+}
+
+// combine_cols at the smallest KMAX that holds top_k (<= 32).
+__device__ __forceinline__ bool combine_cols_k(const int32_t *route_pos, const uint16_t *scores, const uint16_t *y,
+                                               const uint16_t *sig, uint16_t *out, int hidden, int top_k,
+                                               int shared_row, int t, int c, const int32_t *done, int need,
+                                               volatile int *abort, bool store) {
+    if (top_k <= 8)
+        return combine_cols<8>(route_pos, scores, y, sig, out, hidden, top_k, shared_row, t, c, done, need, abort,
+                               store);
+    if (top_k <= 16)
+        return combine_cols<16>(route_pos, scores, y, sig, out, hidden, top_k, shared_row, t, c, done, need, abort,
+                                store);
+    return combine_cols<32>(route_pos, scores, y, sig, out, hidden, top_k, shared_row, t, c, done, need, abort,
+                            store);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     swiglu_grouped_kernel(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dn,
@@ -248,6 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------ TMA producer
         if (lane == 0) {
+            // weights are read once per step: evict them first, so the
+            // activations, plan and code stay in L2 under the stream
+            const uint64_t wpol = sm100::l2_evict_first_policy();
+            bool xs_seen = false;  // the in-kernel gather was observed complete
             uint32_t stage = 0, sphase = 0;
             uint32_t issued_parity[8];
             bool issued[8] = {false, false, false, false, false, false, false, false};
@@ -281,18 +400,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int r = 0; r < n16; r += 16) sm100::tma_load_2d(dst + r * kBK * 2, map16, bar, k0, tok0 + r);
                     }
                 };
-                // Phase 2 streams its down-weight tiles right away and issues the
-                // activation tiles only once the group's phase 1 has published
-                // them (every phase-1 tile once per epilogue warp).
-                bool dep_ok = ip.phase == 1;
-                const int need = 4 * mb1 * G.ntiles;
+                // Weight tiles stream right away; activation tiles wait for their
+                // producers: phase 2 for the group's phase 1 (every phase-1 tile
+                // once per epilogue warp), phase 1 for the in-kernel gather.
+                const bool p1 = ip.phase == 1;
+                bool dep_ok = p1 ? (xs_seen || !P.gather_x) : false;
+                const int32_t *dep_ctr = p1 ? &P.plan->xs_ready : &P.done1[ip.g];
+                const int need = p1 ? P.gather_need : 4 * mb1 * G.ntiles;
+                const CUtensorMap *bmap = p1 ? &tm_x : &tm_act, *bmap16 = p1 ? &tm_x16 : &tm_act16;
                 int pending[8];
                 int n_pending = 0;
                 bool ok = true;
                 for (int kb = kb0; kb < kb0 + kspan; ++kb) {
                     if (!dep_ok && n_pending > 0 && !sm100::mbar_try_wait(&tail->empty[stage], sphase ^ 1)) {
                         // out of free stages: the earlier stages need their activation tiles
-                        if (!wait_count(&P.done1[ip.g], need, abort)) {
+                        if (!wait_count(dep_ctr, need, abort)) {
                             *abort = 1;
                             atomicExch(&P.plan->error, 2);
                             ok = false;
@@ -302,7 +424,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         dep_ok = true;
                         for (int j = 0; j < n_pending; ++j) {
                             const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                            load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps], pk * kBK);
+                            load_b(bmap, bmap16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps], pk * kBK);
                         }
                         n_pending = 0;
                     }
@@ -316,34 +438,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int k0 = kb * kBK;
                     if (ip.phase == 1) {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d(st, &tm_gu, fb, k0, row0, G.weight);
-                            sm100::tma_load_3d(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight);
+                            sm100::tma_load_3d_hint(st, &tm_gu, fb, k0, row0, G.weight, wpol);
+                            sm100::tma_load_3d_hint(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight, wpol);
                         } else {
-                            sm100::tma_load_2d(st, &tm_sg, fb, k0, row0);
-                            sm100::tma_load_2d(st + kATile, &tm_su, fb, k0, row0);
+                            sm100::tma_load_2d_hint(st, &tm_sg, fb, k0, row0, wpol);
+                            sm100::tma_load_2d_hint(st + kATile, &tm_su, fb, k0, row0, wpol);
                         }
-                        load_b(&tm_x, &tm_x16, st + 2 * kATile, fb, k0);
                     } else {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d(st, &tm_dn, fb, k0, row0, G.weight);
-                            sm100::tma_load_3d(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight);
+                            sm100::tma_load_3d_hint(st, &tm_dn, fb, k0, row0, G.weight, wpol);
+                            sm100::tma_load_3d_hint(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight, wpol);
                         } else {
-                            sm100::tma_load_2d(st, &tm_sd, fb, k0, row0);
-                            sm100::tma_load_2d(st + kATile, &tm_sd, fb, k0, row0 + kBM);
+                            sm100::tma_load_2d_hint(st, &tm_sd, fb, k0, row0, wpol);
+                            sm100::tma_load_2d_hint(st + kATile, &tm_sd, fb, k0, row0 + kBM, wpol);
                         }
-                        if (!dep_ok && sm100::ld_acquire(&P.done1[ip.g]) >= need) {
-                            sm100::fence_proxy_async_global();
-                            dep_ok = true;
-                            for (int j = 0; j < n_pending; ++j) {
-                                const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                                load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps],
-                                       pk * kBK);
-                            }
-                            n_pending = 0;
-                        }
-                        if (dep_ok) load_b(&tm_act, &tm_act16, st + 2 * kATile, fb, k0);
-                        else pending[n_pending++] = stage | (kb << 8);
                     }
+                    if (!dep_ok && sm100::ld_acquire(dep_ctr) >= need) {
+                        sm100::fence_proxy_async_global();
+                        dep_ok = true;
+                        for (int j = 0; j < n_pending; ++j) {
+                            const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
+                            load_b(bmap, bmap16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps], pk * kBK);
+                        }
+                        n_pending = 0;
+                    }
+                    if (dep_ok) load_b(bmap, bmap16, st + 2 * kATile, fb, k0);
+                    else pending[n_pending++] = stage | (kb << 8);
                     issued[stage] = true;
                     issued_parity[stage] = sphase;
                     if (++stage == S::kStages) {
@@ -352,20 +472,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (ok && n_pending > 0) {
-                    if (!wait_count(&P.done1[ip.g], need, abort)) {
+                    if (!wait_count(dep_ctr, need, abort)) {
                         *abort = 1;
                         atomicExch(&P.plan->error, 2);
                         ok = false;
                     } else {
                         sm100::fence_proxy_async_global();
+                        dep_ok = true;
                         for (int j = 0; j < n_pending; ++j) {
                             const int ps = pending[j] & 0xff, pk = pending[j] >> 8;
-                            load_b(&tm_act, &tm_act16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps],
-                                   pk * kBK);
+                            load_b(bmap, bmap16, smem + ps * S::kStage + 2 * kATile, &tail->full[ps], pk * kBK);
                         }
                         n_pending = 0;
                     }
                 }
+                if (p1 && dep_ok) xs_seen = true;
                 if (!ok) break;
             }
             if (*abort) {
@@ -381,6 +502,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // --------------------------------------------------------- MMA issuer
         if (lane == 0) {
+            // weights are read once per step: evict them first, so the
+            // activations, plan and code stay in L2 under the stream
+            const uint64_t wpol = sm100::l2_evict_first_policy();
+            bool xs_seen = false;  // the in-kernel gather was observed complete
             uint32_t stage = 0, sphase = 0;
             int acc = 0;
             bool any = false;
@@ -441,6 +566,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int et = threadIdx.x - 64;  // 0..127
         int acc = 0;
+        if (P.gather_x) {
+            // The token gather of the routed and shared rows (xs[p] = x[token
+            // of route p]), spread over every CTA's epilogue warps while the
+            // producers start the weight stream; phase-1 activation loads wait
+            // for all of them to publish.
+            const int shared = V.groups[n_groups - 1].weight < 0 ? 1 : 0;
+            const int nr = n_groups - shared;
+            const int placed = nr > 0 ? V.groups[nr - 1].begin + V.groups[nr - 1].count : 0;
+            const int routes = P.tokens * P.top_k, units = P.hidden / 8;
+            const int64_t total_units = static_cast<int64_t>(placed + (shared ? P.tokens : 0)) * units;
+            for (int64_t i = static_cast<int64_t>(blockIdx.x) * 128 + et; i < total_units;
+                 i += static_cast<int64_t>(gridDim.x) * 128) {
+                const int qr = static_cast<int>(i / units), cu = static_cast<int>(i % units);
+                const int p = qr < placed ? qr : routes + (qr - placed);
+                const int tk = p < routes ? P.route_token[p] : p - routes;
+                reinterpret_cast<uint4 *>(P.xs)[static_cast<int64_t>(p) * units + cu] =
+                    ld_cached(P.x + static_cast<size_t>(tk) * P.hidden + cu * 8);
+            }
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                sm100::fence_proxy_async_global();
+                atomicAdd(&P.plan->xs_ready, 1);
+            }
+        }
+        if (P.plan->items3 > 0)  // warm the combine's code: token 0, nothing stored, no wait
+            combine_cols_k(P.route_pos, P.scores, P.y, P.sig, P.out, P.hidden, P.top_k,
+                           P.sig ? V.groups[n_groups - 1].begin : 0, 0, et * 8, &P.plan->done2_total, 0, abort, false);
         for (int it = 0;; ++it) {
             const int slot = it & 3;
             if (!wait_bar(&tail->ifull[slot], (it >> 2) & 1, abort)) break;
@@ -453,78 +606,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (ip.phase == 3) {
                 const int halves = P.hidden / kCombineCols;
                 const int t = ip.g / halves, c = (ip.g % halves) * kCombineCols + et * 8;
-                int pos[32];
-                float wt[32];
-                bool ok = true;
-                for (int k = 0; k < P.top_k; ++k) {
-                    const size_t o = static_cast<size_t>(t) * P.top_k + k;
-                    pos[k] = P.route_pos[o];
-                    wt[k] = bf2f(P.scores[o]);
-                }
-                // Every route row and shared row exists once all phase-2 items
-                // (4 epilogue warps each) have published.
-                if (lane == 0) ok = wait_count(&P.plan->done2_total, 4 * items2, abort);
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) {
+                const int shared_row = P.sig ? V.groups[n_groups - 1].begin + t : 0;
+                // every route row and shared row exists once all phase-2 items
+                // (4 epilogue warps each) have published
+                if (!combine_cols_k(P.route_pos, P.scores, P.y, P.sig, P.out, P.hidden, P.top_k, shared_row, t, c,
+                                    &P.plan->done2_total, 4 * items2, abort, true)) {
                     *abort = 1;
                     atomicExch(&P.plan->error, 3);
                     break;
                 }
-                __threadfence();
-                for (int a = 1; a < P.top_k; ++a) {
-                    for (int b = a; b > 0 && pos[b] < pos[b - 1]; --b) {
-                        const int tp = pos[b];
-                        pos[b] = pos[b - 1];
-                        pos[b - 1] = tp;
-                        const float tw = wt[b];
-                        wt[b] = wt[b - 1];
-                        wt[b - 1] = tw;
-                    }
-                }
-                // Issue every row load first, then the ordered BF16 sums.
-                uint4 shv = make_uint4(0, 0, 0, 0);
-                if (P.sig) {
-                    const int prow = V.groups[n_groups - 1].begin + t;
-                    shv = __ldcg(reinterpret_cast<const uint4 *>(P.y + static_cast<size_t>(prow) * P.hidden + c));
-                }
-                float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                for (int k0 = 0; k0 < P.top_k; k0 += 8) {
-                    uint4 v[8];
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int k = k0 + j;
-                        v[j] = make_uint4(0, 0, 0, 0);
-                        if (k < P.top_k && pos[k] >= 0)
-                            v[j] = __ldcg(
-                                reinterpret_cast<const uint4 *>(P.y + static_cast<size_t>(pos[k]) * P.hidden + c));
-                    }
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int k = k0 + j;
-                        if (k >= P.top_k || pos[k] < 0) continue;
-                        const uint32_t vw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            o8[2 * h] = rbf(o8[2 * h] + rbf(bf16_lo(vw[h]) * wt[k]));
-                            o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(bf16_hi(vw[h]) * wt[k]));
-                        }
-                    }
-                }
-                if (P.sig) {
-                    const float sg = bf2f(P.sig[t]);
-                    const uint32_t vw[4] = {shv.x, shv.y, shv.z, shv.w};
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        o8[2 * h] = rbf(o8[2 * h] + rbf(sg * bf16_lo(vw[h])));
-                        o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(sg * bf16_hi(vw[h])));
-                    }
-                }
-                uint4 o;
-                o.x = pack_bf16x2(o8[0], o8[1]);
-                o.y = pack_bf16x2(o8[2], o8[3]);
-                o.z = pack_bf16x2(o8[4], o8[5]);
-                o.w = pack_bf16x2(o8[6], o8[7]);
-                *reinterpret_cast<uint4 *>(P.out + static_cast<size_t>(t) * P.hidden + c) = o;
                 continue;
             }
 
@@ -793,6 +883,10 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.route_token = L.route_token;
     P.rows_out = L.rows_out;
     P.stage_error = L.stage_error;
+    P.x = L.x;
+    P.xs = const_cast<uint16_t *>(L.xs);
+    P.gather_x = L.gather_x;
+    P.gather_need = 4 * L.ctas;
     P.tokens = L.tokens;
     P.top_k = L.top_k;
     P.hidden = L.hidden;

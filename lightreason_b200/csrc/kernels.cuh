@@ -47,7 +47,8 @@ struct GroupedGroup {
     int32_t ntiles;  // token tiles of width BN
 };
 struct GroupedPlan {
-    int32_t num_groups, items1, items2, items3, work, error, done2_total, pad;
+    int32_t num_groups, items1, items2, items3, work, error, done2_total;
+    int32_t xs_ready;  // epilogue warps that finished the in-kernel token gather
 };
 struct GroupedLaunch {
     const uint16_t *gate_up, *down;  // banks: [bank_experts, 2I, H], [bank_experts, H, I]
@@ -69,6 +70,8 @@ struct GroupedLaunch {
     const int32_t *route_token;  // [rows] route -> token
     uint16_t *rows_out;            // [T, H]: write y per token (top_k 1, no shared), or null
     const int32_t *stage_error;    // nonzero: the host staging gave up; folded into plan->error
+    const uint16_t *x;             // gather_x: tokens [T, H], gathered into xs by the kernel itself
+    int gather_x;
     int tokens, top_k, hidden, inner, bn, ks, ctas;
 };
 struct PlanArgs;

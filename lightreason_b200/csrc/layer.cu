@@ -401,7 +401,10 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     }
     if (int rc = mark(3)) return rc;
     uint16_t *xs = at<uint16_t>(ws, L.xs), *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
-    if (int rc = launch_gather_tokens(x, route_token, offsets, E, R, shared ? tokens : 0, H, xs, s)) return rc;
+    // At decode widths the grouped kernel gathers the token rows itself (its
+    // epilogue warps are idle while the first weight tiles stream in).
+    if (!fused_combine)
+        if (int rc = launch_gather_tokens(x, route_token, offsets, E, R, shared ? tokens : 0, H, xs, s)) return rc;
     if (int rc = mark(4)) return rc;
     GroupedLaunch GL{};
     GL.gate_up = gu_base;
@@ -433,6 +436,8 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.route_token = route_token;
     GL.rows_out = rows_mode ? out : nullptr;
     GL.stage_error = counters + 2;
+    GL.x = x;
+    GL.gather_x = fused_combine ? 1 : 0;
     GL.tokens = tokens;
     GL.top_k = K;
     GL.hidden = H;
