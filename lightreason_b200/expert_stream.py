@@ -64,6 +64,8 @@ class TransferStats:
     tokens: int = 0
     resident_bytes: int = 0
     pinned_bytes: int = 0
+    replayed_layer_calls: int = 0   # calls served by a captured graph (scheduled_graph.replay_experts)
+    mixer_replays: int = 0          # mixer forwards served by a captured graph (packed_native.mixer_graphs)
 
 
 class ExpertPool:
