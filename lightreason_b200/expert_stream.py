@@ -108,6 +108,8 @@ class ExpertPool:
         self.stats.resident_bytes = self.stats.pinned_bytes = 0
 
     def _check_context(self):
+        if torch.cuda.is_current_stream_capturing():
+            return  # a CUDA-graph capture records on its own side stream; the replay runs on the caller's
         owner = (threading.get_ident(), torch.cuda.current_stream(self.device).cuda_stream)
         if self._owner is None:
             self._owner = owner
