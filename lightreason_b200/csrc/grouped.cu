@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // weights are read once per step: evict them first, so the
             // activations, plan and code stay in L2 under the stream
-            const uint64_t wpol = sm100::l2_evict_first_policy();
+            const uint64_t wpol = sm100::l2_evict_first_policy(), npol = sm100::l2_evict_normal_policy();
             bool xs_seen = false;  // the in-kernel gather was observed complete
             uint32_t stage = 0, sphase = 0;
             uint32_t issued_parity[8];
@@ -387,6 +387,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kb0 = ip.phase == 1 ? ip.ks * kspan : 0;
                 const int row0 = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM);
                 const int tok0 = G.begin + ip.nt * BN;
+                // a group of one token tile reads each weight tile once: evict it
+                // first; with several tiles the later ones re-read it from L2
+                const uint64_t ipol = G.ntiles == 1 ? wpol : npol;
                 // Token tiles are loaded (and multiplied) only as wide as their
                 // rows, rounded up to 16: a full tile in one box of BN rows, a
                 // partial one in boxes of 16.
@@ -438,19 +441,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int k0 = kb * kBK;
                     if (ip.phase == 1) {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d_hint(st, &tm_gu, fb, k0, row0, G.weight, wpol);
-                            sm100::tma_load_3d_hint(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight, wpol);
+                            sm100::tma_load_3d_hint(st, &tm_gu, fb, k0, row0, G.weight, ipol);
+                            sm100::tma_load_3d_hint(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight, ipol);
                         } else {
-                            sm100::tma_load_2d_hint(st, &tm_sg, fb, k0, row0, wpol);
-                            sm100::tma_load_2d_hint(st + kATile, &tm_su, fb, k0, row0, wpol);
+                            sm100::tma_load_2d_hint(st, &tm_sg, fb, k0, row0, ipol);
+                            sm100::tma_load_2d_hint(st + kATile, &tm_su, fb, k0, row0, ipol);
                         }
                     } else {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d_hint(st, &tm_dn, fb, k0, row0, G.weight, wpol);
-                            sm100::tma_load_3d_hint(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight, wpol);
+                            sm100::tma_load_3d_hint(st, &tm_dn, fb, k0, row0, G.weight, ipol);
+                            sm100::tma_load_3d_hint(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight, ipol);
                         } else {
-                            sm100::tma_load_2d_hint(st, &tm_sd, fb, k0, row0, wpol);
-                            sm100::tma_load_2d_hint(st + kATile, &tm_sd, fb, k0, row0 + kBM, wpol);
+                            sm100::tma_load_2d_hint(st, &tm_sd, fb, k0, row0, ipol);
+                            sm100::tma_load_2d_hint(st + kATile, &tm_sd, fb, k0, row0 + kBM, ipol);
                         }
                     }
                     if (!dep_ok && sm100::ld_acquire(dep_ctr) >= need) {
@@ -504,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             // weights are read once per step: evict them first, so the
             // activations, plan and code stay in L2 under the stream
-            const uint64_t wpol = sm100::l2_evict_first_policy();
+            const uint64_t wpol = sm100::l2_evict_first_policy(), npol = sm100::l2_evict_normal_policy();
             bool xs_seen = false;  // the in-kernel gather was observed complete
             uint32_t stage = 0, sphase = 0;
             int acc = 0;
