@@ -48,6 +48,19 @@ __device__ __forceinline__ float dot8(uint4 w, uint4 a, float acc) {
     return acc;
 }
 
+// One eager BF16 combine step on two packed values at once: acc = bf16(acc +
+// bf16(v * w)), each operation rounded to nearest even (the _rn forms are
+// never contracted into an FMA, which would drop the product's rounding).
+// The product of two BF16 values is exact in FP32, so the BF16 multiply
+// equals rbf(float(v) * float(w)); likewise the add.
+__device__ __forceinline__ uint32_t bf16x2_mul_add(uint32_t acc, uint32_t v, uint32_t w2) {
+    const __nv_bfloat162 p = __hmul2_rn(*reinterpret_cast<const __nv_bfloat162 *>(&v),
+                                        *reinterpret_cast<const __nv_bfloat162 *>(&w2));
+    const __nv_bfloat162 r = __hadd2_rn(*reinterpret_cast<const __nv_bfloat162 *>(&acc), p);
+    return *reinterpret_cast<const uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t bf16x2_splat(uint16_t w) { return static_cast<uint32_t>(w) * 0x10001u; }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int s = 16; s; s >>= 1) v += __shfl_xor_sync(0xffffffffu, v, s);

@@ -142,11 +142,11 @@ __global__ void __launch_bounds__(256, MINB) combine_kernel(const uint16_t *__re
     if (i >= static_cast<int64_t>(tokens) * chunks) return;
     const int t = static_cast<int>(i / chunks), c = static_cast<int>(i % chunks) * 8;
     int pos[KMAX];
-    float wt[KMAX];
+    uint16_t wt[KMAX];
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
         pos[k] = k < top_k ? __ldg(route_pos + static_cast<size_t>(t) * top_k + k) : -1;
-        wt[k] = k < top_k ? bf2f(__ldg(scores + static_cast<size_t>(t) * top_k + k)) : 0.f;
+        wt[k] = k < top_k ? __ldg(scores + static_cast<size_t>(t) * top_k + k) : 0;
     }
 #pragma unroll
     for (int a = 1; a < KMAX; ++a) {
@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(256, MINB) combine_kernel(const uint16_t *__re
             // -1 (no route) sorts last
             const bool swap = static_cast<unsigned>(pos[b]) < static_cast<unsigned>(pos[b - 1]);
             const int p0 = pos[b - 1], p1 = pos[b];
-            const float w0 = wt[b - 1], w1 = wt[b];
+            const uint16_t w0 = wt[b - 1], w1 = wt[b];
             pos[b - 1] = swap ? p1 : p0;
             pos[b] = swap ? p0 : p1;
             wt[b - 1] = swap ? w1 : w0;
@@ -169,31 +169,24 @@ __global__ void __launch_bounds__(256, MINB) combine_kernel(const uint16_t *__re
                            : make_uint4(0, 0, 0, 0);
     const uint4 sv = shared_y ? __ldcg(reinterpret_cast<const uint4 *>(shared_y + static_cast<size_t>(t) * hidden + c))
                               : make_uint4(0, 0, 0, 0);
-    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // packed BF16 pairs: acc = bf16(acc + bf16(v * w)) per route, ascending position
+    uint4 o = make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
         if (pos[k] < 0) continue;
-        const uint32_t vw[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            acc[2 * q] = rbf(acc[2 * q] + rbf(bf16_lo(vw[q]) * wt[k]));
-            acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(bf16_hi(vw[q]) * wt[k]));
-        }
+        const uint32_t w2 = bf16x2_splat(wt[k]);
+        o.x = bf16x2_mul_add(o.x, v[k].x, w2);
+        o.y = bf16x2_mul_add(o.y, v[k].y, w2);
+        o.z = bf16x2_mul_add(o.z, v[k].z, w2);
+        o.w = bf16x2_mul_add(o.w, v[k].w, w2);
     }
     if (shared_y) {
-        const float sg = bf2f(sig[t]);
-        const uint32_t vw[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            acc[2 * q] = rbf(acc[2 * q] + rbf(sg * bf16_lo(vw[q])));
-            acc[2 * q + 1] = rbf(acc[2 * q + 1] + rbf(sg * bf16_hi(vw[q])));
-        }
+        const uint32_t s2 = bf16x2_splat(sig[t]);
+        o.x = bf16x2_mul_add(o.x, sv.x, s2);
+        o.y = bf16x2_mul_add(o.y, sv.y, s2);
+        o.z = bf16x2_mul_add(o.z, sv.z, s2);
+        o.w = bf16x2_mul_add(o.w, sv.w, s2);
     }
-    uint4 o;
-    o.x = pack_bf16x2(acc[0], acc[1]);
-    o.y = pack_bf16x2(acc[2], acc[3]);
-    o.z = pack_bf16x2(acc[4], acc[5]);
-    o.w = pack_bf16x2(acc[6], acc[7]);
     *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
 }
 

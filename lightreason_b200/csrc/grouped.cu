@@ -226,7 +226,8 @@ __device__ __noinline__ bool combine_cols(const int32_t *__restrict__ route_pos,
     }
     uint4 shv = make_uint4(0, 0, 0, 0);
     if (sig) shv = __ldcg(reinterpret_cast<const uint4 *>(y + static_cast<size_t>(shared_row) * hidden + c));
-    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    // packed BF16 pairs: acc = bf16(acc + bf16(v * w)) per route, ascending position
+    uint4 o = make_uint4(0, 0, 0, 0);
 #pragma unroll
     for (int k0 = 0; k0 < KMAX; k0 += 8) {
         if (k0 >= top_k) break;
@@ -242,32 +243,21 @@ __device__ __noinline__ bool combine_cols(const int32_t *__restrict__ route_pos,
         for (int j = 0; j < 8; ++j) {
             const int k = k0 + j;
             if (pos[k] < 0 || pos[k] == INT_MAX) continue;
-            const float w = bf2f(wb[k]);
-            const uint32_t vw[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                o8[2 * h] = rbf(o8[2 * h] + rbf(bf16_lo(vw[h]) * w));
-                o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(bf16_hi(vw[h]) * w));
-            }
+            const uint32_t w2 = bf16x2_splat(wb[k]);
+            o.x = bf16x2_mul_add(o.x, v[j].x, w2);
+            o.y = bf16x2_mul_add(o.y, v[j].y, w2);
+            o.z = bf16x2_mul_add(o.z, v[j].z, w2);
+            o.w = bf16x2_mul_add(o.w, v[j].w, w2);
         }
     }
     if (sig) {
-        const float sg = bf2f(sig[t]);
-        const uint32_t vw[4] = {shv.x, shv.y, shv.z, shv.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            o8[2 * h] = rbf(o8[2 * h] + rbf(sg * bf16_lo(vw[h])));
-            o8[2 * h + 1] = rbf(o8[2 * h + 1] + rbf(sg * bf16_hi(vw[h])));
-        }
+        const uint32_t s2 = bf16x2_splat(sig[t]);
+        o.x = bf16x2_mul_add(o.x, shv.x, s2);
+        o.y = bf16x2_mul_add(o.y, shv.y, s2);
+        o.z = bf16x2_mul_add(o.z, shv.z, s2);
+        o.w = bf16x2_mul_add(o.w, shv.w, s2);
     }
-    if (store) {
-        uint4 o;
-        o.x = pack_bf16x2(o8[0], o8[1]);
-        o.y = pack_bf16x2(o8[2], o8[3]);
-        o.z = pack_bf16x2(o8[4], o8[5]);
-        o.w = pack_bf16x2(o8[6], o8[7]);
-        *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
-    }
+    if (store) *reinterpret_cast<uint4 *>(out + static_cast<size_t>(t) * hidden + c) = o;
     return true;
 }
 

@@ -84,8 +84,17 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t *__restrict_
     const int q = threadIdx.x / experts, e = threadIdx.x % experts;
     const bool mine = q < S;
     const int c_begin = mine ? chunks * q / S : 0, c_end = mine ? chunks * (q + 1) / S : 0;
+    // 16 loads in flight per round (a serial chain of dependent adds
+    // otherwise waits out one L2 round trip per chunk)
+    constexpr int kU = 16;
     int sum = 0;
-    for (int c = c_begin; c < c_end; ++c) sum += hist[static_cast<size_t>(c) * experts + e];
+    for (int c = c_begin; c < c_end; c += kU) {
+        int v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) v[u] = c + u < c_end ? hist[static_cast<size_t>(c + u) * experts + e] : 0;
+#pragma unroll
+        for (int u = 0; u < kU; ++u) sum += v[u];
+    }
     part[threadIdx.x] = sum;
     __syncthreads();
     int total = 0, before = 0;
@@ -113,11 +122,17 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t *__restrict_
     __syncthreads();
     if (mine) {
         int base = part[e] + before;
-        for (int c = c_begin; c < c_end; ++c) {
-            const size_t o = static_cast<size_t>(c) * experts + e;
-            const int v = hist[o];
-            hist[o] = base;
-            base += v;
+        for (int c = c_begin; c < c_end; c += kU) {
+            int v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) v[u] = c + u < c_end ? hist[static_cast<size_t>(c + u) * experts + e] : 0;
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                if (c + u < c_end) {
+                    hist[static_cast<size_t>(c + u) * experts + e] = base;
+                    base += v[u];
+                }
+            }
         }
     }
 }

@@ -4,7 +4,7 @@
 //
 // One CTA per (128 router rows, BN tokens, K split): the router rows are the
 // M = 128 operand and the token tile the N operand, both K-major with the
-// 128-byte swizzle, streamed by TMA through a 4-stage ring.  With ks > 1 K
+// 128-byte swizzle, streamed by TMA through an 8-stage ring.  With ks > 1 K
 // splits (few tokens: more CTAs than row blocks x token tiles) each CTA writes
 // FP32 partials part[split][t][e], which the selection kernel sums in split
 // order before the one BF16 rounding.  Thread 0 issues the loads
@@ -23,7 +23,7 @@ namespace lrb {
 
 namespace {
 
-constexpr int kRows = 128, kK = 64, kStagesTc = 4;
+constexpr int kRows = 128, kK = 64, kStagesTc = 8;
 constexpr uint64_t kRouterWaitNs = 2000000000ull;
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -84,8 +84,8 @@ __global__ void __launch_bounds__(128, 1)
     const int nk = hidden / kK / gridDim.z, kb_first = blockIdx.z * nk;
     if (threadIdx.x == 0) {
         constexpr uint32_t idesc = sm100::idesc_bf16_f32(kRows, BN);
-        bool issued[kStagesTc] = {false, false, false, false};
-        uint32_t issued_parity[kStagesTc] = {0, 0, 0, 0};
+        bool issued[kStagesTc] = {};
+        uint32_t issued_parity[kStagesTc] = {};
         auto load = [&](int kb) {
             const int s = kb % kStagesTc;
             uint8_t *st = smem + s * kStage;
