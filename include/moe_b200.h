@@ -104,7 +104,7 @@ int moe_permute(const int64_t *idx, int tokens, int top_k, int experts, int32_t 
                 int32_t *num_active, int32_t *bad_routes, void *stream);
 
 /* The same permute, same outputs, for many routes: above 2048 routes it runs
- * on many CTAs (per-chunk counts, one scan, placement) with a caller scratch
+ * on many CTAs (per-chunk counts, a column scan, placement) with a caller scratch
  * `hist` of moe_permute_hist_ints(tokens, top_k, experts) int32s (0: not
  * needed, and moe_permute runs). */
 int moe_permute_hist_ints(int tokens, int top_k, int experts);

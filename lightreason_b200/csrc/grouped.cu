@@ -754,6 +754,9 @@ __global__ void __launch_bounds__(1024) grouped_plan_kernel(PlanArgs a) {
 
 // xs[p] = x[route_token[p]] for the placed routes (p < offsets[experts]) and,
 // when the shared expert runs, xs[routes + t] = x[t]; 16 bytes per thread.
+// One warp per row: the row's token is read once, then the 16-byte units of
+// the row (hidden / 8, 8 per lane at hidden 2048) are all loaded before any
+// is stored.
 __global__ void __launch_bounds__(256) gather_tokens_kernel(const uint16_t *__restrict__ x,
                                                             const int32_t *__restrict__ route_token,
                                                             const int32_t *__restrict__ offsets, int experts,
@@ -761,18 +764,31 @@ __global__ void __launch_bounds__(256) gather_tokens_kernel(const uint16_t *__re
                                                             uint16_t *__restrict__ xs) {
     grid_dependency_wait();
     grid_dependency_trigger();
+    const int lane = threadIdx.x & 31;
     const int units = hidden / 8;
     const int placed = offsets[experts];
     // rows to fill: the placed routes, then the shared rows (routes past the
     // placed ones were dropped and own no row)
-    const int64_t total = static_cast<int64_t>(placed + shared_rows) * units;
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const int q = static_cast<int>(i / units), c = static_cast<int>(i % units);
+    const int rows = placed + shared_rows;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); q < rows; q += warps) {
         const int p = q < placed ? q : routes + (q - placed);
         const int t = p < routes ? route_token[p] : p - routes;
-        reinterpret_cast<uint4 *>(xs)[static_cast<int64_t>(p) * units + c] =
-            ld_cached(x + static_cast<size_t>(t) * hidden + c * 8);
+        const uint4 *src = reinterpret_cast<const uint4 *>(x + static_cast<size_t>(t) * hidden);
+        uint4 *dst = reinterpret_cast<uint4 *>(xs + static_cast<size_t>(p) * hidden);
+        for (int c0 = 0; c0 < units; c0 += 8 * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * 32 + lane;
+                if (c < units) v[u] = ld_cached(src + c);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * 32 + lane;
+                if (c < units) dst[c] = v[u];
+            }
+        }
     }
 }
 
@@ -915,8 +931,8 @@ int launch_grouped_plan(const PlanArgs &a, cudaStream_t stream) {
 
 int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const int32_t *offsets, int experts,
                          int routes, int shared_rows, int hidden, uint16_t *xs, cudaStream_t stream) {
-    const int64_t units = static_cast<int64_t>(routes + shared_rows) * (hidden / 8);
-    const int grid = static_cast<int>(std::min<int64_t>((units + 255) / 256, 148 * 16));
+    const int64_t rows = static_cast<int64_t>(routes) + shared_rows;  // a bound on the rows to fill
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 7) / 8, static_cast<int64_t>(sm_count()) * 8));
     if (grid == 0) return MOE_OK;
     return launch_pdl(gather_tokens_kernel, dim3(grid), dim3(256), 0, stream, "gather_tokens_kernel", x,
                       route_token, offsets, experts, routes, shared_rows, hidden, xs);

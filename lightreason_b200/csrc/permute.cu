@@ -35,11 +35,11 @@ __global__ void __launch_bounds__(1024) permute_kernel(const int64_t *__restrict
 
 // Wide permute: the route order r is cut into chunks of kChunk routes, one per
 // warp.  count: each warp writes its chunk's per-expert counts to hist[c][e];
-// scan (one CTA): hist[c][e] becomes the first position of chunk c's routes of
-// expert e (expert offsets + the counts of earlier chunks), plus offsets,
-// active experts and the dropped-route count; place: each warp re-walks its
-// chunk and puts every route at its chunk base plus its rank among the equal
-// experts before it.  The scattered position writes spread over many SMs.
+// column scan (a CTA per 32 experts): hist[c][e] becomes the count of expert e
+// in the earlier chunks, and the last CTA turns the column totals into the
+// expert offsets, active experts and the dropped-route count; place: each warp
+// re-walks its chunk and puts every route at offsets[e] + hist[c][e] plus its
+// rank among the equal experts before it.  The scattered position writes spread over many SMs.
 constexpr int kChunk = 128;
 constexpr int kWarpsPerCta = 8;
 
@@ -50,6 +50,7 @@ __global__ void __launch_bounds__(256) permute_count_kernel(const int64_t *__res
     grid_dependency_trigger();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x * kWarpsPerCta + warp;
+    if (c == 0 && lane == 0) hist[static_cast<size_t>(chunks) * experts + experts] = 0;  // the column scan's counter
     if (c >= chunks) return;
     int32_t *cnt = cnt_smem + warp * experts;
     for (int e = lane; e < experts; e += 32) cnt[e] = 0;
@@ -71,57 +72,47 @@ __global__ void __launch_bounds__(256) permute_count_kernel(const int64_t *__res
     for (int e = lane; e < experts; e += 32) hist[static_cast<size_t>(c) * experts + e] = cnt[e];
 }
 
-__global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t *__restrict__ hist, int chunks, int experts,
-                                                            int routes, int32_t *__restrict__ offsets,
-                                                            int32_t *__restrict__ active,
-                                                            int32_t *__restrict__ num_active,
-                                                            int32_t *__restrict__ bad_routes) {
-    __shared__ int32_t part[1024];
-    __shared__ int scratch[33];
+// Column scan: CTA b owns experts [32b, 32b + 32), one per lane, and its 32
+// warps split the chunks.  hist[c][e] becomes the count of expert e in the
+// chunks before c; the column totals go to totals[e].  The last CTA to finish
+// (a counter zeroed by the count kernel) scans the totals into the expert
+// offsets, the active experts and the dropped-route count.
+__global__ void __launch_bounds__(1024) permute_colscan_kernel(int32_t *__restrict__ hist, int chunks, int experts,
+                                                               int routes, int32_t *__restrict__ totals,
+                                                               int32_t *__restrict__ done,
+                                                               int32_t *__restrict__ offsets,
+                                                               int32_t *__restrict__ active,
+                                                               int32_t *__restrict__ num_active,
+                                                               int32_t *__restrict__ bad_routes) {
+    __shared__ int part[32][33];
+    __shared__ int scratch[100];
+    __shared__ int last;
     grid_dependency_wait();
     grid_dependency_trigger();
-    const int S = blockDim.x / experts;  // threads per expert, each over a contiguous run of chunks
-    const int q = threadIdx.x / experts, e = threadIdx.x % experts;
-    const bool mine = q < S;
-    const int c_begin = mine ? chunks * q / S : 0, c_end = mine ? chunks * (q + 1) / S : 0;
-    // 16 loads in flight per round (a serial chain of dependent adds
-    // otherwise waits out one L2 round trip per chunk)
-    constexpr int kU = 16;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x * 32 + lane;
+    const bool col = e < experts;
+    const int per = (chunks + 31) / 32;
+    const int c_begin = min(chunks, warp * per), c_end = min(chunks, c_begin + per);
+    constexpr int kU = 8;
     int sum = 0;
     for (int c = c_begin; c < c_end; c += kU) {
         int v[kU];
 #pragma unroll
-        for (int u = 0; u < kU; ++u) v[u] = c + u < c_end ? hist[static_cast<size_t>(c + u) * experts + e] : 0;
+        for (int u = 0; u < kU; ++u) v[u] = col && c + u < c_end ? hist[static_cast<size_t>(c + u) * experts + e] : 0;
 #pragma unroll
         for (int u = 0; u < kU; ++u) sum += v[u];
     }
-    part[threadIdx.x] = sum;
+    part[warp][lane] = sum;
     __syncthreads();
-    int total = 0, before = 0;
-    if (mine)
-        for (int j = 0; j < S; ++j) {
-            const int v = part[j * experts + e];
-            if (j < q) before += v;
-            total += v;
-        }
-    const bool lead = mine && q == 0;
-    int all = 0;
-    const int excl = block_exclusive_scan(lead ? total : 0, scratch, &all);
-    if (lead) {
-        offsets[e] = excl;
-        if (e == experts - 1) offsets[experts] = excl + total;
+    int before = 0, total = 0;
+    for (int w = 0; w < 32; ++w) {
+        const int v = part[w][lane];
+        if (w < warp) before += v;
+        total += v;
     }
-    int n_active = 0;
-    const int apos = block_exclusive_scan(lead && total > 0 ? 1 : 0, scratch, &n_active);
-    if (lead && total > 0) active[apos] = e;
-    if (threadIdx.x == 0) {
-        *num_active = n_active;
-        if (bad_routes) *bad_routes = routes - all;
-    }
-    if (lead) part[e] = excl;
-    __syncthreads();
-    if (mine) {
-        int base = part[e] + before;
+    if (col) {
+        int run = before;
         for (int c = c_begin; c < c_end; c += kU) {
             int v[kU];
 #pragma unroll
@@ -129,17 +120,39 @@ __global__ void __launch_bounds__(1024) permute_scan_kernel(int32_t *__restrict_
 #pragma unroll
             for (int u = 0; u < kU; ++u) {
                 if (c + u < c_end) {
-                    hist[static_cast<size_t>(c + u) * experts + e] = base;
-                    base += v[u];
+                    hist[static_cast<size_t>(c + u) * experts + e] = run;
+                    run += v[u];
                 }
             }
         }
+        if (warp == 0) totals[e] = total;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(done, 1) == static_cast<int>(gridDim.x) - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int x = threadIdx.x;
+    int t = 0;
+    if (x < experts) t = __ldcg(totals + x);
+    int3 all;
+    const int3 ex = block_exclusive_scan3(make_int3(t, t > 0 ? 1 : 0, 0), scratch, &all);
+    if (x < experts) {
+        offsets[x] = ex.x;
+        if (x == experts - 1) offsets[experts] = ex.x + t;
+        if (t > 0) active[ex.y] = x;
+    }
+    if (x == 0) {
+        *num_active = all.y;
+        if (bad_routes) *bad_routes = routes - all.x;
     }
 }
 
 __global__ void __launch_bounds__(256) permute_place_kernel(const int64_t *__restrict__ idx, int tokens, int top_k,
                                                             int experts, int chunks,
                                                             const int32_t *__restrict__ hist,
+                                                            const int32_t *__restrict__ offsets,
                                                             int32_t *__restrict__ perm_token,
                                                             int32_t *__restrict__ perm_slot,
                                                             int32_t *__restrict__ route_pos) {
@@ -150,7 +163,7 @@ __global__ void __launch_bounds__(256) permute_place_kernel(const int64_t *__res
     const int c = blockIdx.x * kWarpsPerCta + warp;
     if (c >= chunks) return;
     int32_t *base = base_smem + warp * experts;
-    for (int e = lane; e < experts; e += 32) base[e] = hist[static_cast<size_t>(c) * experts + e];
+    for (int e = lane; e < experts; e += 32) base[e] = hist[static_cast<size_t>(c) * experts + e] + offsets[e];
     __syncwarp();
     const int routes = tokens * top_k;
     int64_t v[kChunk / 32];
@@ -182,7 +195,8 @@ __global__ void __launch_bounds__(256) permute_place_kernel(const int64_t *__res
 
 int permute_hist_ints(int tokens, int top_k, int experts) {
     const int64_t routes = static_cast<int64_t>(tokens) * top_k;
-    return routes <= kOneCtaRoutes ? 0 : static_cast<int>((routes + kChunk - 1) / kChunk) * experts;
+    // chunk counts, then the column totals and the column scan's counter
+    return routes <= kOneCtaRoutes ? 0 : static_cast<int>((routes + kChunk - 1) / kChunk) * experts + experts + 1;
 }
 
 int permute_smem_bytes(int warps, int experts) {
@@ -210,11 +224,13 @@ int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32
         if (int rc = launch_pdl(permute_count_kernel, dim3(ctas), dim3(256), smem, stream, "permute_count_kernel", idx,
                                 tokens, top_k, experts, chunks, hist))
             return rc;
-        if (int rc = launch_pdl(permute_scan_kernel, dim3(1), dim3(1024), 0, stream, "permute_scan_kernel", hist,
-                                chunks, experts, static_cast<int>(routes), offsets, active, num_active, bad_routes))
+        int32_t *totals = hist + static_cast<size_t>(chunks) * experts;
+        if (int rc = launch_pdl(permute_colscan_kernel, dim3((experts + 31) / 32), dim3(1024), 0, stream,
+                                "permute_colscan_kernel", hist, chunks, experts, static_cast<int>(routes), totals,
+                                totals + experts, offsets, active, num_active, bad_routes))
             return rc;
         return launch_pdl(permute_place_kernel, dim3(ctas), dim3(256), smem, stream, "permute_place_kernel", idx,
-                          tokens, top_k, experts, chunks, hist, perm_token, perm_slot, route_pos);
+                          tokens, top_k, experts, chunks, hist, offsets, perm_token, perm_slot, route_pos);
     }
     const int smem = permute_smem_bytes(32, experts);
     static bool configured = false;

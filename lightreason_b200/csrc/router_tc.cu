@@ -7,9 +7,9 @@
 // 128-byte swizzle, streamed by TMA through an 8-stage ring.  With ks > 1 K
 // splits (few tokens: more CTAs than row blocks x token tiles) each CTA writes
 // FP32 partials part[split][t][e], which the selection kernel sums in split
-// order before the one BF16 rounding.  Thread 0 issues the loads
-// and the tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator; all four
-// warps then read their 32 TMEM lanes (= router rows) and write BF16 logits,
+// order before the one BF16 rounding.  Warp 0 issues the loads and warp 1
+// the tcgen05.mma (M=128, N=BN, K=16) into a TMEM accumulator, each stage
+// handed back to the loads by a commit; all four warps then read their 32 TMEM lanes (= router rows) and write BF16 logits,
 // 32 consecutive experts of one token per warp store.  Every wait is bounded:
 // on timeout the CTA records an error in *error, drains its own copies and
 // products, and returns.
@@ -82,26 +82,42 @@ __global__ void __launch_bounds__(128, 1)
 
     const int row0 = blockIdx.x * kRows, t0 = blockIdx.y * BN;
     const int nk = hidden / kK / gridDim.z, kb_first = blockIdx.z * nk;
-    if (threadIdx.x == 0) {
-        constexpr uint32_t idesc = sm100::idesc_bf16_f32(kRows, BN);
+    volatile int *failed_v = &failed;
+    if (warp == 0 && lane == 0) {
+        // TMA producer: refills a stage as soon as the products reading it
+        // have committed, independently of the MMA issue below
         bool issued[kStagesTc] = {};
         uint32_t issued_parity[kStagesTc] = {};
-        auto load = [&](int kb) {
+        for (int kb = 0; kb < nk; ++kb) {
             const int s = kb % kStagesTc;
+            const uint32_t ph = (kb / kStagesTc) & 1;
+            if (*failed_v || !wait_bounded(&empty[s], ph ^ 1)) {
+                *failed_v = 1;
+                break;
+            }
             uint8_t *st = smem + s * kStage;
             sm100::mbar_expect_tx(&full[s], kStage);
             sm100::tma_load_2d(st, &tm_w, &full[s], (kb_first + kb) * kK, row0);
             sm100::tma_load_2d(st + kA, &tm_x, &full[s], (kb_first + kb) * kK, t0);
             issued[s] = true;
-            issued_parity[s] = (kb / kStagesTc) & 1;
-        };
-        for (int kb = 0; kb < nk && kb < kStagesTc; ++kb) load(kb);
-        bool ok = true, any_mma = false;
+            issued_parity[s] = ph;
+        }
+        if (*failed_v) {
+            if (error) atomicExch(error, 6);
+            // drain: every issued copy lands before the CTA leaves
+            for (int s = 0; s < kStagesTc; ++s)
+                if (issued[s]) wait_bounded(&full[s], issued_parity[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: products back to back, each stage released by a commit
+        constexpr uint32_t idesc = sm100::idesc_bf16_f32(kRows, BN);
+        bool any_mma = false;
         for (int kb = 0; kb < nk; ++kb) {
             const int s = kb % kStagesTc;
             const uint32_t ph = (kb / kStagesTc) & 1;
-            if (!wait_bounded(&full[s], ph)) {
-                ok = false;
+            if (*failed_v || !wait_bounded(&full[s], ph)) {
+                *failed_v = 1;
+                if (error) atomicExch(error, 6);
                 break;
             }
             sm100::tc_fence_after();
@@ -112,23 +128,6 @@ __global__ void __launch_bounds__(128, 1)
                 sm100::mma_bf16(tmem, a + 2 * kk, b + 2 * kk, idesc, (kb | kk) != 0);
             sm100::mma_commit(&empty[s]);
             any_mma = true;
-            // Refill the previous stage once the products reading it are done,
-            // so that this step's products stay in flight meanwhile.
-            const int prev = kb - 1;
-            if (prev >= 0 && prev + kStagesTc < nk) {
-                if (!wait_bounded(&empty[prev % kStagesTc], (prev / kStagesTc) & 1)) {
-                    ok = false;
-                    break;
-                }
-                load(prev + kStagesTc);
-            }
-        }
-        if (!ok) {
-            failed = 1;
-            if (error) atomicExch(error, 6);
-            // drain: every issued copy lands before the CTA leaves
-            for (int s = 0; s < kStagesTc; ++s)
-                if (issued[s]) wait_bounded(&full[s], issued_parity[s]);
         }
         if (any_mma) sm100::mma_commit(&done);
         else sm100::mbar_arrive(&done);
@@ -136,7 +135,7 @@ __global__ void __launch_bounds__(128, 1)
     __syncwarp();
     const bool ready = wait_bounded(&done, 0);
     sm100::tc_fence_after();
-    if (ready && !failed) {
+    if (ready && !*failed_v) {
         const int row = row0 + warp * 32 + lane;
         const uint32_t taddr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
 #pragma unroll
