@@ -4,8 +4,8 @@
 // group's expert stay in registers (16-byte streaming loads), and every routed
 // token is dotted against both; bf16(gate), bf16(up), bf16(silu), bf16(s*u)
 // are the eager rounding points (modeling_qwen3_5_moe.py:745-746,
-// edge35b/cpu_experts.c:59-62).  down: one warp per (group, output row) over
-// the group's activation rows (:747, cpu_experts.c:68).  The weight stream
+// edge35b/cpu_experts.c:59-62).  down: one warp per (group, 4 output rows)
+// over the group's activation rows (:747, cpu_experts.c:68).  The weight stream
 // dominates (6 MiB per expert), so each weight byte is loaded exactly once.
 #include <cstring>
 
@@ -14,48 +14,56 @@
 
 namespace lrb {
 
+// gate/up: one warp per row r of one group (the CTA's group): the gate row
+// and the up row stay in registers; the group's token rows are staged in
+// shared memory four at a time, so a warp holds only its 2 x 4 KiB of weights
+// and two CTAs fit on an SM with every weight load in flight.
 template <int NW, class Src>
-__global__ void __launch_bounds__(256) gate_up_kernel(const Src src, const uint16_t *__restrict__ x, int inner,
-                                                      uint16_t *__restrict__ act) {
+__global__ void __launch_bounds__(256, 2) gate_up_kernel(const Src src, const uint16_t *__restrict__ x, int inner,
+                                                         uint16_t *__restrict__ act) {
     constexpr int H = NW * 256;
+    __shared__ uint4 xs[4][H / 8];
     const int g = blockIdx.y;
+    grid_dependency_wait();  // the groups come from the routing kernels before
+    grid_dependency_trigger();
+    if (blockIdx.x == 0 && g == 0 && threadIdx.x == 0) src.on_start();
     if (g >= src.n()) return;
     const Group G = src.get(g);
+    if (G.count <= 0) return;
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= inner || G.count <= 0) return;
+    const bool live = row < inner;
     uint4 wg[NW], wu[NW];
-    const uint16_t *gr = G.gate + static_cast<size_t>(row) * H;
-    const uint16_t *ur = G.up + static_cast<size_t>(row) * H;
+    if (live) {
+        const uint16_t *gr = G.gate + static_cast<size_t>(row) * H;
+        const uint16_t *ur = G.up + static_cast<size_t>(row) * H;
 #pragma unroll
-    for (int i = 0; i < NW; ++i) {
-        wg[i] = ld_stream(gr + (lane + 32 * i) * 8);
-        wu[i] = ld_stream(ur + (lane + 32 * i) * 8);
+        for (int i = 0; i < NW; ++i) {
+            wg[i] = ld_stream(gr + (lane + 32 * i) * 8);
+            wu[i] = ld_stream(ur + (lane + 32 * i) * 8);
+        }
     }
     for (int j0 = 0; j0 < G.count; j0 += 4) {
-        float ag[4] = {0.f, 0.f, 0.f, 0.f}, au[4] = {0.f, 0.f, 0.f, 0.f};
+        const int nj = min(4, G.count - j0);
+        __syncthreads();  // the previous round's token rows are consumed
+        for (int i = threadIdx.x; i < nj * (H / 8); i += blockDim.x) {
+            const int j = i / (H / 8), c = i % (H / 8);
+            xs[j][c] = ld_cached(x + static_cast<size_t>(src.token(G.begin + j0 + j)) * H + c * 8);
+        }
+        __syncthreads();
+        if (!live) continue;
+        for (int j = 0; j < nj; ++j) {
+            float ag = 0.f, au = 0.f;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (j0 + j < G.count) {
-                const uint16_t *xr = x + static_cast<size_t>(src.token(G.begin + j0 + j)) * H;
-#pragma unroll
-                for (int i = 0; i < NW; ++i) {
-                    const uint4 a = ld_cached(xr + (lane + 32 * i) * 8);
-                    ag[j] = dot8(wg[i], a, ag[j]);
-                    au[j] = dot8(wu[i], a, au[j]);
-                }
+            for (int i = 0; i < NW; ++i) {
+                const uint4 a = xs[j][lane + 32 * i];
+                ag = dot8(wg[i], a, ag);
+                au = dot8(wu[i], a, au);
             }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            ag[j] = warp_sum(ag[j]);
-            au[j] = warp_sum(au[j]);
-        }
-        if (lane == 0) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (j0 + j >= G.count) break;
-                const float gv = rbf(ag[j]), uv = rbf(au[j]);
+            ag = warp_sum(ag);
+            au = warp_sum(au);
+            if (lane == 0) {
+                const float gv = rbf(ag), uv = rbf(au);
                 const float s = rbf(silu_f32(gv));
                 act[static_cast<size_t>(G.begin + j0 + j) * inner + row] = f2bf(s * uv);
             }
@@ -63,38 +71,55 @@ __global__ void __launch_bounds__(256) gate_up_kernel(const Src src, const uint1
     }
 }
 
+// down: one warp per four output rows of one group, their 4 x 1 KiB of
+// weights requested before the activations exist (programmatic launch: the
+// groups were complete before the gate/up kernel started, so this kernel may
+// read them while that kernel still runs; only the activations wait).
 template <int NI, class Src>
-__global__ void __launch_bounds__(256) down_kernel(const Src src, const uint16_t *__restrict__ act, int hidden,
+__global__ void __launch_bounds__(256, 3) down_kernel(const Src src, const uint16_t *__restrict__ act, int hidden,
                                                    uint16_t *__restrict__ y) {
     constexpr int I = NI * 256;
+    constexpr int R = 4;  // rows per warp
     const int g = blockIdx.y;
-    if (g >= src.n()) return;
+    if (g >= src.n()) {
+        grid_dependency_wait();
+        return;
+    }
     const Group G = src.get(g);
     const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (row >= hidden || G.count <= 0) return;
-    uint4 wd[NI];
-    const uint16_t *dr = G.down + static_cast<size_t>(row) * I;
+    const int row0 = (blockIdx.x * 8 + (threadIdx.x >> 5)) * R;
+    if (row0 >= hidden || G.count <= 0) {
+        grid_dependency_wait();
+        return;
+    }
+    uint4 wd[R][NI];
 #pragma unroll
-    for (int i = 0; i < NI; ++i) wd[i] = ld_stream(dr + (lane + 32 * i) * 8);
-    for (int j0 = 0; j0 < G.count; j0 += 4) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < R; ++r) {
+        const uint16_t *dr = G.down + static_cast<size_t>(min(row0 + r, hidden - 1)) * I;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (j0 + j < G.count) {
-                const uint16_t *ar = act + static_cast<size_t>(G.begin + j0 + j) * I;
+        for (int i = 0; i < NI; ++i) wd[r][i] = ld_stream(dr + (lane + 32 * i) * 8);
+    }
+    grid_dependency_wait();
+    grid_dependency_trigger();
+    for (int j = 0; j < G.count; ++j) {
+        const uint16_t *ar = act + static_cast<size_t>(G.begin + j) * I;
+        uint4 a[NI];
 #pragma unroll
-                for (int i = 0; i < NI; ++i) acc[j] = dot8(wd[i], ld_cached(ar + (lane + 32 * i) * 8), acc[j]);
-            }
+        for (int i = 0; i < NI; ++i) a[i] = ld_cached(ar + (lane + 32 * i) * 8);
+        float acc[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            acc[r] = 0.f;
+#pragma unroll
+            for (int i = 0; i < NI; ++i) acc[r] = dot8(wd[r][i], a[i], acc[r]);
+            acc[r] = warp_sum(acc[r]);
         }
+        if (lane < R && row0 + lane < hidden) {
+            float v = acc[0];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[j] = warp_sum(acc[j]);
-        if (lane == 0) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if (j0 + j >= G.count) break;
-                y[static_cast<size_t>(G.begin + j0 + j) * hidden + row] = f2bf(acc[j]);
-            }
+            for (int r = 1; r < R; ++r)
+                if (lane == r) v = acc[r];
+            y[static_cast<size_t>(G.begin + j) * hidden + row0 + lane] = f2bf(v);
         }
     }
 }
@@ -103,25 +128,27 @@ template <class Src>
 int launch_experts(const Src &src, int max_groups, const uint16_t *x, int hidden, int inner, uint16_t *act,
                    uint16_t *y, cudaStream_t stream, cudaEvent_t between) {
     if (max_groups <= 0) return MOE_OK;
-    const dim3 gu_grid((inner + 7) / 8, max_groups), dn_grid((hidden + 7) / 8, max_groups);
-    if (hidden == 2048) gate_up_kernel<8, Src><<<gu_grid, 256, 0, stream>>>(src, x, inner, act);
-    else if (hidden == 1024) gate_up_kernel<4, Src><<<gu_grid, 256, 0, stream>>>(src, x, inner, act);
-    else if (hidden == 4096) gate_up_kernel<16, Src><<<gu_grid, 256, 0, stream>>>(src, x, inner, act);
+    const dim3 gu_grid((inner + 7) / 8, max_groups), dn_grid((hidden + 31) / 32, max_groups);
+    int rc;
+    if (hidden == 2048) rc = launch_pdl(gate_up_kernel<8, Src>, gu_grid, dim3(256), 0, stream, "gate_up_kernel", src, x, inner, act);
+    else if (hidden == 1024) rc = launch_pdl(gate_up_kernel<4, Src>, gu_grid, dim3(256), 0, stream, "gate_up_kernel", src, x, inner, act);
+    else if (hidden == 4096) rc = launch_pdl(gate_up_kernel<16, Src>, gu_grid, dim3(256), 0, stream, "gate_up_kernel", src, x, inner, act);
     else return set_error(MOE_EINVAL, "experts: hidden %d not in {1024, 2048, 4096}", hidden);
-    LRB_LAUNCHED("gate_up_kernel");
+    if (rc) return rc;
     if (between) LRB_CUDA(cudaEventRecord(between, stream));
-    if (inner == 512) down_kernel<2, Src><<<dn_grid, 256, 0, stream>>>(src, act, hidden, y);
-    else if (inner == 256) down_kernel<1, Src><<<dn_grid, 256, 0, stream>>>(src, act, hidden, y);
-    else if (inner == 1024) down_kernel<4, Src><<<dn_grid, 256, 0, stream>>>(src, act, hidden, y);
+    if (inner == 512) rc = launch_pdl(down_kernel<2, Src>, dn_grid, dim3(256), 0, stream, "down_kernel", src, act, hidden, y);
+    else if (inner == 256) rc = launch_pdl(down_kernel<1, Src>, dn_grid, dim3(256), 0, stream, "down_kernel", src, act, hidden, y);
+    else if (inner == 1024) rc = launch_pdl(down_kernel<4, Src>, dn_grid, dim3(256), 0, stream, "down_kernel", src, act, hidden, y);
     else return set_error(MOE_EINVAL, "experts: inner %d not in {256, 512, 1024}", inner);
-    LRB_LAUNCHED("down_kernel");
-    return MOE_OK;
+    return rc;
 }
 
 template int launch_experts<DeviceGroups>(const DeviceGroups &, int, const uint16_t *, int, int, uint16_t *,
                                           uint16_t *, cudaStream_t, cudaEvent_t);
 template int launch_experts<ParamGroups>(const ParamGroups &, int, const uint16_t *, int, int, uint16_t *,
                                          uint16_t *, cudaStream_t, cudaEvent_t);
+template int launch_experts<PlanGroups>(const PlanGroups &, int, const uint16_t *, int, int, uint16_t *,
+                                        uint16_t *, cudaStream_t, cudaEvent_t);
 
 // Per token: the routed contributions in ascending route position (= ascending
 // expert id), acc = bf16(acc + bf16(y * w)) as index_add_ on BF16 does

@@ -26,6 +26,7 @@ struct DeviceGroups {
     __device__ __forceinline__ int n() const { return *num_groups; }
     __device__ __forceinline__ Group get(int g) const { return groups[g]; }
     __device__ __forceinline__ int token(int p) const { return route_token[p]; }
+    __device__ __forceinline__ void on_start() const {}
 };
 
 // Groups passed by value (pointer-table entry points, one route per group).
@@ -37,6 +38,7 @@ struct ParamGroups {
     __device__ __forceinline__ int n() const { return count; }
     __device__ __forceinline__ Group get(int g) const { return groups[g]; }
     __device__ __forceinline__ int token(int p) const { return tokens[p]; }
+    __device__ __forceinline__ void on_start() const {}
 };
 
 // Grouped tensor-core experts (grouped.cu).
@@ -49,6 +51,44 @@ struct GroupedGroup {
 struct GroupedPlan {
     int32_t num_groups, items1, items2, items3, work, error, done2_total;
     int32_t xs_ready;  // epilogue warps that finished the in-kernel token gather
+};
+
+// The grouped kernel's plan read as pointer groups, for the warp-per-row
+// expert kernels at the narrowest widths: weight index -> bank rows (expert
+// id or HBM slot; -1 = the shared expert), the host-staging error folded
+// into the plan's error word once.
+struct PlanGroups {
+    const GroupedGroup *groups;
+    GroupedPlan *plan;
+    const int32_t *route_token;
+    const uint16_t *gate_up, *down, *sh_gate, *sh_up, *sh_down;
+    int64_t gate_up_stride, down_stride;  // elements per bank entry
+    int inner, hidden;
+    const int32_t *stage_error;
+    __device__ __forceinline__ int n() const { return plan->num_groups; }
+    __device__ __forceinline__ Group get(int g) const {
+        const GroupedGroup G = groups[g];
+        Group r;
+        if (G.weight >= 0) {
+            r.gate = gate_up + static_cast<int64_t>(G.weight) * gate_up_stride;
+            r.up = r.gate + static_cast<int64_t>(inner) * hidden;
+            r.down = down + static_cast<int64_t>(G.weight) * down_stride;
+        } else {
+            r.gate = sh_gate;
+            r.up = sh_up;
+            r.down = sh_down;
+        }
+        r.begin = G.begin;
+        r.count = G.count;
+        return r;
+    }
+    __device__ __forceinline__ int token(int p) const { return route_token[p]; }
+    __device__ __forceinline__ void on_start() const {
+        if (stage_error) {
+            const int e = *stage_error;
+            if (e) atomicCAS(&plan->error, 0, e);
+        }
+    }
 };
 struct GroupedLaunch {
     const uint16_t *gate_up, *down;  // banks: [bank_experts, 2I, H], [bank_experts, H, I]

@@ -37,6 +37,12 @@ struct Layout {
 constexpr int kFusedRoutingMaxTokens = 16;
 bool decode_routing(int tokens, int experts) { return tokens <= kFusedRoutingMaxTokens && experts <= 256; }
 
+// At the narrowest widths the experts run as warp-per-row GEMVs (every warp
+// of the GPU streaming weight rows, no pipeline fill per work item) followed
+// by the standalone combine, instead of the tensor-core grouped kernel.
+constexpr int kGemvMaxTokens = 2;
+bool gemv_experts(int tokens, bool rows_mode) { return tokens <= kGemvMaxTokens && !rows_mode; }
+
 Layout layout(int tokens, int experts, int top_k, int hidden, int inner) {
     const size_t T = tokens, E = experts, K = top_k, R = T * K;
     Layout L{};
@@ -316,7 +322,8 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     // Decode widths combine inside the expert kernel (one launch less on the
     // latency path); wider calls run the standalone combine after it, whose
     // parallelism the persistent kernel's epilogue warps cannot match.
-    const bool fused_combine = tokens <= kDecodeMaxTokens && !rows_mode;
+    const bool gemv = gemv_experts(tokens, rows_mode != 0);
+    const bool fused_combine = tokens <= kDecodeMaxTokens && !rows_mode && !gemv;
     pa.combine = fused_combine ? 1 : 0;
 
     if (decode) {
@@ -403,9 +410,23 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     uint16_t *xs = at<uint16_t>(ws, L.xs), *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
     // At decode widths the grouped kernel gathers the token rows itself (its
     // epilogue warps are idle while the first weight tiles stream in).
-    if (!fused_combine)
+    if (!fused_combine && !gemv)
         if (int rc = launch_gather_tokens(x, route_token, offsets, E, R, shared ? tokens : 0, H, xs, s)) return rc;
     if (int rc = mark(4)) return rc;
+    if (gemv) {
+        PlanGroups pg{groups, plan, route_token, gu_base, dn_base, shared ? w->shared_gate : nullptr,
+                      shared ? w->shared_up : nullptr, shared ? w->shared_down : nullptr, gu_str, dn_str, I, H,
+                      counters + 2};
+        const int max_groups = std::min(E, R) + (shared ? 1 : 0);
+        if (int rc = launch_experts(pg, max_groups, x, H, I, act, y, s, nullptr)) return rc;
+        if (int rc = mark(5)) return rc;
+        if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
+                                    shared ? sig : nullptr, out, s))
+            return rc;
+        if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
+        if (int rc = mark(6)) return rc;
+        return mark(7);
+    }
     GroupedLaunch GL{};
     GL.gate_up = gu_base;
     GL.down = dn_base;
