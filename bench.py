@@ -54,17 +54,38 @@ GATE_UP_BYTES = 2 * INNER * HIDDEN * 2       # 4,194,304 B per expert
 DOWN_BYTES = HIDDEN * INNER * 2              # 2,097,152 B per expert
 EXPERT_BYTES = GATE_UP_BYTES + DOWN_BYTES    # 6,291,456 B
 STAGES = ("router", "route", "gather", "xs", "experts", "combine", "unused")
-KERNEL_NAMES = {"router": "router_split_kernel | router_logits_kernel",
-                "route": "route_decode_kernel | router_select+permute+grouped_plan kernels",
-                "gather": "stage_experts_kernel", "xs": "gather_tokens_kernel",
-                "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down; + combine at T <= 64)",
-                "combine": "combine_kernel (T > 64)", "unused": "-"}
+KERNEL_NAMES = {"router": "router_split_kernel (T <= 16) | router_tc_kernel",
+                "route": "route_decode_kernel (T <= 16) | router_select+permute+grouped_plan kernels",
+                "gather": "stage_experts_kernel", "xs": "gather_tokens_kernel (T > 64)",
+                "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down; + token gather and combine at T <= 64)",
+                "combine": "combine_kernel (T <= 2 and T > 64)", "unused": "-"}
+GEMV_MAX_TOKENS = 2  # the layer's warp-per-row expert path (gate_up_kernel + down_kernel) up to this width
+
+
+def kernel_name(stage: str, tokens: int) -> str:
+    if stage == "experts" and tokens <= GEMV_MAX_TOKENS:
+        return "gate_up_kernel + down_kernel (warp-per-row GEMV experts, T <= 2)"
+    return KERNEL_NAMES[stage]
+
+
+def launches_per_step(tokens: int) -> int:
+    """Kernels of one moe_layer_forward call with HBM-resident experts."""
+    if tokens <= GEMV_MAX_TOKENS:
+        return 5  # router_split, route_decode, gate_up, down, combine
+    if tokens <= 16:
+        return 3  # router_split, route_decode, grouped (gathers and combines itself)
+    routes = tokens * TOP_K
+    permute = 1 if routes <= 2048 else 3  # one-CTA sort, or count + column scan + place
+    if tokens <= 64:
+        return 4 + permute  # router_tc, router_select, permute, grouped_plan, grouped
+    return 6 + permute  # router_tc, router_select, permute, grouped_plan, gather_tokens, grouped, combine
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the dominant kernel, from the ncu captures summarised under profiles/.
 PROFILED_TRAFFIC = {
-    1: (451_650_000, "profiles/swiglu_grouped_kernel_T16_config1.md"),
-    3: (2_004_844_000, "profiles/swiglu_grouped_kernel_T4096_config3.md"),
+    0: (56_680_000, "profiles/launches_layer_config0_T1.md (gate_up_kernel + down_kernel)"),
+    1: (454_122_240, "profiles/swiglu_grouped_kernel_T16_config1.md"),
+    3: (2_062_540_000, "profiles/launches_layer_config3_T4096.md"),
 }
 
 CACHE_SLOTS = 128  # experts the e2e_cached variant keeps in HBM (half of the bank, ~0.8 GB)
@@ -402,7 +423,7 @@ def run_ours(args, cfg, world, rank, local):
     routes = tokens * TOP_K
     # algorithmic bytes per launch of each expert kernel (groups = U routed + shared)
     rows = routes + tokens
-    fused = tokens <= 64   # the expert kernel runs the combine itself at decode widths
+    fused = GEMV_MAX_TOKENS < tokens <= 64   # the grouped kernel runs the combine itself at decode widths
     combine_bytes = rows * HIDDEN * 2 + tokens * HIDDEN * 2 + routes * 6
     algo = {
         # grouped kernel: every selected expert's weights (+ shared) once, the
@@ -425,7 +446,7 @@ def run_ours(args, cfg, world, rank, local):
     layer_bytes = [u * EXPERT_BYTES + EXPERT_BYTES + EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 4
                    for u in u_per_step]
     layer_gbs = statistics.mean(b / (m / 1e3) / 1e9 for b, m in zip(layer_bytes, ms))
-    launches_per_step = 4 if tokens <= 64 else 7  # decode: router_split, route_decode, gather, grouped
+    n_launches = launches_per_step(tokens)
     result = {
         "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -437,7 +458,7 @@ def run_ours(args, cfg, world, rank, local):
                    "distinct_experts_per_step": round(u_mean, 2),
                    "parallelism": "single-gpu" if world == 1 else f"replicas{world}",
                    "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window"},
-        "roofline": {"bound": "hbm", "kernel": KERNEL_NAMES[dominant], "achieved": round(achieved, 1),
+        "roofline": {"bound": "hbm", "kernel": kernel_name(dominant, tokens), "achieved": round(achieved, 1),
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(achieved / hbm_peak, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json hbm_gbs)" if peak_src == "measured" else
                      "fallback 6650 GB/s",
@@ -448,7 +469,7 @@ def run_ours(args, cfg, world, rank, local):
                      "layer_gbs": round(layer_gbs, 1), "layer_frac": round(layer_gbs / hbm_peak, 4),
                      "stage_us_with_event_overhead": {k: round(1e3 * statistics.mean(v), 2)
                                                       for k, v in stage_ms.items()}},
-        "gpu_launches": launches_per_step * args.steps,
+        "gpu_launches": n_launches * args.steps,
         "clocks": clocks,
         "wall_s_timed_loop": round(wall, 4),
     }
