@@ -169,7 +169,7 @@ def test_permute_drops_out_of_range_ids(dev):
     assert active[:int(n_active.item())].cpu().numpy().tolist() == [1, 3, 7]
 
 
-@pytest.mark.parametrize("tokens", [1, 8, 16, 64])
+@pytest.mark.parametrize("tokens", [1, 2, 3, 8, 16, 64])
 def test_layer_matches_oracle(dev, case13, tokens):
     x = S.hidden_states(200 + tokens, tokens)
     out, idx, sc, lg = case13.run(x)
@@ -203,7 +203,7 @@ def test_host_resident_experts_match_hbm_resident(dev, case13):
         assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("tokens", [1, 16])
+@pytest.mark.parametrize("tokens", [1, 2, 16])
 def test_packed_host_experts_match_hbm_resident(dev, case13, tokens):
     """Experts kept in pinned host RAM in the lossless row codec decode on their
     way into HBM: the layer output is bit-identical to the HBM-resident one."""
@@ -214,7 +214,8 @@ def test_packed_host_experts_match_hbm_resident(dev, case13, tokens):
         assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("packed,slots,tokens", [(True, 128, 16), (False, 128, 16), (True, 200, 4), (True, 64, 8)])
+@pytest.mark.parametrize("packed,slots,tokens", [(True, 128, 16), (False, 128, 16), (True, 200, 4), (True, 64, 8),
+                                                  (True, 16, 2)])
 def test_expert_cache_matches_hbm_resident(dev, case13, packed, slots, tokens):
     """The expert cache over host banks: over a run of calls (hits, misses and
     evictions; slots == min(E, T*top_k) evicts on nearly every call) every
