@@ -643,7 +643,11 @@ def run_ep(args, cfg, world, rank, local):
     achieved, peak, unit = (gbs, hbm_peak, "GB/s") if bound == "hbm" else (tfs, tensor_peak, "TFLOP/s")
     # router tc + select, permute (3 when wide), dispatch, collect, local permute/plan/gather/grouped, return,
     # finish, combine  (NCCL: dispatch, unpack instead of collect/return/finish)
-    launches = 14 if transport == "p2p" else 12
+    # router_tc + router_select, permute (count, column scan, place), the
+    # exchange's own kernels (p2p: dispatch, collect, return, finish; NCCL and
+    # one rank: ep_dispatch, ep_unpack), the local layer in rows mode
+    # (permute x3, plan, gather, grouped), the ordered combine
+    launches = 16 if transport == "p2p" else 14
     if peer is not None:
         peer.close()
     timing = ("each timed step one CUDA-graph replay of the whole rank step (no host synchronisation), CUDA "
@@ -742,7 +746,7 @@ def run_stack(args, cfg, world, rank, local):
                      "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
                      "peak_source": f"{peak_src} (MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback",
                      "traffic": None, "algorithmic_bytes_per_step": int(sum(layer_bytes))},
-        "gpu_launches": 4 * n_layers * args.steps,
+        "gpu_launches": launches_per_step(tokens) * n_layers * args.steps,
         "clocks": clocks,
     }
 

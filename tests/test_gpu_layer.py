@@ -183,6 +183,30 @@ def test_layer_matches_oracle(dev, case13, tokens):
     assert_close(out[same], w_out[same], what="layer output")
 
 
+@pytest.mark.parametrize("top_k", [4, 16])
+@pytest.mark.parametrize("tokens", [1, 2, 16, 100])
+def test_layer_other_top_k_matches_oracle(dev, case13, top_k, tokens):
+    """top_k other than 8 through every width class: the warp-per-row path
+    (T <= 2), the grouped kernel with its own combine (16), the general
+    routing with the standalone combine (100)."""
+    c = case13
+    layer = native.Layer(router=c.router, gate_up=c.gu_dev, down=c.dn_dev, bias=c.bias, shared_gate=c.sh[0],
+                         shared_up=c.sh[1], shared_down=c.sh[2], shared_gate_w=c.sh[3], top_k=top_k)
+    x_bits = S.hidden_states(400 + tokens + top_k, tokens)
+    x = to_dev(x_bits, dev)
+    idx = torch.empty((tokens, top_k), dtype=torch.int64, device=dev)
+    lg = torch.empty((tokens, 256), dtype=torch.bfloat16, device=dev)
+    out = bits(layer(x, idx_out=idx, logits_out=lg))
+    w = c.w
+    w_out, w_idx, _, w_lg = O.moe_layer(x_bits, w.router, w.bias, w.gate_up, w.down, w.sh_gate, w.sh_up, w.sh_down,
+                                        w.sh_gate_w, top_k=top_k)
+    idx = idx.cpu().numpy()
+    compare_ids(idx, w_idx, S.bf16_bits_to_f32(w_lg) + w.bias, slack_ulps=1.0)
+    same = np.all(idx == w_idx, axis=1)
+    assert same.mean() > 0.9
+    assert_close(out[same], w_out[same], what=f"layer output, top_k {top_k}")
+
+
 @pytest.mark.parametrize("name", golden_layers())
 def test_layer_matches_transformers_golden(dev, name):
     g = load_golden(name)
