@@ -5,9 +5,12 @@
 // kernels use programmatic dependent launch, so each one's prologue overlaps
 // its predecessor.
 //
-// Decode widths (T <= 64): split-K router partials, then one CTA that sums
-// them, selects, permutes and plans, a token gather, and the grouped kernel.
-// Wider calls: router GEMV, selection, permute and plan as separate kernels.
+// T <= 2: split-K router partials, one CTA that sums them, selects, permutes
+// and plans, then warp-per-row GEMV experts and the combine.  T <= 16: the
+// same routing, then the grouped kernel, which gathers the token rows and
+// runs the combine itself (so too up to 64 tokens, after the spread-out
+// routing).  Wider calls: tensor-core router, selection, permute and plan as
+// separate kernels, a token gather, the grouped kernel and the combine.
 #include <algorithm>
 
 #include "common.cuh"
