@@ -495,10 +495,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // --------------------------------------------------------- MMA issuer
         if (lane == 0) {
-            // weights are read once per step: evict them first, so the
-            // activations, plan and code stay in L2 under the stream
-            const uint64_t wpol = sm100::l2_evict_first_policy(), npol = sm100::l2_evict_normal_policy();
-            bool xs_seen = false;  // the in-kernel gather was observed complete
             uint32_t stage = 0, sphase = 0;
             int acc = 0;
             bool any = false;
