@@ -64,8 +64,11 @@ template <int BN>
 struct GroupedShape {
     static constexpr int kBTile = BN * kBK * 2 < 1024 ? 1024 : BN * kBK * 2;
     static constexpr int kStage = 2 * kATile + kBTile;
-    static constexpr int kStages = BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
-    static constexpr int kTmemCols = 4 * BN < 32 ? 32 : 4 * BN;  // two buffers of (gate, up)
+    static constexpr int kStages = BN >= 256 ? 3 : BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
+    // accumulator buffers of (gate, up): two, so the epilogue of one item
+    // overlaps the products of the next, while they fit the 512 TMEM columns
+    static constexpr int kBufs = 4 * BN <= 512 ? 2 : 1;
+    static constexpr int kTmemCols = 2 * BN * kBufs < 32 ? 32 : 2 * BN * kBufs;
     static constexpr int kPlanBytes = 2 * (kSmemGroups + 1) * 4 + kSmemGroups * 16;
     static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 512 /*barriers*/ + kPlanBytes;
 };
@@ -510,8 +513,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const GroupedGroup G = V.groups[ip.g];
                 const int n16 = (min(BN, G.count - ip.nt * BN) + 15) & ~15;
                 const uint32_t idesc = sm100::idesc_bf16_f32(kBM, n16);
-                const int buf = acc & 1;
-                if (!wait_bar(&tail->tempty[buf], ((acc >> 1) & 1) ^ 1, abort)) break;
+                const int buf = acc % S::kBufs;
+                if (!wait_bar(&tail->tempty[buf], ((acc / S::kBufs) & 1) ^ 1, abort)) break;
                 sm100::tc_fence_after();
                 const uint32_t d_gate = tmem + buf * 2 * BN, d_up = d_gate + BN;
                 bool ok = true;
@@ -608,8 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 
             const GroupedGroup G = V.groups[ip.g];
-            const int buf = acc & 1;
-            if (!wait_bar(&tail->tfull[buf], (acc >> 1) & 1, abort)) break;
+            const int buf = acc % S::kBufs;
+            if (!wait_bar(&tail->tfull[buf], (acc / S::kBufs) & 1, abort)) break;
             __syncwarp();
             sm100::tc_fence_after();
             const int row = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM) + q * 32 + lane;
