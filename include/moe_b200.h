@@ -152,6 +152,26 @@ int moe_expert_block_rows_noalloc(const uint16_t *const *gate_up, const uint16_t
                                   const uint16_t *input, const int32_t *token_ids,
                                   uint16_t *output, int tokens, int experts, void *stream);
 
+/* The ordered combine on its own: out[t] = bf16(acc + bf16(y[p] * w)) over
+ * token t's routes p = route_pos[t][k] (rows of y in route order, -1 = a
+ * dropped route) in ascending p, w = scores[t][k] (BF16), then
+ * + bf16(sig[t] * shared_rows[t]) when shared_rows != NULL; top_k <= 16.
+ * Replaces _ordered_sum (edge35b/fused_experts.py:27-37) and _combine
+ * (edge35b/block_experts.py:31-49), the index_add_ of
+ * modeling_qwen3_5_moe.py:749-750 and the gated add of :788-790.
+ *
+ * The shared expert on its own (modeling_qwen3_5_moe.py:698-711, :779):
+ * out[t] = down(bf16(silu(bf16(gate . x_t))) * bf16(up . x_t)) in BF16 with
+ * FP32 accumulation, and with gate_w != NULL sig[t] = bf16(sigmoid(x_t .
+ * gate_w)); gate/up [inner, hidden], down [hidden, inner]; tokens <= 128;
+ * workspace of moe_shared_expert_workspace_bytes(tokens, inner). */
+int moe_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, const uint16_t *shared_rows,
+                const uint16_t *sig, int tokens, int top_k, int hidden, uint16_t *out, void *stream);
+size_t moe_shared_expert_workspace_bytes(int tokens, int inner);
+int moe_shared_expert(const uint16_t *x, const uint16_t *gate, const uint16_t *up, const uint16_t *down,
+                      const uint16_t *gate_w, int tokens, int hidden, int inner, uint16_t *out, uint16_t *sig,
+                      void *workspace, size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------
  * One MoE layer.  moe_layer_forward replaces Qwen3_5MoeSparseMoeBlock.forward
  * (modeling_qwen3_5_moe.py:781-792: router + shared expert + experts + gate)

@@ -258,11 +258,78 @@ int expert_pairs(const uint16_t *const *gate_up, const uint16_t *const *down, co
                           nullptr);
 }
 
+// sig[t] = bf16(sigmoid(bf16(x[t] . w))): the shared-expert gate
+// (modeling_qwen3_5_moe.py:779), one warp per token, FP32 accumulation in
+// the lane order of the router's gate dot.
+__global__ void __launch_bounds__(256) shared_gate_kernel(const uint16_t *__restrict__ x,
+                                                          const uint16_t *__restrict__ w, int tokens, int hidden,
+                                                          uint16_t *__restrict__ sig) {
+    grid_dependency_wait();
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= tokens) return;
+    const uint16_t *xr = x + static_cast<size_t>(t) * hidden;
+    float acc = 0.f;
+    for (int c0 = 0; c0 < hidden; c0 += 8 * 256) {
+        uint4 wv[8], xv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int c = c0 + u * 256 + lane * 8;
+            wv[u] = c < hidden ? ld_cached(w + c) : make_uint4(0, 0, 0, 0);
+            xv[u] = c < hidden ? ld_cached(xr + c) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (c0 + u * 256 + lane * 8 < hidden) acc = dot8(wv[u], xv[u], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) sig[t] = f2bf(sigmoid_f32(rbf(acc)));
+}
+
 }  // namespace
 
 }  // namespace lrb
 
 extern "C" {
+
+int moe_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, const uint16_t *shared_rows,
+                const uint16_t *sig, int tokens, int top_k, int hidden, uint16_t *out, void *stream) {
+    LRB_REQUIRE(y && route_pos && scores && out && (!shared_rows || sig), "moe_combine: null pointer");
+    LRB_REQUIRE(hidden > 0 && hidden % 8 == 0 && tokens >= 0 && top_k >= 1 && top_k <= 16,
+                "moe_combine: bad shape");
+    if (int rc = lrb::require_sm100()) return rc;
+    return lrb::launch_combine(y, route_pos, scores, tokens, top_k, hidden, shared_rows, sig, out,
+                               lrb::as_stream(stream));
+}
+
+size_t moe_shared_expert_workspace_bytes(int tokens, int inner) {
+    return tokens > 0 && inner > 0 ? static_cast<size_t>(tokens) * inner * sizeof(uint16_t) : 0;
+}
+
+int moe_shared_expert(const uint16_t *x, const uint16_t *gate, const uint16_t *up, const uint16_t *down,
+                      const uint16_t *gate_w, int tokens, int hidden, int inner, uint16_t *out, uint16_t *sig,
+                      void *workspace, size_t workspace_bytes, void *stream) {
+    LRB_REQUIRE(x && gate && up && down && out && (!gate_w || sig), "moe_shared_expert: null pointer");
+    LRB_REQUIRE(tokens >= 0 && tokens <= lrb::kMaxParamGroups, "moe_shared_expert: tokens %d outside [0, %d]", tokens,
+                lrb::kMaxParamGroups);
+    LRB_REQUIRE((hidden == 1024 || hidden == 2048 || hidden == 4096) && (inner == 256 || inner == 512 || inner == 1024),
+                "moe_shared_expert: shapes %d x %d unsupported", hidden, inner);
+    if (tokens == 0) return MOE_OK;
+    LRB_REQUIRE(workspace && workspace_bytes >= moe_shared_expert_workspace_bytes(tokens, inner),
+                "moe_shared_expert: workspace below moe_shared_expert_workspace_bytes");
+    if (int rc = lrb::require_sm100()) return rc;
+    lrb::ParamGroups src;
+    memset(&src, 0, sizeof src);
+    src.count = 1;
+    src.groups[0] = lrb::Group{gate, up, down, 0, tokens};
+    for (int t = 0; t < tokens; ++t) src.tokens[t] = t;
+    cudaStream_t s = lrb::as_stream(stream);
+    if (int rc = lrb::launch_experts(src, 1, x, hidden, inner, static_cast<uint16_t *>(workspace), out, s, nullptr))
+        return rc;
+    if (!gate_w) return MOE_OK;
+    return lrb::launch_pdl(lrb::shared_gate_kernel, dim3((tokens + 7) / 8), dim3(256), 0, s, "shared_gate_kernel", x,
+                           gate_w, tokens, hidden, sig);
+}
 
 int moe_expert_rows(const uint16_t *const *gate_up, const uint16_t *const *down, const uint16_t *input,
                     uint16_t *output, int experts, void *workspace, size_t workspace_bytes, void *stream) {

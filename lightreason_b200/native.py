@@ -88,6 +88,9 @@ _SIGNATURES = {
     "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_ep_unpack": ([_p, _i, _p, _p], _i),
     "moe_ep_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),
+    "moe_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),
+    "moe_shared_expert_workspace_bytes": ([_i, _i], _sz),
+    "moe_shared_expert": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p, _sz, _p], _i),
 }
 
 EXPORTED = tuple(_SIGNATURES)
@@ -476,6 +479,46 @@ def gather_compact_tail(sources, destinations, sizes, prefix_tables, tail, src, 
                                         _ptr(tail), _ptr(src), _ptr(dst), _ptr(count), _ptr(entries), _ptr(resident),
                                         experts, entries.shape[1], banks, _stream(src.device)),
           "moe_gather_compact_tail")
+
+
+# ---------------------------------------------------- combine, shared expert ---
+
+def combine(y, route_pos, scores, *, shared_rows=None, sig=None, out=None):
+    """moe_combine on the current stream: the ordered BF16 combine of route
+    rows y [rows, H] for route_pos / scores [T, K] (+ the gated shared rows)."""
+    for name, t in (("y", y), ("scores", scores)):
+        _bf16_2d(t, name)
+    _table("route_pos", route_pos, torch.int32, 2)
+    tokens, top_k = route_pos.shape
+    _require(tuple(scores.shape) == (tokens, top_k), "scores must be [T, K] like route_pos")
+    _require((shared_rows is None) == (sig is None), "shared_rows and sig go together")
+    hidden = y.shape[1]
+    if out is None:
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=y.device)
+    check(lib().moe_combine(_ptr(y), _ptr(route_pos), _ptr(scores), _ptr(shared_rows), _ptr(sig), tokens, top_k,
+                            hidden, _ptr(out), _stream(y.device)), "moe_combine")
+    return out
+
+
+def shared_expert(x, gate, up, down, gate_w=None):
+    """moe_shared_expert on the current stream: (out [T, H], sig [T] or None)."""
+    for name, t in (("x", x), ("gate", gate), ("up", up), ("down", down)):
+        _bf16_2d(t, name)
+    tokens, hidden = x.shape
+    inner = gate.shape[0]
+    out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=x.device)
+    sig = torch.empty(tokens, dtype=torch.bfloat16, device=x.device) if gate_w is not None else None
+    ws = torch.empty(max(lib().moe_shared_expert_workspace_bytes(tokens, inner), 16), dtype=torch.uint8,
+                     device=x.device)
+    check(lib().moe_shared_expert(_ptr(x), _ptr(gate), _ptr(up), _ptr(down), _ptr(gate_w), tokens, hidden, inner,
+                                  _ptr(out), _ptr(sig), _ptr(ws), ws.numel(), _stream(x.device)),
+          "moe_shared_expert")
+    return out, sig
+
+
+def _bf16_2d(t, name):
+    _require(t.is_cuda and t.dtype == torch.bfloat16 and t.is_contiguous() and t.dim() == 2,
+             f"{name} must be a contiguous CUDA BF16 matrix")
 
 
 # ---------------------------------------------------------------- codecs ---

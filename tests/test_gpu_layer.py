@@ -207,6 +207,36 @@ def test_layer_other_top_k_matches_oracle(dev, case13, top_k, tokens):
     assert_close(out[same], w_out[same], what=f"layer output, top_k {top_k}")
 
 
+@pytest.mark.parametrize("tokens", [1, 16, 100])
+def test_shared_expert_matches_oracle(dev, case13, tokens):
+    """moe_shared_expert (the shared MLP and its sigmoid gate on their own)."""
+    c, w = case13, case13.w
+    x_bits = S.hidden_states(500 + tokens, tokens)
+    out, sig = native.shared_expert(to_dev(x_bits, dev), c.sh[0], c.sh[1], c.sh[2], gate_w=c.sh[3])
+    torch.cuda.synchronize()
+    w_out, w_sig = O.shared_expert(x_bits, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w)
+    assert_close(bits(out), w_out, what="shared expert")
+    assert_close(bits(sig), w_sig, what="shared gate")
+
+
+@pytest.mark.parametrize("tokens,top_k", [(1, 8), (37, 8), (200, 16)])
+def test_combine_matches_oracle(dev, tokens, top_k):
+    """moe_combine on random route rows with the gated shared rows:
+    bit-identical to the oracle's ordered BF16 combine."""
+    rng = np.random.default_rng(tokens * 31 + top_k)
+    idx = np.stack([rng.choice(256, top_k, replace=False) for _ in range(tokens)]).astype(np.int64)
+    _, _, _, rpos = O.permute(idx, 256)
+    rows = int(rpos.max()) + 1
+    y = S.f32_to_bf16_bits(rng.standard_normal((rows, 2048)).astype(np.float32))
+    sc = S.f32_to_bf16_bits(rng.random((tokens, top_k)).astype(np.float32))
+    sh = S.f32_to_bf16_bits(rng.standard_normal((tokens, 2048)).astype(np.float32))
+    sg = S.f32_to_bf16_bits(rng.random(tokens).astype(np.float32))
+    got = native.combine(to_dev(y, dev), torch.from_numpy(np.ascontiguousarray(rpos, dtype=np.int32)).to(dev),
+                         to_dev(sc, dev), shared_rows=to_dev(sh, dev), sig=to_dev(sg, dev))
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(got), O.combine(y, rpos, sc, sh, sg))
+
+
 @pytest.mark.parametrize("name", golden_layers())
 def test_layer_matches_transformers_golden(dev, name):
     g = load_golden(name)
