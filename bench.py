@@ -58,20 +58,22 @@ KERNEL_NAMES = {"router": "router_split_kernel (T <= 16) | router_tc_kernel",
                 "route": "route_decode_kernel (T <= 16) | router_select+permute+grouped_plan kernels",
                 "gather": "stage_experts_kernel", "xs": "gather_tokens_kernel (T > 64)",
                 "experts": "swiglu_grouped_kernel (tcgen05 gate/up + down; + token gather and combine at T <= 64)",
-                "combine": "combine_kernel (T <= 2 and T > 64)", "unused": "-"}
-GEMV_MAX_TOKENS = 2  # the layer's warp-per-row expert path (gate_up_kernel + down_kernel) up to this width
+                "combine": "combine_kernel (T > 64)", "unused": "-"}
+# up to this width the layer runs its experts as one fused_decode_kernel
+# (gate/up, down and the ordered combine in one persistent launch)
+FUSED_DECODE_MAX_TOKENS = 2
 
 
 def kernel_name(stage: str, tokens: int) -> str:
-    if stage == "experts" and tokens <= GEMV_MAX_TOKENS:
-        return "gate_up_kernel + down_kernel (warp-per-row GEMV experts, T <= 2)"
+    if stage == "experts" and tokens <= FUSED_DECODE_MAX_TOKENS:
+        return "fused_decode_kernel (gate/up + down + ordered combine, one persistent launch, T <= 2)"
     return KERNEL_NAMES[stage]
 
 
 def launches_per_step(tokens: int) -> int:
     """Kernels of one moe_layer_forward call with HBM-resident experts."""
-    if tokens <= GEMV_MAX_TOKENS:
-        return 5  # router_split, route_decode, gate_up, down, combine
+    if tokens <= FUSED_DECODE_MAX_TOKENS:
+        return 3  # router_split, route_decode, fused_decode
     if tokens <= 16:
         return 3  # router_split, route_decode, grouped (gathers and combines itself)
     routes = tokens * TOP_K
@@ -83,7 +85,6 @@ def launches_per_step(tokens: int) -> int:
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the dominant kernel, from the ncu captures summarised under profiles/.
 PROFILED_TRAFFIC = {
-    0: (56_680_000, "profiles/launches_layer_config0_T1.md (gate_up_kernel + down_kernel)"),
     1: (454_122_240, "profiles/swiglu_grouped_kernel_T16_config1.md"),
     3: (2_062_540_000, "profiles/launches_layer_config3_T4096.md"),
 }
@@ -423,15 +424,23 @@ def run_ours(args, cfg, world, rank, local):
     routes = tokens * TOP_K
     # algorithmic bytes per launch of each expert kernel (groups = U routed + shared)
     rows = routes + tokens
-    fused = GEMV_MAX_TOKENS < tokens <= 64   # the grouped kernel runs the combine itself at decode widths
+    fused = FUSED_DECODE_MAX_TOKENS < tokens <= 64   # the grouped kernel runs the combine itself at decode widths
     combine_bytes = rows * HIDDEN * 2 + tokens * HIDDEN * 2 + routes * 6
-    algo = {
+    if tokens <= FUSED_DECODE_MAX_TOKENS:
+        # fused_decode_kernel: every selected expert's weights (+ shared) once,
+        # the token rows in, activations out and back in, routes and weights in,
+        # the layer output out (per-route outputs stay in shared memory)
+        expert_algo = [(u + 1) * EXPERT_BYTES + 2 * tokens * HIDDEN * 2 + 2 * rows * INNER * 2 + routes * 6
+                       for u in u_per_step]
+    else:
         # grouped kernel: every selected expert's weights (+ shared) once, the
         # routed token rows in, activations out and back in, per-route outputs
         # out (+ the combine at decode widths: per-route outputs read back, the
         # layer output written)
-        "experts": [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
-                    + (combine_bytes if fused else 0) for u in u_per_step],
+        expert_algo = [(u + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
+                       + (combine_bytes if fused else 0) for u in u_per_step]
+    algo = {
+        "experts": expert_algo,
         "combine": [combine_bytes] * len(used),
         "router": [EXPERTS * HIDDEN * 2 + HIDDEN * 2 + tokens * HIDDEN * 2 + tokens * EXPERTS * 2] * len(used),
     }

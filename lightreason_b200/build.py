@@ -20,7 +20,7 @@ OUT_DIR = PKG / "_native"
 LIB = OUT_DIR / "libmoe_b200.so"
 SOURCES = ["host.cu", "router.cu", "permute.cu", "experts.cu", "layer.cu", "gather.cu", "grouped.cu",
            "expert_rows_noalloc.cu", "expert_parallel.cu", "router_tc.cu", "primary.cu", "ep_p2p.cu",
-           "codec.cu"]
+           "codec.cu", "decode.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

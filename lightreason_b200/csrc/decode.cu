@@ -1,0 +1,441 @@
+// The expert stage of one layer step at the narrowest decode widths, fused:
+// gate/up, the SiLU gate, down and the ordered combine in one persistent
+// kernel, one CTA per SM (modeling_qwen3_5_moe.py:745-750 and :788-790;
+// edge35b/cpu_experts.c:59-68; edge35b/fused_experts.py:27-37).
+//
+// Why one kernel: at T <= 2 the step moves ~57 MB of weights (8 routed experts
+// and the shared one) and nothing else of size, so the time goes to the
+// dependency chain (gate/up -> down -> combine as three launches, each with a
+// grid-completion wait) and to streaming weights through registers.  Here a
+// producer thread per CTA streams the CTA's share of the weights into a
+// shared-memory ring with bulk copies of 16-32 KB (the per-SM copy rate grows
+// with the bytes of each ring handoff), eight consumer warps in two groups of
+// four do the dot products out of the ring, and the only grid-wide wait is the
+// one the math needs: down reads every activation of its group.
+//
+// Work split (the same formula in every CTA, no table): the gate/up rows go to
+// the CTAs as quads (rows 4k..4k+3 of one group's gate and up), evenly, since
+// the grid-wide wait follows them.  The hidden columns are cut into units of 8;
+// CTA c owns units c, c + A, ... (A = CTAs) and computes down rows 8u..8u+7 of
+// EVERY group, so it holds every routed row of its columns and runs the
+// ordered combine for them itself -- no second grid wait and no y round trip
+// through global memory.  Ring items: the CTA's quads (gate rows, then up
+// rows: 16H bytes; warp j of the consumer group that takes the item handles
+// row pair j), then its down chunks (8 rows x I of one group and unit, 16I
+// bytes) four to an item (warp j takes chunk j).  The down chunks enter the
+// ring as the last quads leave it, so at decode widths they are in shared
+// memory by the time the grid-wide wait ends.
+//
+// Phase A (quads): act[row] = bf16(bf16(silu(bf16(gate))) * bf16(up)) per
+// routed token of the group, the eager rounding points; stored to global
+// memory.  Then the CTA publishes (fence + counter) and waits until every CTA
+// has (bounded, 2 s).  Phase B (chunks): every activation row is staged in
+// shared memory once, y[row][col] = bf16(down . act[row]) for each row of the
+// group, kept in shared memory.  Combine: per (token, 8 columns) the routed
+// rows in ascending route position (the order is ranked once per token at
+// start), acc = bf16(acc + bf16(y * w)), then the gated shared row, as the
+// standalone combine kernel does.
+//
+// Every wait is bounded; on timeout the CTA raises the plan's error word,
+// skips the rest of its math, waits (bounded) for its own copies in flight and
+// returns.  All CTAs must be resident at once: the grid is one CTA per SM and
+// the kernel takes most of an SM's shared memory.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.cuh"
+#include "sm100.cuh"
+
+namespace lrb {
+namespace {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = 32 * kConsumerWarps;
+constexpr int kFusedThreads = kConsumers + 32;  // + the producer warp
+constexpr int kSub = 4;                         // warps (row pairs, down chunks) per ring item
+constexpr int kUnit = 8;                        // hidden columns per unit (rows of a down chunk)
+constexpr int kMaxSlots = 32;
+constexpr int kFusedMaxTopK = 16;
+constexpr uint64_t kFusedWaitNs = 2000000000ull;  // 2 s: far beyond any legal wait
+
+struct FusedParams {
+    PlanGroups src;
+    const uint16_t *x;          // [T, H] token rows
+    uint16_t *act;              // [rows, I] activations, phase A -> phase B
+    const int32_t *route_pos;   // [T, K] route position of (token, slot), -1 = dropped
+    const uint16_t *scores;     // [T, K] BF16 routing weights
+    const uint16_t *sig;        // [T] BF16 shared-expert gate, null without a shared expert
+    uint16_t *out;              // [T, H]
+    int tokens, top_k, rows;    // rows = T * K (+ T with a shared expert)
+    int max_groups, slots, units_max;
+};
+
+// Shared-memory layout in bytes, computed the same way on host and device.
+struct FusedLayout {
+    int slot_bytes, ring, xs, acts, ys, grp, tok, pos, spos, wt, swt, bars, total;
+};
+__host__ __device__ inline int fused_align16(int v) { return (v + 15) & ~15; }
+__host__ __device__ inline FusedLayout fused_layout(int slots, int T, int H, int I, int rows, int max_groups, int K,
+                                                    int units_max) {
+    FusedLayout L{};
+    L.slot_bytes = 4 * kSub * H > 16 * kSub * I ? 4 * kSub * H : 16 * kSub * I;
+    int o = 0;
+    L.ring = o;
+    o += slots * L.slot_bytes;
+    L.xs = o;
+    o += fused_align16(T * H * 2);
+    L.acts = o;
+    o += fused_align16(rows * I * 2);
+    L.ys = o;
+    o += fused_align16(units_max * rows * kUnit * 2);
+    L.grp = o;
+    o += fused_align16(max_groups * static_cast<int>(sizeof(GroupedGroup)));
+    L.tok = o;
+    o += fused_align16(rows * 4);
+    L.pos = o;
+    o += fused_align16(T * K * 4);
+    L.spos = o;
+    o += fused_align16(T * K * 4);
+    L.wt = o;
+    o += fused_align16(T * K * 2);
+    L.swt = o;
+    o += fused_align16(T * K * 2);
+    L.bars = o;
+    o += 2 * kMaxSlots * 8 + 16;  // full[], empty[], abort flag, group count
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ uint64_t fused_now() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ bool fused_wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    if (sm100::mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = fused_now();
+    for (uint32_t i = 1;; ++i) {
+        if (sm100::mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if ((i & 63) == 0 && fused_now() - t0 > kFusedWaitNs) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// The consumer warps only (the producer warp leaves early).
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
+
+template <int NW, int NI>
+__global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const FusedParams P) {
+    constexpr int H = NW * 256, I = NI * 256;
+    constexpr int HU = H / 8, IU = I / 8;  // 16-byte units of a row
+    constexpr int QPG = I / kSub;          // quads per group
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int T = P.tokens, K = P.top_k, rows = P.rows, S = P.slots;
+    const FusedLayout L = fused_layout(S, T, H, I, rows, P.max_groups, K, P.units_max);
+    uint8_t *ring = smem + L.ring;
+    uint4 *xs = reinterpret_cast<uint4 *>(smem + L.xs);
+    uint4 *acts = reinterpret_cast<uint4 *>(smem + L.acts);
+    uint16_t *ys = reinterpret_cast<uint16_t *>(smem + L.ys);
+    GroupedGroup *grp = reinterpret_cast<GroupedGroup *>(smem + L.grp);
+    int32_t *tok = reinterpret_cast<int32_t *>(smem + L.tok);
+    int32_t *pos_s = reinterpret_cast<int32_t *>(smem + L.pos);
+    int32_t *spos = reinterpret_cast<int32_t *>(smem + L.spos);
+    uint16_t *wt_s = reinterpret_cast<uint16_t *>(smem + L.wt);
+    uint16_t *swt = reinterpret_cast<uint16_t *>(smem + L.swt);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
+    uint64_t *empty = full + kMaxSlots;
+    volatile int *abort = reinterpret_cast<volatile int *>(empty + kMaxSlots);
+    int *n_groups = reinterpret_cast<int *>(empty + kMaxSlots) + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            sm100::mbar_init(&full[s], 1);
+            sm100::mbar_init(&empty[s], kSub);
+        }
+        *abort = 0;
+        sm100::fence_barrier_init();
+    }
+    grid_dependency_wait();  // the plan and the routes come from the routing kernels
+    grid_dependency_trigger();
+    if (blockIdx.x == 0 && threadIdx.x == 0) P.src.on_start();
+    if (threadIdx.x == 32) *n_groups = P.src.n();
+    for (int g = threadIdx.x; g < P.max_groups; g += blockDim.x) grp[g] = P.src.groups[g];
+    __syncthreads();  // group table in place: the producer can start
+
+    // ---- work split (identical in every thread of every CTA)
+    const int n = min(*n_groups, P.max_groups);
+    const int A = gridDim.x, c = blockIdx.x;
+    constexpr int HW = H / kUnit;  // column units
+    const int my_units = HW / A + (c < HW % A ? 1 : 0);
+    const int64_t quads = static_cast<int64_t>(n) * QPG;
+    const int64_t qa0 = quads * c / A;
+    const int nquads = static_cast<int>(quads * (c + 1) / A - qa0);
+    const int nchunks = my_units * n;  // chunk ci: unit ci / n, group ci % n
+    const int items = nquads + (nchunks + kSub - 1) / kSub;
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------------------------------- producer
+        if (lane == 0) {
+            int issued = 0;
+            for (int it = 0; it < items; ++it) {
+                const int s = it % S;
+                if (it >= S && !fused_wait_bar(&empty[s], ((it / S) - 1) & 1, abort)) break;
+                uint8_t *dst = ring + s * L.slot_bytes;
+                if (it < nquads) {
+                    const int64_t k = qa0 + it;
+                    const Group G = P.src.resolve(grp[k / QPG]);
+                    const size_t r0 = static_cast<size_t>(k % QPG) * kSub;
+                    sm100::mbar_expect_tx(&full[s], 4 * kSub * H);
+                    sm100::bulk_load(dst, G.gate + r0 * H, 2 * kSub * H, &full[s]);
+                    sm100::bulk_load(dst + 2 * kSub * H, G.up + r0 * H, 2 * kSub * H, &full[s]);
+                } else {
+                    const int ci0 = (it - nquads) * kSub, nc = min(kSub, nchunks - ci0);
+                    sm100::mbar_expect_tx(&full[s], nc * 16 * I);
+                    for (int jj = 0; jj < nc; ++jj) {
+                        const int ci = ci0 + jj;
+                        const Group G = P.src.resolve(grp[ci % n]);
+                        const size_t u = c + (ci / n) * A;
+                        sm100::bulk_load(dst + jj * 16 * I, G.down + u * kUnit * I, 16 * I, &full[s]);
+                    }
+                }
+                issued = it + 1;
+            }
+            // Every copy this thread issued lands before the CTA leaves.
+            for (int it = max(0, issued - S); it < issued; ++it) {
+                const uint64_t t0 = fused_now();
+                while (!sm100::mbar_try_wait(&full[it % S], (it / S) & 1) && fused_now() - t0 < kFusedWaitNs) {
+                }
+            }
+        }
+        return;
+    }
+
+    // ----------------------------------- consumers: token rows, route order
+    for (int i = threadIdx.x; i < rows; i += kConsumers) tok[i] = P.src.route_token[i];
+    for (int i = threadIdx.x; i < T * K; i += kConsumers) {
+        const int p = P.route_pos[i];
+        pos_s[i] = (p >= 0 && p < rows) ? p : -1;
+        wt_s[i] = P.scores[i];
+    }
+    for (int i = threadIdx.x; i < T * HU; i += kConsumers) xs[i] = ld_cached(P.x + static_cast<size_t>(i) * 8);
+    consumers_sync();
+    // Each token's routes in ascending position (dropped ones last, ties in
+    // slot order: the stable order of the standalone combine's sort).
+    for (int i = threadIdx.x; i < T * K; i += kConsumers) {
+        const int t = i / K, k = i % K;
+        const unsigned me = static_cast<unsigned>(pos_s[i]);
+        int rank = 0;
+        for (int k2 = 0; k2 < K; ++k2) {
+            const unsigned o = static_cast<unsigned>(pos_s[t * K + k2]);
+            rank += (o < me || (o == me && k2 < k)) ? 1 : 0;
+        }
+        spos[t * K + rank] = pos_s[i];
+        swt[t * K + rank] = wt_s[i];
+    }
+    const int wg = warp / kSub, j = warp % kSub;
+
+    // ------------------------------------------------ phase A: gate/up quads
+    int it = wg;
+    for (; it < nquads; it += kConsumerWarps / kSub) {
+        const int s = it % S;
+        if (!fused_wait_bar(&full[s], (it / S) & 1, abort)) break;
+        const int64_t k = qa0 + it;
+        const GroupedGroup G = grp[k / QPG];
+        const int r = static_cast<int>(k % QPG) * kSub + j;
+        const uint4 *gs = reinterpret_cast<const uint4 *>(ring + s * L.slot_bytes) + j * HU;
+        const uint4 *us = gs + kSub * HU;
+        for (int jj = 0; jj < G.count; ++jj) {
+            const int t = min(max(tok[G.begin + jj], 0), T - 1);
+            const uint4 *xr = xs + t * HU;
+            float ag = 0.f, au = 0.f;
+#pragma unroll
+            for (int i = 0; i < NW; ++i) {
+                const uint4 a = xr[lane + 32 * i];
+                ag = dot8(gs[lane + 32 * i], a, ag);
+                au = dot8(us[lane + 32 * i], a, au);
+            }
+            ag = warp_sum(ag);
+            au = warp_sum(au);
+            if (lane == 0) {
+                const float gv = rbf(ag), uv = rbf(au);
+                const float sv = rbf(silu_f32(gv));
+                P.act[static_cast<size_t>(G.begin + jj) * I + r] = f2bf(sv * uv);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) sm100::mbar_arrive(&empty[s]);
+    }
+
+    // ------------------------------- publish the activations, wait for all
+    consumers_sync();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(&P.src.plan->act_ready, 1);
+        if (!*abort) {
+            const uint64_t t0 = fused_now();
+            while (sm100::ld_acquire(&P.src.plan->act_ready) < A) {
+                if (fused_now() - t0 > kFusedWaitNs) {
+                    *abort = 1;
+                    break;
+                }
+            }
+        }
+    }
+    consumers_sync();
+    if (!*abort) {
+        const uint4 *act16 = reinterpret_cast<const uint4 *>(P.act);
+        for (int i = threadIdx.x; i < rows * IU; i += kConsumers) acts[i] = __ldcg(act16 + i);
+    }
+    consumers_sync();
+
+    // ------------------------------------------- phase B: down chunks -> ys
+    if (!*abort) {
+        for (; it < items; it += kConsumerWarps / kSub) {
+            const int s = it % S;
+            if (!fused_wait_bar(&full[s], (it / S) & 1, abort)) break;
+            const int ci = (it - nquads) * kSub + j, ul = ci / n;
+            const GroupedGroup G = grp[ci % n];
+            const uint4 *ds = reinterpret_cast<const uint4 *>(ring + s * L.slot_bytes) + j * 8 * IU;
+            for (int jj = 0; ci < nchunks && jj < G.count; ++jj) {
+                const int row = G.begin + jj;
+                uint4 a[NI];
+#pragma unroll
+                for (int i = 0; i < NI; ++i) a[i] = acts[row * IU + lane + 32 * i];
+                float acc[8];
+#pragma unroll
+                for (int q8 = 0; q8 < 8; ++q8) {
+                    acc[q8] = 0.f;
+#pragma unroll
+                    for (int i = 0; i < NI; ++i) acc[q8] = dot8(ds[q8 * IU + lane + 32 * i], a[i], acc[q8]);
+                    acc[q8] = warp_sum(acc[q8]);
+                }
+                if (lane < 8) {
+                    float v = acc[0];
+#pragma unroll
+                    for (int q8 = 1; q8 < 8; ++q8)
+                        if (lane == q8) v = acc[q8];
+                    ys[(ul * rows + row) * kUnit + lane] = f2bf(v);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&empty[s]);
+        }
+    }
+    consumers_sync();
+
+    // ---------------------------- ordered combine of my columns, a unit a task
+    if (!*abort) {
+        for (int task = threadIdx.x; task < T * my_units; task += kConsumers) {
+            const int t = task / my_units, ul = task % my_units;
+            const uint4 *yu = reinterpret_cast<const uint4 *>(ys + ul * rows * kUnit);
+            constexpr int kRowU = kUnit / 8;  // uint4 per ys row
+            uint4 o = make_uint4(0, 0, 0, 0);
+            for (int k = 0; k < K; ++k) {
+                const int p = spos[t * K + k];
+                if (p < 0) break;  // dropped routes sort last
+                const uint4 v = yu[p * kRowU];
+                const uint32_t w2 = bf16x2_splat(swt[t * K + k]);
+                o.x = bf16x2_mul_add(o.x, v.x, w2);
+                o.y = bf16x2_mul_add(o.y, v.y, w2);
+                o.z = bf16x2_mul_add(o.z, v.z, w2);
+                o.w = bf16x2_mul_add(o.w, v.w, w2);
+            }
+            if (P.sig) {
+                const uint4 v = yu[(T * K + t) * kRowU];
+                const uint32_t s2 = bf16x2_splat(P.sig[t]);
+                o.x = bf16x2_mul_add(o.x, v.x, s2);
+                o.y = bf16x2_mul_add(o.y, v.y, s2);
+                o.z = bf16x2_mul_add(o.z, v.z, s2);
+                o.w = bf16x2_mul_add(o.w, v.w, s2);
+            }
+            const int col = (c + ul * A) * kUnit;
+            *reinterpret_cast<uint4 *>(P.out + static_cast<size_t>(t) * H + col) = o;
+        }
+    }
+    if (threadIdx.x == 0 && *abort) atomicCAS(&P.src.plan->error, 0, 1);
+}
+
+int smem_optin() {
+    static int v = -1;
+    if (v < 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
+    }
+    return v;
+}
+
+template <int NW, int NI>
+int launch_fused(const FusedParams &p, int smem, cudaStream_t stream) {
+    static bool configured = false;
+    if (!configured) {
+        LRB_CUDA(cudaFuncSetAttribute(fused_decode_kernel<NW, NI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      smem_optin()));
+        configured = true;
+    }
+    return launch_pdl(fused_decode_kernel<NW, NI>, dim3(sm_count()), dim3(kFusedThreads), static_cast<size_t>(smem),
+                      stream, "fused_decode_kernel", p);
+}
+
+template <int NW>
+int launch_fused_i(const FusedParams &p, int inner, int smem, cudaStream_t stream) {
+    switch (inner) {
+        case 256: return launch_fused<NW, 1>(p, smem, stream);
+        case 512: return launch_fused<NW, 2>(p, smem, stream);
+        case 1024: return launch_fused<NW, 4>(p, smem, stream);
+        default: return set_error(MOE_EINVAL, "fused decode: inner %d not in {256, 512, 1024}", inner);
+    }
+}
+
+}  // namespace
+
+bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_groups, bool shared) {
+    if (tokens < 1 || tokens > kFusedDecodeMaxTokens || top_k < 1 || top_k > kFusedMaxTopK) return false;
+    if ((hidden != 1024 && hidden != 2048 && hidden != 4096) || (inner != 256 && inner != 512 && inner != 1024))
+        return false;
+    const int A = sm_count();
+    if (A <= 0) return false;
+    const int rows = tokens * top_k + (shared ? tokens : 0);
+    const int units_max = (hidden / kUnit + A - 1) / A;
+    const FusedLayout L0 = fused_layout(0, tokens, hidden, inner, rows, max_groups, top_k, units_max);
+    const int slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes);
+    return slots >= 4;
+}
+
+int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
+                        const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
+                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream) {
+    if (!fused_decode_fits(tokens, top_k, hidden, inner, max_groups, sig != nullptr))
+        return set_error(MOE_EINVAL, "fused decode: tokens %d / top_k %d / shape %dx%d out of range", tokens, top_k,
+                         hidden, inner);
+    FusedParams p{};
+    p.src = src;
+    p.x = x;
+    p.act = act;
+    p.route_pos = route_pos;
+    p.scores = scores;
+    p.sig = sig;
+    p.out = out;
+    p.tokens = tokens;
+    p.top_k = top_k;
+    p.rows = tokens * top_k + (sig ? tokens : 0);
+    p.max_groups = max_groups;
+    const int A = sm_count();
+    p.units_max = (hidden / kUnit + A - 1) / A;
+    const FusedLayout L0 = fused_layout(0, tokens, hidden, inner, p.rows, max_groups, top_k, p.units_max);
+    p.slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes);
+    const int smem = fused_layout(p.slots, tokens, hidden, inner, p.rows, max_groups, top_k, p.units_max).total;
+    switch (hidden) {
+        case 1024: return launch_fused_i<4>(p, inner, smem, stream);
+        case 2048: return launch_fused_i<8>(p, inner, smem, stream);
+        case 4096: return launch_fused_i<16>(p, inner, smem, stream);
+        default: return set_error(MOE_EINVAL, "fused decode: hidden %d not in {1024, 2048, 4096}", hidden);
+    }
+}
+
+}  // namespace lrb

@@ -50,7 +50,8 @@ struct GroupedGroup {
 };
 struct GroupedPlan {
     int32_t num_groups, items1, items2, items3, work, error, done2_total;
-    int32_t xs_ready;  // epilogue warps that finished the in-kernel token gather
+    int32_t xs_ready;   // epilogue warps that finished the in-kernel token gather
+    int32_t act_ready;  // CTAs of the fused decode kernel that published their activations
 };
 
 // The grouped kernel's plan read as pointer groups, for the warp-per-row
@@ -66,8 +67,8 @@ struct PlanGroups {
     int inner, hidden;
     const int32_t *stage_error;
     __device__ __forceinline__ int n() const { return plan->num_groups; }
-    __device__ __forceinline__ Group get(int g) const {
-        const GroupedGroup G = groups[g];
+    __device__ __forceinline__ Group get(int g) const { return resolve(groups[g]); }
+    __device__ __forceinline__ Group resolve(const GroupedGroup G) const {
         Group r;
         if (G.weight >= 0) {
             r.gate = gate_up + static_cast<int64_t>(G.weight) * gate_up_stride;
@@ -187,5 +188,15 @@ int launch_experts(const Src &src, int max_groups, const uint16_t *x, int hidden
 
 int launch_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, int tokens, int top_k,
                    int hidden, const uint16_t *shared_y, const uint16_t *sig, uint16_t *out, cudaStream_t stream);
+
+// The fused expert stage for T <= kFusedDecodeMaxTokens (csrc/decode.cu):
+// gate/up, down and the ordered combine in one persistent launch over the
+// routing plan.  fused_decode_fits: the shape and widths it takes (its shared
+// memory holds the token rows, every activation row and a ring of weight rows).
+constexpr int kFusedDecodeMaxTokens = 2;
+bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_groups, bool shared);
+int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
+                        const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
+                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream);
 
 }  // namespace lrb

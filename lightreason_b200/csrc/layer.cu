@@ -263,6 +263,14 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     LRB_REQUIRE(staged || (w->gate_up && w->down), "moe_layer_forward: expert banks required");
     const int64_t gu_stride = w->gate_up_stride ? w->gate_up_stride : static_cast<int64_t>(2) * I * H;
     const int64_t dn_stride = w->down_stride ? w->down_stride : static_cast<int64_t>(H) * I;
+    // Rows are read with 16-byte loads, TMA and bulk copies: a misaligned base
+    // is an argument error here rather than a fault on the device.
+    auto a16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    LRB_REQUIRE(a16(x) && a16(out) && a16(w->router) && a16(w->gate_up) && a16(w->down) && a16(w->shared_gate) &&
+                    a16(w->shared_up) && a16(w->shared_down) && a16(w->shared_gate_w) && a16(io->host_gate_up) &&
+                    a16(io->host_down) && a16(io->gate_up_slots) && a16(io->down_slots) && gu_stride % 8 == 0 &&
+                    dn_stride % 8 == 0,
+                "moe_layer_forward: row pointers must be 16-byte aligned and expert strides multiples of 8");
     const Layout L = layout(tokens, E, K, H, I);
     LRB_REQUIRE(workspace && workspace_bytes >= L.total, "moe_layer_forward: workspace %zu < %zu bytes",
                 workspace_bytes, L.total);
@@ -421,11 +429,19 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
                       shared ? w->shared_up : nullptr, shared ? w->shared_down : nullptr, gu_str, dn_str, I, H,
                       counters + 2};
         const int max_groups = std::min(E, R) + (shared ? 1 : 0);
-        if (int rc = launch_experts(pg, max_groups, x, H, I, act, y, s, nullptr)) return rc;
-        if (int rc = mark(5)) return rc;
-        if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,
-                                    shared ? sig : nullptr, out, s))
-            return rc;
+        if (fused_decode_fits(tokens, K, H, I, max_groups, shared)) {
+            if (int rc = launch_fused_decode(pg, max_groups, x, act, route_pos, scores, shared ? sig : nullptr, out,
+                                             tokens, K, H, I, s))
+                return rc;
+            if (int rc = mark(5)) return rc;
+        } else {
+            if (int rc = launch_experts(pg, max_groups, x, H, I, act, y, s, nullptr)) return rc;
+            if (int rc = mark(5)) return rc;
+            if (int rc = launch_combine(y, route_pos, scores, tokens, K, H,
+                                        shared ? y + static_cast<size_t>(R) * H : nullptr, shared ? sig : nullptr, out,
+                                        s))
+                return rc;
+        }
         if (io->status) LRB_CUDA(cudaMemcpyAsync(io->status, &plan->error, sizeof(int32_t), cudaMemcpyDeviceToDevice, s));
         if (int rc = mark(6)) return rc;
         return mark(7);

@@ -81,6 +81,7 @@ __device__ __forceinline__ void plan_block(const PlanArgs &a, int *scratch) {
         if (a.stage_error) *a.stage_error = 0;
         a.plan->done2_total = 0;
         a.plan->xs_ready = 0;
+        a.plan->act_ready = 0;
     }
     __syncthreads();
 }
@@ -185,6 +186,7 @@ __device__ void route_plan_block(IdxOf idx_of, int tokens, int top_k, int expert
         if (a.stage_error) *a.stage_error = 0;
         a.plan->done2_total = 0;
         a.plan->xs_ready = 0;
+        a.plan->act_ready = 0;
     }
     if (a.shared)
         for (int t = threadIdx.x; t < a.tokens; t += blockDim.x) a.route_token[a.routes + t] = t;
