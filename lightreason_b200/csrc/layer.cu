@@ -6,7 +6,8 @@
 // its predecessor.
 //
 // T <= 2: split-K router partials, one CTA that sums them, selects, permutes
-// and plans, then warp-per-row GEMV experts and the combine.  T <= 16: the
+// and plans, then one fused kernel for gate/up, down and the combine (the
+// warp-per-row GEMVs and the combine for shapes it cannot hold).  T <= 16: the
 // same routing, then the grouped kernel, which gathers the token rows and
 // runs the combine itself (so too up to 64 tokens, after the spread-out
 // routing).  Wider calls: tensor-core router, selection, permute and plan as
@@ -40,9 +41,9 @@ struct Layout {
 constexpr int kFusedRoutingMaxTokens = 16;
 bool decode_routing(int tokens, int experts) { return tokens <= kFusedRoutingMaxTokens && experts <= 256; }
 
-// At the narrowest widths the experts run as warp-per-row GEMVs (every warp
-// of the GPU streaming weight rows, no pipeline fill per work item) followed
-// by the standalone combine, instead of the tensor-core grouped kernel.
+// At the narrowest widths the experts run without the tensor-core grouped
+// kernel: as fused_decode_kernel (csrc/decode.cu), or, for shapes it cannot
+// hold in shared memory, as warp-per-row GEMVs and the standalone combine.
 constexpr int kGemvMaxTokens = 2;
 bool gemv_experts(int tokens, bool rows_mode) { return tokens <= kGemvMaxTokens && !rows_mode; }
 
