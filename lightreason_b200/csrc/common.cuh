@@ -34,6 +34,11 @@ __device__ __forceinline__ uint4 ld_stream(const void *p) {
 __device__ __forceinline__ uint4 ld_cached(const void *p) {
     return __ldg(reinterpret_cast<const uint4 *>(p));
 }
+// Ask L2 to fetch [p, p + bytes) from DRAM (no data returns to the SM; p and
+// bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 
 // acc += dot(8 BF16 weights, 8 BF16 activations) in FP32 FMA.
 __device__ __forceinline__ float dot8(uint4 w, uint4 a, float acc) {

@@ -53,6 +53,7 @@ constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = 32 * kConsumerWarps;
 constexpr int kFusedThreads = kConsumers + 32;  // + the producer warp
 constexpr int kSub = 4;                         // warps (row pairs, down chunks) per ring item
+constexpr int kGroups = kConsumerWarps / kSub;  // consumer groups; they take the ring items in turn
 constexpr int kUnit = 8;                        // hidden columns per unit (rows of a down chunk)
 constexpr int kMaxSlots = 32;
 constexpr int kFusedMaxTopK = 16;
@@ -125,6 +126,13 @@ __device__ __forceinline__ bool fused_wait_bar(uint64_t *bar, uint32_t parity, v
     }
 }
 
+// Slice blockIdx.x of gridDim.x of [p, p + bytes) into L2 (bytes % 16 == 0).
+__device__ __forceinline__ void prefetch_slice(const uint16_t *p, size_t bytes) {
+    const size_t per = (bytes / gridDim.x + 15) & ~static_cast<size_t>(15);
+    const size_t off = per * blockIdx.x;
+    if (off < bytes) prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(p) + off, static_cast<uint32_t>(min(per, bytes - off)));
+}
+
 // The consumer warps only (the producer warp leaves early).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 
@@ -159,6 +167,13 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
         }
         *abort = 0;
         sm100::fence_barrier_init();
+    }
+    // The shared expert's rows do not depend on the routing: this CTA's slice
+    // of them goes to L2 while the routing kernels still run.
+    if (threadIdx.x == 64 && P.sig && P.src.sh_gate) {
+        prefetch_slice(P.src.sh_gate, static_cast<size_t>(I) * H * 2);
+        prefetch_slice(P.src.sh_up, static_cast<size_t>(I) * H * 2);
+        prefetch_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
     }
     grid_dependency_wait();  // the plan and the routes come from the routing kernels
     grid_dependency_trigger();
@@ -241,7 +256,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
 
     // ------------------------------------------------ phase A: gate/up quads
     int it = wg;
-    for (; it < nquads; it += kConsumerWarps / kSub) {
+    for (; it < nquads; it += kGroups) {
         const int s = it % S;
         if (!fused_wait_bar(&full[s], (it / S) & 1, abort)) break;
         const int64_t k = qa0 + it;
@@ -295,7 +310,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
 
     // ------------------------------------------- phase B: down chunks -> ys
     if (!*abort) {
-        for (; it < items; it += kConsumerWarps / kSub) {
+        for (; it < items; it += kGroups) {
             const int s = it % S;
             if (!fused_wait_bar(&full[s], (it / S) & 1, abort)) break;
             const int ci = (it - nquads) * kSub + j, ul = ci / n;
@@ -403,7 +418,7 @@ bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_gro
     const int rows = tokens * top_k + (shared ? tokens : 0);
     const int units_max = (hidden / kUnit + A - 1) / A;
     const FusedLayout L0 = fused_layout(0, tokens, hidden, inner, rows, max_groups, top_k, units_max);
-    const int slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes);
+    const int slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes) / kGroups * kGroups;
     return slots >= 4;
 }
 
@@ -428,7 +443,11 @@ int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x
     const int A = sm_count();
     p.units_max = (hidden / kUnit + A - 1) / A;
     const FusedLayout L0 = fused_layout(0, tokens, hidden, inner, p.rows, max_groups, top_k, p.units_max);
-    p.slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes);
+    // A multiple of the consumer groups: slot s then only ever holds the items of
+    // group s % kGroups, which that group consumes in order, so no consumer
+    // waits on a slot phase that another group has not consumed yet (a wait
+    // two phases ahead would pass on the older phase of the same parity).
+    p.slots = std::min(kMaxSlots, (smem_optin() - L0.total) / L0.slot_bytes) / kGroups * kGroups;
     const int smem = fused_layout(p.slots, tokens, hidden, inner, p.rows, max_groups, top_k, p.units_max).total;
     switch (hidden) {
         case 1024: return launch_fused_i<4>(p, inner, smem, stream);
