@@ -39,6 +39,14 @@ __device__ __forceinline__ uint4 ld_cached(const void *p) {
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
+// This CTA's slice (blockIdx.x of gridDim.x) of [p, p + bytes) into L2 (p and
+// bytes multiples of 16).
+__device__ __forceinline__ void prefetch_l2_slice(const void *p, size_t bytes) {
+    const size_t per = (bytes / gridDim.x + 15) & ~static_cast<size_t>(15);
+    const size_t off = per * blockIdx.x;
+    if (off < bytes)
+        prefetch_l2_bulk(static_cast<const uint8_t *>(p) + off, static_cast<uint32_t>(per < bytes - off ? per : bytes - off));
+}
 
 // acc += dot(8 BF16 weights, 8 BF16 activations) in FP32 FMA.
 __device__ __forceinline__ float dot8(uint4 w, uint4 a, float acc) {

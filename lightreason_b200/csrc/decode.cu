@@ -126,13 +126,6 @@ __device__ __forceinline__ bool fused_wait_bar(uint64_t *bar, uint32_t parity, v
     }
 }
 
-// Slice blockIdx.x of gridDim.x of [p, p + bytes) into L2 (bytes % 16 == 0).
-__device__ __forceinline__ void prefetch_slice(const uint16_t *p, size_t bytes) {
-    const size_t per = (bytes / gridDim.x + 15) & ~static_cast<size_t>(15);
-    const size_t off = per * blockIdx.x;
-    if (off < bytes) prefetch_l2_bulk(reinterpret_cast<const uint8_t *>(p) + off, static_cast<uint32_t>(min(per, bytes - off)));
-}
-
 // The consumer warps only (the producer warp leaves early).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 
@@ -171,9 +164,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     // The shared expert's rows do not depend on the routing: this CTA's slice
     // of them goes to L2 while the routing kernels still run.
     if (threadIdx.x == 64 && P.sig && P.src.sh_gate) {
-        prefetch_slice(P.src.sh_gate, static_cast<size_t>(I) * H * 2);
-        prefetch_slice(P.src.sh_up, static_cast<size_t>(I) * H * 2);
-        prefetch_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
+        prefetch_l2_slice(P.src.sh_gate, static_cast<size_t>(I) * H * 2);
+        prefetch_l2_slice(P.src.sh_up, static_cast<size_t>(I) * H * 2);
+        prefetch_l2_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
     }
     grid_dependency_wait();  // the plan and the routes come from the routing kernels
     grid_dependency_trigger();

@@ -97,6 +97,7 @@ struct GroupedParams {
     uint16_t *rows_out;              // [T, H] per-token y rows instead of y (top_k 1), or null
     const int32_t *stage_error;      // host-staging error word, or null
     const uint16_t *x;               // gather_x: token rows [T, H]
+    const uint16_t *sh_gate, *sh_up, *sh_down;  // shared expert rows (null: none), prefetched to L2 at start
     uint16_t *xs;                    // gather_x: route-ordered rows the kernel fills
     int gather_x, gather_need;       // gather in the kernel; epilogue warps that must publish it
     int tokens, top_k, hidden, inner, ks;
@@ -321,6 +322,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         sm100::tmem_alloc(&tail->tmem_base, S::kTmemCols);
         sm100::tmem_relinquish();
+    }
+    // The shared expert's rows do not depend on the routing: this CTA's slice
+    // of them goes to L2 while the routing kernels still run.
+    if (threadIdx.x == 64 && P.sh_gate) {
+        prefetch_l2_slice(P.sh_gate, static_cast<size_t>(P.inner) * P.hidden * 2);
+        prefetch_l2_slice(P.sh_up, static_cast<size_t>(P.inner) * P.hidden * 2);
+        prefetch_l2_slice(P.sh_down, static_cast<size_t>(P.hidden) * P.inner * 2);
     }
     sm100::tc_fence_before();
     __syncthreads();
@@ -892,6 +900,9 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.rows_out = L.rows_out;
     P.stage_error = L.stage_error;
     P.x = L.x;
+    P.sh_gate = L.sh_gate && L.sh_up && L.sh_down ? L.sh_gate : nullptr;
+    P.sh_up = L.sh_up;
+    P.sh_down = L.sh_down;
     P.xs = const_cast<uint16_t *>(L.xs);
     P.gather_x = L.gather_x;
     P.gather_need = 4 * L.ctas;
