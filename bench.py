@@ -66,14 +66,14 @@ FUSED_DECODE_MAX_TOKENS = 2
 
 def kernel_name(stage: str, tokens: int) -> str:
     if stage == "experts" and tokens <= FUSED_DECODE_MAX_TOKENS:
-        return "fused_decode_kernel (gate/up + down + ordered combine, one persistent launch, T <= 2)"
+        return "fused_decode_kernel (routing, gate/up, down, ordered combine in one persistent launch, T <= 2)"
     return KERNEL_NAMES[stage]
 
 
 def launches_per_step(tokens: int) -> int:
     """Kernels of one moe_layer_forward call with HBM-resident experts."""
     if tokens <= FUSED_DECODE_MAX_TOKENS:
-        return 3  # router_split, route_decode, fused_decode
+        return 2  # router_split, fused_decode (which selects and plans in every CTA)
     if tokens <= 16:
         return 3  # router_split, route_decode, grouped (gathers and combines itself)
     routes = tokens * TOP_K
@@ -429,10 +429,10 @@ def run_ours(args, cfg, world, rank, local):
     combine_bytes = rows * HIDDEN * 2 + tokens * HIDDEN * 2 + routes * 6
     if tokens <= FUSED_DECODE_MAX_TOKENS:
         # fused_decode_kernel: every selected expert's weights (+ shared) once,
-        # the token rows in, activations out and back in, routes and weights in,
-        # the layer output out (per-route outputs stay in shared memory)
-        expert_algo = [(u + 1) * EXPERT_BYTES + 2 * tokens * HIDDEN * 2 + 2 * rows * INNER * 2 + routes * 6
-                       for u in u_per_step]
+        # the router partials in, the token rows in, activations out and back
+        # in, the layer output out (per-route outputs stay in shared memory)
+        expert_algo = [(u + 1) * EXPERT_BYTES + 4 * tokens * (EXPERTS + 1) * 4 + 2 * tokens * HIDDEN * 2
+                       + 2 * rows * INNER * 2 for u in u_per_step]
     else:
         # grouped kernel: every selected expert's weights (+ shared) once, the
         # routed token rows in, activations out and back in, per-route outputs

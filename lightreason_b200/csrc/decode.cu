@@ -42,8 +42,11 @@
 // the kernel takes most of an SM's shared memory.
 #include <algorithm>
 
+#include <climits>
+
 #include "common.cuh"
 #include "kernels.cuh"
+#include "routing.cuh"
 #include "sm100.cuh"
 
 namespace lrb {
@@ -65,15 +68,26 @@ struct FusedParams {
     uint16_t *act;              // [rows, I] activations, phase A -> phase B
     const int32_t *route_pos;   // [T, K] route position of (token, slot), -1 = dropped
     const uint16_t *scores;     // [T, K] BF16 routing weights
-    const uint16_t *sig;        // [T] BF16 shared-expert gate, null without a shared expert
+    const uint16_t *sig;        // [T] BF16 shared-expert gate (written here when route != 0)
     uint16_t *out;              // [T, H]
     int tokens, top_k, rows;    // rows = T * K (+ T with a shared expert)
-    int max_groups, slots, units_max;
+    int max_groups, slots, units_max, has_shared;
+    // route != 0: the routing runs in the kernel (every CTA selects from the
+    // router's FP32 partials and plans in shared memory; CTA 0 writes the
+    // routing outputs); route_pos, scores and src's group table are unused.
+    int route, experts;
+    const float *part;          // [4][T][E + 1] router partials (column E: the shared-expert gate)
+    const float *bias;          // [E] selection bias or null
+    uint16_t *logits_out;       // [T, E]
+    int64_t *idx_out;           // [T, K]
+    uint16_t *scores_out;       // [T, K]
+    int32_t *route_pos_out;     // [T, K]
+    int32_t *counters;          // [0] distinct routed experts, [1] dropped routes
 };
 
 // Shared-memory layout in bytes, computed the same way on host and device.
 struct FusedLayout {
-    int slot_bytes, ring, xs, acts, ys, grp, tok, pos, spos, wt, swt, bars, total;
+    int slot_bytes, ring, xs, acts, ys, grp, tok, pos, spos, wt, swt, sig, bars, total;
 };
 __host__ __device__ inline int fused_align16(int v) { return (v + 15) & ~15; }
 __host__ __device__ inline FusedLayout fused_layout(int slots, int T, int H, int I, int rows, int max_groups, int K,
@@ -101,6 +115,8 @@ __host__ __device__ inline FusedLayout fused_layout(int slots, int T, int H, int
     o += fused_align16(T * K * 2);
     L.swt = o;
     o += fused_align16(T * K * 2);
+    L.sig = o;
+    o += fused_align16(T * 2);
     L.bars = o;
     o += 2 * kMaxSlots * 8 + 16;  // full[], empty[], abort flag, group count
     L.total = o;
@@ -126,6 +142,124 @@ __device__ __forceinline__ bool fused_wait_bar(uint64_t *bar, uint32_t parity, v
     }
 }
 
+// Routing for T <= 2 inside the kernel, the arithmetic of route_decode_kernel
+// and route_plan_block (csrc/router.cu, csrc/plan.cuh): logits = bf16(the sum
+// of the K-quarter partials in order), top-k on logits + bias, BF16 weights,
+// the shared-expert gate bf16(sigmoid(bf16 logit)); routes r = k * T + t placed
+// in ascending expert order, stable in r (the eager order); one group per
+// distinct expert in ascending order, the shared expert's group last.  Warp t
+// selects for token t, then warp 0 plans (at most 32 routes: one per lane).
+// Every thread of the CTA calls it; sel holds T * K ints of scratch.
+template <int VPL>
+__device__ __forceinline__ void fused_route(const FusedParams &P, GroupedGroup *grp, int32_t *tok, int32_t *pos_s,
+                                            uint16_t *wt_s, uint16_t *sig_s, int32_t *sel, int *n_groups) {
+    const int T = P.tokens, K = P.top_k, E = P.experts, R = T * K, cols = E + 1;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool out = blockIdx.x == 0;
+    if (warp < T) {
+        const int t = warp;
+        const float *__restrict__ part = P.part;
+        const float *__restrict__ bias = P.bias;
+        // every load of the token first (one L2 round trip), then the sums
+        float p[VPL][kRouterSplit], b[VPL], gp[kRouterSplit];
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            const int e = min(lane + 32 * v, E - 1);
+#pragma unroll
+            for (int k = 0; k < kRouterSplit; ++k) p[v][k] = part[(static_cast<size_t>(k) * T + t) * cols + e];
+            b[v] = bias ? bias[e] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < kRouterSplit; ++k) gp[k] = part[(static_cast<size_t>(k) * T + t) * cols + E];
+        float z[VPL];
+        uint16_t lg[VPL];
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            float sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < kRouterSplit; ++k) sum += p[v][k];
+            lg[v] = f2bf(sum);
+            z[v] = lane + 32 * v < E ? bf2f(lg[v]) + b[v] : -INFINITY;
+        }
+        uint16_t sg = 0;
+        if (P.has_shared) {
+            float sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < kRouterSplit; ++k) sum += gp[k];
+            sg = f2bf(sigmoid_f32(bf2f(f2bf(sum))));
+            if (lane == 0) sig_s[t] = sg;
+        }
+        int e;
+        float w;
+        warp_topk<VPL>([&](int j) { return z[j >> 5]; }, E, K, &e, &w);
+        if (lane < K) {
+            sel[t * K + lane] = e;
+            wt_s[t * K + lane] = f2bf(w);
+        }
+        if (out) {
+#pragma unroll
+            for (int v = 0; v < VPL; ++v)
+                if (lane + 32 * v < E) P.logits_out[static_cast<size_t>(t) * E + lane + 32 * v] = lg[v];
+            if (lane == 0 && P.has_shared) const_cast<uint16_t *>(P.sig)[t] = sg;
+            if (lane < K) {
+                P.idx_out[static_cast<size_t>(t) * K + lane] = e;
+                P.scores_out[static_cast<size_t>(t) * K + lane] = f2bf(w);
+            }
+        }
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int e = INT_MAX, t = 0, k = 0;
+        if (lane < R) {
+            t = lane % T;
+            k = lane / T;
+            e = sel[t * K + k];
+        }
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const bool leader = lane < R && lane == __ffs(peers) - 1;
+        const unsigned leaders = __ballot_sync(0xffffffffu, leader);
+        int p = 0, g = 0;
+        for (int j = 0; j < R; ++j) {
+            const int ej = __shfl_sync(0xffffffffu, e, j);
+            p += (ej < e || (ej == e && j < lane)) ? 1 : 0;
+            g += (((leaders >> j) & 1u) && ej < e) ? 1 : 0;
+        }
+        const int routed = __popc(leaders);
+        if (lane < R) {
+            pos_s[t * K + k] = p;
+            tok[p] = t;
+            if (out) P.route_pos_out[t * K + k] = p;
+        }
+        if (leader) {
+            GroupedGroup G;
+            G.weight = e;
+            G.begin = p;
+            G.count = __popc(peers);
+            G.ntiles = 1;
+            grp[g] = G;
+        }
+        if (P.has_shared && lane < T) tok[R + lane] = lane;
+        if (lane == 0) {
+            int n = routed;
+            if (P.has_shared) {
+                GroupedGroup G;
+                G.weight = -1;
+                G.begin = R;
+                G.count = T;
+                G.ntiles = 1;
+                grp[n++] = G;
+            }
+            *n_groups = n;
+            if (out) {
+                P.counters[0] = routed;
+                P.counters[1] = 0;
+                P.src.plan->num_groups = n;
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // The consumer warps only (the producer warp leaves early).
 __device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory"); }
 
@@ -147,6 +281,7 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     int32_t *spos = reinterpret_cast<int32_t *>(smem + L.spos);
     uint16_t *wt_s = reinterpret_cast<uint16_t *>(smem + L.wt);
     uint16_t *swt = reinterpret_cast<uint16_t *>(smem + L.swt);
+    uint16_t *sig_s = reinterpret_cast<uint16_t *>(smem + L.sig);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
     uint64_t *empty = full + kMaxSlots;
     volatile int *abort = reinterpret_cast<volatile int *>(empty + kMaxSlots);
@@ -163,17 +298,21 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     }
     // The shared expert's rows do not depend on the routing: this CTA's slice
     // of them goes to L2 while the routing kernels still run.
-    if (threadIdx.x == 64 && P.sig && P.src.sh_gate) {
+    if (threadIdx.x == 64 && P.has_shared && P.src.sh_gate) {
         prefetch_l2_slice(P.src.sh_gate, static_cast<size_t>(I) * H * 2);
         prefetch_l2_slice(P.src.sh_up, static_cast<size_t>(I) * H * 2);
         prefetch_l2_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
     }
-    grid_dependency_wait();  // the plan and the routes come from the routing kernels
+    grid_dependency_wait();  // the plan (or the router partials) come from the routing kernels
     grid_dependency_trigger();
-    if (blockIdx.x == 0 && threadIdx.x == 0) P.src.on_start();
-    if (threadIdx.x == 32) *n_groups = P.src.n();
-    for (int g = threadIdx.x; g < P.max_groups; g += blockDim.x) grp[g] = P.src.groups[g];
-    __syncthreads();  // group table in place: the producer can start
+    if (P.route) {
+        fused_route<8>(P, grp, tok, pos_s, wt_s, sig_s, spos, n_groups);  // group table in place
+    } else {
+        if (blockIdx.x == 0 && threadIdx.x == 0) P.src.on_start();
+        if (threadIdx.x == 32) *n_groups = P.src.n();
+        for (int g = threadIdx.x; g < P.max_groups; g += blockDim.x) grp[g] = P.src.groups[g];
+        __syncthreads();  // group table in place: the producer can start
+    }
 
     // ---- work split (identical in every thread of every CTA)
     const int n = min(*n_groups, P.max_groups);
@@ -224,11 +363,15 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     }
 
     // ----------------------------------- consumers: token rows, route order
-    for (int i = threadIdx.x; i < rows; i += kConsumers) tok[i] = P.src.route_token[i];
-    for (int i = threadIdx.x; i < T * K; i += kConsumers) {
-        const int p = P.route_pos[i];
-        pos_s[i] = (p >= 0 && p < rows) ? p : -1;
-        wt_s[i] = P.scores[i];
+    if (!P.route) {
+        for (int i = threadIdx.x; i < rows; i += kConsumers) tok[i] = P.src.route_token[i];
+        for (int i = threadIdx.x; i < T * K; i += kConsumers) {
+            const int p = P.route_pos[i];
+            pos_s[i] = (p >= 0 && p < rows) ? p : -1;
+            wt_s[i] = P.scores[i];
+        }
+        if (P.has_shared)
+            for (int t = threadIdx.x; t < T; t += kConsumers) sig_s[t] = P.sig[t];
     }
     for (int i = threadIdx.x; i < T * HU; i += kConsumers) xs[i] = ld_cached(P.x + static_cast<size_t>(i) * 8);
     consumers_sync();
@@ -353,9 +496,9 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
                 o.z = bf16x2_mul_add(o.z, v.z, w2);
                 o.w = bf16x2_mul_add(o.w, v.w, w2);
             }
-            if (P.sig) {
+            if (P.has_shared) {
                 const uint4 v = yu[(T * K + t) * kRowU];
-                const uint32_t s2 = bf16x2_splat(P.sig[t]);
+                const uint32_t s2 = bf16x2_splat(sig_s[t]);
                 o.x = bf16x2_mul_add(o.x, v.x, s2);
                 o.y = bf16x2_mul_add(o.y, v.y, s2);
                 o.z = bf16x2_mul_add(o.z, v.z, s2);
@@ -417,11 +560,27 @@ bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_gro
 
 int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
                         const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
-                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream) {
+                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream,
+                        const FusedDecodeRoute *route) {
     if (!fused_decode_fits(tokens, top_k, hidden, inner, max_groups, sig != nullptr))
         return set_error(MOE_EINVAL, "fused decode: tokens %d / top_k %d / shape %dx%d out of range", tokens, top_k,
                          hidden, inner);
+    if (route && (!route->part || route->experts < 1 || route->experts > 256 || tokens * top_k > 32 ||
+                  !route->logits || !route->idx || !route->scores || !route->route_pos || !route->counters))
+        return set_error(MOE_EINVAL, "fused decode: in-kernel routing needs partials and outputs, experts <= 256");
     FusedParams p{};
+    if (route) {
+        p.route = 1;
+        p.experts = route->experts;
+        p.part = route->part;
+        p.bias = route->bias;
+        p.logits_out = route->logits;
+        p.idx_out = route->idx;
+        p.scores_out = route->scores;
+        p.route_pos_out = route->route_pos;
+        p.counters = route->counters;
+    }
+    p.has_shared = sig != nullptr ? 1 : 0;
     p.src = src;
     p.x = x;
     p.act = act;

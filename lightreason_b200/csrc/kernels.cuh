@@ -162,8 +162,12 @@ int check_router_args(int tokens, int hidden, int experts, int top_k);
 // that sums them, selects, permutes and plans.
 constexpr int kDecodeMaxTokens = 64;
 constexpr int kRouterSplit = 4;
+// zero_words: n_zero int32 words set to 0 once the previous kernel in the
+// stream is complete (the fused decode kernel's plan words when it routes
+// itself), or null.
 int launch_router_split(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
-                        int experts, float *part, cudaStream_t stream);
+                        int experts, float *part, cudaStream_t stream, int32_t *zero_words = nullptr,
+                        int n_zero = 0);
 struct DecodeRouteArgs {
     const float *part;            // [kRouterSplit][T][E+1] router partials (null with route_in)
     const float *bias;
@@ -193,10 +197,26 @@ int launch_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *
 // gate/up, down and the ordered combine in one persistent launch over the
 // routing plan.  fused_decode_fits: the shape and widths it takes (its shared
 // memory holds the token rows, every activation row and a ring of weight rows).
+// With route != null the kernel also routes (experts <= 256): it reads the
+// router's FP32 partials, selects and plans in every CTA, and writes the
+// routing outputs below (sig then receives the shared-expert gate); the plan
+// words from error to act_ready must have been zeroed after the previous
+// kernel (router_split's zero_words).
 constexpr int kFusedDecodeMaxTokens = 2;
+struct FusedDecodeRoute {
+    const float *part;   // [kRouterSplit][T][E + 1] router partials
+    const float *bias;   // [E] or null
+    int experts;
+    uint16_t *logits;    // [T, E]
+    int64_t *idx;        // [T, K]
+    uint16_t *scores;    // [T, K]
+    int32_t *route_pos;  // [T, K]
+    int32_t *counters;   // [0] distinct routed experts, [1] dropped routes
+};
 bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_groups, bool shared);
 int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
                         const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
-                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream);
+                        int tokens, int top_k, int hidden, int inner, cudaStream_t stream,
+                        const FusedDecodeRoute *route = nullptr);
 
 }  // namespace lrb

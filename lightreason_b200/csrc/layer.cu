@@ -5,14 +5,16 @@
 // kernels use programmatic dependent launch, so each one's prologue overlaps
 // its predecessor.
 //
-// T <= 2: split-K router partials, one CTA that sums them, selects, permutes
-// and plans, then one fused kernel for gate/up, down and the combine (the
+// T <= 2: split-K router partials, then one fused kernel that selects and
+// plans in every CTA and runs gate/up, down and the combine (with host-staged
+// experts or given routes the one-CTA routing kernel plans first; the
 // warp-per-row GEMVs and the combine for shapes it cannot hold).  T <= 16: the
 // same routing, then the grouped kernel, which gathers the token rows and
 // runs the combine itself (so too up to 64 tokens, after the spread-out
 // routing).  Wider calls: tensor-core router, selection, permute and plan as
 // separate kernels, a token gather, the grouped kernel and the combine.
 #include <algorithm>
+#include <cstddef>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -337,12 +339,21 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     const bool gemv = gemv_experts(tokens, rows_mode != 0);
     const bool fused_combine = tokens <= kDecodeMaxTokens && !rows_mode && !gemv;
     pa.combine = fused_combine ? 1 : 0;
+    // At the narrowest widths with HBM-resident experts the fused decode kernel
+    // also routes (every CTA selects and plans from the router partials), so
+    // route_decode_kernel and its launch gap leave the chain; router_split then
+    // zeroes the plan words the fused kernel counts on (error .. act_ready).
+    const int gemv_groups = std::min(E, R) + (shared ? 1 : 0);
+    const bool self_route = gemv && decode && !routed_in && !staged && E <= 256 &&
+                            fused_decode_fits(tokens, K, H, I, gemv_groups, shared);
+    static_assert(offsetof(GroupedPlan, act_ready) == offsetof(GroupedPlan, error) + 3 * sizeof(int32_t),
+                  "plan words error .. act_ready are contiguous");
 
     if (decode) {
         float *rpart = at<float>(ws, L.rpart);
         if (!routed_in) {
             if (int rc = launch_router_split(x, w->router, shared ? w->shared_gate_w : nullptr, tokens, H, E, rpart,
-                                             s))
+                                             s, self_route ? &plan->error : nullptr, self_route ? 4 : 0))
                 return rc;
         }
         if (int rc = mark(1)) return rc;
@@ -365,7 +376,8 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         ra.active = active;
         ra.num_active = counters + 0;
         ra.bad_routes = counters + 1;
-        if (int rc = launch_route_decode(ra, pa, s)) return rc;
+        if (!self_route)
+            if (int rc = launch_route_decode(ra, pa, s)) return rc;
         if (int rc = mark(2)) return rc;
     } else {
         LRB_CUDA(cudaMemsetAsync(counters + 4, 0, sizeof(int32_t), s));
@@ -428,11 +440,13 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     if (gemv) {
         PlanGroups pg{groups, plan, route_token, gu_base, dn_base, shared ? w->shared_gate : nullptr,
                       shared ? w->shared_up : nullptr, shared ? w->shared_down : nullptr, gu_str, dn_str, I, H,
-                      counters + 2};
-        const int max_groups = std::min(E, R) + (shared ? 1 : 0);
+                      self_route ? nullptr : counters + 2};
+        const int max_groups = gemv_groups;
         if (fused_decode_fits(tokens, K, H, I, max_groups, shared)) {
+            const FusedDecodeRoute fr{at<float>(ws, L.rpart), w->router_bias, E, logits, idx, scores, route_pos,
+                                      counters};
             if (int rc = launch_fused_decode(pg, max_groups, x, act, route_pos, scores, shared ? sig : nullptr, out,
-                                             tokens, K, H, I, s))
+                                             tokens, K, H, I, s, self_route ? &fr : nullptr))
                 return rc;
             if (int rc = mark(5)) return rc;
         } else {

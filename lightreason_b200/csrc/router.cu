@@ -152,7 +152,8 @@ template <int NW>
 __global__ void __launch_bounds__(256) router_split_kernel(const uint16_t *__restrict__ x,
                                                            const uint16_t *__restrict__ router,
                                                            const uint16_t *__restrict__ gate_w, int tokens,
-                                                           int experts, float *__restrict__ part) {
+                                                           int experts, float *__restrict__ part,
+                                                           int32_t *__restrict__ zero_words, int n_zero) {
     constexpr int H = NW * 256 * kRouterSplit;
     constexpr int kUnits = NW * 32;                 // 16-byte units of one token's K quarter
     constexpr int kTB = 16;                         // tokens staged per round
@@ -172,6 +173,8 @@ __global__ void __launch_bounds__(256) router_split_kernel(const uint16_t *__res
         for (int i = 0; i < NW; ++i) w[i] = ld_stream(wrow + (lane + 32 * i) * 8);
     }
     grid_dependency_wait();  // x may come from the previous kernel
+    if (zero_words && blockIdx.x == 0 && blockIdx.y == 0 && static_cast<int>(threadIdx.x) < n_zero)
+        zero_words[threadIdx.x] = 0;
     for (int t0 = 0; t0 < tokens; t0 += kTB) {
         const int nt = min(kTB, tokens - t0);
         uint4 v[kPer];
@@ -326,19 +329,19 @@ int launch_router_select(const uint16_t *logits, const float *bias, int tokens, 
 }
 
 int launch_router_split(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
-                        int experts, float *part, cudaStream_t stream) {
+                        int experts, float *part, cudaStream_t stream, int32_t *zero_words, int n_zero) {
     const int rows = experts + (gate_w != nullptr);
     const dim3 grid((rows + 7) / 8, kRouterSplit);
     switch (hidden) {
         case 2048:
             return launch_pdl(router_split_kernel<2>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
-                              gate_w, tokens, experts, part);
+                              gate_w, tokens, experts, part, zero_words, n_zero);
         case 1024:
             return launch_pdl(router_split_kernel<1>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
-                              gate_w, tokens, experts, part);
+                              gate_w, tokens, experts, part, zero_words, n_zero);
         case 4096:
             return launch_pdl(router_split_kernel<4>, grid, dim3(256), 0, stream, "router_split_kernel", x, router,
-                              gate_w, tokens, experts, part);
+                              gate_w, tokens, experts, part, zero_words, n_zero);
         default:
             return set_error(MOE_EINVAL, "router: hidden %d not in {1024, 2048, 4096}", hidden);
     }
