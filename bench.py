@@ -85,7 +85,7 @@ def launches_per_step(tokens: int) -> int:
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the dominant kernel, from the ncu captures summarised under profiles/.
 PROFILED_TRAFFIC = {
-    0: (56_688_000, "profiles/fused_decode_kernel_T1_config0.md"),
+    0: (57_046_528, "profiles/launches_layer_config0_T1.md (fused_decode_kernel)"),
     1: (454_122_240, "profiles/swiglu_grouped_kernel_T16_config1.md"),
     3: (2_062_540_000, "profiles/launches_layer_config3_T4096.md"),
 }
