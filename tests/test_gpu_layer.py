@@ -186,8 +186,9 @@ def test_layer_matches_oracle(dev, case13, tokens):
 @pytest.mark.parametrize("top_k", [4, 16])
 @pytest.mark.parametrize("tokens", [1, 2, 16, 100])
 def test_layer_other_top_k_matches_oracle(dev, case13, top_k, tokens):
-    """top_k other than 8 through every width class: the warp-per-row path
-    (T <= 2), the grouped kernel with its own combine (16), the general
+    """top_k other than 8 through every width class: the fused decode kernel,
+    which also routes (T <= 2; top_k 16 at T = 2 fills its 32-route plan), the
+    grouped kernel with its own combine (16), the general
     routing with the standalone combine (100)."""
     c = case13
     layer = native.Layer(router=c.router, gate_up=c.gu_dev, down=c.dn_dev, bias=c.bias, shared_gate=c.sh[0],
