@@ -36,6 +36,13 @@
 // start), acc = bf16(acc + bf16(y * w)), then the gated shared row, as the
 // standalone combine kernel does.
 //
+// Routing in the kernel (HBM-resident experts, no given routes): every CTA
+// also sums the router's K-quarter partials, selects the top-k of each token
+// and builds the eager-order plan in shared memory (fused_route), so the
+// one-CTA routing kernel and its launch gap leave the chain; CTA 0 writes the
+// ids, weights, logits and shared-expert gate.  Before its grid-dependency wait
+// each CTA also asks L2 for its slice of the shared expert's rows.
+//
 // Every wait is bounded; on timeout the CTA raises the plan's error word,
 // skips the rest of its math, waits (bounded) for its own copies in flight and
 // returns.  All CTAs must be resident at once: the grid is one CTA per SM and
