@@ -60,3 +60,26 @@ def test_workspace_query_is_host_only(so):
     assert 0 < small < big
     # y for T*K + T routes of 2048 BF16 dominates
     assert big >= (4096 * 9) * 2048 * 2
+
+
+def test_layer_rejects_misaligned_rows_before_device_use(so):
+    """Rows are read with 16-byte loads, TMA and bulk copies: a pointer off a
+    16-byte boundary (say, a view that starts mid-row in a BF16 tensor) or an
+    expert stride that is not a multiple of 8 elements is an argument error
+    reported by the call, not a fault on the device."""
+    good, bad = 1 << 20, (1 << 20) + 2
+    ws = native.layer_workspace_bytes(1, 256, 8, 2048, 512)
+
+    def call(x=good, out=good, **fields):
+        w = native.LayerWeights(router=good, gate_up=good, down=good, experts=256, hidden=2048, inner=512,
+                                top_k=8)
+        for k, v in fields.items():
+            setattr(w, k, v)
+        return so.moe_layer_forward(ctypes.byref(w), ctypes.c_void_p(x), 1, ctypes.c_void_p(out), None,
+                                    ctypes.c_void_p(good), ws, None)
+
+    for kwargs in (dict(x=bad), dict(out=bad), dict(gate_up=bad), dict(down=bad), dict(router=bad),
+                   dict(shared_gate=bad, shared_up=good, shared_down=good, shared_gate_w=good, shared_inner=512),
+                   dict(gate_up_stride=2 * 512 * 2048 + 4)):
+        assert call(**kwargs) == native.MOE_EINVAL, kwargs
+        assert b"16-byte aligned" in so.moe_last_error(), kwargs
