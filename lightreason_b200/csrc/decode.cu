@@ -75,7 +75,7 @@ struct FusedParams {
     uint16_t *act;              // [rows, I] activations, phase A -> phase B
     const int32_t *route_pos;   // [T, K] route position of (token, slot), -1 = dropped
     const uint16_t *scores;     // [T, K] BF16 routing weights
-    const uint16_t *sig;        // [T] BF16 shared-expert gate (written here when route != 0)
+    uint16_t *sig;              // [T] BF16 shared-expert gate (written here when route != 0)
     uint16_t *out;              // [T, H]
     int tokens, top_k, rows;    // rows = T * K (+ T with a shared expert)
     int max_groups, slots, units_max, has_shared;
@@ -207,7 +207,7 @@ __device__ __forceinline__ void fused_route(const FusedParams &P, GroupedGroup *
 #pragma unroll
             for (int v = 0; v < VPL; ++v)
                 if (lane + 32 * v < E) P.logits_out[static_cast<size_t>(t) * E + lane + 32 * v] = lg[v];
-            if (lane == 0 && P.has_shared) const_cast<uint16_t *>(P.sig)[t] = sg;
+            if (lane == 0 && P.has_shared) P.sig[t] = sg;
             if (lane < K) {
                 P.idx_out[static_cast<size_t>(t) * K + lane] = e;
                 P.scores_out[static_cast<size_t>(t) * K + lane] = f2bf(w);
@@ -566,7 +566,7 @@ bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_gro
 }
 
 int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
-                        const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
+                        const int32_t *route_pos, const uint16_t *scores, uint16_t *sig, uint16_t *out,
                         int tokens, int top_k, int hidden, int inner, cudaStream_t stream,
                         const FusedDecodeRoute *route) {
     if (!fused_decode_fits(tokens, top_k, hidden, inner, max_groups, sig != nullptr))

@@ -215,7 +215,7 @@ struct FusedDecodeRoute {
 };
 bool fused_decode_fits(int tokens, int top_k, int hidden, int inner, int max_groups, bool shared);
 int launch_fused_decode(const PlanGroups &src, int max_groups, const uint16_t *x, uint16_t *act,
-                        const int32_t *route_pos, const uint16_t *scores, const uint16_t *sig, uint16_t *out,
+                        const int32_t *route_pos, const uint16_t *scores, uint16_t *sig, uint16_t *out,
                         int tokens, int top_k, int hidden, int inner, cudaStream_t stream,
                         const FusedDecodeRoute *route = nullptr);
 
