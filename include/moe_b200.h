@@ -146,7 +146,10 @@ int moe_expert_block_rows(const uint16_t *const *gate_up, const uint16_t *const 
  * instead of a caller workspace.  At most 128 pairs (larger tables are
  * rejected with MOE_EINVAL); token_ids == NULL means one token (expert_rows).
  * The first call on each device looks up the array's device address; make it
- * before any stream capture.  All calls on a device share the array: calls
+ * before any stream capture.  The address is kept for the life of the
+ * process: do not call this entry point again on a device after
+ * cudaDeviceReset (or any reset of its primary context), which would leave
+ * the kept address stale.  All calls on a device share the array: calls
  * that can overlap on the GPU race and must be ordered on one stream. */
 int moe_expert_block_rows_noalloc(const uint16_t *const *gate_up, const uint16_t *const *down,
                                   const uint16_t *input, const int32_t *token_ids,

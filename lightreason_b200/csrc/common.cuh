@@ -98,25 +98,53 @@ int set_error(int status, const char *fmt, ...);
 int cuda_error(cudaError_t err, const char *where);
 int check_launch(const char *where);
 int require_sm100();
+// The opt-in shared-memory limit per block of the current device.
+int smem_optin();
+// Raise `kernel`'s dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute belongs to the (function, device) pair, so
+// it is set once per device that launches the kernel (thread-safe).
+int ensure_dynamic_smem(const void *kernel, int bytes, const char *name);
+template <class... KArgs>
+int ensure_dynamic_smem(void (*kernel)(KArgs...), int bytes, const char *name) {
+    return ensure_dynamic_smem(reinterpret_cast<const void *>(kernel), bytes, name);
+}
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 
 template <class... KArgs, class... Args>
-int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char *name,
-               Args &&...args) {
+int launch_ex(bool cooperative, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+              const char *name, Args &&...args) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = cooperative ? 2 : 1;
     const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
     if (err != cudaSuccess) return cuda_error(err, name);
     return MOE_OK;
+}
+
+template <class... KArgs, class... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const char *name,
+               Args &&...args) {
+    return launch_ex(false, kernel, grid, block, smem, stream, name, std::forward<Args>(args)...);
+}
+
+// As launch_pdl, for a kernel whose CTAs wait on one another: the cooperative
+// attribute makes the launch wait until every CTA of the grid can be resident
+// at once (kernels on other streams may hold SMs), so the wait cannot stall
+// on a CTA that has not been scheduled.
+template <class... KArgs, class... Args>
+int launch_pdl_cooperative(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           const char *name, Args &&...args) {
+    return launch_ex(true, kernel, grid, block, smem, stream, name, std::forward<Args>(args)...);
 }
 
 }  // namespace lrb

@@ -45,8 +45,9 @@
 //
 // Every wait is bounded; on timeout the CTA raises the plan's error word,
 // skips the rest of its math, waits (bounded) for its own copies in flight and
-// returns.  All CTAs must be resident at once: the grid is one CTA per SM and
-// the kernel takes most of an SM's shared memory.
+// returns.  All CTAs must be resident at once: the grid is one CTA per SM,
+// the kernel takes most of an SM's shared memory, and it is launched with the
+// cooperative attribute so that the launch waits until every CTA fits.
 #include <algorithm>
 
 #include <climits>
@@ -518,26 +519,12 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     if (threadIdx.x == 0 && *abort) atomicCAS(&P.src.plan->error, 0, 1);
 }
 
-int smem_optin() {
-    static int v = -1;
-    if (v < 0) {
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess) return 0;
-        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) v = 0;
-    }
-    return v;
-}
-
 template <int NW, int NI>
 int launch_fused(const FusedParams &p, int smem, cudaStream_t stream) {
-    static bool configured = false;
-    if (!configured) {
-        LRB_CUDA(cudaFuncSetAttribute(fused_decode_kernel<NW, NI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      smem_optin()));
-        configured = true;
-    }
-    return launch_pdl(fused_decode_kernel<NW, NI>, dim3(sm_count()), dim3(kFusedThreads), static_cast<size_t>(smem),
-                      stream, "fused_decode_kernel", p);
+    if (int rc = ensure_dynamic_smem(fused_decode_kernel<NW, NI>, smem_optin(), "cudaFuncSetAttribute(fused_decode)"))
+        return rc;
+    return launch_pdl_cooperative(fused_decode_kernel<NW, NI>, dim3(sm_count()), dim3(kFusedThreads),
+                                  static_cast<size_t>(smem), stream, "fused_decode_kernel", p);
 }
 
 template <int NW>

@@ -21,6 +21,9 @@
 // with cudaGetSymbolAddress once per device, with that device current, the
 // first time this entry point runs on it; later calls reuse the cached
 // address.  Make that first call on each device before any stream capture.
+// The cached address lives as long as the process: after cudaDeviceReset (or
+// any reset of the device's primary context) the module is loaded again at a
+// new address, so this entry point must not be used on that device again.
 //
 // Sharing: all calls on a device use the same array, and it keeps whatever the
 // last call left in it.  Nothing in it has to start at zero: within one call,
@@ -72,14 +75,13 @@ extern "C" int moe_expert_block_rows_noalloc(const uint16_t *const *gate_up, con
                 "moe_expert_block_rows_noalloc: %d pairs exceed the built-in scratch of %d pairs (%zu bytes); "
                 "use moe_expert_block_rows with a workspace",
                 experts, kMaxPairs, kScratchBytes);
+    LRB_REQUIRE(token_ids != nullptr || tokens == 1,
+                "moe_expert_block_rows_noalloc: token_ids may be NULL only for one token");
     if (experts == 0) return MOE_OK;
     void *scratch = nullptr;
     if (int rc = lrb::require_sm100()) return rc;
     if (int rc = scratch_address(&scratch)) return rc;
-    if (!token_ids) {
-        LRB_REQUIRE(tokens == 1, "moe_expert_block_rows_noalloc: token_ids may be NULL only for one token");
-        return moe_expert_rows(gate_up, down, input, output, experts, scratch, kScratchBytes, stream);
-    }
+    if (!token_ids) return moe_expert_rows(gate_up, down, input, output, experts, scratch, kScratchBytes, stream);
     return moe_expert_block_rows(gate_up, down, input, token_ids, output, tokens, experts, scratch, kScratchBytes,
                                  stream);
 }

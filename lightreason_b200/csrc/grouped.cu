@@ -872,13 +872,7 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
         if (int rc = make_map_bf16(&am, L.act, 2, dims, str, BN)) return rc;
         if (int rc = make_map_bf16(&am16, L.act, 2, dims, str, 16)) return rc;
     }
-    static std::once_flag once;
-    static cudaError_t attr_err = cudaSuccess;
-    std::call_once(once, [] {
-        attr_err = cudaFuncSetAttribute(swiglu_grouped_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        S::kSmem);
-    });
-    if (attr_err != cudaSuccess) return cuda_error(attr_err, "cudaFuncSetAttribute(grouped)");
+    if (int rc = ensure_dynamic_smem(swiglu_grouped_kernel<BN>, S::kSmem, "cudaFuncSetAttribute(grouped)")) return rc;
     GroupedParams P{};
     P.groups = L.groups;
     P.plan = L.plan;

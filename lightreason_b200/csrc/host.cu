@@ -1,6 +1,8 @@
 // Status reporting, device checks and host-memory mapping for the C ABI.
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -37,6 +39,37 @@ int sm_count() {
         cached[device] = n > 0 ? n : 148;
     }
     return cached[device];
+}
+
+int smem_optin() {
+    static int cached[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 0;
+    if (!cached[device]) {
+        int v = 0;
+        if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess) return 0;
+        cached[device] = v;
+    }
+    return cached[device];
+}
+
+int ensure_dynamic_smem(const void *kernel, int bytes, const char *name) {
+    struct Entry {
+        const void *kernel;
+        int device;
+        int bytes;
+    };
+    static std::mutex mu;
+    static std::vector<Entry> done;
+    int device = 0;
+    LRB_CUDA(cudaGetDevice(&device));
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry &e : done)
+        if (e.kernel == kernel && e.device == device && e.bytes >= bytes) return MOE_OK;
+    const cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err != cudaSuccess) return cuda_error(err, name);
+    done.push_back({kernel, device, bytes});
+    return MOE_OK;
 }
 
 int require_sm100() {

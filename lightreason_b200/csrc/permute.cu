@@ -212,14 +212,11 @@ int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32
         const int ctas = (chunks + kWarpsPerCta - 1) / kWarpsPerCta;
         const size_t smem = sizeof(int32_t) * kWarpsPerCta * experts;
         if (smem > 48 * 1024) {
-            static bool wide = false;
-            if (!wide) {
-                LRB_CUDA(cudaFuncSetAttribute(permute_count_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(sizeof(int32_t) * kWarpsPerCta * 1024)));
-                LRB_CUDA(cudaFuncSetAttribute(permute_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                              static_cast<int>(sizeof(int32_t) * kWarpsPerCta * 1024)));
-                wide = true;
-            }
+            const int most = static_cast<int>(sizeof(int32_t) * kWarpsPerCta * 1024);
+            if (int rc = ensure_dynamic_smem(permute_count_kernel, most, "cudaFuncSetAttribute(permute_count)"))
+                return rc;
+            if (int rc = ensure_dynamic_smem(permute_place_kernel, most, "cudaFuncSetAttribute(permute_place)"))
+                return rc;
         }
         if (int rc = launch_pdl(permute_count_kernel, dim3(ctas), dim3(256), smem, stream, "permute_count_kernel", idx,
                                 tokens, top_k, experts, chunks, hist))
@@ -233,12 +230,8 @@ int launch_permute(const int64_t *idx, int tokens, int top_k, int experts, int32
                           tokens, top_k, experts, chunks, hist, offsets, perm_token, perm_slot, route_pos);
     }
     const int smem = permute_smem_bytes(32, experts);
-    static bool configured = false;
-    if (!configured) {
-        LRB_CUDA(cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      permute_smem_bytes(32, 1024)));
-        configured = true;
-    }
+    if (int rc = ensure_dynamic_smem(permute_kernel, permute_smem_bytes(32, 1024), "cudaFuncSetAttribute(permute)"))
+        return rc;
     permute_kernel<<<1, 1024, smem, stream>>>(idx, tokens, top_k, experts, offsets, perm_token, perm_slot, route_pos,
                                                active, num_active, bad_routes);
     LRB_LAUNCHED("permute_kernel");

@@ -355,13 +355,12 @@ int route_decode_smem(int tokens, int experts, int top_k) {
 int launch_route_decode(const DecodeRouteArgs &r, const PlanArgs &plan, cudaStream_t stream) {
     LRB_REQUIRE(r.tokens <= kDecodeMaxTokens, "route_decode: tokens %d > %d", r.tokens, kDecodeMaxTokens);
     const int smem = route_decode_smem(r.tokens, r.experts, r.top_k);
-    static bool configured[2] = {false, false};
     const int v = r.experts <= 256 ? 0 : 1;
-    if (!configured[v]) {
+    {
         const int most = route_decode_smem(kDecodeMaxTokens, v ? 1024 : 256, 32);
-        if (v == 0) LRB_CUDA(cudaFuncSetAttribute(route_decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
-        else LRB_CUDA(cudaFuncSetAttribute(route_decode_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
-        configured[v] = true;
+        const int rc = v == 0 ? ensure_dynamic_smem(route_decode_kernel<8>, most, "cudaFuncSetAttribute(route_decode)")
+                              : ensure_dynamic_smem(route_decode_kernel<32>, most, "cudaFuncSetAttribute(route_decode)");
+        if (rc) return rc;
     }
     if (v == 0)
         return launch_pdl(route_decode_kernel<8>, dim3(1), dim3(1024), smem, stream, "route_decode_kernel", r, plan);

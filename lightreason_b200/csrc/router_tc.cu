@@ -187,11 +187,7 @@ int launch_router_tc_bn(const uint16_t *x, const uint16_t *router, int tokens, i
         const uint64_t str[1] = {static_cast<uint64_t>(hidden) * 2};
         if (int rc = make_map_bf16(&tx, x, 2, dims, str, BN)) return rc;
     }
-    static bool configured = false;
-    if (!configured) {
-        LRB_CUDA(cudaFuncSetAttribute(router_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem));
-        configured = true;
-    }
+    if (int rc = ensure_dynamic_smem(router_tc_kernel<BN>, kSmem, "cudaFuncSetAttribute(router_tc)")) return rc;
     const dim3 grid((experts + kRows - 1) / kRows, (tokens + BN - 1) / BN, part ? ks : 1);
     return launch_pdl(router_tc_kernel<BN>, grid, dim3(128), kSmem, stream, "router_tc_kernel", tw, tx, tokens,
                       experts, hidden, logits, part, error);

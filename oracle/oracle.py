@@ -31,7 +31,8 @@ _i64 = ctypes.c_int64
 def build() -> None:
     """Compile the checker (and the reference's CPU code when its tree is mounted)."""
     subprocess.run(["make", "-s", "-C", str(HERE), "oracle"], check=True)
-    root = os.environ.get("REFERENCE_ROOT", "/root/reference")
+    # the reference checkout: REFERENCE_ROOT, else a sibling of this repository
+    root = os.environ.get("REFERENCE_ROOT", str(HERE.parent.parent / "reference"))
     if Path(root, "edge35b", "cpu_experts.c").exists():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REFERENCE_ROOT={root}"], check=True)
 

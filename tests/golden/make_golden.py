@@ -1,7 +1,8 @@
 """Generate the golden fixtures in tests/golden/ from the reference itself.
 
-Run where the reference tree is mounted (REFERENCE_ROOT, default the mount
-point of this build) after `make -C oracle ref`:
+Run where the reference tree is checked out (REFERENCE_ROOT, default a
+sibling directory `reference` next to this repository) after
+`make -C oracle ref`:
 
     python tests/golden/make_golden.py
 
@@ -108,7 +109,7 @@ def make_layer(tokens: int, seed: int, bias_kind: str) -> None:
 
 
 def _reference_modules():
-    root = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
+    root = Path(os.environ.get("REFERENCE_ROOT", str(ROOT.parent / "reference")))
     sys.path.insert(0, str(root))
     so = ctypes.CDLL(str(ROOT / "oracle" / "_ref" / "libref_tiles.so"))
     so.ref_pack_cpu_read_tiles.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_size_t]

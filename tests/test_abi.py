@@ -54,6 +54,17 @@ def test_argument_checks_precede_device_use(so):
     assert so.moe_expert_rows(None, None, None, None, 129, None, 0, None) == native.MOE_EINVAL
 
 
+def test_noalloc_argument_checks_precede_device_use(so):
+    """The allocation-free expert rows refuse a table beyond their built-in
+    128-pair array, and NULL token ids with more than one token, before any
+    device call."""
+    fake = ctypes.c_void_p(16)
+    assert so.moe_expert_block_rows_noalloc(fake, fake, fake, fake, fake, 1, 129, None) == native.MOE_EINVAL
+    assert b"built-in scratch" in so.moe_last_error()
+    assert so.moe_expert_block_rows_noalloc(fake, fake, fake, None, fake, 2, 8, None) == native.MOE_EINVAL
+    assert b"token_ids may be NULL only for one token" in so.moe_last_error()
+
+
 def test_workspace_query_is_host_only(so):
     small = native.layer_workspace_bytes(1, 256, 8, 2048, 512)
     big = native.layer_workspace_bytes(4096, 256, 8, 2048, 512)

@@ -5,10 +5,13 @@ and may not allocate device memory themselves (a native worker standing in for
 the reference's cpu_experts.c call, or a server that forbids allocation while
 it runs): its intermediate activations live in a fixed array inside the
 library.  This file checks it, through the C ABI, against the workspace entry
-point moe_expert_block_rows on two calls in a row -- the second call finds the
-first call's leftovers in the shared array -- and checks that tables larger
-than the built-in array are refused.  It is collected last and sets itself up,
-so it passes alone in a fresh process as well as after the other tests.
+point moe_expert_block_rows on consecutive calls -- each later call finds the
+earlier call's leftovers in the shared array -- including a table of exactly
+128 pairs, which fills the array to its last byte.  Both entry points run the
+same kernels in the same order, so the outputs must be bit-identical.  Tables
+larger than the built-in array are refused.  It is collected last and sets
+itself up, so it passes alone in a fresh process as well as after the other
+tests.
 """
 
 from __future__ import annotations
@@ -21,7 +24,6 @@ import torch
 
 from lightreason_b200 import build, native
 from lightreason_b200 import synthetic as S
-from tests.helpers import assert_close
 
 pytestmark = pytest.mark.gpu
 
@@ -57,8 +59,9 @@ def test_noalloc_rows_match_workspace_entry_point_on_consecutive_calls():
     w.ensure(experts)
     gu_dev = {e: _dev(w.gate_up[e], dev) for e in experts}
     dn_dev = {e: _dev(w.down[e], dev) for e in experts}
-    # two calls in a row with different tables: 24 pairs over 5 tokens, then 9 pairs over 3
-    for call, (pairs, tokens) in enumerate(((24, 5), (9, 3))):
+    # calls in a row with different tables: 24 pairs over 5 tokens, 9 pairs
+    # over 3, then the largest table (128 pairs over 16 tokens, the whole array)
+    for call, (pairs, tokens) in enumerate(((24, 5), (9, 3), (128, 16))):
         pair_experts = rng.choice(experts, size=pairs)
         token_ids = rng.integers(0, tokens, size=pairs).tolist()
         gu = [gu_dev[e] for e in pair_experts]
@@ -68,7 +71,7 @@ def test_noalloc_rows_match_workspace_entry_point_on_consecutive_calls():
         got = torch.full_like(want, 7.0)
         _noalloc(lib, gu, dn, x, token_ids, got)
         torch.cuda.synchronize()
-        assert_close(_bits(got), _bits(want), what=f"noalloc call {call}")
+        assert np.array_equal(_bits(got), _bits(want)), f"noalloc call {call}: output differs from the workspace path"
     # one token, no token ids: the expert_rows form
     gu = [gu_dev[e] for e in experts]
     dn = [dn_dev[e] for e in experts]
@@ -77,7 +80,7 @@ def test_noalloc_rows_match_workspace_entry_point_on_consecutive_calls():
     got = torch.empty_like(want)
     _noalloc(lib, gu, dn, x1, None, got)
     torch.cuda.synchronize()
-    assert_close(_bits(got), _bits(want), what="noalloc expert_rows form")
+    assert np.array_equal(_bits(got), _bits(want)), "noalloc expert_rows form differs from the workspace path"
 
 
 def test_noalloc_rejects_tables_beyond_its_scratch():
