@@ -352,6 +352,17 @@ int moe_gather_compact_tail(const int64_t *sources, const int64_t *destinations,
  *   exponent when the tile's exponents span at most 8 (else 255, raw, its 384
  *   packed bytes zeroed); packed + 384 t = 256 low bytes + 128 bytes of 4-bit
  *   codes.  *encoded (device uint64, not cleared) += tiles encoded.
+ * moe_tilecodec_compact replaces the compact-row assembly of
+ *   edge35b/gpu_resident_experts.py:22-42 encode (after pack_cpu_read_tiles):
+ *   for `rows` rows of tiles_per_row tiles each (raw [rows][tiles*256],
+ *   packed / bases from moe_tilecodec_pack of the same rows), a row r with
+ *   data_offsets[r] >= 0 gets at arena + data_offsets[r] its tiles back to
+ *   back -- 384 packed bytes per encoded tile, the 512 source bytes of a raw
+ *   one -- and at arena + header_offsets[r] one uint32 per tile, (raw tiles
+ *   before it << 8) | base; sizes[r] = its data bytes.  A row whose data or
+ *   headers would leave [0, arena_bytes) or start off a 16-byte boundary gets
+ *   sizes[r] = -1 and is not written; data_offsets[r] < 0 skips the row
+ *   (sizes[r] = 0).  data_offsets, header_offsets, sizes: device int64 [rows].
  * ------------------------------------------------------------------------ */
 size_t moe_rowcodec_workspace_bytes(int rows, int64_t n);
 int moe_rowcodec_plan(const uint16_t *bank, int rows, int64_t n, int64_t *meta, int64_t *total, void *workspace,
@@ -360,6 +371,9 @@ int moe_rowcodec_pack(const uint16_t *bank, int rows, int64_t n, const int64_t *
                       void *workspace, size_t workspace_bytes, void *stream);
 int moe_tilecodec_pack(const uint16_t *raw, int64_t tiles, uint8_t *packed, uint8_t *bases,
                        unsigned long long *encoded, void *stream);
+int moe_tilecodec_compact(const uint16_t *raw, const uint8_t *packed, const uint8_t *bases, int rows,
+                          int64_t tiles_per_row, uint8_t *arena, int64_t arena_bytes, const int64_t *data_offsets,
+                          const int64_t *header_offsets, int64_t *sizes, void *stream);
 
 /* ------------------------------------------------------------------------
  * Expert parallelism (no counterpart in the reference, which runs its MoE

@@ -51,18 +51,19 @@ def row_bytes(n: int, escapes: int) -> int:
 
 
 def pack_row(bits, base: int, escapes: int, output: np.ndarray) -> None:
+    """Write one row's packed bytes into `output` (exactly row_bytes long)."""
     bits = _flat_bits(bits)
     n = bits.size
-    exponent = ((bits >> 7) & 0xFF).astype(np.int32) - base
-    outside = np.flatnonzero((exponent < 0) | (exponent >= WINDOW))
-    if outside.size != escapes or output.size != row_bytes(n, escapes):
+    delta = ((bits >> 7) & 0xFF).astype(np.int32) - base
+    # a delta outside [0, 16) has bits above the low nibble (negative ones too)
+    escaped = np.flatnonzero(delta & ~0xF)
+    if escaped.size != escapes or output.size != row_bytes(n, escapes):
         raise ValueError("BF16 row disagrees with its packed layout")
-    nib = (exponent & 0xF).astype(np.uint8)
-    output[:n] = ((bits >> 8) & 0x80).astype(np.uint8) | (bits & 0x7F).astype(np.uint8)
-    output[n:3 * n // 2] = nib[0::2] | (nib[1::2] << 4)
-    tail = output[3 * n // 2:]
-    tail[:4 * escapes].view("<i4")[:] = outside.astype(np.int32)
-    tail[4 * escapes:].view("<u2")[:] = bits[outside]
+    sign_fraction = ((bits >> 8) & 0x80 | bits & 0x7F).astype(np.uint8)
+    pairs = (delta & 0xF).astype(np.uint8).reshape(-1, 2)
+    nibbles = pairs[:, 0] | (pairs[:, 1] << 4)
+    output[:] = np.concatenate((sign_fraction, nibbles, escaped.astype("<i4").view(np.uint8),
+                                bits[escaped].astype("<u2").view(np.uint8)))
 
 
 def restore_row(packed: np.ndarray, n: int, base: int, escapes: int) -> np.ndarray:
@@ -80,48 +81,78 @@ def restore_row(packed: np.ndarray, n: int, base: int, escapes: int) -> np.ndarr
 
 
 def pack_verified_row(row, output, base: int, escapes: int) -> None:
+    """pack_row, then decode the bytes again and require the original bits (the
+    reference's audit; no 1% rule here)."""
     pack_row(row, base, escapes, output)
-    if not np.array_equal(_flat_bits(row), restore_row(output, _flat_bits(row).size, base, escapes)):
+    bits = _flat_bits(row)
+    if not np.array_equal(restore_row(output, bits.size, base, escapes), bits):
         raise RuntimeError("Packed expert did not round-trip to the original BF16 bits")
+
+
+def _bank_rows(bits) -> np.ndarray:
+    a = np.asarray(bits)
+    if a.dtype != np.uint16:
+        a = a.view(np.uint16)
+    return a.reshape(a.shape[0], -1)
+
+
+def _bank_windows(rows: np.ndarray, *, check=None, threads: int = 1):
+    """(bases, escapes) int64 arrays for every row of a bank [E, n]: exponent
+    histograms per row (check() runs before each row's), then the 16-exponent
+    window sums of all rows at once from the cumulative histograms."""
+    if rows.shape[1] % 8 or not 0 < rows.shape[1] < 2 ** 31:
+        raise ValueError("Expected a flat BF16 bit array whose length is a positive multiple of 8")
+
+    def hist(row):
+        if check is not None:
+            check()
+        return np.bincount((row >> 7) & 0xFF, minlength=256)
+
+    if threads > 1 and len(rows) > 1:
+        with ThreadPoolExecutor(threads) as pool:
+            hists = np.stack(list(pool.map(hist, rows)))
+    else:
+        hists = np.stack([hist(r) for r in rows]) if len(rows) else np.zeros((0, 256), np.int64)
+    cum = np.zeros((len(rows), 257), dtype=np.int64)
+    np.cumsum(hists, axis=1, out=cum[:, 1:])
+    inside = cum[:, WINDOW:] - cum[:, :-WINDOW]             # [E, 241]
+    bases = inside.argmax(axis=1)                            # first maximum wins
+    escapes = rows.shape[1] - np.take_along_axis(inside, bases[:, None], axis=1)[:, 0]
+    return bases.astype(np.int64), escapes.astype(np.int64)
+
+
+def _layout(n: int, bases: np.ndarray, escapes: np.ndarray):
+    """Plan rows from the windows: a row with escapes above 1% of n stays raw
+    (None); packed rows follow each other at 16-byte-aligned offsets."""
+    packed = escapes * 100 <= n
+    span = np.where(packed, (row_bytes(n, 0) + 6 * escapes + ALIGN - 1) // ALIGN * ALIGN, 0)
+    offsets = np.zeros(len(span), dtype=np.int64)
+    np.cumsum(span[:-1], out=offsets[1:])
+    rows = [(int(o), int(b), int(e)) if p else None for o, b, e, p in zip(offsets, bases, escapes, packed)]
+    return rows, int(span.sum())
 
 
 def plan_bank(bits, *, check=None):
     """Rows of a bank [E, ...]: (offset, base, escapes), or None for a row kept
-    raw (escapes above 1% of its values); offsets aligned to 16 bytes."""
-    rows, size = [], 0
-    for row in np.asarray(bits).reshape(len(bits), -1):
-        if check is not None:
-            check()
-        base, escapes = exponent_window(row)
-        if escapes * 100 > row.size:
-            rows.append(None)
-            continue
-        rows.append((size, base, escapes))
-        size = (size + row_bytes(row.size, escapes) + ALIGN - 1) & ~(ALIGN - 1)
-    return rows, size
+    raw (escapes above 1% of its values); offsets aligned to 16 bytes.
+    check() (e.g. a cancellation hook) runs once per row."""
+    rows = _bank_rows(bits)
+    return _layout(rows.shape[1], *_bank_windows(rows, check=check))
 
 
 def pack_bank(bank: np.ndarray, *, threads: int = 0):
     """Pack a whole bank [E, ...] (uint16 BF16 bits).  Returns (packed uint8
     buffer, plan rows as in plan_bank).  Every packed row is verified."""
-    bank = np.ascontiguousarray(bank)
-    flat = bank.reshape(bank.shape[0], -1).view(np.uint16)
-    with ThreadPoolExecutor(threads or min(32, os.cpu_count() or 1)) as pool:
-        windows = list(pool.map(exponent_window, flat))
-    rows, size = [], 0
-    for (base, escapes), row in zip(windows, flat):
-        if escapes * 100 > row.size:
-            rows.append(None)
-            continue
-        rows.append((size, base, escapes))
-        size = (size + row_bytes(row.size, escapes) + ALIGN - 1) & ~(ALIGN - 1)
+    rows = _bank_rows(np.ascontiguousarray(bank))
+    workers = threads or min(32, os.cpu_count() or 1)
+    plan, size = _layout(rows.shape[1], *_bank_windows(rows, threads=workers))
     out = np.zeros(max(size, ALIGN), dtype=np.uint8)
+    todo = [(e, p) for e, p in enumerate(plan) if p is not None]
 
-    def fill(e):
-        if rows[e] is not None:
-            off, base, escapes = rows[e]
-            pack_verified_row(flat[e], out[off:off + row_bytes(flat.shape[1], escapes)], base, escapes)
+    def fill(item):
+        e, (off, base, escapes) = item
+        pack_verified_row(rows[e], out[off:off + row_bytes(rows.shape[1], escapes)], base, escapes)
 
-    with ThreadPoolExecutor(threads or min(32, os.cpu_count() or 1)) as pool:
-        list(pool.map(fill, range(len(rows))))
-    return out, rows
+    with ThreadPoolExecutor(workers) as pool:
+        list(pool.map(fill, todo))
+    return out, plan

@@ -235,6 +235,87 @@ __global__ void __launch_bounds__(256) tilecodec_pack_kernel(const uint16_t *__r
     if (threadIdx.x == 0 && count) atomicAdd(encoded, static_cast<unsigned long long>(count));
 }
 
+// Compact rows of the resident tile codec.  In a compact row, tile t starts at
+// byte 384 t + 128 p(t), p(t) = raw tiles (base 255) before t: every tile
+// takes its 384 packed bytes, and a raw tile 128 more (its 512 source bytes).
+// So the only state that crosses tiles is that running count.  One CTA per
+// row: a first pass counts the row's raw tiles and checks that the row fits
+// the arena at its offsets (else sizes[r] = -1 and nothing is written); then
+// chunks of 1024 tiles are scanned (ballot + warp scan) into p(t), each tile's
+// header (p(t) << 8) | base is written, and the warps copy the tiles with
+// 16-byte stores (an encoded tile from `packed`, a raw one from `raw`).
+__global__ void __launch_bounds__(1024) tilecodec_compact_kernel(const uint16_t *__restrict__ raw,
+                                                                 const uint8_t *__restrict__ packed,
+                                                                 const uint8_t *__restrict__ bases,
+                                                                 int64_t tiles_per_row, uint8_t *__restrict__ arena,
+                                                                 int64_t arena_bytes,
+                                                                 const int64_t *__restrict__ data_off,
+                                                                 const int64_t *__restrict__ header_off,
+                                                                 int64_t *__restrict__ sizes) {
+    __shared__ int warp_incl[32];
+    __shared__ int prior_s[1024];
+    __shared__ uint8_t base_s[1024];
+    __shared__ int total_s;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t r = blockIdx.x;
+    const int64_t doff = data_off[r], hoff = header_off[r];
+    const uint8_t *rb = bases + r * tiles_per_row;
+    if (doff < 0) {
+        if (threadIdx.x == 0) sizes[r] = 0;
+        return;
+    }
+    if (threadIdx.x == 0) total_s = 0;
+    __syncthreads();
+    int mine = 0;
+    for (int64_t t = threadIdx.x; t < tiles_per_row; t += blockDim.x) mine += rb[t] == 255;
+    mine = __reduce_add_sync(0xffffffffu, mine);
+    if (lane == 0 && mine) atomicAdd(&total_s, mine);
+    __syncthreads();
+    const int64_t bytes = 384 * tiles_per_row + 128 * static_cast<int64_t>(total_s);
+    const bool fits = doff % 16 == 0 && hoff % 16 == 0 && hoff >= 0 && doff + bytes <= arena_bytes &&
+                      hoff + 4 * tiles_per_row <= arena_bytes;
+    if (threadIdx.x == 0) sizes[r] = fits ? bytes : -1;
+    if (!fits) return;
+    uint8_t *data = arena + doff;
+    uint32_t *hdr = reinterpret_cast<uint32_t *>(arena + hoff);
+    const uint8_t *rp = packed + r * tiles_per_row * 384;
+    const uint16_t *rr = raw + r * tiles_per_row * 256;
+    int carry = 0;
+    for (int64_t c0 = 0; c0 < tiles_per_row; c0 += 1024) {
+        const int64_t t = c0 + threadIdx.x;
+        const uint8_t b = t < tiles_per_row ? rb[t] : uint8_t(0);
+        const unsigned flags = __ballot_sync(0xffffffffu, t < tiles_per_row && b == 255);
+        if (lane == 0) warp_incl[warp] = __popc(flags);
+        __syncthreads();
+        if (warp == 0) {
+            int v = warp_incl[lane];
+#pragma unroll
+            for (int s = 1; s < 32; s <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, v, s);
+                if (lane >= s) v += u;
+            }
+            warp_incl[lane] = v;
+        }
+        __syncthreads();
+        const int prior = carry + (warp ? warp_incl[warp - 1] : 0) + __popc(flags & ((1u << lane) - 1u));
+        prior_s[threadIdx.x] = prior;
+        base_s[threadIdx.x] = b;
+        if (t < tiles_per_row) hdr[t] = (static_cast<uint32_t>(prior) << 8) | b;
+        carry += warp_incl[31];
+        __syncthreads();
+        const int n = static_cast<int>(tiles_per_row - c0 < 1024 ? tiles_per_row - c0 : 1024);
+        for (int i = warp; i < n; i += 32) {
+            const int64_t tile = c0 + i;
+            uint4 *dst = reinterpret_cast<uint4 *>(data + 384 * tile + 128 * static_cast<int64_t>(prior_s[i]));
+            if (base_s[i] == 255)
+                dst[lane] = reinterpret_cast<const uint4 *>(rr + tile * 256)[lane];
+            else if (lane < 24)
+                dst[lane] = reinterpret_cast<const uint4 *>(rp + tile * 384)[lane];
+        }
+        __syncthreads();  // prior_s, base_s and warp_incl are rewritten by the next chunk
+    }
+}
+
 }  // namespace lrb
 
 extern "C" {
@@ -313,6 +394,23 @@ int moe_tilecodec_pack(const uint16_t *raw, int64_t tiles, uint8_t *packed, uint
     lrb::tilecodec_pack_kernel<<<static_cast<unsigned>(blocks), 256, 0, lrb::as_stream(stream)>>>(raw, tiles, packed,
                                                                                                  bases, encoded);
     LRB_LAUNCHED("tilecodec_pack_kernel");
+    return MOE_OK;
+}
+
+int moe_tilecodec_compact(const uint16_t *raw, const uint8_t *packed, const uint8_t *bases, int rows,
+                          int64_t tiles_per_row, uint8_t *arena, int64_t arena_bytes, const int64_t *data_offsets,
+                          const int64_t *header_offsets, int64_t *sizes, void *stream) {
+    LRB_REQUIRE(raw && packed && bases && arena && data_offsets && header_offsets && sizes && rows >= 0 &&
+                    tiles_per_row > 0 && tiles_per_row < (int64_t(1) << 31) && arena_bytes > 0,
+                "moe_tilecodec_compact: bad arguments");
+    LRB_REQUIRE(reinterpret_cast<uintptr_t>(raw) % 16 == 0 && reinterpret_cast<uintptr_t>(packed) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(arena) % 16 == 0,
+                "moe_tilecodec_compact: raw, packed and arena must be 16-byte aligned");
+    if (rows == 0) return MOE_OK;
+    if (int rc = lrb::require_sm100()) return rc;
+    lrb::tilecodec_compact_kernel<<<rows, 1024, 0, lrb::as_stream(stream)>>>(
+        raw, packed, bases, tiles_per_row, arena, arena_bytes, data_offsets, header_offsets, sizes);
+    LRB_LAUNCHED("tilecodec_compact_kernel");
     return MOE_OK;
 }
 

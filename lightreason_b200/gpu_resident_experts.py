@@ -50,44 +50,84 @@ def pack_tiles(raw_bits: np.ndarray):
     return packed, bases, int(ok.sum())
 
 
-def encode(source):
-    """Compact row of a BF16 tensor or uint16 array: (data, headers|None,
-    encoded tiles, raw tiles).  Keeps the raw bytes when packing does not save
-    space (edge35b/gpu_resident_experts.py:22-42 semantics)."""
+def _flat_bits(source) -> np.ndarray:
     if isinstance(source, torch.Tensor):
         source = source.detach().cpu().contiguous().view(torch.int16).numpy()
-    raw = np.ascontiguousarray(source).view(np.uint8).reshape(-1, RAW_TILE_BYTES)
-    packed, bases, encoded = pack_tiles(raw.view(np.uint16))
-    compressed = bases != RAW_TILE
-    raw_before = np.cumsum(~compressed, dtype=np.uint32) - (~compressed)
-    headers = (raw_before << 8) | bases
-    lengths = np.where(compressed, PACKED_TILE_BYTES, RAW_TILE_BYTES)
-    if int(lengths.sum()) + headers.nbytes >= raw.nbytes:
-        return raw.reshape(-1).copy(), None, 0, len(raw)
-    tiles = np.empty_like(raw)
-    tiles[compressed, :PACKED_TILE_BYTES] = packed[compressed]
-    tiles[~compressed] = raw[~compressed]
-    data = tiles[np.arange(RAW_TILE_BYTES) < lengths[:, None]]
-    return data, headers.view(np.uint8), encoded, len(raw) - encoded
+    return np.ascontiguousarray(source).view(np.uint16).reshape(-1)
+
+
+def compact_layout(bases: np.ndarray):
+    """Byte layout of a compact row from its tile bases: (tile start offsets,
+    headers uint32, data bytes).  Tile t starts at 384 t + 128 p(t), p(t) =
+    raw tiles before t, since every tile takes its 384 packed bytes and a raw
+    tile 128 more; its header is (p(t) << 8) | base."""
+    is_raw = (np.asarray(bases) == RAW_TILE).astype(np.int64)
+    prior = np.zeros_like(is_raw)
+    np.cumsum(is_raw[:-1], out=prior[1:])
+    starts = PACKED_TILE_BYTES * np.arange(is_raw.size) + (RAW_TILE_BYTES - PACKED_TILE_BYTES) * prior
+    headers = ((prior << 8) | np.asarray(bases, dtype=np.int64)).astype("<u4")
+    return starts, headers, PACKED_TILE_BYTES * is_raw.size + (RAW_TILE_BYTES - PACKED_TILE_BYTES) * int(is_raw.sum())
+
+
+def encode(source):
+    """Compact row of a BF16 tensor or uint16 array: (data, headers|None,
+    encoded tiles, raw tiles), the result edge35b/gpu_resident_experts.py:22-42
+    returns.  A row whose compact bytes plus headers would not be smaller than
+    its raw bytes is returned raw (headers None)."""
+    bits = _flat_bits(source)
+    packed, bases, encoded = pack_tiles(bits)
+    tiles = bases.size
+    starts, headers, data_bytes = compact_layout(bases)
+    if data_bytes + headers.nbytes >= bits.nbytes:
+        return bits.view(np.uint8).copy(), None, 0, tiles
+    data = np.empty(data_bytes, dtype=np.uint8)
+    sources = (packed, bits.view(np.uint8).reshape(tiles, RAW_TILE_BYTES))
+    for raw_tile, width in ((False, PACKED_TILE_BYTES), (True, RAW_TILE_BYTES)):
+        sel = (bases == RAW_TILE) == raw_tile
+        data[starts[sel, None] + np.arange(width)] = sources[raw_tile][sel, :width]
+    return data, headers.view(np.uint8), encoded, tiles - encoded
+
+
+def _device_bits(source, device) -> torch.Tensor:
+    if isinstance(source, torch.Tensor):
+        return source.detach().reshape(-1).view(torch.int16).to(device)
+    return torch.from_numpy(_flat_bits(source).view(np.int16)).to(device)
 
 
 def device_rows(weights, raw: torch.Tensor):
-    """Descriptors [n, 3] (device int64) for independently owned compact device
-    rows of `weights` (sequence of BF16 rows); rows that do not pack point at
-    the matching row of `raw`.  Returns (descriptors, owners, bytes)."""
-    rows, owners, total = [], [], 0
-    for i, source in enumerate(weights):
-        data, meta, _, _ = encode(source)
-        if meta is None:
-            rows.append((0, 0, raw[i].data_ptr()))
-            total += raw[i].numel() * raw[i].element_size()
-        else:
-            d = torch.from_numpy(data).to(raw.device)
-            h = torch.from_numpy(meta).to(raw.device)
-            owners.extend((d, h))
-            rows.append((d.data_ptr(), h.data_ptr(), -1))
-            total += data.size + meta.size
-    return torch.tensor(rows, dtype=torch.int64, device=raw.device), owners, total
+    """Descriptors [n, 3] (device int64) of compact device copies of `weights`
+    (a sequence of equally sized BF16 rows: tensors or uint16 arrays), built on
+    the device: moe_tilecodec_pack then moe_tilecodec_compact into one arena,
+    each row's data and headers 128-byte aligned.  A row that does not shrink
+    points at the matching row of `raw` instead (`(0, 0, raw ptr)`), a compact
+    one is `(data ptr, headers ptr, -1)` (edge35b/gpu_resident_experts.py:45-59
+    descriptors).  Returns (descriptors, owners, bytes of the device rows)."""
+    from lightreason_b200 import native
+
+    device = raw.device
+    rows = torch.stack([_device_bits(w, device) for w in weights])
+    n_rows, n = rows.shape
+    tiles = n // TILE_VALUES
+    packed, bases, _ = native.tilecodec_pack(rows.reshape(-1))
+    raw_tiles = (bases.view(n_rows, tiles) == RAW_TILE).sum(dim=1).cpu().numpy().astype(np.int64)
+    data_bytes = PACKED_TILE_BYTES * tiles + (RAW_TILE_BYTES - PACKED_TILE_BYTES) * raw_tiles
+    header_bytes = 4 * tiles
+    shrinks = data_bytes + header_bytes < RAW_TILE_BYTES * tiles
+    align = lambda v: (v + 127) // 128 * 128  # noqa: E731
+    span = np.where(shrinks, align(data_bytes) + align(header_bytes), 0)
+    first = np.concatenate(([0], np.cumsum(span)[:-1]))
+    data_off = np.where(shrinks, first, -1)
+    header_off = np.where(shrinks, first + align(data_bytes), 0)
+    arena = torch.empty(max(int(span.sum()), 128), dtype=torch.uint8, device=device)
+    written = native.tilecodec_compact(rows, packed, bases, arena, torch.from_numpy(data_off).to(device),
+                                       torch.from_numpy(header_off).to(device))
+    if not torch.equal(written.cpu(), torch.from_numpy(np.where(shrinks, data_bytes, 0))):
+        raise RuntimeError("Compact expert rows did not fit their arena layout")
+    base = arena.data_ptr()
+    table = [(base + int(d), base + int(h), -1) if keep else (0, 0, raw[i].data_ptr())
+             for i, (keep, d, h) in enumerate(zip(shrinks, data_off, header_off))]
+    total = int(np.where(shrinks, data_bytes + header_bytes, RAW_TILE_BYTES * tiles).sum())
+    return torch.tensor(table, dtype=torch.int64, device=device), [arena], total
 
 
 class ResidentArena:

@@ -77,6 +77,7 @@ _SIGNATURES = {
     "moe_rowcodec_plan": ([_p, _i, ctypes.c_int64, _p, _p, _p, _sz, _p], _i),
     "moe_rowcodec_pack": ([_p, _i, ctypes.c_int64, _p, _p, _p, _sz, _p], _i),
     "moe_tilecodec_pack": ([_p, ctypes.c_int64, _p, _p, _p, _p], _i),
+    "moe_tilecodec_compact": ([_p, _p, _p, _i, ctypes.c_int64, _p, ctypes.c_int64, _p, _p, _p, _p], _i),
     "moe_ipc_alloc": ([_sz, ctypes.POINTER(_p), _p], _i),
     "moe_ipc_free": ([_p], _i),
     "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
@@ -588,6 +589,31 @@ def tilecodec_pack(raw: "torch.Tensor"):
     check(lib().moe_tilecodec_pack(_ptr(raw), tiles, _ptr(packed), _ptr(bases), _ptr(encoded),
                                    _stream(raw.device)), "moe_tilecodec_pack")
     return packed, bases, int(encoded.item())
+
+
+def tilecodec_compact(raw: "torch.Tensor", packed: "torch.Tensor", bases: "torch.Tensor", arena: "torch.Tensor",
+                      data_offsets: "torch.Tensor", header_offsets: "torch.Tensor") -> "torch.Tensor":
+    """moe_tilecodec_compact on the current stream: assemble the compact rows of
+    the resident tile codec from raw rows [rows, n] (CUDA, 16-bit BF16 bits)
+    and their moe_tilecodec_pack output into `arena` (CUDA uint8) at the given
+    byte offsets (CUDA int64 [rows]; a negative data offset keeps the row out).
+    Returns the per-row data bytes (CUDA int64 [rows]; -1 = did not fit)."""
+    raw = _bits_view(raw, "raw")
+    _require(raw.dim() == 2 and raw.shape[1] % 256 == 0, "raw must be [rows, n] with n a multiple of 256")
+    rows, tiles = raw.shape[0], raw.shape[1] // 256
+    _require(packed.is_cuda and packed.dtype == torch.uint8 and packed.numel() == rows * tiles * 384,
+             "packed must be the CUDA uint8 output of tilecodec_pack for these rows")
+    _require(bases.is_cuda and bases.dtype == torch.uint8 and bases.numel() == rows * tiles,
+             "bases must be the CUDA uint8 output of tilecodec_pack for these rows")
+    _require(arena.is_cuda and arena.dtype == torch.uint8 and arena.is_contiguous(), "arena must be CUDA uint8")
+    for name, t in (("data_offsets", data_offsets), ("header_offsets", header_offsets)):
+        _require(t.is_cuda and t.dtype == torch.int64 and t.numel() == rows and t.is_contiguous(),
+                 f"{name} must be a CUDA int64 tensor of one entry per row")
+    sizes = torch.empty(rows, dtype=torch.int64, device=raw.device)
+    check(lib().moe_tilecodec_compact(_ptr(raw), _ptr(packed), _ptr(bases), rows, tiles, _ptr(arena), arena.numel(),
+                                      _ptr(data_offsets), _ptr(header_offsets), _ptr(sizes), _stream(raw.device)),
+          "moe_tilecodec_compact")
+    return sizes
 
 
 def prefix_table(bases) -> "torch.Tensor":

@@ -176,3 +176,79 @@ def test_packed_host_banks_encoders_agree(dev):
         assert torch.equal(x, y)
     da, db = a.descriptors.cpu(), b.descriptors.cpu()
     assert torch.equal(da[..., 1:], db[..., 1:])
+
+
+def _compact_on_device(rows_bits: np.ndarray, dev, shrinks=None):
+    """moe_tilecodec_pack + moe_tilecodec_compact of rows [n_rows, n]; each row
+    at a 256-byte-aligned offset with its headers after it.  Returns (arena
+    bytes, data offsets, header offsets, written sizes)."""
+    rows = to_dev(rows_bits, dev).reshape(rows_bits.shape)
+    n_rows, n = rows_bits.shape
+    tiles = n // 256
+    packed, bases, _ = native.tilecodec_pack(rows.reshape(-1))
+    cap = (512 * tiles + 4 * tiles + 512 + 255) // 256 * 256
+    data_off = np.arange(n_rows, dtype=np.int64) * cap
+    if shrinks is not None:
+        data_off = np.where(shrinks, data_off, -1)
+    header_off = np.arange(n_rows, dtype=np.int64) * cap + 512 * tiles + 256
+    arena = torch.full((n_rows * cap,), 0xA5, dtype=torch.uint8, device=dev)
+    sizes = native.tilecodec_compact(rows, packed, bases, arena, torch.from_numpy(data_off).to(dev),
+                                     torch.from_numpy(header_off).to(dev))
+    return arena.cpu().numpy(), data_off, header_off, sizes.cpu().numpy()
+
+
+def test_tile_compact_rows_reference_vectors(dev):
+    """Device compact-row assembly on the seed-7091 row (24 encoded + 8 raw
+    tiles) gives the reference encode()'s data and headers byte for byte."""
+    z = load_golden("codec_vectors.npz")
+    bits = z["tiles7091_bits"].reshape(1, -1)
+    arena, doff, hoff, sizes = _compact_on_device(bits, dev)
+    data, headers = z["tiles7091_data"], z["tiles7091_headers"]
+    assert sizes[0] == data.size
+    assert np.array_equal(arena[doff[0]:doff[0] + data.size], data)
+    assert np.array_equal(arena[hoff[0]:hoff[0] + headers.size], headers)
+    assert np.all(arena[doff[0] + data.size:hoff[0]] == 0xA5)   # nothing written past the row
+
+
+@pytest.mark.parametrize("tiles", [1, 33, 1024, 1025, 8192])
+def test_tile_compact_rows_match_host_encoder(dev, tiles):
+    """Rows across the kernel's 1024-tile chunk boundary, with raw tiles at
+    random places and a skipped row, against the host encode()."""
+    rng = np.random.default_rng(tiles + 5)
+    n_rows = 3
+    words = rng.integers(0, 2 ** 16, (n_rows, tiles * 256), dtype=np.uint16)
+    span = np.repeat(rng.choice([4, 8, 13], size=(n_rows, tiles), p=[0.6, 0.25, 0.15]), 256, axis=1)
+    exps = (100 + rng.integers(0, 2 ** 16, words.shape) % span).astype(np.uint16)
+    words = (words & 0x80FF) | ((exps << 8) & 0x7F00)
+    shrinks = np.array([True, False, True])
+    arena, doff, hoff, sizes = _compact_on_device(words, dev, shrinks)
+    assert sizes[1] == 0
+    for r in (0, 2):
+        packed, bases, _ = gre.pack_tiles(words[r])
+        starts, headers, data_bytes = gre.compact_layout(bases)
+        assert sizes[r] == data_bytes
+        # the host encoder returns the row raw when it does not shrink; lay it
+        # out compactly here anyway to compare every tile
+        want = np.empty(data_bytes, dtype=np.uint8)
+        for t in range(tiles):
+            src = words[r].view(np.uint8)[t * 512:(t + 1) * 512] if bases[t] == 255 else packed[t]
+            want[starts[t]:starts[t] + src.size] = src
+        assert np.array_equal(arena[doff[r]:doff[r] + data_bytes], want), f"row {r} data"
+        assert np.array_equal(arena[hoff[r]:hoff[r] + 4 * tiles], headers.view(np.uint8)), f"row {r} headers"
+        data, hdr, _, _ = gre.encode(words[r])
+        if hdr is not None:
+            assert np.array_equal(data, want) and np.array_equal(hdr, headers.view(np.uint8))
+
+
+def test_tile_compact_refuses_rows_outside_the_arena(dev):
+    """A row whose data would run past the arena is reported (-1) and left
+    unwritten; the call itself succeeds."""
+    bits = load_golden("codec_vectors.npz")["tiles7091_bits"].reshape(1, -1)
+    rows = to_dev(bits, dev).reshape(bits.shape)
+    packed, bases, _ = native.tilecodec_pack(rows.reshape(-1))
+    arena = torch.full((4096,), 0x5A, dtype=torch.uint8, device=dev)
+    off = torch.zeros(1, dtype=torch.int64, device=dev)
+    sizes = native.tilecodec_compact(rows, packed, bases, arena, off, off)
+    torch.cuda.synchronize()
+    assert int(sizes.item()) == -1
+    assert bool((arena == 0x5A).all())
