@@ -38,6 +38,10 @@ from lightreason_b200 import native
 from lightreason_b200.native import _ptr, _require, check, lib
 
 
+# phases of one peer-exchange rank step, in launch order
+EP_STAGES = ("router", "permute", "dispatch", "collect", "local_layer", "return", "finish", "combine")
+
+
 def shard(experts: int, world: int, rank: int) -> range:
     _require(world >= 1 and experts % world == 0, f"{experts} experts do not shard evenly over {world} ranks")
     el = experts // world
@@ -190,10 +194,15 @@ class ExpertParallelLayer:
         return out
 
     # -- one distributed step
-    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stage_events=None) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, out: torch.Tensor | None = None, stage_events=None,
+                ep_events=None) -> torch.Tensor:
+        """One rank step.  stage_events: the local layer's stage events (as in
+        native.Layer.forward).  ep_events (peer exchange only): None or
+        len(EP_STAGES) + 1 torch.cuda.Event recorded on the compute stream at
+        the boundaries of the step's phases."""
         _require(self.exchange is not None, "forward needs an exchange (use run_virtual_ranks for one process)")
         if isinstance(self.exchange, PeerExchange):
-            return self._forward_peer(x, torch.empty_like(x) if out is None else out, stage_events)
+            return self._forward_peer(x, torch.empty_like(x) if out is None else out, stage_events, ep_events)
         self.dispatch(x)
         self.last_splits = exchange_step(self, self.exchange,
                                          lambda received: self.compute(received, stage_events))
@@ -218,34 +227,49 @@ class ExpertParallelLayer:
         self.p_rsplit = self.rsplit
         self._peer_ready = True
 
-    def _forward_peer(self, x, out, stage_events):
+    def _forward_peer(self, x, out, stage_events, ep_events=None):
         ex = self.exchange
         self._peer_buffers()
         native._cuda_bf16(x, "x")
         tokens = x.shape[0]
         _require(tokens <= self.max_tokens and x.shape[1] == self.hidden, "x must be [T <= tokens, H]")
+        _require(ep_events is None or len(ep_events) == len(EP_STAGES) + 1,
+                 f"ep_events must hold {len(EP_STAGES) + 1} events")
         self.tokens = tokens
         s = native._stream(self.dev)
         a = ctypes.byref(ex.args)
+
+        def mark(i):
+            if ep_events is not None:
+                ep_events[i].record()
+        mark(0)
         check(lib().moe_router_topk_ws(_ptr(x), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
                                        tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits),
                                        _ptr(self.idx), None, _ptr(self.scores), _ptr(self.sig),
                                        _ptr(self.p_rsplit), self.p_rsplit.numel(), s), "moe_router_topk_ws")
+        mark(1)
         c = self.counters.data_ptr()
         check(lib().moe_permute_wide(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
                                      _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos),
                                      _ptr(self.active), c, c + 4, _ptr(self.p_hist), s), "moe_permute_wide")
+        mark(2)
         check(lib().moe_ep_p2p_dispatch(a, _ptr(x), _ptr(self.idx), _ptr(self.offsets), _ptr(self.perm_token),
                                         _ptr(self.perm_slot), s), "moe_ep_p2p_dispatch")
+        mark(3)
         check(lib().moe_ep_p2p_collect(a, _ptr(x), tokens, _ptr(self.p_route_in), _ptr(self.p_ret_addr), s),
               "moe_ep_p2p_collect")
+        mark(4)
         self.local.forward_rows_raw(ex.rows_ptr, ex.rows, self.p_route_in, self.p_yin, stage_events=stage_events)
+        mark(5)
         check(lib().moe_ep_p2p_return(a, self.p_yin[ex.own_rows:].data_ptr(), _ptr(self.p_ret_addr), s),
               "moe_ep_p2p_return")
+        mark(6)
         check(lib().moe_ep_p2p_finish(a, s), "moe_ep_p2p_finish")
+        mark(7)
         check(lib().moe_ep_combine(ctypes.c_void_p(ex.ret_ptr), _ptr(self.route_pos), _ptr(self.scores),
                                    _ptr(self.p_yin), _ptr(self.sig), tokens, self.top_k, self.hidden, _ptr(out), s),
               "moe_ep_combine")
+        mark(8)
         return out
 
 
@@ -361,4 +385,4 @@ def run_virtual_ranks(layers: list[ExpertParallelLayer], xs: list[torch.Tensor],
     return [layer.combine(o) for layer, o in zip(layers, outs)]
 
 
-__all__ = ["ExpertParallelLayer", "PeerExchange", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]
+__all__ = ["EP_STAGES", "ExpertParallelLayer", "PeerExchange", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]
