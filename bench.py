@@ -259,8 +259,10 @@ def timed_steps(run_step, steps, warmup, flush, world, n_events=0, event_slots=(
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     rows = None
     if n_events:
-        rows = [[torch.cuda.Event(enable_timing=True) if j in event_slots else None for j in range(n_events)]
-                for _ in range(steps)]
+        # external: an event recorded from Python inside the capture becomes an
+        # external event node, which the host can time after a replay
+        rows = [[torch.cuda.Event(enable_timing=True, external=True) if j in event_slots else None
+                 for j in range(n_events)] for _ in range(steps)]
         for row in rows:
             for e in row:
                 if e is not None:
@@ -417,12 +419,25 @@ def time_cpu_reference(w, gu, dn, xs, steps, warmup, threads=None) -> dict:
             "sample": f"median of {steps} steps (after {warmup} warm-up) of {tokens} tokens through {path}"}
 
 
+_BANKS = {}
+
+
+def host_layer(seed: int, bias: str):
+    """(LayerWeights, gate_up [E, 2I, H], down [E, H, I]) on the host; the
+    expert banks depend on the seed only (the bias is drawn separately), so
+    configs with one seed share one draw."""
+    if seed not in _BANKS:
+        _BANKS.clear()
+        _BANKS[seed] = S.layer_weights(seed).stacked()
+    gu, dn = _BANKS[seed]
+    return S.layer_weights(seed, bias=bias), gu, dn
+
+
 def cpu_inputs(cfg):
     """Weights (host) and the input pool of rank 0, shared by the cpu_baseline
     leg and the reference arm."""
     seed = cfg["seed"]
-    w = S.layer_weights(seed, bias=cfg["bias"])
-    gu, dn = w.stacked()
+    w, gu, dn = host_layer(seed, cfg["bias"])
     tokens = cfg.get("cpu_sample", cfg["tokens"])
     xs = [S.hidden_states(input_seed(cfg, 0), cfg["tokens"], step=i)[:tokens] for i in range(POOL)]
     return w, gu, dn, xs
@@ -480,8 +495,7 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
     pk = peaks()
     tokens, seed = cfg["tokens"], cfg["seed"]
     t_setup = time.perf_counter()
-    w = S.layer_weights(seed, bias=cfg["bias"])
-    gu, dn = w.stacked()
+    w, gu, dn = host_layer(seed, cfg["bias"])
     d = lambda a: to_dev(a, dev)  # noqa: E731
     sh = dict(shared_gate=d(w.sh_gate), shared_up=d(w.sh_up), shared_down=d(w.sh_down), shared_gate_w=d(w.sh_gate_w))
     bias = torch.from_numpy(w.bias).to(dev)

@@ -175,7 +175,7 @@ def test_layer_matches_oracle(dev, case13, tokens):
     out, idx, sc, lg = case13.run(x)
     w_out, w_idx, w_sc, w_lg = case13.oracle(x)
     z = S.bf16_bits_to_f32(w_lg) + case13.w.bias
-    compare_ids(idx, w_idx, z, slack_ulps=1.0)
+    compare_ids(idx, w_idx, z, slack_ulps=1.0, case=f"layer T={tokens}")
     same = np.all(idx == w_idx, axis=1)
     assert same.mean() > 0.9
     assert_close(lg, w_lg, what="logits")
@@ -202,7 +202,8 @@ def test_layer_other_top_k_matches_oracle(dev, case13, top_k, tokens):
     w_out, w_idx, _, w_lg = O.moe_layer(x_bits, w.router, w.bias, w.gate_up, w.down, w.sh_gate, w.sh_up, w.sh_down,
                                         w.sh_gate_w, top_k=top_k)
     idx = idx.cpu().numpy()
-    compare_ids(idx, w_idx, S.bf16_bits_to_f32(w_lg) + w.bias, slack_ulps=1.0)
+    compare_ids(idx, w_idx, S.bf16_bits_to_f32(w_lg) + w.bias, slack_ulps=1.0,
+                case=f"layer T={tokens} top_k={top_k}")
     same = np.all(idx == w_idx, axis=1)
     assert same.mean() > 0.9
     assert_close(out[same], w_out[same], what=f"layer output, top_k {top_k}")
@@ -245,7 +246,7 @@ def test_layer_matches_transformers_golden(dev, name):
     x = S.hidden_states(int(g["seed"]), int(g["tokens"]))
     out, idx, sc, lg = case.run(x)
     z = S.bf16_bits_to_f32(g["logits"]) + case.w.bias
-    compare_ids(idx, g["idx"], z, slack_ulps=1.0)
+    compare_ids(idx, g["idx"], z, slack_ulps=1.0, case=f"golden {name}")
     same = np.all(idx == g["idx"], axis=1)
     assert_close(out[same], g["out"][same], what="layer output vs transformers eager")
 
@@ -319,23 +320,40 @@ def test_route_in_is_the_experts_forward(dev, case13):
     assert_close(bits(out), want, what="experts forward")
 
 
-def test_layer_prefill_4096_sampled_tokens(dev, case14):
-    """T=4096 with Zipf(1.1) routing: ids and outputs of a token sample against
-    the oracle (a token's output depends on its own row only)."""
-    tokens = 4096
-    x = S.hidden_states(400, tokens)
+def oracle_with_routes(w, x_bits, idx, scores):
+    """The oracle's expert path, combine and shared expert for given routes
+    (ids and BF16 scores), for tokens whose selection the GPU decided through
+    a near tie."""
+    offsets, ptok, _, rpos = O.permute(np.ascontiguousarray(idx, dtype=np.int64), 256)
+    y = O.experts_by_route(x_bits, w.gate_up, w.down, offsets, ptok, 256)
+    sh, sig = O.shared_expert(x_bits, w.sh_gate, w.sh_up, w.sh_down, w.sh_gate_w)
+    return O.combine(y, rpos, np.ascontiguousarray(scores), sh, sig)
+
+
+@pytest.mark.parametrize("tokens", [4096, 8192])
+def test_layer_prefill_full_width_matches_oracle(dev, case14, tokens):
+    """configs[3] (T = 4096, Zipf(1.1) routing) and twice that, every token:
+    logits, ids (tier 2, near ties counted), scores and outputs against the
+    oracle; the tokens whose selection moved through a near tie are checked
+    too -- their ids must be the oracle's selection on the GPU's own logits
+    (tier 1), and their outputs the oracle's for the GPU's routes."""
+    x = S.hidden_states(400 + tokens, tokens)
     out, idx, sc, lg = case14.run(x)
-    rng = np.random.default_rng(0)
-    sample = np.sort(rng.choice(tokens, 24, replace=False))
-    w_out, w_idx, w_sc, w_lg = case14.oracle(np.ascontiguousarray(x[sample]))
+    w_out, w_idx, w_sc, w_lg = case14.oracle(x)
+    assert_close(lg, w_lg, what="prefill logits")
     z = S.bf16_bits_to_f32(w_lg) + case14.w.bias
-    compare_ids(idx[sample], w_idx, z, slack_ulps=1.0)
-    same = np.all(idx[sample] == w_idx, axis=1)
-    assert_close(out[sample][same], w_out[same], what="prefill output")
-    # every token has 8 distinct ids in range, scores sum to ~1
-    assert (idx >= 0).all() and (idx < 256).all()
-    assert all(len(set(r)) == 8 for r in idx[:512].tolist())
-    np.testing.assert_allclose(S.bf16_bits_to_f32(sc).sum(1), 1.0, atol=3e-2)
+    excused = compare_ids(idx, w_idx, z, slack_ulps=1.0, case=f"prefill T={tokens}")
+    assert excused <= tokens // 50, f"{excused} near-tie tokens of {tokens}"
+    same = np.all(idx == w_idx, axis=1)
+    assert_close(sc[same], w_sc[same], what="prefill scores")
+    assert_close(out[same], w_out[same], what="prefill output")
+    moved = np.flatnonzero(~same)
+    if moved.size:
+        own_idx, _, own_sc = O.router_select(lg[moved], case14.w.bias)
+        assert np.array_equal(own_idx, idx[moved])
+        assert_close(sc[moved], own_sc, what="near-tie tokens' scores")
+        want = oracle_with_routes(case14.w, np.ascontiguousarray(x[moved]), idx[moved], sc[moved])
+        assert_close(out[moved], want, what="near-tie tokens' outputs")
 
 
 def test_graph_capture_replays_with_new_routes(dev, case13):
@@ -376,3 +394,28 @@ def test_expert_rows_against_cpu_experts(dev, case13):
                                                              [case13.dn[e] for e in experts], tok))
     assert_close(got1, want1, what="expert_rows")
     assert_close(got4, want4, what="expert_block_rows")
+
+
+def test_layer_on_two_devices_in_one_process():
+    """One process drives the layer on device 0 and then on device 1: kernel
+    attributes (the shared-memory opt-ins) are per device, so every width
+    class must launch on the second device too, with the same bits."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    build.build()
+    w = S.layer_weights(17, experts=64)
+    gu, dn = w.stacked()
+    got = {}
+    for d in (0, 1):
+        dev = torch.device("cuda", d)
+        with torch.cuda.device(dev):
+            native.device_check(d)
+            layer = native.Layer(router=to_dev(w.router, dev), gate_up=to_dev(gu, dev), down=to_dev(dn, dev),
+                                 bias=torch.from_numpy(w.bias).to(dev), shared_gate=to_dev(w.sh_gate, dev),
+                                 shared_up=to_dev(w.sh_up, dev), shared_down=to_dev(w.sh_down, dev),
+                                 shared_gate_w=to_dev(w.sh_gate_w, dev))
+            for tokens in (1, 16, 100):
+                got[d, tokens] = bits(layer(to_dev(S.hidden_states(70 + tokens, tokens), dev)))
+            torch.cuda.synchronize(dev)
+    for tokens in (1, 16, 100):
+        assert np.array_equal(got[0, tokens], got[1, tokens]), tokens

@@ -6,7 +6,9 @@
 * Whole-stack capture: the patched blocks of a two-layer stack captured as
   one caller-owned CUDA graph and replayed on new tokens equal eager (the
   layer chain has no host round trip; the reference's Scheduled path reads
-  the ids on the host and cannot be captured whole).
+  the ids on the host and cannot be captured whole); three 35B-shaped layers
+  at the configs[2] width captured as one graph match the oracle on every
+  replay.
 * packed_native.mixer_graphs: single-token mixers replayed from per-layer
   graphs keep outputs and the live cache state bit-identical to the mixer's
   own forward over several decode steps (a capturable stand-in with the
@@ -105,6 +107,60 @@ def test_whole_stack_graph_equals_eager(dev, model):
             assert np.array_equal(bits(out), w)
         del g
     pool.clear()
+
+
+def test_stack_graph_replay_matches_oracle(dev):
+    """configs[2] in miniature: three layers at the 35B shapes (256 experts,
+    Zipf(1.1) routing, each with its own weights) at the decode width B = 64,
+    captured as one CUDA graph over static input buffers and replayed on two
+    new batches; every layer's ids (tier 2) and outputs of every replay
+    against the oracle."""
+    from oracle import oracle as O
+    from tests.helpers import assert_close, compare_ids
+
+    tokens, n_layers = 64, 3
+    ws, layers = [], []
+    for li in range(n_layers):
+        w = S.layer_weights(2000 + li, layer=li, bias="zipf")
+        gu, dn = w.stacked()
+        for e in range(256):
+            w.gate_up[e], w.down[e] = gu[e], dn[e]
+        layers.append(native.Layer(router=to_dev(w.router, dev), gate_up=to_dev(gu, dev), down=to_dev(dn, dev),
+                                   bias=torch.from_numpy(w.bias).to(dev), shared_gate=to_dev(w.sh_gate, dev),
+                                   shared_up=to_dev(w.sh_up, dev), shared_down=to_dev(w.sh_down, dev),
+                                   shared_gate_w=to_dev(w.sh_gate_w, dev)))
+        ws.append(w)
+    static = [torch.zeros((tokens, 2048), dtype=torch.bfloat16, device=dev) for _ in layers]
+    outs = [torch.empty_like(x) for x in static]
+    idxs = [torch.empty((tokens, 8), dtype=torch.int64, device=dev) for _ in layers]
+    lgs = [torch.empty((tokens, 256), dtype=torch.bfloat16, device=dev) for _ in layers]
+
+    def step():
+        for layer, x, o, i, lg in zip(layers, static, outs, idxs, lgs):
+            layer(x, out=o, idx_out=i, logits_out=lg)
+
+    step()  # workspaces exist before the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for rep in range(2):
+        xs = [S.hidden_states(3000 + 10 * rep + li, tokens) for li in range(n_layers)]
+        for x, b in zip(static, xs):
+            x.copy_(to_dev(b, dev))
+        g.replay()
+        torch.cuda.synchronize()
+        for li, (w, b) in enumerate(zip(ws, xs)):
+            w_out, w_idx, _, w_lg = O.moe_layer(b, w.router, w.bias, w.gate_up, w.down, w.sh_gate, w.sh_up,
+                                                w.sh_down, w.sh_gate_w)
+            idx = idxs[li].cpu().numpy()
+            assert_close(bits(lgs[li]), w_lg, what=f"replay {rep} layer {li} logits")
+            compare_ids(idx, w_idx, S.bf16_bits_to_f32(w_lg) + w.bias, slack_ulps=1.0,
+                        case=f"stack replay {rep} layer {li} T={tokens}")
+            same = np.all(idx == w_idx, axis=1)
+            assert same.mean() > 0.9
+            assert_close(bits(outs[li])[same], w_out[same], what=f"replay {rep} layer {li} output")
+    del g
 
 
 class _LiveCache:
