@@ -22,8 +22,10 @@ per-N values form one weak-scaling series.
               CPU router on a token sample (near ties of one BF16 ulp excused
               and counted).  A mismatch makes every rank exit non-zero;
   * ep_stages_us: per-phase times of the rank step (router, permute,
-              dispatch, collect, local layer, return, finish, combine) and
-              the NVLink bytes and rates of dispatch and return;
+              publish, experts -- the owner's plan and the grouped kernel,
+              which pulls the token rows over NVLink and stores the expert
+              rows into their senders' memory -- finish, combine) and the
+              NVLink bytes the rank moves;
   * cpu_baseline (rank 0, N = 1): the reference's CPU path of the same
               workload on the host cores;
   * configs (N = 1): configs[0..3] as sub-records, each with its step time,
@@ -841,6 +843,10 @@ def run_ep(args, world, rank, local) -> dict:
     log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, experts "
         f"{mine.start}..{mine.stop - 1}, transport {transport}")
 
+    # the expert kernel's own events: two around the grouped kernel on the
+    # peer exchange, the local layer's eight stage events on NCCL
+    k_events, k_slots = (2, (0, 1)) if transport == "p2p" else (8, (4, 5))
+
     def dev_step(i, ev):
         layer(xs[i % POOL], out=out, stage_events=ev)
 
@@ -880,28 +886,28 @@ def run_ep(args, world, rank, local) -> dict:
         torch.cuda.synchronize()
         ms, _, _ = run(dev_step, args.steps, args.warmup, flush, world) if run is timed_steps else run(dev_step)
         if run is timed_steps:
-            _, krows, _ = run(dev_step, args.steps, args.warmup, flush, world, n_events=8, event_slots=(4, 5))
+            _, krows, _ = run(dev_step, args.steps, args.warmup, flush, world, n_events=k_events, event_slots=k_slots)
             _, erows, _ = run(ep_step, args.steps, args.warmup, flush, world, n_events=len(EP_STAGES) + 1,
                               event_slots=tuple(range(len(EP_STAGES) + 1)))
             e2e_ms, _, _ = run(e2e_step, args.steps, args.warmup, flush, world)
         else:
-            _, krows, _ = run(dev_step, 8, (4, 5))
+            _, krows, _ = run(dev_step, k_events, k_slots)
             erows = None
             e2e_ms, _, _ = run(e2e_step)
         if peer is not None:
             peer.check()
     clocks = sampler.summary()
-    kern_ms = between(krows, 4, 5)
+    kern_ms = between(krows, *k_slots)
     total_ms = dist_max(sum(ms), world)
     e2e_total = dist_max(sum(e2e_ms), world)
     value = world * tokens * args.steps / (total_ms / 1e3)
 
     # this rank's work in the last timed step
     if transport == "p2p":
-        route_in = layer.p_route_in[:, 0].cpu().numpy()
-        own, cap = peer.own_rows, peer.capacity
-        per_sender = [int((route_in[own + s * cap: own + (s + 1) * cap] >= 0).sum()) for s in range(world)]
-        local_ids = route_in[own:][route_in[own:] >= 0]
+        st = layer.peer_stats()
+        per_sender = st["rows_per_sender"]
+        received_rows = st["rows_received"]
+        u_local = st["local_experts_with_rows"]
         sent = layer.offsets.cpu().numpy()
         el = EXPERTS // world
         to_self = int(sent[(rank + 1) * el] - sent[rank * el])
@@ -913,23 +919,33 @@ def run_ep(args, world, rank, local) -> dict:
         received = sum(m[s][rank] for s in range(world))
         from_peers = received - m[rank][rank]
         local_ids = layer.recv_meta[:received].cpu().numpy()
-    received_rows = int(local_ids.size)
-    u_local = len(set(local_ids.tolist()))
+        received_rows = int(local_ids.size)
+        u_local = len(set(local_ids.tolist()))
     rows = tokens + received_rows
-    # grouped kernel in rows mode: local experts' + the shared expert's weights,
-    # the route-ordered rows in, activations out and back in, rows out
-    kernel_bytes = (u_local + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
+    # grouped kernel: local experts' + the shared expert's weights, the
+    # route-ordered rows in, activations out and back in, rows out; on the
+    # peer exchange also its row gather (each row read from its sender, over
+    # NVLink or locally, and written into the route-ordered buffer)
+    gather_bytes = 2 * rows * HIDDEN * 2 if transport == "p2p" else 0
+    kernel_bytes = ((u_local + 1) * EXPERT_BYTES + rows * HIDDEN * 2 + 2 * rows * INNER * 2 + rows * HIDDEN * 2
+                    + gather_bytes)
     kernel_flops = rows * EXPERT_FLOPS_PER_ROW
     traffic, traffic_src = profiled_traffic(f"config4_world{world}_grouped")
     stages = None
-    nvlink = {"dispatch_bytes": leaving * HIDDEN * 2, "return_bytes": from_peers * HIDDEN * 2}
+    # rows crossing NVLink per step for this rank: its tokens' rows the owners
+    # pull and the expert rows they store back (routes leaving), and the rows
+    # it pulls from its senders and stores back to them (routes received)
+    nvlink = {"rows_pulled_from_peers": from_peers, "rows_returned_to_peers": from_peers,
+              "own_rows_pulled_by_peers": leaving, "own_rows_returned_by_peers": leaving,
+              "bytes_in": (from_peers + leaving) * HIDDEN * 2, "bytes_out": (from_peers + leaving) * HIDDEN * 2}
     if erows is not None:
         st = stage_times(erows, EP_STAGES)
         stages = {k: round(1e3 * statistics.median(v), 2) for k, v in st.items()}
-        for name, nbytes in (("dispatch", nvlink["dispatch_bytes"]), ("return", nvlink["return_bytes"])):
-            t_ms = statistics.median(st[name])
-            nvlink[f"{name}_gbs"] = round(nbytes / (t_ms / 1e3) / 1e9, 1) if nbytes else None
         stages["step_with_event_overhead"] = round(1e3 * statistics.median(between(erows, 0, len(EP_STAGES))), 2)
+        stages["grouped_kernel"] = round(1e3 * statistics.median(kern_ms), 2)
+        t_ms = statistics.median(st["experts"])
+        if from_peers:
+            nvlink["experts_stage_gbs_per_direction"] = round(2 * from_peers * HIDDEN * 2 / 2 / (t_ms / 1e3) / 1e9, 1)
     if peer is not None:
         peer.close()
 
@@ -949,11 +965,11 @@ def run_ep(args, world, rank, local) -> dict:
               "events around it, max over ranks of the summed step times" if transport == "p2p" else
               "CUDA events around each whole step on the compute stream (includes the host read of the "
               "all-to-all split sizes), max over ranks of the summed step times")
-    # router_tc + router_select; permute count/colscan/place; dispatch, collect;
-    # local layer in rows mode (permute x3, grouped_plan, gather_tokens,
-    # grouped); return, finish; combine  (NCCL: ep_dispatch, ep_unpack instead
-    # of dispatch/collect/return/finish)
-    launches = 16 if transport == "p2p" else 14
+    # p2p: router_tc + router_select; permute count/colscan/place; publish;
+    # plan, grouped; finish; combine.  NCCL: router x2, permute x3,
+    # ep_dispatch, ep_unpack, the local layer in rows mode (permute x3,
+    # grouped_plan, gather_tokens, grouped), combine
+    launches = 10 if transport == "p2p" else 14
     res = {
         "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -966,7 +982,8 @@ def run_ep(args, world, rank, local) -> dict:
                    "rank0_routes_leaving": leaving, "rank0_distinct_local_experts": u_local,
                    "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window",
                    "timing": timing},
-        "roofline": roofline("swiglu_grouped_kernel (rank 0: local experts + shared, rows mode)", kernel_bytes,
+        "roofline": roofline("swiglu_grouped_kernel (rank 0: local experts + shared expert; in-kernel row pull "
+                             "and return over NVLink)", kernel_bytes,
                              kernel_flops, statistics.mean(kern_ms), pk, traffic=traffic,
                              traffic_source=traffic_src),
         "e2e": {"value": round(world * tokens * args.steps / (e2e_total / 1e3), 2), "unit": "tokens/s",

@@ -403,38 +403,45 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
                    int hidden, uint16_t *out, void *stream);
 
 /* ------------------------------------------------------------------------
- * Expert-parallel exchange over NVLink peer memory (no host synchronisation;
- * no counterpart in the reference).  Every rank allocates one symmetric
- * buffer with moe_ipc_alloc (zero-filled; the 64-byte handle goes to the
- * peers, which map it with moe_ipc_open) holding, at the byte offsets below:
- * flags_dispatch uint32[world], flags_return uint32[world], count int32[world],
- * meta int32[world][capacity][2], rows BF16[own_rows + world*capacity][hidden]
- * (at off_rx: the rank's own tokens, then sender s's rows at own_rows +
- * s*capacity) and ret BF16[capacity][hidden]; capacity >= tokens * top_k,
- * own_rows >= tokens.  `peers` lists every rank's buffer as mapped in this
+ * Expert-parallel step over NVLink peer memory, with the exchange fused into
+ * the expert kernel (no host synchronisation; no counterpart in the
+ * reference).  Every rank allocates one symmetric buffer with moe_ipc_alloc
+ * (zero-filled; the 64-byte handle goes to the peers, which map it with
+ * moe_ipc_open) holding, at the byte offsets below: flags_publish
+ * uint32[world], flags_return uint32[world], count int32[world], meta
+ * int32[world][capacity][4], tokens BF16[own_rows][hidden] (the rank's own
+ * token rows) and ret BF16[capacity][hidden]; capacity >= own_rows * top_k,
+ * own_rows >= the tokens of any step, offsets of tokens, meta and ret
+ * 16-byte aligned.  `peers` lists every rank's buffer as mapped in this
  * process (its own included); step (uint32, start at 1), sync (int32[2],
  * zero) and error are this rank's device words.  One step:
  *   moe_router_topk(_ws), moe_permute(_wide) of the rank's own tokens;
- *   moe_ep_p2p_dispatch   rows and (local expert, position) into the owners'
- *                         rows / meta, then releases their flags_dispatch;
- *   moe_ep_p2p_collect    copies the own tokens into rows, waits for every
- *                         sender, writes route_in [own_rows + world*capacity]
- *                         (own tokens -> the shared expert, local id
- *                         local_experts; slots no sender filled -> -1) and each
- *                         received row's return address;
- *   moe_layer_forward     rows_mode over the rows region (x = buffer + off_rx,
- *                         own_rows + world*capacity tokens), local experts
- *                         plus the shared expert appended as local expert El;
- *   moe_ep_p2p_return     rows back to their senders' ret, releases
- *                         flags_return;
- *   moe_ep_p2p_finish     waits for every return, advances *step;
- *   moe_ep_combine        over ret (in the permuted order), scores, the shared
- *                         rows and sig.
- * Waits give up after 1 s with *error = 1 (dispatch) or 2 (return); the GPU
- * is never left waiting. */
+ *   moe_ep_p2p_publish  copies x into tokens and writes one entry (local
+ *                       expert, position, token) per route into the owning
+ *                       rank's meta, then releases its flags_publish; no
+ *                       token row crosses a link here;
+ *   moe_ep_p2p_experts  on the owner: waits for every sender, plans one group
+ *                       per local expert with routes plus the shared expert
+ *                       over the own tokens, then runs the grouped tensor-core
+ *                       kernel, which pulls each row from its sender's tokens
+ *                       over NVLink and stores its down row into the sender's
+ *                       ret (the shared expert's rows into shared_rows
+ *                       [tokens, hidden]); gate_up [El+1, 2I, H] and down
+ *                       [El+1, H, I] hold the local experts, then the shared
+ *                       expert; stats (or NULL): int32 [2 + world] = rows
+ *                       received, local experts with rows, rows per sender;
+ *                       kernel_events (or NULL): two cudaEvent_t recorded
+ *                       around the grouped kernel;
+ *   moe_ep_p2p_finish   releases every sender's flags_return, waits for every
+ *                       owner's, advances *step;
+ *   moe_ep_combine      over ret (in the permuted order), scores, shared_rows
+ *                       and sig.
+ * Waits give up (1 s for the flags, 2 s inside the expert kernel) with
+ * *error = 1 (publish), 2 (return) or 3 (expert kernel); the GPU is never
+ * left waiting. */
 typedef struct moe_ep_p2p {
     const int64_t *peers;
-    int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
+    int64_t off_flags_publish, off_flags_return, off_count, off_meta, off_tokens, off_ret;
     int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
     int32_t *sync, *error;
@@ -444,13 +451,13 @@ int moe_ipc_alloc(size_t bytes, void **ptr, void *handle64);
 int moe_ipc_free(void *ptr);
 int moe_ipc_open(const void *handle64, void **ptr);
 int moe_ipc_close(void *ptr);
-int moe_ep_p2p_dispatch(const moe_ep_p2p *p, const uint16_t *x, const int64_t *idx,
-                        const int32_t *offsets, const int32_t *perm_token,
-                        const int32_t *perm_slot, void *stream);
-int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int64_t *route_in,
-                       int64_t *ret_addr, void *stream);
-int moe_ep_p2p_return(const moe_ep_p2p *p, const uint16_t *rows, const int64_t *ret_addr,
-                      void *stream);
+int moe_ep_p2p_publish(const moe_ep_p2p *p, const uint16_t *x, int tokens, const int64_t *idx,
+                       const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot,
+                       void *stream);
+size_t moe_ep_p2p_workspace_bytes(const moe_ep_p2p *p, int inner);
+int moe_ep_p2p_experts(const moe_ep_p2p *p, const uint16_t *gate_up, const uint16_t *down, int inner,
+                       int tokens, uint16_t *shared_rows, int32_t *stats, void *workspace,
+                       size_t workspace_bytes, void *const *kernel_events, void *stream);
 int moe_ep_p2p_finish(const moe_ep_p2p *p, void *stream);
 
 #ifdef __cplusplus

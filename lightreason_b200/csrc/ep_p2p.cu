@@ -1,40 +1,49 @@
-// Expert-parallel exchange over NVLink peer memory, without host
-// synchronisation: every rank owns one symmetric buffer (same layout on all
-// ranks, mapped into every peer by CUDA IPC), and the ranks' kernels meet
-// through release/acquire flags in those buffers.
+// Expert-parallel exchange over NVLink peer memory, fused with the experts
+// and without host synchronisation: every rank owns one symmetric buffer (same
+// layout on all ranks, mapped into every peer by CUDA IPC), and the ranks'
+// kernels meet through release/acquire flags in those buffers.
 //
-// Symmetric buffer of rank q (W ranks, C = capacity rows per source, T0 own
-// token rows):
-//   flags_dispatch uint32 [W]   step at which rank s finished writing into q
-//   flags_return   uint32 [W]   step at which rank d finished returning q's rows
-//   count          int32  [W]   rows rank s wrote into q this step
-//   meta           int32  [W][C][2]  (local expert on q, position on s)
-//   rows           bf16   [T0 + W*C][H]  q's own tokens, then rank s's rows at
-//                                        T0 + s*C: the local layer's input
-//   ret            bf16   [C][H]     q's own routes' expert rows, by position
+// Symmetric buffer of rank q (W ranks, C = capacity routes per sender, T0 =
+// own token rows):
+//   flags_publish uint32 [W]      step at which rank s published its routes to q
+//   flags_return  uint32 [W]      step at which rank d finished q's rows
+//   count         int32  [W]      routes rank s sent to q this step
+//   meta          int32  [W][C][4] (local expert on q, position on s, token on s, 0)
+//   tokens        bf16   [T0][H]  q's own token rows, read by the owners
+//   ret           bf16   [C][H]   q's routes' expert rows, by position
 //
 // One step on rank r (the step number lives in device memory and advances at
 // the end of the step, so a captured CUDA graph replays correctly):
-//   dispatch  route position p of expert e goes to rank d = e / El, slot
-//             j = p - offsets[d * El]: row x[perm_token[p]] -> d.rx[r][j],
-//             (e % El, p) -> d.meta[r][j]; the last CTA writes d.count[r] and
-//             releases d.flags_dispatch[r] = step.
-//   collect   copy the own tokens into rows[0, T); wait for every
-//             flags_dispatch[s] == step; route_in of every row = its local
-//             expert (own tokens: the shared expert, El; rows no sender wrote:
-//             -1, dropped by the layer, whose token gather is the one
-//             compaction) and the peer address each received row returns to.
-//   return    after the local layer (rows mode): each received row -> its
-//             sender's ret[p]; the last CTA releases s.flags_return[r] = step.
-//   finish    wait for every flags_return[d] == step, advance the step; the
-//             ordered combine then reads ret.
+//   publish  x -> r.tokens; route position p of expert e goes to rank
+//            d = e / El as entry j = p - offsets[d * El] of d.meta[r]:
+//            (e % El, p, token); the last CTA writes d.count[r] and releases
+//            d.flags_publish[r] = step.  No token row moves here.
+//   experts  plan (one CTA): wait for every flags_publish[s] == step, then lay
+//            out one group per local expert with routes (ascending id; within
+//            it sender by sender, each sender's routes in its own order) and
+//            the shared expert's group of the own tokens last, and for every
+//            row the address it is read from (sender s's tokens row) and the
+//            address its down output goes to (s.ret[p], or for a shared row
+//            the caller's shared_rows[t]).  Then the grouped tensor-core
+//            kernel in address-table mode: its gather warps pull the rows
+//            over NVLink as the weights start streaming, and its epilogue
+//            stores every down row straight into the sender's ret.
+//   finish   releases s.flags_return[r] = step for every s (r's reads of their
+//            tokens and its writes into their ret are complete), waits for
+//            every flags_return[d] == step (r.ret is complete), advances the
+//            step; the ordered combine then reads ret.
+// Buffer reuse across steps is ordered by the flags: a rank overwrites its
+// tokens and the owners' meta only in the next step, after every owner
+// released it in finish, i.e. after the owners' kernels that read them.
 // Every wait is bounded (globaltimer): on timeout the kernel stores an error
-// code in *error and returns, so a missing peer cannot hang the GPU.
+// code in *error and carries on without the missing data, so a missing peer
+// cannot hang the GPU.
 //
 // The reference runs its MoE layer on one GPU; this exchange has no
 // counterpart there.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "routing.cuh"
 
 namespace lrb {
 
@@ -103,117 +112,200 @@ __device__ __forceinline__ bool last_cta(int32_t *counter) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(256) ep_p2p_dispatch_kernel(EpP2PArgs a, const uint16_t *__restrict__ x,
-                                                              const int64_t *__restrict__ idx,
-                                                              const int32_t *__restrict__ offsets,
-                                                              const int32_t *__restrict__ perm_token,
-                                                              const int32_t *__restrict__ perm_slot) {
+__global__ void __launch_bounds__(256) ep_p2p_publish_kernel(EpP2PArgs a, const uint16_t *__restrict__ x,
+                                                             int tokens, const int64_t *__restrict__ idx,
+                                                             const int32_t *__restrict__ offsets,
+                                                             const int32_t *__restrict__ perm_token,
+                                                             const int32_t *__restrict__ perm_slot) {
     grid_dependency_wait();
     const uint32_t step = *a.step;
     const int lane = threadIdx.x & 31;
-    const int routes = offsets[a.experts];
-    const int warps = gridDim.x * (blockDim.x >> 5);
     const int El = a.local_experts;
-    for (int p = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < routes; p += warps) {
+    // the own token rows, where the owners read them
+    uint16_t *own = reinterpret_cast<uint16_t *>(peer_base(a, a.rank) + a.off_tokens);
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += warps)
+        warp_copy_row(x + static_cast<size_t>(t) * a.hidden, own + static_cast<size_t>(t) * a.hidden, a.hidden, lane);
+    // one 16-byte entry per route into its owner's meta
+    const int routes = offsets[a.experts];
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < routes; p += gridDim.x * blockDim.x) {
         const int t = perm_token[p], k = perm_slot[p];
         const int e = static_cast<int>(idx[static_cast<size_t>(t) * a.top_k + k]);
         const int d = e / El;
         const int j = p - offsets[d * El];
-        uint8_t *dst = peer_base(a, d);
-        const size_t slot = static_cast<size_t>(a.rank) * a.capacity + j;
-        warp_copy_row(x + static_cast<size_t>(t) * a.hidden,
-                      reinterpret_cast<uint16_t *>(dst + a.off_rx) + (a.own_rows + slot) * a.hidden, a.hidden, lane);
-        if (lane == 0) {
-            int32_t *meta = reinterpret_cast<int32_t *>(dst + a.off_meta) + slot * 2;
-            meta[0] = e % El;
-            meta[1] = p;
-        }
+        if (j < 0 || j >= a.capacity) continue;  // cannot happen for a valid permute
+        int4 *meta = reinterpret_cast<int4 *>(peer_base(a, d) + a.off_meta) + static_cast<size_t>(a.rank) * a.capacity;
+        meta[j] = make_int4(e - d * El, p, t, 0);
     }
     if (last_cta(a.sync + 0)) {
         if (threadIdx.x < a.world) {
             const int d = threadIdx.x;
             uint8_t *dst = peer_base(a, d);
             const int lo = min(d * El, a.experts), hi = min((d + 1) * El, a.experts);
-            reinterpret_cast<int32_t *>(dst + a.off_count)[a.rank] = offsets[hi] - offsets[lo];
+            reinterpret_cast<int32_t *>(dst + a.off_count)[a.rank] = min(offsets[hi] - offsets[lo], a.capacity);
             __threadfence_system();
-            st_release_sys(reinterpret_cast<uint32_t *>(dst + a.off_flags_dispatch) + a.rank, step);
+            st_release_sys(reinterpret_cast<uint32_t *>(dst + a.off_flags_publish) + a.rank, step);
         }
         if (threadIdx.x == 0) a.sync[0] = 0;
     }
 }
 
-// route_in [own_rows + W*C] int64 and ret_addr [W*C] int64, both indexed like
-// the rows region (the layer's input and output rows).
-__global__ void __launch_bounds__(256) ep_p2p_collect_kernel(EpP2PArgs a, const uint16_t *__restrict__ x,
-                                                             int tokens, int64_t *__restrict__ route_in,
-                                                             int64_t *__restrict__ ret_addr) {
-    grid_dependency_wait();
+// The owner's plan (one CTA of 1024 threads), see the file comment.  cnt is
+// the [El][W] table of routes per (local expert, sender); E = El * W <= 1024.
+struct EpPlanOut {
+    GroupedGroup *groups;
+    GroupedPlan *plan;
+    int32_t *off1, *off2, *done1, *done2, *row_ready;
+    int64_t *src_rows, *dst_rows;
+    uint16_t *shared_rows;
+    uint16_t *trash_row;  // one row [H] that catches a malformed entry's output
+    int32_t *stats;  // [2 + W]: rows received, local experts with rows, rows per sender
+    int tokens, bn, mb1, mb2;
+};
+
+__global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOut o) {
+    __shared__ int cnt[1024], base[1024], first[1024];
+    __shared__ int sent[64], valid[64];
+    __shared__ int scratch[33];
     __shared__ int ok;
+    grid_dependency_wait();
+    grid_dependency_trigger();
     const uint32_t step = *a.step;
+    const int W = a.world, El = a.local_experts, E = El * W, C = a.capacity;
     uint8_t *self = peer_base(a, a.rank);
-    uint16_t *rows = reinterpret_cast<uint16_t *>(self + a.off_rx);
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    // own tokens first: the shared expert's rows (no wait needed)
-    for (int t = gw; t < a.own_rows; t += warps) {
-        if (t < tokens) warp_copy_row(x + static_cast<size_t>(t) * a.hidden, rows + static_cast<size_t>(t) * a.hidden,
-                                      a.hidden, lane);
-        if (lane == 0) route_in[t] = t < tokens ? a.local_experts : -1;
-    }
     if (threadIdx.x == 0) {
-        ok = wait_flags(reinterpret_cast<const uint32_t *>(self + a.off_flags_dispatch), a.world, step);
+        ok = wait_flags(reinterpret_cast<const uint32_t *>(self + a.off_flags_publish), W, step);
         if (!ok) atomicExch(a.error, 1);
     }
+    for (int i = threadIdx.x; i < E; i += blockDim.x) cnt[i] = 0;
     __syncthreads();
-    if (!ok) return;
     const int32_t *count = reinterpret_cast<const int32_t *>(self + a.off_count);
-    const int32_t *meta = reinterpret_cast<const int32_t *>(self + a.off_meta);
-    const int slots = a.world * a.capacity;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < slots; i += gridDim.x * blockDim.x) {
-        const int q = i / a.capacity, j = i - q * a.capacity;
-        if (j < count[q]) {
-            route_in[a.own_rows + i] = meta[static_cast<size_t>(i) * 2];
-            ret_addr[i] = a.peers[q] + a.off_ret + static_cast<int64_t>(meta[static_cast<size_t>(i) * 2 + 1]) *
-                                                       a.hidden * 2;
-        } else {
-            route_in[a.own_rows + i] = -1;
+    const int4 *meta = reinterpret_cast<const int4 *>(self + a.off_meta);
+    if (threadIdx.x < W) sent[threadIdx.x] = ok ? min(max(__ldcg(count + threadIdx.x), 0), C) : 0;
+    __syncthreads();
+    // routes per (local expert, sender); the entries of a sender are in its
+    // permuted order, so ascending in local expert
+    for (int s = 0; s < W; ++s)
+        for (int j = threadIdx.x; j < sent[s]; j += blockDim.x) {
+            const int le = __ldcg(meta + static_cast<size_t>(s) * C + j).x;
+            if (le >= 0 && le < El) atomicAdd(&cnt[le * W + s], 1);
+        }
+    __syncthreads();
+    if (threadIdx.x < W) {
+        int v = 0;
+        for (int le = 0; le < El; ++le) v += cnt[le * W + threadIdx.x];
+        valid[threadIdx.x] = v;
+    }
+    // base[le][s]: the first row of sender s's routes in expert le's group
+    // (scan in (le, s) order); first[le][s]: sender s's first entry of expert
+    // le (scan in (s, le) order, minus the entries of the senders before s)
+    int routed = 0, dummy = 0;
+    const int i = threadIdx.x;
+    const int v_ls = i < E ? cnt[i] : 0;
+    const int b = block_exclusive_scan(v_ls, scratch, &routed);
+    if (i < E) base[i] = b;
+    const int s_major = i < E ? cnt[(i % El) * W + i / El] : 0;  // entry i = (s, le) = (i / El, i % El)
+    const int f = block_exclusive_scan(s_major, scratch, &dummy);
+    __syncthreads();
+    if (i < E) {
+        const int s = i / El, le = i % El;
+        int before = 0;  // entries of the senders before s
+        for (int s2 = 0; s2 < s; ++s2) before += valid[s2];
+        first[le * W + s] = f - before;
+    }
+    // groups: local experts with rows in ascending id, then the shared expert
+    int tot_le = 0;
+    if (i < El)
+        for (int s = 0; s < W; ++s) tot_le += cnt[i * W + s];
+    int n_active = 0;
+    const int g = block_exclusive_scan(tot_le > 0 ? 1 : 0, scratch, &n_active);
+    const int nt = (tot_le + o.bn - 1) / o.bn;
+    int t1 = 0, t2 = 0;
+    const int e1 = block_exclusive_scan(tot_le > 0 ? o.mb1 * nt : 0, scratch, &t1);
+    const int e2 = block_exclusive_scan(tot_le > 0 ? o.mb2 * nt : 0, scratch, &t2);
+    if (i < El && tot_le > 0) {
+        GroupedGroup G;
+        G.weight = i;
+        G.begin = base[i * W];
+        G.count = tot_le;
+        G.ntiles = nt;
+        o.groups[g] = G;
+        o.off1[g] = e1;
+        o.off2[g] = e2;
+        o.done1[g] = 0;
+        o.done2[g] = 0;
+        o.row_ready[g] = 0;
+    }
+    if (threadIdx.x == 0) {
+        GroupedGroup G;  // the shared expert: bank entry El, the own tokens
+        G.weight = El;
+        G.begin = routed;
+        G.count = o.tokens;
+        G.ntiles = (o.tokens + o.bn - 1) / o.bn;
+        const int n = n_active;
+        o.groups[n] = G;
+        o.off1[n] = t1;
+        o.off2[n] = t2;
+        o.done1[n] = 0;
+        o.done2[n] = 0;
+        o.row_ready[n] = 0;
+        o.off1[n + 1] = t1 + o.mb1 * G.ntiles;
+        o.off2[n + 1] = t2 + o.mb2 * G.ntiles;
+        o.plan->num_groups = n + 1;
+        o.plan->items1 = t1 + o.mb1 * G.ntiles;
+        o.plan->items2 = t2 + o.mb2 * G.ntiles;
+        o.plan->items3 = 0;
+        o.plan->work = 0;
+        o.plan->error = ok ? 0 : 4;
+        o.plan->done2_total = 0;
+        o.plan->xs_ready = 0;
+        o.plan->act_ready = 0;
+        if (o.stats) {
+            o.stats[0] = routed;
+            o.stats[1] = n_active;
         }
     }
-}
-
-// rows [W*C, H]: the local layer's unweighted rows of the received slots
-// (the layer's output rows past the own tokens).
-__global__ void __launch_bounds__(256) ep_p2p_return_kernel(EpP2PArgs a, const uint16_t *__restrict__ rows,
-                                                            const int64_t *__restrict__ ret_addr) {
-    grid_dependency_wait();
-    const uint32_t step = *a.step;
-    const int lane = threadIdx.x & 31;
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    const int32_t *count = reinterpret_cast<const int32_t *>(peer_base(a, a.rank) + a.off_count);
-    if (*a.error == 0) {
-        const int slots = a.world * a.capacity;
-        for (int i = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); i < slots; i += warps) {
-            const int q = i / a.capacity, j = i - q * a.capacity;
-            if (j < count[q])
-                warp_copy_row(rows + static_cast<size_t>(i) * a.hidden, reinterpret_cast<uint16_t *>(ret_addr[i]),
-                              a.hidden, lane);
+    if (o.stats && threadIdx.x < W) o.stats[2 + threadIdx.x] = sent[threadIdx.x];
+    // the address tables: routed rows, then the shared rows.  Every routed row
+    // first gets a harmless pair (the own first token row, the trash row), so
+    // no row is left with a stale address even if a sender's entries were
+    // malformed; a valid permute then overwrites each of them once.
+    const int64_t rowb = static_cast<int64_t>(a.hidden) * 2;
+    const int64_t own = a.peers[a.rank] + a.off_tokens;
+    for (int r = threadIdx.x; r < routed; r += blockDim.x) {
+        o.src_rows[r] = own;
+        o.dst_rows[r] = reinterpret_cast<int64_t>(o.trash_row);
+    }
+    __syncthreads();
+    for (int s = 0; s < W; ++s) {
+        const int64_t peer = a.peers[s];
+        for (int j = threadIdx.x; j < sent[s]; j += blockDim.x) {
+            const int4 m = __ldcg(meta + static_cast<size_t>(s) * C + j);
+            if (m.x < 0 || m.x >= El || m.y < 0 || m.y >= C || m.z < 0 || m.z >= a.own_rows) continue;
+            const int row = base[m.x * W + s] + (j - first[m.x * W + s]);
+            if (row < 0 || row >= routed) continue;
+            o.src_rows[row] = peer + a.off_tokens + m.z * rowb;
+            o.dst_rows[row] = peer + a.off_ret + m.y * rowb;
         }
     }
-    if (last_cta(a.sync + 1)) {
-        if (threadIdx.x < a.world) {
-            uint8_t *src = peer_base(a, threadIdx.x);
-            st_release_sys(reinterpret_cast<uint32_t *>(src + a.off_flags_return) + a.rank, step);
-        }
-        if (threadIdx.x == 0) a.sync[1] = 0;
+    for (int t = threadIdx.x; t < o.tokens; t += blockDim.x) {
+        o.src_rows[routed + t] = own + t * rowb;
+        o.dst_rows[routed + t] = reinterpret_cast<int64_t>(o.shared_rows) + t * rowb;
     }
 }
 
 __global__ void ep_p2p_finish_kernel(EpP2PArgs a) {
     grid_dependency_wait();
     const uint32_t step = *a.step;
-    uint8_t *self = peer_base(a, a.rank);
+    if (threadIdx.x < a.world) {
+        // this rank's reads of the peers' tokens and its stores into their ret
+        // (by the expert kernel, which ended with a system fence) are complete
+        __threadfence_system();
+        st_release_sys(reinterpret_cast<uint32_t *>(peer_base(a, threadIdx.x) + a.off_flags_return) + a.rank, step);
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
+        uint8_t *self = peer_base(a, a.rank);
         if (!wait_flags(reinterpret_cast<const uint32_t *>(self + a.off_flags_return), a.world, step))
             atomicExch(a.error, 2);
         *a.step = step + 1;
@@ -228,20 +320,25 @@ int check_p2p(const moe_ep_p2p *p) {
     LRB_REQUIRE(p && p->peers && p->step && p->sync && p->error, "ep_p2p: null argument");
     LRB_REQUIRE(p->world >= 1 && p->world <= 64 && p->rank >= 0 && p->rank < p->world,
                 "ep_p2p: rank %d / world %d out of range", p->rank, p->world);
-    LRB_REQUIRE(p->experts % p->world == 0 && p->local_experts == p->experts / p->world,
-                "ep_p2p: %d experts do not shard over %d ranks", p->experts, p->world);
-    LRB_REQUIRE(p->hidden > 0 && p->hidden % 8 == 0 && p->capacity > 0 && p->top_k >= 1, "ep_p2p: bad shape");
+    LRB_REQUIRE(p->experts % p->world == 0 && p->local_experts == p->experts / p->world && p->experts <= 1024,
+                "ep_p2p: %d experts do not shard over %d ranks (at most 1024 experts)", p->experts, p->world);
+    LRB_REQUIRE(p->hidden > 0 && p->hidden % 1024 == 0 && p->capacity > 0 && p->top_k >= 1 && p->own_rows > 0 &&
+                    p->capacity >= p->own_rows * p->top_k,
+                "ep_p2p: bad shape (hidden %d, capacity %d, own rows %d, top_k %d)", p->hidden, p->capacity,
+                p->own_rows, p->top_k);
+    LRB_REQUIRE(p->off_tokens % 16 == 0 && p->off_ret % 16 == 0 && p->off_meta % 16 == 0,
+                "ep_p2p: token rows, ret and meta offsets must be 16-byte aligned");
     return MOE_OK;
 }
 
 lrb::EpP2PArgs args_of(const moe_ep_p2p *p) {
     lrb::EpP2PArgs a{};
     a.peers = p->peers;
-    a.off_flags_dispatch = p->off_flags_dispatch;
+    a.off_flags_publish = p->off_flags_publish;
     a.off_flags_return = p->off_flags_return;
     a.off_count = p->off_count;
     a.off_meta = p->off_meta;
-    a.off_rx = p->off_rx;
+    a.off_tokens = p->off_tokens;
     a.off_ret = p->off_ret;
     a.world = p->world;
     a.rank = p->rank;
@@ -254,11 +351,52 @@ lrb::EpP2PArgs args_of(const moe_ep_p2p *p) {
     a.step = p->step;
     a.sync = p->sync;
     a.error = p->error;
-
     return a;
 }
 
 int copy_grid() { return lrb::sm_count() * 2; }
+
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Workspace of moe_ep_p2p_experts: the plan of the grouped kernel, the
+// address tables and the route-ordered rows and activations, for the most
+// rows an owner can receive (every sender's capacity) plus its own tokens.
+struct ExpertsLayout {
+    size_t groups, plan, off1, off2, done1, done2, ready, split, src, dst, trash, xs, act, total;
+    int rows;
+};
+ExpertsLayout experts_layout(const moe_ep_p2p *p, int inner) {
+    ExpertsLayout L{};
+    const size_t G = static_cast<size_t>(p->local_experts) + 1;
+    L.rows = p->own_rows + p->world * p->capacity;
+    size_t o = 0;
+    auto take = [&](size_t bytes) {
+        const size_t at = o;
+        o = align_up(o + bytes);
+        return at;
+    };
+    L.groups = take(G * sizeof(lrb::GroupedGroup));
+    L.plan = take(sizeof(lrb::GroupedPlan));
+    L.off1 = take((G + 1) * 4);
+    L.off2 = take((G + 1) * 4);
+    L.done1 = take(G * 4);
+    L.done2 = take(G * 4);
+    L.ready = take(G * 4);
+    L.split = take(16);
+    L.src = take(static_cast<size_t>(L.rows) * 8);
+    L.dst = take(static_cast<size_t>(L.rows) * 8);
+    L.trash = take(static_cast<size_t>(p->hidden) * 2);
+    L.xs = take(static_cast<size_t>(L.rows) * p->hidden * 2);
+    L.act = take(static_cast<size_t>(L.rows) * inner * 2);
+    L.total = o;
+    return L;
+}
+
+template <class T>
+T *at(void *base, size_t offset) {
+    return reinterpret_cast<T *>(static_cast<char *>(base) + offset);
+}
 
 }  // namespace
 
@@ -296,35 +434,106 @@ int moe_ipc_close(void *ptr) {
     return MOE_OK;
 }
 
-int moe_ep_p2p_dispatch(const moe_ep_p2p *p, const uint16_t *x, const int64_t *idx, const int32_t *offsets,
-                        const int32_t *perm_token, const int32_t *perm_slot, void *stream) {
+int moe_ep_p2p_publish(const moe_ep_p2p *p, const uint16_t *x, int tokens, const int64_t *idx,
+                       const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot, void *stream) {
     if (int rc = check_p2p(p)) return rc;
-    LRB_REQUIRE(x && idx && offsets && perm_token && perm_slot, "moe_ep_p2p_dispatch: null input");
-    return lrb::launch_pdl(lrb::ep_p2p_dispatch_kernel, dim3(copy_grid()), dim3(256), 0,
-                           static_cast<cudaStream_t>(stream), "ep_p2p_dispatch_kernel", args_of(p), x, idx, offsets,
-                           perm_token, perm_slot);
+    LRB_REQUIRE(x && idx && offsets && perm_token && perm_slot, "moe_ep_p2p_publish: null input");
+    LRB_REQUIRE(tokens >= 0 && tokens <= p->own_rows, "moe_ep_p2p_publish: tokens %d > own rows %d", tokens,
+                p->own_rows);
+    LRB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, "moe_ep_p2p_publish: x must be 16-byte aligned");
+    return lrb::launch_pdl(lrb::ep_p2p_publish_kernel, dim3(copy_grid()), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), "ep_p2p_publish_kernel", args_of(p), x, tokens, idx,
+                           offsets, perm_token, perm_slot);
 }
 
-int moe_ep_p2p_collect(const moe_ep_p2p *p, const uint16_t *x, int tokens, int64_t *route_in, int64_t *ret_addr,
-                       void *stream) {
-    if (int rc = check_p2p(p)) return rc;
-    LRB_REQUIRE(x && route_in && ret_addr && tokens >= 0 && tokens <= p->own_rows,
-                "moe_ep_p2p_collect: bad input (tokens %d, own rows %d)", tokens, p->own_rows);
-    return lrb::launch_pdl(lrb::ep_p2p_collect_kernel, dim3(copy_grid()), dim3(256), 0,
-                           static_cast<cudaStream_t>(stream), "ep_p2p_collect_kernel", args_of(p), x, tokens,
-                           route_in, ret_addr);
+size_t moe_ep_p2p_workspace_bytes(const moe_ep_p2p *p, int inner) {
+    if (check_p2p(p) != MOE_OK || (inner != 256 && inner != 512 && inner != 1024)) return 0;
+    return experts_layout(p, inner).total;
 }
 
-int moe_ep_p2p_return(const moe_ep_p2p *p, const uint16_t *rows, const int64_t *ret_addr, void *stream) {
+int moe_ep_p2p_experts(const moe_ep_p2p *p, const uint16_t *gate_up, const uint16_t *down, int inner, int tokens,
+                       uint16_t *shared_rows, int32_t *stats, void *workspace, size_t workspace_bytes,
+                       void *const *kernel_events, void *stream) {
+    using namespace lrb;
     if (int rc = check_p2p(p)) return rc;
-    LRB_REQUIRE(rows && ret_addr, "moe_ep_p2p_return: null input");
-    return lrb::launch_pdl(lrb::ep_p2p_return_kernel, dim3(copy_grid()), dim3(256), 0,
-                           static_cast<cudaStream_t>(stream), "ep_p2p_return_kernel", args_of(p), rows, ret_addr);
+    LRB_REQUIRE(gate_up && down && shared_rows, "moe_ep_p2p_experts: null input");
+    LRB_REQUIRE(inner == 256 || inner == 512 || inner == 1024, "moe_ep_p2p_experts: inner %d not in {256, 512, 1024}",
+                inner);
+    LRB_REQUIRE(tokens >= 1 && tokens <= p->own_rows, "moe_ep_p2p_experts: tokens %d outside [1, %d]", tokens,
+                p->own_rows);
+    auto a16 = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    LRB_REQUIRE(a16(gate_up) && a16(down) && a16(shared_rows) && a16(workspace),
+                "moe_ep_p2p_experts: banks, shared_rows and workspace must be 16-byte aligned");
+    const ExpertsLayout L = experts_layout(p, inner);
+    LRB_REQUIRE(workspace && workspace_bytes >= L.total, "moe_ep_p2p_experts: workspace %zu < %zu bytes",
+                workspace_bytes, L.total);
+    if (int rc = require_sm100()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int H = p->hidden, I = inner, El = p->local_experts;
+    const int bn = grouped_bn_for(L.rows);
+    EpPlanOut o{};
+    o.groups = at<GroupedGroup>(workspace, L.groups);
+    o.plan = at<GroupedPlan>(workspace, L.plan);
+    o.off1 = at<int32_t>(workspace, L.off1);
+    o.off2 = at<int32_t>(workspace, L.off2);
+    o.done1 = at<int32_t>(workspace, L.done1);
+    o.done2 = at<int32_t>(workspace, L.done2);
+    o.row_ready = at<int32_t>(workspace, L.ready);
+    o.src_rows = at<int64_t>(workspace, L.src);
+    o.dst_rows = at<int64_t>(workspace, L.dst);
+    o.shared_rows = shared_rows;
+    o.trash_row = at<uint16_t>(workspace, L.trash);
+    o.stats = stats;
+    o.tokens = tokens;
+    o.bn = bn;
+    o.mb1 = I / 128;
+    o.mb2 = H / 256;
+    if (int rc = launch_pdl(ep_p2p_plan_kernel, dim3(1), dim3(1024), 0, s, "ep_p2p_plan_kernel", args_of(p), o))
+        return rc;
+    cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+    if (kernel_events) LRB_CUDA(cudaStreamIsCapturing(s, &capturing));
+    auto mark = [&](int i) -> int {
+        if (kernel_events && kernel_events[i])
+            LRB_CUDA(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(kernel_events[i]), s,
+                                              capturing == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
+                                                                                         : cudaEventRecordDefault));
+        return MOE_OK;
+    };
+    if (int rc = mark(0)) return rc;
+    GroupedLaunch GL{};
+    GL.gate_up = gate_up;
+    GL.down = down;
+    GL.gate_up_stride = static_cast<int64_t>(2) * I * H;
+    GL.down_stride = static_cast<int64_t>(H) * I;
+    GL.bank_experts = El + 1;
+    GL.xs = at<uint16_t>(workspace, L.xs);
+    GL.act = at<uint16_t>(workspace, L.act);
+    GL.rows = L.rows;
+    GL.groups = o.groups;
+    GL.plan = o.plan;
+    GL.off1 = o.off1;
+    GL.off2 = o.off2;
+    GL.done1 = o.done1;
+    GL.done2 = o.done2;
+    GL.split_cnt = at<int32_t>(workspace, L.split);
+    GL.src_rows = o.src_rows;
+    GL.dst_rows = o.dst_rows;
+    GL.row_ready = o.row_ready;
+    GL.error_out = p->error;
+    GL.tokens = tokens;
+    GL.top_k = 1;
+    GL.hidden = H;
+    GL.inner = I;
+    GL.bn = bn;
+    GL.ks = 1;  // the plan's item counts have no K split
+    GL.ctas = sm_count();
+    if (int rc = launch_grouped(GL, s)) return rc;
+    return mark(1);
 }
 
 int moe_ep_p2p_finish(const moe_ep_p2p *p, void *stream) {
     if (int rc = check_p2p(p)) return rc;
-    return lrb::launch_pdl(lrb::ep_p2p_finish_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream),
+    return lrb::launch_pdl(lrb::ep_p2p_finish_kernel, dim3(1), dim3(64), 0, static_cast<cudaStream_t>(stream),
                            "ep_p2p_finish_kernel", args_of(p));
 }
 

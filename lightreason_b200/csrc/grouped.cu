@@ -27,12 +27,24 @@
 // weights; the last split of a tile sums the FP32 partials in split order, so
 // results do not depend on timing.
 //
-// Per CTA (192 threads, one CTA per SM): warp 0 issues TMA loads of 64-wide K
+// Per CTA (256 threads, one CTA per SM): warp 0 issues TMA loads of 64-wide K
 // slices (128B swizzle) into a ring of stages; warp 1 allocates TMEM and issues
 // tcgen05.mma (M=128, N=BN, K=16) into a double-buffered FP32 accumulator;
 // warps 2-5 read the accumulator with tcgen05.ld, write BF16 results and run
-// the combine.  Every wait is bounded (globaltimer); on timeout the CTA raises
-// the plan's error word, drains its own TMA and MMA work and returns.
+// the combine; warps 6-7 gather the token rows in address-table mode.  Every
+// wait is bounded (globaltimer); on timeout the CTA raises the plan's error
+// word, drains its own TMA and MMA work and returns.
+//
+// Address-table mode (src_rows / dst_rows, the expert-parallel step): row p
+// of the plan is read from the 16-byte-aligned address src_rows[p] -- this
+// GPU's memory or a peer's over NVLink -- and its down output is stored to
+// dst_rows[p], again local or a peer's.  Warps 6-7 of every CTA copy the rows
+// into the route-ordered buffer in plan order, two rows in flight per warp,
+// and count each finished row into its group; a phase-1 item's token tiles
+// wait only for its own group's rows, so the tensor cores start on the first
+// groups while later rows are still crossing the links.  The epilogue warps
+// end with a system-scope fence, so their stores into peers' memory are
+// visible before the caller releases the peers.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -53,7 +65,7 @@ namespace {
 constexpr int kBM = 128;                // weight rows per tile (MMA M)
 constexpr int kBK = 64;                 // K per stage: one 128-byte swizzle atom of BF16
 constexpr int kATile = kBM * kBK * 2;   // 16 KiB
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;           // warps 0 TMA, 1 MMA, 2-5 epilogue, 6-7 row gather
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s: far beyond any legal wait
 constexpr int kCombineCols = 1024;       // columns per phase-3 item (128 threads x 8)
 constexpr int kSmemGroups = 257;         // plans up to this many groups are staged in shared memory
@@ -100,6 +112,10 @@ struct GroupedParams {
     const uint16_t *sh_gate, *sh_up, *sh_down;  // shared expert rows (null: none), prefetched to L2 at start
     uint16_t *xs;                    // gather_x: route-ordered rows the kernel fills
     int gather_x, gather_need;       // gather in the kernel; epilogue warps that must publish it
+    const int64_t *src_rows;         // address-table mode: row p is read from src_rows[p] (or null)
+    const int64_t *dst_rows;         // and its down output stored to dst_rows[p]
+    int32_t *row_ready;              // [num_groups] rows gathered per group (address-table mode)
+    int32_t *error_out;              // or null: set to 3 when a wait of this kernel gave up
     int tokens, top_k, hidden, inner, ks;
 };
 
@@ -408,9 +424,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // producers: phase 2 for the group's phase 1 (every phase-1 tile
                 // once per epilogue warp), phase 1 for the in-kernel gather.
                 const bool p1 = ip.phase == 1;
-                bool dep_ok = p1 ? (xs_seen || !P.gather_x) : false;
-                const int32_t *dep_ctr = p1 ? &P.plan->xs_ready : &P.done1[ip.g];
-                const int need = p1 ? P.gather_need : 4 * mb1 * G.ntiles;
+                const bool tables = P.src_rows != nullptr;
+                bool dep_ok = p1 ? (!tables && (xs_seen || !P.gather_x)) : false;
+                const int32_t *dep_ctr = p1 ? (tables ? &P.row_ready[ip.g] : &P.plan->xs_ready) : &P.done1[ip.g];
+                const int need = p1 ? (tables ? G.count : P.gather_need) : 4 * mb1 * G.ntiles;
                 const CUtensorMap *bmap = p1 ? &tm_x : &tm_act, *bmap16 = p1 ? &tm_x16 : &tm_act16;
                 int pending[8];
                 int n_pending = 0;
@@ -490,7 +507,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                         n_pending = 0;
                     }
                 }
-                if (p1 && dep_ok) xs_seen = true;
+                if (p1 && dep_ok && !tables) xs_seen = true;
                 if (!ok) break;
             }
             if (*abort) {
@@ -561,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-    } else {
+    } else if (warp < 6) {
         // ------------------------------------------------- epilogue + combine
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int et = threadIdx.x - 64;  // 0..127
@@ -689,10 +706,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ++acc;
             } else {
                 // rows_out: column c of the tile is route p0 + c, whose token the
-                // lanes hold (lane c % 32 of register c / 32) and broadcast.
+                // lanes hold (lane c % 32 of register c / 32) and broadcast; in
+                // address-table mode they hold the row's destination address.
                 constexpr int kTokRegs = BN < 32 ? 1 : BN / 32;
                 int tok[kTokRegs];
-                if (P.rows_out) {
+                long long dsta[kTokRegs];
+                if (P.dst_rows) {
+#pragma unroll
+                    for (int i = 0; i < kTokRegs; ++i) {
+                        const int c = i * 32 + lane;
+                        dsta[i] = c < nvalid ? P.dst_rows[p0 + c] : 0;
+                    }
+                } else if (P.rows_out) {
 #pragma unroll
                     for (int i = 0; i < kTokRegs; ++i) {
                         const int c = i * 32 + lane;
@@ -712,7 +737,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 16; ++j) {
                         if (c0 + j >= nvalid) continue;  // warp-uniform
                         uint16_t *dst;
-                        if (P.rows_out) {
+                        if (P.dst_rows) {
+                            dst = reinterpret_cast<uint16_t *>(
+                                __shfl_sync(0xffffffffu, dsta[(c0 + j) >> 5], (c0 + j) & 31));
+                        } else if (P.rows_out) {
                             const int t = __shfl_sync(0xffffffffu, tok[(c0 + j) >> 5], (c0 + j) & 31);
                             dst = P.rows_out + static_cast<size_t>(t) * P.hidden;
                         } else {
@@ -738,6 +766,59 @@ __global__ void __launch_bounds__(kThreads, 1)
                 else atomicAdd(&P.plan->done2_total, 1);
             }
         }
+        // rows stored into peers' memory are visible system-wide before the
+        // caller's next kernel releases the peers
+        if (P.dst_rows) __threadfence_system();
+    } else if (P.src_rows && !*abort) {
+        // ------------------------------------------ row gather (address tables)
+        // Rows in plan order over every CTA's two gather warps, two rows in
+        // flight per warp; each finished row counts into its group.
+        const int n_rows = V.groups[n_groups - 1].begin + V.groups[n_groups - 1].count;
+        const int units = P.hidden / 8;  // 16-byte units of a row (128 or more, a multiple of 32)
+        const int gw = blockIdx.x * 2 + (warp - 6), ngw = gridDim.x * 2;
+        auto group_of = [&](int p) {  // the group whose rows hold p (groups are contiguous, ascending)
+            int lo = 0, hi = n_groups;
+            while (hi - lo > 1) {
+                const int mid = (lo + hi) >> 1;
+                if (V.groups[mid].begin <= p) lo = mid;
+                else hi = mid;
+            }
+            return lo;
+        };
+        for (int q0 = gw; q0 < n_rows; q0 += 2 * ngw) {
+            const int q1 = q0 + ngw;
+            const bool two = q1 < n_rows;
+            const uint4 *s0 = reinterpret_cast<const uint4 *>(P.src_rows[q0]);
+            const uint4 *s1 = two ? reinterpret_cast<const uint4 *>(P.src_rows[q1]) : s0;
+            uint4 *d0 = reinterpret_cast<uint4 *>(P.xs) + static_cast<int64_t>(q0) * units;
+            uint4 *d1 = reinterpret_cast<uint4 *>(P.xs) + static_cast<int64_t>(q1) * units;
+            for (int c0 = 0; c0 < units; c0 += 8 * 32) {
+                uint4 a[8], b[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c0 + u * 32 < units) a[u] = __ldcg(s0 + c0 + u * 32 + lane);
+                if (two) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (c0 + u * 32 < units) b[u] = __ldcg(s1 + c0 + u * 32 + lane);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (c0 + u * 32 < units) d0[c0 + u * 32 + lane] = a[u];
+                if (two) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (c0 + u * 32 < units) d1[c0 + u * 32 + lane] = b[u];
+                }
+            }
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) {
+                sm100::fence_proxy_async_global();
+                atomicAdd(&P.row_ready[group_of(q0)], 1);
+                if (two) atomicAdd(&P.row_ready[group_of(q1)], 1);
+            }
+        }
     }
 
     sm100::tc_fence_before();
@@ -747,7 +828,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tc_fence_after();
         sm100::tmem_dealloc(tmem, S::kTmemCols);
     }
-    if (threadIdx.x == 0 && *abort) atomicCAS(&P.plan->error, 0, 1);
+    if (threadIdx.x == 0 && *abort) {
+        atomicCAS(&P.plan->error, 0, 1);
+        if (P.error_out) atomicCAS(P.error_out, 0, 3);
+    }
 }
 
 // Standalone plan for the general (prefill) path; the decode path runs the
@@ -900,6 +984,10 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.xs = const_cast<uint16_t *>(L.xs);
     P.gather_x = L.gather_x;
     P.gather_need = 4 * L.ctas;
+    P.src_rows = L.src_rows;
+    P.dst_rows = L.dst_rows;
+    P.row_ready = L.row_ready;
+    P.error_out = L.error_out;
     P.tokens = L.tokens;
     P.top_k = L.top_k;
     P.hidden = L.hidden;
@@ -945,6 +1033,8 @@ int launch_gather_tokens(const uint16_t *x, const int32_t *route_token, const in
 int launch_grouped(const GroupedLaunch &L, cudaStream_t stream) {
     LRB_REQUIRE(L.hidden % kBM == 0 && L.inner % kBM == 0 && L.hidden % kCombineCols == 0,
                 "grouped: hidden must be a multiple of 1024 and inner of 128");
+    LRB_REQUIRE((L.src_rows == nullptr) == (L.dst_rows == nullptr) && (!L.src_rows || (L.row_ready && !L.gather_x)),
+                "grouped: address tables need both tables and the row counters, without gather_x");
     LRB_REQUIRE(L.ks == 1 || L.ks == 2 || L.ks == 4, "grouped: K split %d not in {1, 2, 4}", L.ks);
     LRB_REQUIRE(L.top_k <= 32, "grouped: top_k %d > 32", L.top_k);
     switch (L.bn) {

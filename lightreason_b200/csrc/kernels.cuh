@@ -113,6 +113,12 @@ struct GroupedLaunch {
     const int32_t *stage_error;    // nonzero: the host staging gave up; folded into plan->error
     const uint16_t *x;             // gather_x: tokens [T, H], gathered into xs by the kernel itself
     int gather_x;
+    // Address tables (or null): row p of the plan is read from src_rows[p] and
+    // its down output (no combine) stored to dst_rows[p]; row_ready[g] counts
+    // the rows of group g gathered (zeroed by the plan).
+    const int64_t *src_rows, *dst_rows;
+    int32_t *row_ready;
+    int32_t *error_out;  // or null: set to 3 when a wait of the kernel gave up
     int tokens, top_k, hidden, inner, bn, ks, ctas;
 };
 struct PlanArgs;
@@ -128,7 +134,7 @@ int launch_grouped(const GroupedLaunch &L, cudaStream_t stream);
 // Expert-parallel exchange over peer memory (ep_p2p.cu); fields as moe_ep_p2p.
 struct EpP2PArgs {
     const int64_t *peers;
-    int64_t off_flags_dispatch, off_flags_return, off_count, off_meta, off_rx, off_ret;
+    int64_t off_flags_publish, off_flags_return, off_count, off_meta, off_tokens, off_ret;
     int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
     int32_t *sync, *error;

@@ -1,5 +1,10 @@
-"""Expert-parallel MoE layer: one process per GPU, experts sharded by rank,
-token dispatch and combine through NCCL all-to-all.
+"""Expert-parallel MoE layer: one process per GPU, experts sharded by rank.
+
+Two exchanges: PeerExchange (the default), where the expert kernel itself
+pulls token rows from their senders over NVLink peer memory and stores the
+expert rows back into the senders' memory (no host synchronisation), and
+TorchExchange, token dispatch and combine through NCCL all-to-all, whose step
+is described below.
 
 Rank r of `world` owns the global experts [r*El, (r+1)*El), El = E / world,
 and keeps replicas of the router and the shared expert.  One step on rank r:
@@ -39,7 +44,7 @@ from lightreason_b200.native import _ptr, _require, check, lib
 
 
 # phases of one peer-exchange rank step, in launch order
-EP_STAGES = ("router", "permute", "dispatch", "collect", "local_layer", "return", "finish", "combine")
+EP_STAGES = ("router", "permute", "publish", "experts", "finish", "combine")
 
 
 def shard(experts: int, world: int, rank: int) -> range:
@@ -218,16 +223,25 @@ class ExpertParallelLayer:
         _require(ex.capacity >= self.max_tokens * self.top_k and ex.own_rows >= self.max_tokens,
                  "peer exchange sized below tokens * top_k")
         d = self.dev
-        n = ex.rows
-        self.p_route_in = torch.empty((n, 1), dtype=torch.int64, device=d)
-        self.p_yin = torch.empty((n, self.hidden), dtype=torch.bfloat16, device=d)
-        self.p_ret_addr = torch.zeros(max(n - ex.own_rows, 1), dtype=torch.int64, device=d)
         hist = lib().moe_permute_hist_ints(self.max_tokens, self.top_k, self.experts)
         self.p_hist = torch.empty(max(hist, 1), dtype=torch.int32, device=d)
         self.p_rsplit = self.rsplit
+        self.p_shared = torch.empty((self.max_tokens, self.hidden), dtype=torch.bfloat16, device=d)
+        self.p_stats = torch.zeros(2 + self.world, dtype=torch.int32, device=d)
+        inner = self.gate_up.shape[1] // 2
+        self.p_inner = inner
+        ws = lib().moe_ep_p2p_workspace_bytes(ctypes.byref(ex.args), inner)
+        _require(ws > 0, "peer exchange: workspace query failed")
+        self.p_ws = torch.empty(ws, dtype=torch.uint8, device=d)
         self._peer_ready = True
 
     def _forward_peer(self, x, out, stage_events, ep_events=None):
+        """One rank step over the peer exchange: router and permute of the own
+        tokens, publish (own rows into the symmetric buffer, one entry per
+        route into its owner's), the owner's plan and grouped kernel (rows
+        pulled from their senders, expert rows stored into the senders' ret),
+        finish (flags), the ordered combine.  stage_events: None or two CUDA
+        events recorded around the grouped kernel."""
         ex = self.exchange
         self._peer_buffers()
         native._cuda_bf16(x, "x")
@@ -253,33 +267,43 @@ class ExpertParallelLayer:
                                      _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos),
                                      _ptr(self.active), c, c + 4, _ptr(self.p_hist), s), "moe_permute_wide")
         mark(2)
-        check(lib().moe_ep_p2p_dispatch(a, _ptr(x), _ptr(self.idx), _ptr(self.offsets), _ptr(self.perm_token),
-                                        _ptr(self.perm_slot), s), "moe_ep_p2p_dispatch")
+        check(lib().moe_ep_p2p_publish(a, _ptr(x), tokens, _ptr(self.idx), _ptr(self.offsets),
+                                       _ptr(self.perm_token), _ptr(self.perm_slot), s), "moe_ep_p2p_publish")
         mark(3)
-        check(lib().moe_ep_p2p_collect(a, _ptr(x), tokens, _ptr(self.p_route_in), _ptr(self.p_ret_addr), s),
-              "moe_ep_p2p_collect")
+        kev = None
+        if stage_events is not None:
+            for e in stage_events:
+                if not e.cuda_event:
+                    e.record()  # torch creates the CUDA event lazily on first record
+            kev = (native._p * 2)(*[e.cuda_event for e in stage_events])
+        check(lib().moe_ep_p2p_experts(a, _ptr(self.gate_up), _ptr(self.down), self.p_inner, tokens,
+                                       _ptr(self.p_shared), _ptr(self.p_stats), _ptr(self.p_ws), self.p_ws.numel(),
+                                       kev, s), "moe_ep_p2p_experts")
         mark(4)
-        self.local.forward_rows_raw(ex.rows_ptr, ex.rows, self.p_route_in, self.p_yin, stage_events=stage_events)
-        mark(5)
-        check(lib().moe_ep_p2p_return(a, self.p_yin[ex.own_rows:].data_ptr(), _ptr(self.p_ret_addr), s),
-              "moe_ep_p2p_return")
-        mark(6)
         check(lib().moe_ep_p2p_finish(a, s), "moe_ep_p2p_finish")
-        mark(7)
+        mark(5)
         check(lib().moe_ep_combine(ctypes.c_void_p(ex.ret_ptr), _ptr(self.route_pos), _ptr(self.scores),
-                                   _ptr(self.p_yin), _ptr(self.sig), tokens, self.top_k, self.hidden, _ptr(out), s),
+                                   _ptr(self.p_shared), _ptr(self.sig), tokens, self.top_k, self.hidden, _ptr(out), s),
               "moe_ep_combine")
-        mark(8)
+        mark(6)
         return out
+
+    def peer_stats(self) -> dict:
+        """This rank's share of the last peer step (syncs): rows received from
+        each sender, local experts with rows."""
+        v = self.p_stats.tolist()
+        return {"rows_received": v[0], "local_experts_with_rows": v[1], "rows_per_sender": v[2:]}
 
 
 class PeerExchange:
     """Symmetric buffers over NVLink for ExpertParallelLayer: one CUDA-IPC
     buffer per rank (moe_ipc_alloc), mapped by every peer, laid out as
-    moe_ep_p2p describes.  capacity = rows one rank may send to one peer
-    (tokens * top_k: no route is ever dropped); the rows region [tokens +
-    world * capacity, H] is also the local layer's input.  Construct it on
-    every rank of the process group together; close() before the group ends."""
+    moe_ep_p2p describes: flags, counts, one 16-byte meta entry per route a
+    sender may send (capacity = tokens * top_k per sender, so no route is ever
+    dropped), the rank's own token rows [tokens, H], which the owners of its
+    routes read, and the return rows [capacity, H] they write.  Construct it
+    on every rank of the process group together; close() before the group
+    ends."""
 
     def __init__(self, *, world, rank, tokens, top_k, hidden, experts, device, group=None):
         import torch.distributed as dist
@@ -288,12 +312,11 @@ class PeerExchange:
         self.world, self.rank = world, rank
         self.capacity = tokens * top_k
         self.own_rows = tokens
-        self.rows = tokens + world * self.capacity
         cap, h = self.capacity, hidden
         align = lambda v, a: (v + a - 1) // a * a  # noqa: E731
-        off_fd, off_fr, off_count, off_meta = 0, 256, 512, 1024
-        off_rx = align(off_meta + world * cap * 8, 4096)
-        off_ret = align(off_rx + self.rows * h * 2, 4096)
+        off_fp, off_fr, off_count, off_meta = 0, 256, 512, 1024
+        off_tokens = align(off_meta + world * cap * 16, 4096)
+        off_ret = align(off_tokens + tokens * h * 2, 4096)
         total = off_ret + cap * h * 2
         _require(world <= 64, "at most 64 ranks")
         base = ctypes.c_void_p()
@@ -324,9 +347,9 @@ class PeerExchange:
         self.sync = torch.zeros(2, **i32)
         self.error = torch.zeros(1, **i32)
         self.ret_ptr = base.value + off_ret
-        self.rows_ptr = base.value + off_rx
-        self.args = native.EpP2P(peers=self.peers.data_ptr(), off_flags_dispatch=off_fd, off_flags_return=off_fr,
-                                 off_count=off_count, off_meta=off_meta, off_rx=off_rx, off_ret=off_ret, world=world,
+        self.args = native.EpP2P(peers=self.peers.data_ptr(), off_flags_publish=off_fp, off_flags_return=off_fr,
+                                 off_count=off_count, off_meta=off_meta, off_tokens=off_tokens, off_ret=off_ret,
+                                 world=world,
                                  rank=rank, capacity=cap, hidden=hidden, top_k=top_k, experts=experts,
                                  local_experts=experts // world, own_rows=tokens, step=self.step.data_ptr(),
                                  sync=self.sync.data_ptr(), error=self.error.data_ptr())
@@ -338,7 +361,8 @@ class PeerExchange:
         """Raise if a bounded wait of an earlier step gave up (syncs the device)."""
         code = int(self.error.item())
         if code:
-            what = {1: "a sender never released its rows", 2: "a receiver never returned its rows"}.get(code, "unknown")
+            what = {1: "a sender never published its routes", 2: "an owner never returned its rows",
+                    3: "the expert kernel gave up waiting"}.get(code, "unknown")
             raise RuntimeError(f"expert-parallel exchange failed ({code}): {what}")
 
     def close(self) -> None:

@@ -36,8 +36,8 @@ class LayerWeights(ctypes.Structure):
 
 class EpP2P(ctypes.Structure):
     """moe_ep_p2p: the peer-memory exchange of one expert-parallel rank."""
-    _fields_ = [("peers", _p), ("off_flags_dispatch", ctypes.c_int64), ("off_flags_return", ctypes.c_int64),
-                ("off_count", ctypes.c_int64), ("off_meta", ctypes.c_int64), ("off_rx", ctypes.c_int64),
+    _fields_ = [("peers", _p), ("off_flags_publish", ctypes.c_int64), ("off_flags_return", ctypes.c_int64),
+                ("off_count", ctypes.c_int64), ("off_meta", ctypes.c_int64), ("off_tokens", ctypes.c_int64),
                 ("off_ret", ctypes.c_int64), ("world", _i), ("rank", _i), ("capacity", _i), ("hidden", _i),
                 ("top_k", _i), ("experts", _i), ("local_experts", _i), ("own_rows", _i), ("step", _p),
                 ("sync", _p), ("error", _p)]
@@ -82,9 +82,9 @@ _SIGNATURES = {
     "moe_ipc_free": ([_p], _i),
     "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
     "moe_ipc_close": ([_p], _i),
-    "moe_ep_p2p_dispatch": ([ctypes.POINTER(EpP2P), _p, _p, _p, _p, _p, _p], _i),
-    "moe_ep_p2p_collect": ([ctypes.POINTER(EpP2P), _p, _i, _p, _p, _p], _i),
-    "moe_ep_p2p_return": ([ctypes.POINTER(EpP2P), _p, _p, _p], _i),
+    "moe_ep_p2p_publish": ([ctypes.POINTER(EpP2P), _p, _i, _p, _p, _p, _p, _p], _i),
+    "moe_ep_p2p_workspace_bytes": ([ctypes.POINTER(EpP2P), _i], _sz),
+    "moe_ep_p2p_experts": ([ctypes.POINTER(EpP2P), _p, _p, _i, _i, _p, _p, _p, _sz, ctypes.POINTER(_p), _p], _i),
     "moe_ep_p2p_finish": ([ctypes.POINTER(EpP2P), _p], _i),
     "moe_ep_dispatch": ([_p, _p, _p, _p, _p, _i, _i, _i, _i, _i, _p, _p, _p, _p], _i),
     "moe_ep_unpack": ([_p, _i, _p, _p], _i),
