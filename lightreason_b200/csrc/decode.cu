@@ -15,7 +15,10 @@
 //
 // Work split (the same formula in every CTA, no table): the gate/up rows go to
 // the CTAs as quads (rows 4k..4k+3 of one group's gate and up), evenly, since
-// the grid-wide wait follows them.  The hidden columns are cut into units of 8;
+// the grid-wide wait follows them -- the shared expert's quads first, by a
+// split of their own that needs no routing, so each CTA issues them before it
+// waits for the router and they stream while the routing runs; then the
+// routed groups' quads.  The hidden columns are cut into units of 8;
 // CTA c owns units c, c + A, ... (A = CTAs) and computes down rows 8u..8u+7 of
 // EVERY group, so it holds every routed row of its columns and runs the
 // ordered combine for them itself -- no second grid wait and no y round trip
@@ -304,13 +307,24 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
         *abort = 0;
         sm100::fence_barrier_init();
     }
-    // The shared expert's rows do not depend on the routing: this CTA's slice
-    // of them goes to L2 while the routing kernels still run.
-    if (threadIdx.x == 64 && P.has_shared && P.src.sh_gate) {
-        prefetch_l2_slice(P.src.sh_gate, static_cast<size_t>(I) * H * 2);
-        prefetch_l2_slice(P.src.sh_up, static_cast<size_t>(I) * H * 2);
-        prefetch_l2_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
+    // The shared expert's rows do not depend on the routing: this CTA's quads
+    // of its gate/up rows enter the ring (slots 0..) and its slice of the down
+    // rows goes to L2 while the routing kernels still run.
+    const int A = gridDim.x, c = blockIdx.x;
+    const bool sh = P.has_shared && P.src.sh_gate;
+    const int sq0 = sh ? QPG * c / A : 0, nsq = sh ? QPG * (c + 1) / A - sq0 : 0;
+    const int npre = min(nsq, S);  // issued before the wait (ring slots 0..npre-1, first use)
+    __syncthreads();  // barriers initialised before the producer's first copy
+    if (warp == kConsumerWarps && lane == 0) {
+        for (int it = 0; it < npre; ++it) {
+            const size_t r0 = static_cast<size_t>(sq0 + it) * kSub;
+            uint8_t *dst = ring + it * L.slot_bytes;
+            sm100::mbar_expect_tx(&full[it], 4 * kSub * H);
+            sm100::bulk_load(dst, P.src.sh_gate + r0 * H, 2 * kSub * H, &full[it]);
+            sm100::bulk_load(dst + 2 * kSub * H, P.src.sh_up + r0 * H, 2 * kSub * H, &full[it]);
+        }
     }
+    if (threadIdx.x == 64 && sh) prefetch_l2_slice(P.src.sh_down, static_cast<size_t>(H) * I * 2);
     grid_dependency_wait();  // the plan (or the router partials) come from the routing kernels
     grid_dependency_trigger();
     if (P.route) {
@@ -322,29 +336,43 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
         __syncthreads();  // group table in place: the producer can start
     }
 
-    // ---- work split (identical in every thread of every CTA)
+    // ---- work split (identical in every thread of every CTA): items 0..nsq-1
+    // are the CTA's shared-expert quads (the shared group is the last group),
+    // then its share of the routed groups' quads, then its down chunks
     const int n = min(*n_groups, P.max_groups);
-    const int A = gridDim.x, c = blockIdx.x;
+    const int nr = n - (sh ? 1 : 0);  // routed groups
     constexpr int HW = H / kUnit;  // column units
     const int my_units = HW / A + (c < HW % A ? 1 : 0);
-    const int64_t quads = static_cast<int64_t>(n) * QPG;
+    const int64_t quads = static_cast<int64_t>(nr) * QPG;
     const int64_t qa0 = quads * c / A;
-    const int nquads = static_cast<int>(quads * (c + 1) / A - qa0);
+    const int nquads = nsq + static_cast<int>(quads * (c + 1) / A - qa0);
+    // quad item it -> (group, first row)
+    auto quad_of = [&](int it, int *g, int *r0) {
+        if (it < nsq) {
+            *g = n - 1;
+            *r0 = (sq0 + it) * kSub;
+        } else {
+            const int64_t k = qa0 + (it - nsq);
+            *g = static_cast<int>(k / QPG);
+            *r0 = static_cast<int>(k % QPG) * kSub;
+        }
+    };
     const int nchunks = my_units * n;  // chunk ci: unit ci / n, group ci % n
     const int items = nquads + (nchunks + kSub - 1) / kSub;
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------- producer
         if (lane == 0) {
-            int issued = 0;
-            for (int it = 0; it < items; ++it) {
+            int issued = npre;  // the first shared quads went out before the routing
+            for (int it = npre; it < items; ++it) {
                 const int s = it % S;
                 if (it >= S && !fused_wait_bar(&empty[s], ((it / S) - 1) & 1, abort)) break;
                 uint8_t *dst = ring + s * L.slot_bytes;
                 if (it < nquads) {
-                    const int64_t k = qa0 + it;
-                    const Group G = P.src.resolve(grp[k / QPG]);
-                    const size_t r0 = static_cast<size_t>(k % QPG) * kSub;
+                    int g, q0;
+                    quad_of(it, &g, &q0);
+                    const Group G = P.src.resolve(grp[g]);
+                    const size_t r0 = static_cast<size_t>(q0);
                     sm100::mbar_expect_tx(&full[s], 4 * kSub * H);
                     sm100::bulk_load(dst, G.gate + r0 * H, 2 * kSub * H, &full[s]);
                     sm100::bulk_load(dst + 2 * kSub * H, G.up + r0 * H, 2 * kSub * H, &full[s]);
@@ -403,9 +431,10 @@ __global__ void __launch_bounds__(kFusedThreads, 1) fused_decode_kernel(const Fu
     for (; it < nquads; it += kGroups) {
         const int s = it % S;
         if (!fused_wait_bar(&full[s], (it / S) & 1, abort)) break;
-        const int64_t k = qa0 + it;
-        const GroupedGroup G = grp[k / QPG];
-        const int r = static_cast<int>(k % QPG) * kSub + j;
+        int g, q0;
+        quad_of(it, &g, &q0);
+        const GroupedGroup G = grp[g];
+        const int r = q0 + j;
         const uint4 *gs = reinterpret_cast<const uint4 *>(ring + s * L.slot_bytes) + j * HU;
         const uint4 *us = gs + kSub * HU;
         for (int jj = 0; jj < G.count; ++jj) {

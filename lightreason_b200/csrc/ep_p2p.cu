@@ -100,12 +100,16 @@ __device__ __forceinline__ void warp_copy_row(const uint16_t *src, uint16_t *dst
     for (; v < n; v += 32) d[v] = __ldg(s + v);
 }
 
-// Last-CTA election: every CTA fences its (peer) stores, then counts itself in.
+// Last-CTA election: once every thread of the CTA is past its stores, one
+// thread fences at system scope (cumulative: it orders the stores the barrier
+// made visible to it) and counts the CTA in.
 __device__ __forceinline__ bool last_cta(int32_t *counter) {
     __shared__ int is_last;
-    __threadfence_system();
     __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        is_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
+    }
     __syncthreads();
     return is_last != 0;
 }
@@ -186,9 +190,17 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     // routes per (local expert, sender); the entries of a sender are in its
     // permuted order, so ascending in local expert
     for (int s = 0; s < W; ++s)
-        for (int j = threadIdx.x; j < sent[s]; j += blockDim.x) {
-            const int le = __ldcg(meta + static_cast<size_t>(s) * C + j).x;
-            if (le >= 0 && le < El) atomicAdd(&cnt[le * W + s], 1);
+        for (int j0 = 0; j0 < sent[s]; j0 += blockDim.x) {
+            // a sender's entries are sorted by expert: a warp's 32 consecutive
+            // entries share few experts, so count them once per expert
+            const int j = j0 + threadIdx.x;
+            int le = -1;
+            if (j < sent[s]) {
+                le = __ldcg(meta + static_cast<size_t>(s) * C + j).x;
+                if (le < 0 || le >= El) le = -1;
+            }
+            const unsigned same = __match_any_sync(0xffffffffu, le);
+            if (le >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&cnt[le * W + s], __popc(same));
         }
     __syncthreads();
     if (threadIdx.x < W) {
@@ -297,10 +309,11 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
 __global__ void ep_p2p_finish_kernel(EpP2PArgs a) {
     grid_dependency_wait();
     const uint32_t step = *a.step;
+    if (threadIdx.x == 0) __threadfence_system();
+    __syncthreads();
     if (threadIdx.x < a.world) {
         // this rank's reads of the peers' tokens and its stores into their ret
         // (by the expert kernel, which ended with a system fence) are complete
-        __threadfence_system();
         st_release_sys(reinterpret_cast<uint32_t *>(peer_base(a, threadIdx.x) + a.off_flags_return) + a.rank, step);
     }
     __syncthreads();
