@@ -101,15 +101,21 @@ __device__ __forceinline__ void warp_copy_row(const uint16_t *src, uint16_t *dst
 }
 
 // Last-CTA election: once every thread of the CTA is past its stores, one
-// thread fences at system scope (cumulative: it orders the stores the barrier
-// made visible to it) and counts the CTA in.
+// thread counts the CTA in with an acquire-release add at GPU scope, so the
+// last CTA has every CTA's stores ordered before it; its system-scope release
+// of a flag then passes them on to the peer that acquires the flag (release
+// and acquire are cumulative along that chain).  No sequentially consistent
+// system fence is needed; such a fence costs microseconds here.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int32_t *p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ bool last_cta(int32_t *counter) {
     __shared__ int is_last;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        is_last = atomicAdd(counter, 1) == static_cast<int>(gridDim.x) - 1;
-    }
+    if (threadIdx.x == 0) is_last = atom_add_acq_rel_gpu(counter, 1) == static_cast<int>(gridDim.x) - 1;
     __syncthreads();
     return is_last != 0;
 }
@@ -147,7 +153,6 @@ __global__ void __launch_bounds__(256) ep_p2p_publish_kernel(EpP2PArgs a, const 
             uint8_t *dst = peer_base(a, d);
             const int lo = min(d * El, a.experts), hi = min((d + 1) * El, a.experts);
             reinterpret_cast<int32_t *>(dst + a.off_count)[a.rank] = min(offsets[hi] - offsets[lo], a.capacity);
-            __threadfence_system();
             st_release_sys(reinterpret_cast<uint32_t *>(dst + a.off_flags_publish) + a.rank, step);
         }
         if (threadIdx.x == 0) a.sync[0] = 0;
@@ -170,7 +175,7 @@ struct EpPlanOut {
 __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOut o) {
     __shared__ int cnt[1024], base[1024], first[1024];
     __shared__ int sent[64], valid[64];
-    __shared__ int scratch[33];
+    __shared__ int scratch[100];
     __shared__ int ok;
     grid_dependency_wait();
     grid_dependency_trigger();
@@ -190,17 +195,22 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     // routes per (local expert, sender); the entries of a sender are in its
     // permuted order, so ascending in local expert
     for (int s = 0; s < W; ++s)
-        for (int j0 = 0; j0 < sent[s]; j0 += blockDim.x) {
-            // a sender's entries are sorted by expert: a warp's 32 consecutive
-            // entries share few experts, so count them once per expert
-            const int j = j0 + threadIdx.x;
-            int le = -1;
-            if (j < sent[s]) {
-                le = __ldcg(meta + static_cast<size_t>(s) * C + j).x;
-                if (le < 0 || le >= El) le = -1;
+        for (int j0 = 0; j0 < sent[s]; j0 += 4 * static_cast<int>(blockDim.x)) {
+            // four entries per thread with their loads in flight together; a
+            // sender's entries are sorted by expert, so a warp's 32
+            // consecutive entries share few experts: count once per expert
+            int les[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * blockDim.x + threadIdx.x;
+                les[u] = j < sent[s] ? __ldcg(meta + static_cast<size_t>(s) * C + j).x : -1;
             }
-            const unsigned same = __match_any_sync(0xffffffffu, le);
-            if (le >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&cnt[le * W + s], __popc(same));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int le = les[u] >= 0 && les[u] < El ? les[u] : -1;
+                const unsigned same = __match_any_sync(0xffffffffu, le);
+                if (le >= 0 && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&cnt[le * W + s], __popc(same));
+            }
         }
     __syncthreads();
     if (threadIdx.x < W) {
@@ -211,13 +221,13 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     // base[le][s]: the first row of sender s's routes in expert le's group
     // (scan in (le, s) order); first[le][s]: sender s's first entry of expert
     // le (scan in (s, le) order, minus the entries of the senders before s)
-    int routed = 0, dummy = 0;
     const int i = threadIdx.x;
     const int v_ls = i < E ? cnt[i] : 0;
-    const int b = block_exclusive_scan(v_ls, scratch, &routed);
-    if (i < E) base[i] = b;
     const int s_major = i < E ? cnt[(i % El) * W + i / El] : 0;  // entry i = (s, le) = (i / El, i % El)
-    const int f = block_exclusive_scan(s_major, scratch, &dummy);
+    int3 tot_a;
+    const int3 sa = block_exclusive_scan3(make_int3(v_ls, s_major, 0), scratch, &tot_a);
+    const int routed = tot_a.x, b = sa.x, f = sa.y;
+    if (i < E) base[i] = b;
     __syncthreads();
     if (i < E) {
         const int s = i / El, le = i % El;
@@ -229,12 +239,12 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     int tot_le = 0;
     if (i < El)
         for (int s = 0; s < W; ++s) tot_le += cnt[i * W + s];
-    int n_active = 0;
-    const int g = block_exclusive_scan(tot_le > 0 ? 1 : 0, scratch, &n_active);
     const int nt = (tot_le + o.bn - 1) / o.bn;
-    int t1 = 0, t2 = 0;
-    const int e1 = block_exclusive_scan(tot_le > 0 ? o.mb1 * nt : 0, scratch, &t1);
-    const int e2 = block_exclusive_scan(tot_le > 0 ? o.mb2 * nt : 0, scratch, &t2);
+    int3 tot_b;
+    const int3 sb = block_exclusive_scan3(make_int3(tot_le > 0 ? 1 : 0, tot_le > 0 ? o.mb1 * nt : 0,
+                                                    tot_le > 0 ? o.mb2 * nt : 0), scratch, &tot_b);
+    const int n_active = tot_b.x, t1 = tot_b.y, t2 = tot_b.z;
+    const int g = sb.x, e1 = sb.y, e2 = sb.z;
     if (i < El && tot_le > 0) {
         GroupedGroup G;
         G.weight = i;
@@ -309,11 +319,10 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
 __global__ void ep_p2p_finish_kernel(EpP2PArgs a) {
     grid_dependency_wait();
     const uint32_t step = *a.step;
-    if (threadIdx.x == 0) __threadfence_system();
-    __syncthreads();
     if (threadIdx.x < a.world) {
         // this rank's reads of the peers' tokens and its stores into their ret
-        // (by the expert kernel, which ended with a system fence) are complete
+        // (the expert kernel, complete before the dependency wait above) are
+        // ordered before this release
         st_release_sys(reinterpret_cast<uint32_t *>(peer_base(a, threadIdx.x) + a.off_flags_return) + a.rank, step);
     }
     __syncthreads();

@@ -42,9 +42,9 @@
 // into the route-ordered buffer in plan order, two rows in flight per warp,
 // and count each finished row into its group; a phase-1 item's token tiles
 // wait only for its own group's rows, so the tensor cores start on the first
-// groups while later rows are still crossing the links.  The CTA ends with a
-// system-scope fence, so the epilogue's stores into peers' memory are visible
-// before the caller releases the peers.
+// groups while later rows are still crossing the links.  The caller's next
+// kernel, once this grid is complete, releases the peers with a system-scope
+// release, which orders the epilogue's stores into their memory before it.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -820,10 +820,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     sm100::tc_fence_before();
     __syncthreads();
-    // rows the epilogue stored into peers' memory are visible system-wide
-    // before the caller's next kernel releases the peers (one cumulative
-    // fence after the barrier orders every thread's stores)
-    if (threadIdx.x == 0 && P.dst_rows) __threadfence_system();
     if (warp == 1) {
         __syncwarp();
         sm100::tc_fence_after();
