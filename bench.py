@@ -21,8 +21,9 @@ per-N values form one weak-scaling series.
               expert-parallel ones; the ids are also checked against the torch
               CPU router on a token sample (near ties of one BF16 ulp excused
               and counted).  A mismatch makes every rank exit non-zero;
-  * ep_stages_us: per-phase times of the rank step (router, permute,
-              publish, experts -- the owner's plan and the grouped kernel,
+  * ep_stages_us: per-phase times of the rank step (route -- the router,
+              which also publishes the own routes to their owners --,
+              experts -- the owner's plan and the grouped kernel,
               which pulls the token rows over NVLink and stores the expert
               rows into their senders' memory -- finish, combine) and the
               NVLink bytes the rank moves;
@@ -965,11 +966,11 @@ def run_ep(args, world, rank, local) -> dict:
               "events around it, max over ranks of the summed step times" if transport == "p2p" else
               "CUDA events around each whole step on the compute stream (includes the host read of the "
               "all-to-all split sizes), max over ranks of the summed step times")
-    # p2p: router_tc + router_select; permute count/colscan/place; publish;
-    # plan, grouped; finish; combine.  NCCL: router x2, permute x3,
+    # p2p: router_tc + select/publish; plan, grouped; finish; combine.
+    # NCCL: router x2, permute x3,
     # ep_dispatch, ep_unpack, the local layer in rows mode (permute x3,
     # grouped_plan, gather_tokens, grouped), combine
-    launches = 10 if transport == "p2p" else 14
+    launches = 6 if transport == "p2p" else 14
     res = {
         "metric": "MoE-layer throughput (tokens/s) and us/step, fraction of HBM roofline",
         "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,

@@ -413,13 +413,19 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
  * token rows) and ret BF16[capacity][hidden]; capacity >= own_rows * top_k,
  * own_rows >= the tokens of any step, offsets of tokens, meta and ret
  * 16-byte aligned.  `peers` lists every rank's buffer as mapped in this
- * process (its own included); step (uint32, start at 1), sync (int32[2],
+ * process (its own included); step (uint32, start at 1), sync (int32[66],
  * zero) and error are this rank's device words.  One step:
- *   moe_router_topk(_ws), moe_permute(_wide) of the rank's own tokens;
- *   moe_ep_p2p_publish  copies x into tokens and writes one entry (local
- *                       expert, position, token) per route into the owning
- *                       rank's meta, then releases its flags_publish; no
- *                       token row crosses a link here;
+ *   moe_ep_p2p_route    the layer's router over the rank's own tokens (the
+ *                       outputs of moe_router_topk_ws: logits, idx, BF16
+ *                       scores, sig; workspace of
+ *                       moe_ep_p2p_route_workspace_bytes, or NULL for the
+ *                       unsplit logits), copies x into tokens, gives route
+ *                       (t, k) the return row route_pos[t][k] = t * top_k +
+ *                       (rank of its expert among the token's top_k) and
+ *                       writes one entry (local expert, return row, token)
+ *                       per route into the owning rank's meta, then releases
+ *                       its flags_publish; no token row crosses a link here
+ *                       and no permute is needed;
  *   moe_ep_p2p_experts  on the owner: waits for every sender, plans one group
  *                       per local expert with routes plus the shared expert
  *                       over the own tokens, then runs the grouped tensor-core
@@ -434,8 +440,9 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
  *                       around the grouped kernel;
  *   moe_ep_p2p_finish   releases every sender's flags_return, waits for every
  *                       owner's, advances *step;
- *   moe_ep_combine      over ret (in the permuted order), scores, shared_rows
- *                       and sig.
+ *   moe_ep_combine      over ret, route_pos, scores, shared_rows and sig (a
+ *                       token's routes summed in ascending return row, i.e.
+ *                       ascending expert id).
  * Waits give up (1 s for the flags, 2 s inside the expert kernel) with
  * *error = 1 (publish), 2 (return) or 3 (expert kernel); the GPU is never
  * left waiting. */
@@ -451,9 +458,11 @@ int moe_ipc_alloc(size_t bytes, void **ptr, void *handle64);
 int moe_ipc_free(void *ptr);
 int moe_ipc_open(const void *handle64, void **ptr);
 int moe_ipc_close(void *ptr);
-int moe_ep_p2p_publish(const moe_ep_p2p *p, const uint16_t *x, int tokens, const int64_t *idx,
-                       const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot,
-                       void *stream);
+size_t moe_ep_p2p_route_workspace_bytes(const moe_ep_p2p *p, int tokens);
+int moe_ep_p2p_route(const moe_ep_p2p *p, const uint16_t *x, int tokens, const uint16_t *router,
+                     const float *bias, const uint16_t *shared_gate_w, uint16_t *logits, int64_t *idx,
+                     uint16_t *scores, uint16_t *sig, int32_t *route_pos, void *workspace,
+                     size_t workspace_bytes, void *stream);
 size_t moe_ep_p2p_workspace_bytes(const moe_ep_p2p *p, int inner);
 int moe_ep_p2p_experts(const moe_ep_p2p *p, const uint16_t *gate_up, const uint16_t *down, int inner,
                        int tokens, uint16_t *shared_rows, int32_t *stats, void *workspace,

@@ -8,22 +8,30 @@
 //   flags_publish uint32 [W]      step at which rank s published its routes to q
 //   flags_return  uint32 [W]      step at which rank d finished q's rows
 //   count         int32  [W]      routes rank s sent to q this step
-//   meta          int32  [W][C][4] (local expert on q, position on s, token on s, 0)
+//   meta          int32  [W][C][4] (local expert on q, return row on s, token on s, 0)
 //   tokens        bf16   [T0][H]  q's own token rows, read by the owners
 //   ret           bf16   [C][H]   q's routes' expert rows, by position
 //
 // One step on rank r (the step number lives in device memory and advances at
 // the end of the step, so a captured CUDA graph replays correctly):
-//   publish  x -> r.tokens; route position p of expert e goes to rank
-//            d = e / El as entry j = p - offsets[d * El] of d.meta[r]:
-//            (e % El, p, token); the last CTA writes d.count[r] and releases
-//            d.flags_publish[r] = step.  No token row moves here.
+//   route    the tensor-core router's FP32 partials, then one warp per own
+//            token selects its experts (the layer's selection), copies the
+//            token row to r.tokens and gives its routes the return rows
+//            t * K + (rank of the route's expert among the token's K), so
+//            the ordered combine, which sums in ascending row, adds them in
+//            ascending expert id (the eager order); each route to expert e
+//            goes to rank d = e / El as an entry of d.meta[r] (local expert,
+//            return row, token), slots taken per CTA with one atomic per
+//            destination; the last CTA writes d.count[r] and releases
+//            d.flags_publish[r] = step.  No token row moves here, and no
+//            permute of the own routes is needed.
 //   experts  plan (one CTA): wait for every flags_publish[s] == step, then lay
 //            out one group per local expert with routes (ascending id; within
-//            it sender by sender, each sender's routes in its own order) and
+//            it sender by sender; within a sender in the order the plan's
+//            row cursors hand out, which no result depends on) and
 //            the shared expert's group of the own tokens last, and for every
 //            row the address it is read from (sender s's tokens row) and the
-//            address its down output goes to (s.ret[p], or for a shared row
+//            address its down output goes to (s.ret[row], or for a shared row
 //            the caller's shared_rows[t]).  Then the grouped tensor-core
 //            kernel in address-table mode: its gather warps pull the rows
 //            over NVLink as the weights start streaming, and its epilogue
@@ -122,37 +130,65 @@ __device__ __forceinline__ bool last_cta(int32_t *counter) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(256) ep_p2p_publish_kernel(EpP2PArgs a, const uint16_t *__restrict__ x,
-                                                             int tokens, const int64_t *__restrict__ idx,
-                                                             const int32_t *__restrict__ offsets,
-                                                             const int32_t *__restrict__ perm_token,
-                                                             const int32_t *__restrict__ perm_slot) {
+// Selection of the own tokens and publication of their routes, see the file
+// comment.  One warp per token, eight tokens per CTA; send_cnt (sync + 2,
+// zero at entry) counts the slots taken per destination and is zeroed again
+// by the last CTA.
+template <int VPL>
+__global__ void __launch_bounds__(256) ep_p2p_select_kernel(EpP2PArgs a, const uint16_t *__restrict__ x, int tokens,
+                                                            const float *__restrict__ part, int ks,
+                                                            const float *__restrict__ bias,
+                                                            const uint16_t *__restrict__ gate_w,
+                                                            uint16_t *__restrict__ logits, int64_t *__restrict__ idx,
+                                                            uint16_t *__restrict__ scores, uint16_t *__restrict__ sig,
+                                                            int32_t *__restrict__ route_pos) {
+    __shared__ int cta_cnt[64], cta_base[64];
     grid_dependency_wait();
+    grid_dependency_trigger();
     const uint32_t step = *a.step;
-    const int lane = threadIdx.x & 31;
-    const int El = a.local_experts;
-    // the own token rows, where the owners read them
-    uint16_t *own = reinterpret_cast<uint16_t *>(peer_base(a, a.rank) + a.off_tokens);
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    for (int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += warps)
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int El = a.local_experts, K = a.top_k, W = a.world;
+    int32_t *send_cnt = a.sync + 2;
+    if (threadIdx.x < W) cta_cnt[threadIdx.x] = 0;
+    __syncthreads();
+    const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+    int e = -1, row = -1, d = 0, slot = 0;
+    if (t < tokens) {
+        float w;
+        select_token<VPL>(t, logits, bias, tokens, a.experts, K, idx, nullptr, scores, x, gate_w, a.hidden, sig, part,
+                          ks, &e, &w);
+        uint16_t *own = reinterpret_cast<uint16_t *>(peer_base(a, a.rank) + a.off_tokens);
         warp_copy_row(x + static_cast<size_t>(t) * a.hidden, own + static_cast<size_t>(t) * a.hidden, a.hidden, lane);
-    // one 16-byte entry per route into its owner's meta
-    const int routes = offsets[a.experts];
-    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < routes; p += gridDim.x * blockDim.x) {
-        const int t = perm_token[p], k = perm_slot[p];
-        const int e = static_cast<int>(idx[static_cast<size_t>(t) * a.top_k + k]);
-        const int d = e / El;
-        const int j = p - offsets[d * El];
-        if (j < 0 || j >= a.capacity) continue;  // cannot happen for a valid permute
-        int4 *meta = reinterpret_cast<int4 *>(peer_base(a, d) + a.off_meta) + static_cast<size_t>(a.rank) * a.capacity;
-        meta[j] = make_int4(e - d * El, p, t, 0);
+        // the return row: rank of this route's expert among the token's K
+        int rank = 0;
+        for (int j = 0; j < K; ++j) {
+            const int ej = __shfl_sync(0xffffffffu, e, j);
+            rank += (lane < K && ej < e) ? 1 : 0;
+        }
+        if (lane < K) {
+            row = t * K + rank;
+            route_pos[static_cast<size_t>(t) * K + lane] = row;
+            d = e / El;
+            slot = atomicAdd(&cta_cnt[d], 1);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < W && cta_cnt[threadIdx.x] > 0)
+        cta_base[threadIdx.x] = atomicAdd(&send_cnt[threadIdx.x], cta_cnt[threadIdx.x]);
+    __syncthreads();
+    if (row >= 0) {
+        const int j = cta_base[d] + slot;
+        if (j < a.capacity) {  // cannot be exceeded: a rank sends at most own_rows * K routes
+            int4 *meta = reinterpret_cast<int4 *>(peer_base(a, d) + a.off_meta) + static_cast<size_t>(a.rank) * a.capacity;
+            meta[j] = make_int4(e - d * El, row, t, 0);
+        }
     }
     if (last_cta(a.sync + 0)) {
-        if (threadIdx.x < a.world) {
-            const int d = threadIdx.x;
-            uint8_t *dst = peer_base(a, d);
-            const int lo = min(d * El, a.experts), hi = min((d + 1) * El, a.experts);
-            reinterpret_cast<int32_t *>(dst + a.off_count)[a.rank] = min(offsets[hi] - offsets[lo], a.capacity);
+        if (threadIdx.x < W) {
+            const int dd = threadIdx.x;
+            uint8_t *dst = peer_base(a, dd);
+            reinterpret_cast<int32_t *>(dst + a.off_count)[a.rank] = min(send_cnt[dd], a.capacity);
+            send_cnt[dd] = 0;
             st_release_sys(reinterpret_cast<uint32_t *>(dst + a.off_flags_publish) + a.rank, step);
         }
         if (threadIdx.x == 0) a.sync[0] = 0;
@@ -173,8 +209,8 @@ struct EpPlanOut {
 };
 
 __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOut o) {
-    __shared__ int cnt[1024], base[1024], first[1024];
-    __shared__ int sent[64], valid[64];
+    __shared__ int cnt[1024], base[1024];
+    __shared__ int sent[64];
     __shared__ int scratch[100];
     __shared__ int ok;
     grid_dependency_wait();
@@ -196,9 +232,8 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     // permuted order, so ascending in local expert
     for (int s = 0; s < W; ++s)
         for (int j0 = 0; j0 < sent[s]; j0 += 4 * static_cast<int>(blockDim.x)) {
-            // four entries per thread with their loads in flight together; a
-            // sender's entries are sorted by expert, so a warp's 32
-            // consecutive entries share few experts: count once per expert
+            // four entries per thread with their loads in flight together;
+            // equal experts within a warp are counted once
             int les[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
@@ -213,28 +248,15 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
             }
         }
     __syncthreads();
-    if (threadIdx.x < W) {
-        int v = 0;
-        for (int le = 0; le < El; ++le) v += cnt[le * W + threadIdx.x];
-        valid[threadIdx.x] = v;
-    }
     // base[le][s]: the first row of sender s's routes in expert le's group
-    // (scan in (le, s) order); first[le][s]: sender s's first entry of expert
-    // le (scan in (s, le) order, minus the entries of the senders before s)
+    // (scan in (le, s) order); it then serves as the row cursor of that run
     const int i = threadIdx.x;
     const int v_ls = i < E ? cnt[i] : 0;
-    const int s_major = i < E ? cnt[(i % El) * W + i / El] : 0;  // entry i = (s, le) = (i / El, i % El)
     int3 tot_a;
-    const int3 sa = block_exclusive_scan3(make_int3(v_ls, s_major, 0), scratch, &tot_a);
-    const int routed = tot_a.x, b = sa.x, f = sa.y;
+    const int3 sa = block_exclusive_scan3(make_int3(v_ls, 0, 0), scratch, &tot_a);
+    const int routed = tot_a.x, b = sa.x;
     if (i < E) base[i] = b;
     __syncthreads();
-    if (i < E) {
-        const int s = i / El, le = i % El;
-        int before = 0;  // entries of the senders before s
-        for (int s2 = 0; s2 < s; ++s2) before += valid[s2];
-        first[le * W + s] = f - before;
-    }
     // groups: local experts with rows in ascending id, then the shared expert
     int tot_le = 0;
     if (i < El)
@@ -291,7 +313,7 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     // the address tables: routed rows, then the shared rows.  Every routed row
     // first gets a harmless pair (the own first token row, the trash row), so
     // no row is left with a stale address even if a sender's entries were
-    // malformed; a valid permute then overwrites each of them once.
+    // malformed; valid entries then overwrite each of them once.
     const int64_t rowb = static_cast<int64_t>(a.hidden) * 2;
     const int64_t own = a.peers[a.rank] + a.off_tokens;
     for (int r = threadIdx.x; r < routed; r += blockDim.x) {
@@ -301,11 +323,21 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
     __syncthreads();
     for (int s = 0; s < W; ++s) {
         const int64_t peer = a.peers[s];
-        for (int j = threadIdx.x; j < sent[s]; j += blockDim.x) {
-            const int4 m = __ldcg(meta + static_cast<size_t>(s) * C + j);
-            if (m.x < 0 || m.x >= El || m.y < 0 || m.y >= C || m.z < 0 || m.z >= a.own_rows) continue;
-            const int row = base[m.x * W + s] + (j - first[m.x * W + s]);
-            if (row < 0 || row >= routed) continue;
+        for (int j0 = 0; j0 < sent[s]; j0 += blockDim.x) {
+            const int j = j0 + threadIdx.x;
+            int4 m = make_int4(-1, -1, -1, 0);
+            if (j < sent[s]) m = __ldcg(meta + static_cast<size_t>(s) * C + j);
+            const bool ok_m = m.x >= 0 && m.x < El && m.y >= 0 && m.y < C && m.z >= 0 && m.z < a.own_rows;
+            // a row from the run's cursor; equal experts within a warp take
+            // consecutive rows with one shared-memory atomic
+            const int key = ok_m ? m.x : -1;
+            const unsigned same = __match_any_sync(0xffffffffu, key);
+            const int leader = __ffs(same) - 1;
+            int first_row = 0;
+            if (ok_m && (threadIdx.x & 31) == leader) first_row = atomicAdd(&base[m.x * W + s], __popc(same));
+            first_row = __shfl_sync(0xffffffffu, first_row, leader);
+            const int row = first_row + __popc(same & ((1u << (threadIdx.x & 31)) - 1u));
+            if (!ok_m || row < 0 || row >= routed) continue;
             o.src_rows[row] = peer + a.off_tokens + m.z * rowb;
             o.dst_rows[row] = peer + a.off_ret + m.y * rowb;
         }
@@ -375,8 +407,6 @@ lrb::EpP2PArgs args_of(const moe_ep_p2p *p) {
     a.error = p->error;
     return a;
 }
-
-int copy_grid() { return lrb::sm_count() * 2; }
 
 constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
@@ -456,16 +486,48 @@ int moe_ipc_close(void *ptr) {
     return MOE_OK;
 }
 
-int moe_ep_p2p_publish(const moe_ep_p2p *p, const uint16_t *x, int tokens, const int64_t *idx,
-                       const int32_t *offsets, const int32_t *perm_token, const int32_t *perm_slot, void *stream) {
+size_t moe_ep_p2p_route_workspace_bytes(const moe_ep_p2p *p, int tokens) {
+    if (check_p2p(p) != MOE_OK || tokens < 0) return 0;
+    return moe_router_workspace_bytes(tokens, p->experts);
+}
+
+int moe_ep_p2p_route(const moe_ep_p2p *p, const uint16_t *x, int tokens, const uint16_t *router, const float *bias,
+                     const uint16_t *shared_gate_w, uint16_t *logits, int64_t *idx, uint16_t *scores, uint16_t *sig,
+                     int32_t *route_pos, void *workspace, size_t workspace_bytes, void *stream) {
+    using namespace lrb;
     if (int rc = check_p2p(p)) return rc;
-    LRB_REQUIRE(x && idx && offsets && perm_token && perm_slot, "moe_ep_p2p_publish: null input");
-    LRB_REQUIRE(tokens >= 0 && tokens <= p->own_rows, "moe_ep_p2p_publish: tokens %d > own rows %d", tokens,
-                p->own_rows);
-    LRB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, "moe_ep_p2p_publish: x must be 16-byte aligned");
-    return lrb::launch_pdl(lrb::ep_p2p_publish_kernel, dim3(copy_grid()), dim3(256), 0,
-                           static_cast<cudaStream_t>(stream), "ep_p2p_publish_kernel", args_of(p), x, tokens, idx,
-                           offsets, perm_token, perm_slot);
+    if (int rc = check_router_args(tokens, p->hidden, p->experts, p->top_k)) return rc;
+    LRB_REQUIRE(p->top_k <= 16, "moe_ep_p2p_route: top_k %d > 16", p->top_k);
+    LRB_REQUIRE(x && router && logits && idx && scores && route_pos, "moe_ep_p2p_route: null input");
+    LRB_REQUIRE(!shared_gate_w || sig, "moe_ep_p2p_route: shared_gate_w needs a sig output");
+    LRB_REQUIRE(tokens <= p->own_rows, "moe_ep_p2p_route: tokens %d > own rows %d", tokens, p->own_rows);
+    LRB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0, "moe_ep_p2p_route: x must be 16-byte aligned");
+    if (int rc = require_sm100()) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int E = p->experts, H = p->hidden;
+    // the logits: tensor-core partials (summed by the selection) at prefill
+    // widths, the decode logits kernel for one or two tokens
+    const float *part = nullptr;
+    int ks = 1;
+    const uint16_t *gate_sel = shared_gate_w;
+    if (tokens > kDecodeMaxTokens) {
+        const size_t need = moe_router_workspace_bytes(tokens, E);
+        if (need > 0 && workspace && workspace_bytes >= need) {
+            ks = router_tc_splits(tokens, E);
+            part = static_cast<const float *>(workspace);
+        }
+        if (int rc = launch_router_tc(x, router, tokens, H, E, logits, const_cast<float *>(part), ks, nullptr, s))
+            return rc;
+    } else if (tokens > 0) {
+        if (int rc = launch_router_logits(x, router, shared_gate_w, tokens, H, E, logits, sig, s)) return rc;
+        gate_sel = nullptr;  // sig came with the logits
+    }
+    const dim3 grid(static_cast<unsigned>(std::max(1, (tokens + 7) / 8)));
+    if (E <= 256)
+        return launch_pdl(ep_p2p_select_kernel<8>, grid, dim3(256), 0, s, "ep_p2p_select_kernel", args_of(p), x,
+                          tokens, part, ks, bias, gate_sel, logits, idx, scores, sig, route_pos);
+    return launch_pdl(ep_p2p_select_kernel<32>, grid, dim3(256), 0, s, "ep_p2p_select_kernel", args_of(p), x,
+                      tokens, part, ks, bias, gate_sel, logits, idx, scores, sig, route_pos);
 }
 
 size_t moe_ep_p2p_workspace_bytes(const moe_ep_p2p *p, int inner) {

@@ -74,71 +74,12 @@ __global__ void __launch_bounds__(256) router_select_kernel(const uint16_t *__re
                                                             const float *__restrict__ part, int ks) {
     grid_dependency_wait();
     grid_dependency_trigger();
-    const int lane = threadIdx.x & 31;
     const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (t >= tokens) return;
-    uint16_t *row = const_cast<uint16_t *>(logits) + static_cast<size_t>(t) * experts;
-    // Every load of the token issued up front: its logits (or the FP32 K-split
-    // partials, summed in split order and rounded once to BF16, F.linear),
-    // and the shared-expert gate operands, in rounds of 8 per lane.
-    float z[VPL];
-    if (part) {
-        float p[VPL][4];
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-            const int j = min(lane + 32 * v, experts - 1);
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                p[v][k] = k < ks ? part[(static_cast<size_t>(k) * tokens + t) * experts + j] : 0.f;
-        }
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-            const int j = lane + 32 * v;
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-                if (k < ks) s += p[v][k];
-            const uint16_t lg = f2bf(s);
-            if (j < experts) row[j] = lg;
-            z[v] = bf2f(lg) + (bias && j < experts ? bias[j] : 0.0f);
-        }
-    } else {
-        uint16_t lg[VPL];
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) lg[v] = row[min(lane + 32 * v, experts - 1)];
-#pragma unroll
-        for (int v = 0; v < VPL; ++v) {
-            const int j = lane + 32 * v;
-            z[v] = bf2f(lg[v]) + (bias && j < experts ? bias[j] : 0.0f);
-        }
-    }
-    if (gate_w) {
-        const uint16_t *xr = x + static_cast<size_t>(t) * hidden;
-        float acc = 0.f;
-        for (int c0 = 0; c0 < hidden; c0 += 8 * 256) {
-            uint4 wv[8], xv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int c = c0 + u * 256 + lane * 8;
-                wv[u] = c < hidden ? ld_cached(gate_w + c) : make_uint4(0, 0, 0, 0);
-                xv[u] = c < hidden ? ld_cached(xr + c) : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-                if (c0 + u * 256 + lane * 8 < hidden) acc = dot8(wv[u], xv[u], acc);
-        }
-        acc = warp_sum(acc);
-        if (lane == 0) sig[t] = f2bf(sigmoid_f32(rbf(acc)));
-    }
     int e;
     float w;
-    warp_topk<VPL>([&](int j) { return z[j >> 5]; }, experts, top_k, &e, &w);
-    if (lane < top_k) {
-        const size_t o = static_cast<size_t>(t) * top_k + lane;
-        idx[o] = e;
-        if (scores_f32) scores_f32[o] = w;
-        if (scores_bf16) scores_bf16[o] = f2bf(w);
-    }
+    select_token<VPL>(t, logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16, x, gate_w, hidden, sig,
+                      part, ks, &e, &w);
 }
 
 // Decode widths: every (row, K quarter) pair is one warp over all tokens, so

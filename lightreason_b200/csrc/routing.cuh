@@ -260,4 +260,87 @@ __device__ __forceinline__ void warp_topk(ZOf z_of, int experts, int top_k, int 
     *w_out = my_p / sum;
 }
 
+// The selection of one token by one warp (router_select_kernel, and the
+// expert-parallel selection that also publishes the routes): its logits (or
+// the FP32 K-split partials, summed in split order and rounded once to BF16,
+// F.linear) + bias, softmax, top-k, renormalised BF16 weights, and with
+// gate_w the shared-expert gate sig = bf16(sigmoid(bf16(x . w)))
+// (modeling_qwen3_5_moe :762-770, :779, :788).  Lane k < top_k returns the
+// k-th expert and its FP32 weight.
+template <int VPL>
+__device__ __forceinline__ void select_token(int t, const uint16_t *__restrict__ logits,
+                                             const float *__restrict__ bias, int tokens, int experts, int top_k,
+                                             int64_t *__restrict__ idx, float *__restrict__ scores_f32,
+                                             uint16_t *__restrict__ scores_bf16, const uint16_t *__restrict__ x,
+                                             const uint16_t *__restrict__ gate_w, int hidden,
+                                             uint16_t *__restrict__ sig, const float *__restrict__ part, int ks,
+                                             int *e_out, float *w_out) {
+    const int lane = threadIdx.x & 31;
+    uint16_t *row = const_cast<uint16_t *>(logits) + static_cast<size_t>(t) * experts;
+    // Every load of the token issued up front: its logits (or the FP32 K-split
+    // partials, summed in split order and rounded once to BF16, F.linear),
+    // and the shared-expert gate operands, in rounds of 8 per lane.
+    float z[VPL];
+    if (part) {
+        float p[VPL][4];
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            const int j = min(lane + 32 * v, experts - 1);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                p[v][k] = k < ks ? part[(static_cast<size_t>(k) * tokens + t) * experts + j] : 0.f;
+        }
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            const int j = lane + 32 * v;
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (k < ks) s += p[v][k];
+            const uint16_t lg = f2bf(s);
+            if (j < experts) row[j] = lg;
+            z[v] = bf2f(lg) + (bias && j < experts ? bias[j] : 0.0f);
+        }
+    } else {
+        uint16_t lg[VPL];
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) lg[v] = row[min(lane + 32 * v, experts - 1)];
+#pragma unroll
+        for (int v = 0; v < VPL; ++v) {
+            const int j = lane + 32 * v;
+            z[v] = bf2f(lg[v]) + (bias && j < experts ? bias[j] : 0.0f);
+        }
+    }
+    if (gate_w) {
+        const uint16_t *xr = x + static_cast<size_t>(t) * hidden;
+        float acc = 0.f;
+        for (int c0 = 0; c0 < hidden; c0 += 8 * 256) {
+            uint4 wv[8], xv[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * 256 + lane * 8;
+                wv[u] = c < hidden ? ld_cached(gate_w + c) : make_uint4(0, 0, 0, 0);
+                xv[u] = c < hidden ? ld_cached(xr + c) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (c0 + u * 256 + lane * 8 < hidden) acc = dot8(wv[u], xv[u], acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) sig[t] = f2bf(sigmoid_f32(rbf(acc)));
+    }
+    int e;
+    float w;
+    warp_topk<VPL>([&](int j) { return z[j >> 5]; }, experts, top_k, &e, &w);
+    if (lane < top_k) {
+        const size_t o = static_cast<size_t>(t) * top_k + lane;
+        idx[o] = e;
+        if (scores_f32) scores_f32[o] = w;
+        if (scores_bf16) scores_bf16[o] = f2bf(w);
+    }
+    *e_out = e;
+    *w_out = w;
+}
+
+
 }  // namespace lrb

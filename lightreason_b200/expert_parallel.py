@@ -44,7 +44,7 @@ from lightreason_b200.native import _ptr, _require, check, lib
 
 
 # phases of one peer-exchange rank step, in launch order
-EP_STAGES = ("router", "permute", "publish", "experts", "finish", "combine")
+EP_STAGES = ("route", "experts", "finish", "combine")
 
 
 def shard(experts: int, world: int, rank: int) -> range:
@@ -223,9 +223,8 @@ class ExpertParallelLayer:
         _require(ex.capacity >= self.max_tokens * self.top_k and ex.own_rows >= self.max_tokens,
                  "peer exchange sized below tokens * top_k")
         d = self.dev
-        hist = lib().moe_permute_hist_ints(self.max_tokens, self.top_k, self.experts)
-        self.p_hist = torch.empty(max(hist, 1), dtype=torch.int32, device=d)
-        self.p_rsplit = self.rsplit
+        rws = lib().moe_ep_p2p_route_workspace_bytes(ctypes.byref(ex.args), self.max_tokens)
+        self.p_rsplit = self.rsplit if self.rsplit.numel() >= rws else torch.empty(rws, dtype=torch.uint8, device=d)
         self.p_shared = torch.empty((self.max_tokens, self.hidden), dtype=torch.bfloat16, device=d)
         self.p_stats = torch.zeros(2 + self.world, dtype=torch.int32, device=d)
         inner = self.gate_up.shape[1] // 2
@@ -236,9 +235,10 @@ class ExpertParallelLayer:
         self._peer_ready = True
 
     def _forward_peer(self, x, out, stage_events, ep_events=None):
-        """One rank step over the peer exchange: router and permute of the own
-        tokens, publish (own rows into the symmetric buffer, one entry per
-        route into its owner's), the owner's plan and grouped kernel (rows
+        """One rank step over the peer exchange: route (the router over the own
+        tokens, which also puts the own rows into the symmetric buffer and one
+        entry per route into its owner's, each route's return row ordered by
+        expert id within its token), the owner's plan and grouped kernel (rows
         pulled from their senders, expert rows stored into the senders' ret),
         finish (flags), the ordered combine.  stage_events: None or two CUDA
         events recorded around the grouped kernel."""
@@ -257,19 +257,11 @@ class ExpertParallelLayer:
             if ep_events is not None:
                 ep_events[i].record()
         mark(0)
-        check(lib().moe_router_topk_ws(_ptr(x), _ptr(self.router), _ptr(self.bias), _ptr(self.shared_gate_w),
-                                       tokens, self.hidden, self.experts, self.top_k, _ptr(self.logits),
-                                       _ptr(self.idx), None, _ptr(self.scores), _ptr(self.sig),
-                                       _ptr(self.p_rsplit), self.p_rsplit.numel(), s), "moe_router_topk_ws")
+        check(lib().moe_ep_p2p_route(a, _ptr(x), tokens, _ptr(self.router), _ptr(self.bias),
+                                     _ptr(self.shared_gate_w), _ptr(self.logits), _ptr(self.idx), _ptr(self.scores),
+                                     _ptr(self.sig), _ptr(self.route_pos), _ptr(self.p_rsplit),
+                                     self.p_rsplit.numel(), s), "moe_ep_p2p_route")
         mark(1)
-        c = self.counters.data_ptr()
-        check(lib().moe_permute_wide(_ptr(self.idx), tokens, self.top_k, self.experts, _ptr(self.offsets),
-                                     _ptr(self.perm_token), _ptr(self.perm_slot), _ptr(self.route_pos),
-                                     _ptr(self.active), c, c + 4, _ptr(self.p_hist), s), "moe_permute_wide")
-        mark(2)
-        check(lib().moe_ep_p2p_publish(a, _ptr(x), tokens, _ptr(self.idx), _ptr(self.offsets),
-                                       _ptr(self.perm_token), _ptr(self.perm_slot), s), "moe_ep_p2p_publish")
-        mark(3)
         kev = None
         if stage_events is not None:
             for e in stage_events:
@@ -279,13 +271,13 @@ class ExpertParallelLayer:
         check(lib().moe_ep_p2p_experts(a, _ptr(self.gate_up), _ptr(self.down), self.p_inner, tokens,
                                        _ptr(self.p_shared), _ptr(self.p_stats), _ptr(self.p_ws), self.p_ws.numel(),
                                        kev, s), "moe_ep_p2p_experts")
-        mark(4)
+        mark(2)
         check(lib().moe_ep_p2p_finish(a, s), "moe_ep_p2p_finish")
-        mark(5)
+        mark(3)
         check(lib().moe_ep_combine(ctypes.c_void_p(ex.ret_ptr), _ptr(self.route_pos), _ptr(self.scores),
                                    _ptr(self.p_shared), _ptr(self.sig), tokens, self.top_k, self.hidden, _ptr(out), s),
               "moe_ep_combine")
-        mark(6)
+        mark(4)
         return out
 
     def peer_stats(self) -> dict:
@@ -344,7 +336,7 @@ class PeerExchange:
         i32 = dict(dtype=torch.int32, device=device)
         self.peers = torch.tensor(peers, dtype=torch.int64, device=device)
         self.step = torch.ones(1, **i32)
-        self.sync = torch.zeros(2, **i32)
+        self.sync = torch.zeros(2 + 64, **i32)  # two last-CTA counters, a send count per rank
         self.error = torch.zeros(1, **i32)
         self.ret_ptr = base.value + off_ret
         self.args = native.EpP2P(peers=self.peers.data_ptr(), off_flags_publish=off_fp, off_flags_return=off_fr,

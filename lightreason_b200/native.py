@@ -82,7 +82,8 @@ _SIGNATURES = {
     "moe_ipc_free": ([_p], _i),
     "moe_ipc_open": ([_p, ctypes.POINTER(_p)], _i),
     "moe_ipc_close": ([_p], _i),
-    "moe_ep_p2p_publish": ([ctypes.POINTER(EpP2P), _p, _i, _p, _p, _p, _p, _p], _i),
+    "moe_ep_p2p_route_workspace_bytes": ([ctypes.POINTER(EpP2P), _i], _sz),
+    "moe_ep_p2p_route": ([ctypes.POINTER(EpP2P), _p, _i, _p, _p, _p, _p, _p, _p, _p, _p, _p, _sz, _p], _i),
     "moe_ep_p2p_workspace_bytes": ([ctypes.POINTER(EpP2P), _i], _sz),
     "moe_ep_p2p_experts": ([ctypes.POINTER(EpP2P), _p, _p, _i, _i, _p, _p, _p, _sz, ctypes.POINTER(_p), _p], _i),
     "moe_ep_p2p_finish": ([ctypes.POINTER(EpP2P), _p], _i),
