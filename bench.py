@@ -109,6 +109,19 @@ def peaks() -> dict:
     return {"hbm": 6650.0, "tensor": 1590.0, "tensor_sustained": 1400.0, "source": "fallback"}
 
 
+def grouped_mode(width: int) -> str:
+    """Which grouped kernel layout the library runs at this width (tokens of
+    a layer, rows of an expert-parallel owner)."""
+    import os
+
+    from lightreason_b200 import native
+    if native.lib().moe_grouped_paired(width, INNER, HIDDEN):
+        return "CTA pairs (cta_group::2, weights as M = 256)"
+    if width > 512 and os.environ.get("LRB_GROUPED_SWAP") != "1":
+        return "tokens as M = 128, weights as N = 256"
+    return "weights as M = 128, tokens as N"
+
+
 def profiled_traffic(key: str):
     """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of a
     kernel from an ncu capture, as recorded in profiles/dram_traffic.json
@@ -578,6 +591,7 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
         "ms_per_step": round(total_ms / steps, 5), "us_per_step": round(1e3 * total_ms / steps, 2),
         "residency": "all experts in HBM",
         "distinct_experts_per_step": round(float(np.mean(u_per_step)), 2),
+        "grouped_kernel": grouped_mode(tokens),
         "roofline": roofline(kname, b, f, dur, pk, traffic=traffic, traffic_source=traffic_src,
                              layer_gbs=round(layer_gbs, 1), layer_frac=round(layer_gbs / pk["hbm"], 4),
                              stage_us_with_event_overhead={k: round(1e3 * statistics.mean(v), 2)
@@ -981,6 +995,7 @@ def run_ep(args, world, rank, local) -> dict:
                    "experts": EXPERTS, "experts_per_gpu": len(mine), "top_k": TOP_K, "shared_expert": True,
                    "parallelism": f"ep{world}", "transport": transport, "rank0_rows_received": received_rows,
                    "rank0_routes_leaving": leaving, "rank0_distinct_local_experts": u_local,
+                   "grouped_kernel": grouped_mode(tokens + world * tokens * TOP_K),
                    "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window",
                    "timing": timing},
         "roofline": roofline("swiglu_grouped_kernel (rank 0: local experts + shared expert; in-kernel row pull "

@@ -175,6 +175,13 @@ int moe_shared_expert(const uint16_t *x, const uint16_t *gate, const uint16_t *u
                       const uint16_t *gate_w, int tokens, int hidden, int inner, uint16_t *out, uint16_t *sig,
                       void *workspace, size_t workspace_bytes, void *stream);
 
+/* 1 when the grouped expert kernel runs as CTA pairs (tcgen05 cta_group::2,
+ * 256 weight rows per product) at this width -- tokens of a layer, rows of
+ * an expert-parallel owner -- on the current device, else 0.  Pairs run only
+ * with LRB_GROUPED_PAIRS=1 in the environment; the results are the same bit
+ * for bit either way.  No counterpart in the reference. */
+int moe_grouped_paired(int tokens, int inner, int hidden);
+
 /* ------------------------------------------------------------------------
  * One MoE layer.  moe_layer_forward replaces Qwen3_5MoeSparseMoeBlock.forward
  * (modeling_qwen3_5_moe.py:781-792: router + shared expert + experts + gate)

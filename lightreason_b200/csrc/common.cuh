@@ -137,6 +137,29 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     return launch_ex(false, kernel, grid, block, smem, stream, name, std::forward<Args>(args)...);
 }
 
+// As launch_pdl, in clusters of two CTAs (gridDim.x even).
+template <class... KArgs, class... Args>
+int launch_pdl_cluster2(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                        const char *name, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (err != cudaSuccess) return cuda_error(err, name);
+    return MOE_OK;
+}
+
 // As launch_pdl, for a kernel whose CTAs wait on one another: the cooperative
 // attribute makes the launch wait until every CTA of the grid can be resident
 // at once (kernels on other streams may hold SMs), so the wait cannot stall

@@ -570,8 +570,9 @@ int moe_ep_p2p_experts(const moe_ep_p2p *p, const uint16_t *gate_up, const uint1
     o.stats = stats;
     o.tokens = tokens;
     o.bn = bn;
-    o.mb1 = I / 128;
-    o.mb2 = H / 256;
+    const bool pairs = grouped_pairs_for(bn, 1, I, H);
+    o.mb1 = I / (pairs ? 256 : 128);
+    o.mb2 = H / (pairs ? 512 : 256);
     if (int rc = launch_pdl(ep_p2p_plan_kernel, dim3(1), dim3(1024), 0, s, "ep_p2p_plan_kernel", args_of(p), o))
         return rc;
     cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
@@ -611,6 +612,7 @@ int moe_ep_p2p_experts(const moe_ep_p2p *p, const uint16_t *gate_up, const uint1
     GL.bn = bn;
     GL.ks = 1;  // the plan's item counts have no K split
     GL.ctas = sm_count();
+    GL.pairs = pairs;
     if (int rc = launch_grouped(GL, s)) return rc;
     return mark(1);
 }

@@ -49,6 +49,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include <climits>
@@ -72,11 +73,17 @@ constexpr int kSmemGroups = 257;         // plans up to this many groups are sta
 
 }  // namespace
 
-template <int BN>
+// PAIR: a cluster of two CTAs works each item together (tcgen05.mma
+// cta_group::2): each CTA holds 128 of the item's 256 weight rows of an M =
+// 256 product and half of its token tile, so a token tile feeds 512 weight
+// rows per load and every CTA reads fewer operand bytes per FLOP from shared
+// memory, the limit of the single-CTA tile at prefill widths.
+template <int BN, bool PAIR = false>
 struct GroupedShape {
-    static constexpr int kBTile = BN * kBK * 2 < 1024 ? 1024 : BN * kBK * 2;
+    static constexpr int kBRows = PAIR ? BN / 2 : BN;  // token rows of a tile held by one CTA
+    static constexpr int kBTile = kBRows * kBK * 2 < 1024 ? 1024 : kBRows * kBK * 2;
     static constexpr int kStage = 2 * kATile + kBTile;
-    static constexpr int kStages = BN >= 256 ? 3 : BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
+    static constexpr int kStages = PAIR ? 5 : BN >= 256 ? 3 : BN >= 128 ? 4 : (BN >= 64 ? 5 : 6);
     // accumulator buffers of (gate, up): two, so the epilogue of one item
     // overlaps the products of the next, while they fit the 512 TMEM columns
     static constexpr int kBufs = 4 * BN <= 512 ? 2 : 1;
@@ -130,6 +137,21 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
     const uint64_t t0 = now_ns();
     for (uint32_t i = 1;; ++i) {
         if (sm100::mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if ((i & 63) == 0 && now_ns() - t0 > kWaitNs) {
+            *abort = 1;
+            return false;
+        }
+    }
+}
+
+// wait_bar with cluster-scope acquire (barriers other CTAs of the pair arrive on
+// after writing this CTA's shared memory).
+__device__ __forceinline__ bool wait_bar_cluster(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    if (sm100::mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t t0 = now_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (sm100::mbar_try_wait_cluster(bar, parity)) return true;
         if (*abort) return false;
         if ((i & 63) == 0 && now_ns() - t0 > kWaitNs) {
             *abort = 1;
@@ -296,19 +318,32 @@ __device__ __forceinline__ bool combine_cols_k(const int32_t *route_pos, const u
                             store);
 }
 
-template <int BN>
+// TOKM (128-token tiles, single CTA): the token tile is the M = 128 operand
+// and the item's 256 weight rows one N = 256 operand (gate rows then up rows,
+// or the two halves of the down block, which lie back to back in the stage),
+// one product per K step.  The accumulator row of a lane is then one token:
+// the gate and up values of a column sit in the same thread, and each thread
+// stores its token's outputs as contiguous 16-byte vectors instead of one
+// BF16 per token column; the token tile is also read once per K step instead
+// of twice.  Same tiles, items and stage contents as the swapped layout.
+template <int BN, bool PAIR, bool TOKM>
 __global__ void __launch_bounds__(kThreads, 1)
     swiglu_grouped_kernel(const __grid_constant__ CUtensorMap tm_gu, const __grid_constant__ CUtensorMap tm_dn,
                           const __grid_constant__ CUtensorMap tm_sg, const __grid_constant__ CUtensorMap tm_su,
                           const __grid_constant__ CUtensorMap tm_sd, const __grid_constant__ CUtensorMap tm_x,
                           const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_x16,
                           const __grid_constant__ CUtensorMap tm_act16, const GroupedParams P) {
-    using S = GroupedShape<BN>;
+    static_assert(!TOKM || (BN == 128 && !PAIR), "tokens-as-M runs single CTAs on 128-token tiles");
+    using S = GroupedShape<BN, PAIR>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     GroupedSmemTail *tail = reinterpret_cast<GroupedSmemTail *>(smem + S::kStages * S::kStage);
     volatile int *abort = &tail->abort;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // paired mode: this CTA's rank in its pair; rank 0 fetches the items and
+    // issues the products of both
+    const int cta = PAIR ? static_cast<int>(sm100::cluster_ctarank()) : 0;
+    const bool leader = cta == 0;
 
     // Prologue (overlaps the previous kernel under programmatic launch).
     if (threadIdx.x == 0) {
@@ -318,11 +353,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             sm100::mbar_init(&tail->tfull[b], 1);
-            sm100::mbar_init(&tail->tempty[b], 4);
+            sm100::mbar_init(&tail->tempty[b], PAIR ? 8 : 4);  // the epilogue warps of the pair
         }
         for (int i = 0; i < 4; ++i) {
             sm100::mbar_init(&tail->ifull[i], 1);
-            sm100::mbar_init(&tail->iempty[i], 5);
+            // MMA + 4 epilogue warps; paired: the peer's producer and epilogue too
+            sm100::mbar_init(&tail->iempty[i], PAIR ? 10 : 5);
         }
         sm100::mbar_init(&tail->drain, 1);
         tail->abort = 0;
@@ -336,8 +372,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm100::tma_prefetch_map(&tm_sd);
     }
     if (warp == 1) {
-        sm100::tmem_alloc(&tail->tmem_base, S::kTmemCols);
-        sm100::tmem_relinquish();
+        if constexpr (PAIR) {
+            sm100::tmem_alloc_pair(&tail->tmem_base, S::kTmemCols);
+            sm100::tmem_relinquish_pair();
+        } else {
+            sm100::tmem_alloc(&tail->tmem_base, S::kTmemCols);
+            sm100::tmem_relinquish();
+        }
     }
     // The shared expert's rows do not depend on the routing: this CTA's slice
     // of them goes to L2 while the routing kernels still run.
@@ -348,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sm100::tc_fence_before();
     __syncthreads();
+    if constexpr (PAIR) sm100::cluster_sync();  // the peer's barriers exist before any remote arrive
     sm100::tc_fence_after();
     const uint32_t tmem = tail->tmem_base;
     grid_dependency_wait();  // routing and token gather are complete from here on
@@ -360,7 +402,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_groups = P.plan->num_groups;
     const int items1 = P.plan->items1, items2 = P.plan->items2;
     const int total = items1 + items2 + P.plan->items3;
-    const int mb1 = P.inner / kBM, mb2 = P.hidden / (2 * kBM);
+    // weight rows per item: phase 1 kBM of gate and of up (2 kBM paired),
+    // phase 2 2 kBM of down (4 kBM paired)
+    const int mb1 = P.inner / (PAIR ? 2 * kBM : kBM), mb2 = P.hidden / (PAIR ? 4 * kBM : 2 * kBM);
     // Stage the plan in shared memory: every item decode then costs a few
     // shared loads instead of a chain of dependent global ones.
     PlanView V{P.off1, P.off2, P.groups};
@@ -387,38 +431,75 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, sphase = 0;
             uint32_t issued_parity[8];
             bool issued[8] = {false, false, false, false, false, false, false, false};
-            int next = atomicAdd(&P.plan->work, 1);
+            int next = leader ? atomicAdd(&P.plan->work, 1) : 0;
             for (int it = 0;; ++it) {
-                int item = next;
-                if (item >= total) item = -1;
-                else next = atomicAdd(&P.plan->work, 1);  // in flight while this item streams
                 const int slot = it & 3;
-                if (!wait_bar(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort)) break;
-                tail->item[slot] = item;
-                sm100::mbar_arrive(&tail->ifull[slot]);
+                int item;
+                if (PAIR && !leader) {
+                    // the leader hands this CTA the pair's item
+                    if (!wait_bar_cluster(&tail->ifull[slot], (it >> 2) & 1, abort)) break;
+                    item = tail->item[slot];
+                    sm100::mbar_arrive_cluster(sm100::mapa(&tail->iempty[slot], 0));
+                } else {
+                    item = next;
+                    if (item >= total) item = -1;
+                    else next = atomicAdd(&P.plan->work, 1);  // in flight while this item streams
+                    if (PAIR ? !wait_bar_cluster(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort)
+                             : !wait_bar(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort))
+                        break;
+                    tail->item[slot] = item;
+                    if constexpr (PAIR) {
+                        sm100::st_cluster_u32(sm100::mapa(&tail->item[slot], 1), static_cast<uint32_t>(item));
+                        sm100::mbar_arrive_cluster(sm100::mapa(&tail->ifull[slot], 1));
+                    }
+                    sm100::mbar_arrive(&tail->ifull[slot]);
+                }
                 if (item < 0) break;
                 const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
                 if (ip.phase == 3) continue;  // combine: no operand loads
                 const GroupedGroup G = V.groups[ip.g];
                 const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
                 const int kb0 = ip.phase == 1 ? ip.ks * kspan : 0;
-                const int row0 = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM);
-                const int tok0 = G.begin + ip.nt * BN;
+                // this CTA's first weight row (paired: its 128 of the item's 256)
+                const int row0 = PAIR ? ip.mb * (ip.phase == 1 ? 2 * kBM : 4 * kBM) + cta * kBM
+                                      : ip.mb * (ip.phase == 1 ? kBM : 2 * kBM);
                 // a group of one token tile reads each weight tile once: evict it
                 // first; with several tiles the later ones re-read it from L2
                 const uint64_t ipol = G.ntiles == 1 ? wpol : npol;
                 // Token tiles are loaded (and multiplied) only as wide as their
-                // rows, rounded up to 16: a full tile in one box of BN rows, a
-                // partial one in boxes of 16.
-                const int n16 = (min(BN, G.count - ip.nt * BN) + 15) & ~15;
-                const uint32_t bytes = 2 * kATile + n16 * kBK * 2;
+                // rows, rounded up to 16 (32 paired, each CTA holding half): a
+                // full tile in one box, a partial one in boxes of 16 rows.
+                const int nmma = PAIR ? (min(BN, G.count - ip.nt * BN) + 31) & ~31
+                                      : (min(BN, G.count - ip.nt * BN) + 15) & ~15;
+                const int nb = PAIR ? nmma / 2 : nmma;  // token rows this CTA loads
+                const int tok0 = G.begin + ip.nt * BN + cta * nb;
+                const uint32_t bytes = (PAIR ? 2 : 1) * (2 * kATile + nb * kBK * 2);  // on the leader's barrier
                 auto load_b = [&](const CUtensorMap *full_map, const CUtensorMap *map16, uint8_t *dst, uint64_t *bar,
                                   int k0) {
-                    if (n16 == BN) {
+                    if constexpr (PAIR) {
+                        const uint32_t lb = sm100::mapa(bar, 0);
+                        if (nb == S::kBRows) {
+                            sm100::tma_load_2d_pair(dst, full_map, lb, k0, tok0, npol);
+                        } else {
+                            for (int r = 0; r < nb; r += 16)
+                                sm100::tma_load_2d_pair(dst + r * kBK * 2, map16, lb, k0, tok0 + r, npol);
+                        }
+                    } else if (nb == BN) {
                         sm100::tma_load_2d(dst, full_map, bar, k0, tok0);
                     } else {
-                        for (int r = 0; r < n16; r += 16) sm100::tma_load_2d(dst + r * kBK * 2, map16, bar, k0, tok0 + r);
+                        for (int r = 0; r < nb; r += 16) sm100::tma_load_2d(dst + r * kBK * 2, map16, bar, k0, tok0 + r);
                     }
+                };
+                // weight tiles: a bank expert (3-D map) or the shared expert
+                // (2-D); every call names its map, so each TMA instruction reads
+                // a fixed kernel-parameter descriptor
+                auto load_w3 = [&](uint8_t *dst, const CUtensorMap *map, uint64_t *bar, int k0, int r, int e) {
+                    if constexpr (PAIR) sm100::tma_load_3d_pair(dst, map, sm100::mapa(bar, 0), k0, r, e, ipol);
+                    else sm100::tma_load_3d_hint(dst, map, bar, k0, r, e, ipol);
+                };
+                auto load_w2 = [&](uint8_t *dst, const CUtensorMap *map, uint64_t *bar, int k0, int r) {
+                    if constexpr (PAIR) sm100::tma_load_2d_pair(dst, map, sm100::mapa(bar, 0), k0, r, ipol);
+                    else sm100::tma_load_2d_hint(dst, map, bar, k0, r, ipol);
                 };
                 // Weight tiles stream right away; activation tiles wait for their
                 // producers: phase 2 for the group's phase 1 (every phase-1 tile
@@ -427,7 +508,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool tables = P.src_rows != nullptr;
                 bool dep_ok = p1 ? (!tables && (xs_seen || !P.gather_x)) : false;
                 const int32_t *dep_ctr = p1 ? (tables ? &P.row_ready[ip.g] : &P.plan->xs_ready) : &P.done1[ip.g];
-                const int need = p1 ? (tables ? G.count : P.gather_need) : 4 * mb1 * G.ntiles;
+                // phase 2 waits for every epilogue warp of the group's phase-1 items
+                const int need = p1 ? (tables ? G.count : P.gather_need) : (PAIR ? 8 : 4) * mb1 * G.ntiles;
                 const CUtensorMap *bmap = p1 ? &tm_x : &tm_act, *bmap16 = p1 ? &tm_x16 : &tm_act16;
                 int pending[8];
                 int n_pending = 0;
@@ -455,23 +537,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t *st = smem + stage * S::kStage;
                     uint64_t *fb = &tail->full[stage];
-                    sm100::mbar_expect_tx(fb, bytes);
+                    if (leader) sm100::mbar_expect_tx(fb, bytes);
                     const int k0 = kb * kBK;
+                    // the second down block starts kBM rows on (2 kBM paired: the
+                    // other M = 256 product)
+                    const int row1 = row0 + (PAIR ? 2 * kBM : kBM);
                     if (ip.phase == 1) {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d_hint(st, &tm_gu, fb, k0, row0, G.weight, ipol);
-                            sm100::tma_load_3d_hint(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight, ipol);
+                            load_w3(st, &tm_gu, fb, k0, row0, G.weight);
+                            load_w3(st + kATile, &tm_gu, fb, k0, P.inner + row0, G.weight);
                         } else {
-                            sm100::tma_load_2d_hint(st, &tm_sg, fb, k0, row0, ipol);
-                            sm100::tma_load_2d_hint(st + kATile, &tm_su, fb, k0, row0, ipol);
+                            load_w2(st, &tm_sg, fb, k0, row0);
+                            load_w2(st + kATile, &tm_su, fb, k0, row0);
                         }
                     } else {
                         if (G.weight >= 0) {
-                            sm100::tma_load_3d_hint(st, &tm_dn, fb, k0, row0, G.weight, ipol);
-                            sm100::tma_load_3d_hint(st + kATile, &tm_dn, fb, k0, row0 + kBM, G.weight, ipol);
+                            load_w3(st, &tm_dn, fb, k0, row0, G.weight);
+                            load_w3(st + kATile, &tm_dn, fb, k0, row1, G.weight);
                         } else {
-                            sm100::tma_load_2d_hint(st, &tm_sd, fb, k0, row0, ipol);
-                            sm100::tma_load_2d_hint(st + kATile, &tm_sd, fb, k0, row0 + kBM, ipol);
+                            load_w2(st, &tm_sd, fb, k0, row0);
+                            load_w2(st + kATile, &tm_sd, fb, k0, row1);
                         }
                     }
                     if (!dep_ok && sm100::ld_acquire(dep_ctr) >= need) {
@@ -510,7 +595,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (p1 && dep_ok && !tables) xs_seen = true;
                 if (!ok) break;
             }
-            if (*abort) {
+            if (PAIR && *abort) {
+                // A pair's loads complete on the leader's barriers, which the
+                // peer cannot watch: give every load in flight a bounded time
+                // to land (far above any load latency) before the CTA leaves.
+                const uint64_t t0 = now_ns();
+                while (now_ns() - t0 < 200000) __nanosleep(1000);
+            } else if (*abort) {
                 // Let every load this thread issued land before the CTA leaves.
                 for (int s = 0; s < S::kStages; ++s) {
                     if (!issued[s]) continue;
@@ -522,7 +613,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else if (warp == 1) {
         // --------------------------------------------------------- MMA issuer
-        if (lane == 0) {
+        // (paired: the leader's, for both CTAs)
+        if (lane == 0 && leader) {
             uint32_t stage = 0, sphase = 0;
             int acc = 0;
             bool any = false;
@@ -536,10 +628,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (ip.phase == 3) continue;
                 const int kspan = (ip.phase == 1 ? P.hidden / P.ks : P.inner) / kBK;
                 const GroupedGroup G = V.groups[ip.g];
-                const int n16 = (min(BN, G.count - ip.nt * BN) + 15) & ~15;
-                const uint32_t idesc = sm100::idesc_bf16_f32(kBM, n16);
+                const int nmma = PAIR ? (min(BN, G.count - ip.nt * BN) + 31) & ~31
+                                      : (min(BN, G.count - ip.nt * BN) + 15) & ~15;
+                // TOKM: M = 128 token rows (a partial tile's stale rows give
+                // accumulator rows nobody reads), N = 256 weight rows
+                const uint32_t idesc = TOKM ? sm100::idesc_bf16_f32(kBM, 2 * kBM)
+                                            : sm100::idesc_bf16_f32(PAIR ? 2 * kBM : kBM, nmma);
                 const int buf = acc % S::kBufs;
-                if (!wait_bar(&tail->tempty[buf], ((acc / S::kBufs) & 1) ^ 1, abort)) break;
+                if (PAIR ? !wait_bar_cluster(&tail->tempty[buf], ((acc / S::kBufs) & 1) ^ 1, abort)
+                         : !wait_bar(&tail->tempty[buf], ((acc / S::kBufs) & 1) ^ 1, abort))
+                    break;
                 sm100::tc_fence_after();
                 const uint32_t d_gate = tmem + buf * 2 * BN, d_up = d_gate + BN;
                 bool ok = true;
@@ -556,10 +654,19 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
                         const uint32_t accumulate = (kb | kk) != 0;
-                        sm100::mma_bf16(d_gate, a0 + 2 * kk, b + 2 * kk, idesc, accumulate);
-                        sm100::mma_bf16(d_up, a1 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                        if constexpr (TOKM) {
+                            sm100::mma_bf16(d_gate, b + 2 * kk, a0 + 2 * kk, idesc, accumulate);
+                        } else if constexpr (PAIR) {
+                            sm100::mma_bf16_pair(d_gate, a0 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                            sm100::mma_bf16_pair(d_up, a1 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                        } else {
+                            sm100::mma_bf16(d_gate, a0 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                            sm100::mma_bf16(d_up, a1 + 2 * kk, b + 2 * kk, idesc, accumulate);
+                        }
                     }
-                    sm100::mma_commit(&tail->empty[stage]);
+                    // the stage is free in both CTAs once these products are done
+                    if constexpr (PAIR) sm100::mma_commit_pair(&tail->empty[stage], 3);
+                    else sm100::mma_commit(&tail->empty[stage]);
                     any = true;
                     if (++stage == S::kStages) {
                         stage = 0;
@@ -567,12 +674,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (!ok) break;
-                sm100::mma_commit(&tail->tfull[buf]);
+                if constexpr (PAIR) sm100::mma_commit_pair(&tail->tfull[buf], 3);
+                else sm100::mma_commit(&tail->tfull[buf]);
                 ++acc;
             }
             if (*abort && any) {
                 // Wait for this thread's MMAs before TMEM is released.
-                sm100::mma_commit(&tail->drain);
+                if constexpr (PAIR) sm100::mma_commit_pair(&tail->drain, 1);
+                else sm100::mma_commit(&tail->drain);
                 const uint64_t t0 = now_ns();
                 while (!sm100::mbar_try_wait(&tail->drain, 0) && now_ns() - t0 < kWaitNs) {
                 }
@@ -583,6 +692,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;           // TMEM lane quadrant this warp may read
         const int et = threadIdx.x - 64;  // 0..127
         int acc = 0;
+        // an accumulator buffer is free again (paired: on the leader, which
+        // issues the next products into both CTAs' TMEM)
+        auto release_acc = [&](uint64_t *bar) {
+            if constexpr (PAIR) sm100::mbar_arrive_cluster(sm100::mapa(bar, 0));
+            else sm100::mbar_arrive(bar);
+        };
         if (P.gather_x) {
             // The token gather of the routed and shared rows (xs[p] = x[token
             // of route p]), spread over every CTA's epilogue warps while the
@@ -613,13 +728,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                            P.sig ? V.groups[n_groups - 1].begin : 0, 0, et * 8, &P.plan->done2_total, 0, abort, false);
         for (int it = 0;; ++it) {
             const int slot = it & 3;
-            if (!wait_bar(&tail->ifull[slot], (it >> 2) & 1, abort)) break;
+            if (PAIR ? !wait_bar_cluster(&tail->ifull[slot], (it >> 2) & 1, abort)
+                     : !wait_bar(&tail->ifull[slot], (it >> 2) & 1, abort))
+                break;
             const int item = tail->item[slot];
             __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&tail->iempty[slot]);
+            if (lane == 0) {
+                if constexpr (PAIR) sm100::mbar_arrive_cluster(sm100::mapa(&tail->iempty[slot], 0));
+                else sm100::mbar_arrive(&tail->iempty[slot]);
+            }
             if (item < 0) break;
             const ItemPos ip = decode_item(P, V, n_groups, items1, items2, item, mb1, mb2);
 
+            if ((PAIR || TOKM) && (ip.phase == 3 || P.ks > 1)) {  // never planned so (host check)
+                *abort = 1;
+                break;
+            }
             if (ip.phase == 3) {
                 const int halves = P.hidden / kCombineCols;
                 const int t = ip.g / halves, c = (ip.g % halves) * kCombineCols + et * 8;
@@ -640,11 +764,72 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!wait_bar(&tail->tfull[buf], (acc / S::kBufs) & 1, abort)) break;
             __syncwarp();
             sm100::tc_fence_after();
-            const int row = ip.mb * (ip.phase == 1 ? kBM : 2 * kBM) + q * 32 + lane;
+            const int row = (PAIR ? ip.mb * (ip.phase == 1 ? 2 * kBM : 4 * kBM) + cta * kBM
+                                  : ip.mb * (ip.phase == 1 ? kBM : 2 * kBM)) +
+                            q * 32 + lane;
             const int p0 = G.begin + ip.nt * BN;
             const int nvalid = min(BN, G.count - ip.nt * BN);
             const uint32_t t_gate = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * 2 * BN;
-            if (ip.phase == 1 && P.ks > 1) {
+            if constexpr (TOKM) {
+                // lane = token p0 + q * 32 + lane of the tile; columns = the
+                // item's 256 weight rows
+                const int tk = q * 32 + lane;
+                const bool valid = tk < nvalid;
+                if (q * 32 < nvalid) {  // warp-uniform: a warp with no token of the tile reads nothing
+                    if (ip.phase == 1) {
+                        uint16_t *dst = P.act + static_cast<size_t>(p0 + tk) * P.inner + ip.mb * kBM;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < kBM; c0 += 16) {
+                            float g[16], u[16];
+                            __syncwarp();
+                            sm100::tmem_ld16(t_gate + c0, g);
+                            sm100::tmem_ld16(t_gate + kBM + c0, u);
+                            sm100::tmem_wait_ld();
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) {
+                                const float a0v = rbf(silu_f32(rbf(g[2 * j]))) * rbf(u[2 * j]);
+                                const float a1v = rbf(silu_f32(rbf(g[2 * j + 1]))) * rbf(u[2 * j + 1]);
+                                pk[j] = static_cast<uint32_t>(f2bf(a0v)) | (static_cast<uint32_t>(f2bf(a1v)) << 16);
+                            }
+                            if (valid) {
+                                uint4 *o = reinterpret_cast<uint4 *>(dst + c0);
+                                o[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                                o[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            }
+                        }
+                    } else {
+                        uint16_t *dst = nullptr;  // this token's output row
+                        if (valid) {
+                            if (P.dst_rows) dst = reinterpret_cast<uint16_t *>(P.dst_rows[p0 + tk]);
+                            else if (P.rows_out) dst = P.rows_out + static_cast<size_t>(P.route_token[p0 + tk]) * P.hidden;
+                            else dst = P.y + static_cast<size_t>(p0 + tk) * P.hidden;
+                            dst += ip.mb * 2 * kBM;
+                        }
+#pragma unroll 1
+                        for (int c0 = 0; c0 < 2 * kBM; c0 += 16) {
+                            float v[16];
+                            __syncwarp();
+                            sm100::tmem_ld16(t_gate + c0, v);
+                            sm100::tmem_wait_ld();
+                            uint32_t pk[8];
+#pragma unroll
+                            for (int j = 0; j < 8; ++j)
+                                pk[j] = static_cast<uint32_t>(f2bf(v[2 * j])) |
+                                        (static_cast<uint32_t>(f2bf(v[2 * j + 1])) << 16);
+                            if (valid) {
+                                uint4 *o = reinterpret_cast<uint4 *>(dst + c0);
+                                o[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                                o[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            }
+                        }
+                    }
+                }
+                sm100::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) release_acc(&tail->tempty[buf]);
+                ++acc;
+            } else if (ip.phase == 1 && P.ks > 1) {
                 // Write this split's FP32 partials; the last split of the tile
                 // sums all of them in split order and writes the activations.
                 float *mine = P.part + (static_cast<size_t>(ip.tile) * P.ks + ip.ks) * 2 * BN * kBM;
@@ -664,7 +849,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 sm100::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                if (lane == 0) release_acc(&tail->tempty[buf]);
                 ++acc;
                 __threadfence();
                 __syncwarp();
@@ -702,7 +887,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 sm100::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                if (lane == 0) release_acc(&tail->tempty[buf]);
                 ++acc;
             } else {
                 // rows_out: column c of the tile is route p0 + c, whose token the
@@ -724,7 +909,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tok[i] = c < nvalid ? P.route_token[p0 + c] : 0;
                     }
                 }
-                // accumulator 0 holds down rows `row`, accumulator 1 rows `row + 128`
+                // accumulator 0 holds down rows `row`, accumulator 1 rows `row +
+                // 128` (`row + 256` paired: the second M = 256 product)
+                const int row2 = row + (PAIR ? 2 * kBM : kBM);
 #pragma unroll
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     if (c0 >= nvalid) break;  // warp-uniform
@@ -747,12 +934,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                             dst = P.y + static_cast<size_t>(p0 + c0 + j) * P.hidden;
                         }
                         dst[row] = f2bf(v[j]);
-                        dst[row + kBM] = f2bf(v2[j]);
+                        dst[row2] = f2bf(v2[j]);
                     }
                 }
                 sm100::tc_fence_before();
                 __syncwarp();
-                if (lane == 0) sm100::mbar_arrive(&tail->tempty[buf]);
+                if (lane == 0) release_acc(&tail->tempty[buf]);
                 ++acc;
             }
             // Publish this warp's 32 rows: each lane fences its own stores, then
@@ -820,10 +1007,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     sm100::tc_fence_before();
     __syncthreads();
+    // paired: no CTA leaves (or frees TMEM) while the other may still arrive
+    // on its barriers or the leader's products still write its TMEM
+    if constexpr (PAIR) sm100::cluster_sync();
     if (warp == 1) {
         __syncwarp();
         sm100::tc_fence_after();
-        sm100::tmem_dealloc(tmem, S::kTmemCols);
+        if constexpr (PAIR) sm100::tmem_dealloc_pair(tmem, S::kTmemCols);
+        else sm100::tmem_dealloc(tmem, S::kTmemCols);
     }
     if (threadIdx.x == 0 && *abort) {
         atomicCAS(&P.plan->error, 0, 1);
@@ -917,9 +1108,9 @@ int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *
 
 namespace {
 
-template <int BN>
+template <int BN, bool PAIR, bool TOKM = false>
 int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
-    using S = GroupedShape<BN>;
+    using S = GroupedShape<BN, PAIR>;
     CUtensorMap gu{}, dn{}, sg{}, su{}, sd{}, xm{}, am{}, xm16{}, am16{};
     const uint64_t H = L.hidden, I = L.inner, rows = static_cast<uint64_t>(L.rows);
     {
@@ -945,15 +1136,16 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     }
     {
         const uint64_t dims[2] = {H, rows}, str[1] = {H * 2};
-        if (int rc = make_map_bf16(&xm, L.xs, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&xm, L.xs, 2, dims, str, S::kBRows)) return rc;
         if (int rc = make_map_bf16(&xm16, L.xs, 2, dims, str, 16)) return rc;
     }
     {
         const uint64_t dims[2] = {I, rows}, str[1] = {I * 2};
-        if (int rc = make_map_bf16(&am, L.act, 2, dims, str, BN)) return rc;
+        if (int rc = make_map_bf16(&am, L.act, 2, dims, str, S::kBRows)) return rc;
         if (int rc = make_map_bf16(&am16, L.act, 2, dims, str, 16)) return rc;
     }
-    if (int rc = ensure_dynamic_smem(swiglu_grouped_kernel<BN>, S::kSmem, "cudaFuncSetAttribute(grouped)")) return rc;
+    if (int rc = ensure_dynamic_smem(swiglu_grouped_kernel<BN, PAIR, TOKM>, S::kSmem, "cudaFuncSetAttribute(grouped)"))
+        return rc;
     GroupedParams P{};
     P.groups = L.groups;
     P.plan = L.plan;
@@ -990,11 +1182,75 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.hidden = L.hidden;
     P.inner = L.inner;
     P.ks = L.ks;
-    return launch_pdl(swiglu_grouped_kernel<BN>, dim3(L.ctas), dim3(kThreads), S::kSmem, stream,
+    if constexpr (PAIR) {
+        const int pairs = std::min(L.ctas / 2, grouped_pair_clusters());
+        return launch_pdl_cluster2(swiglu_grouped_kernel<BN, true, false>, dim3(2 * pairs), dim3(kThreads), S::kSmem, stream,
+                                   "swiglu_grouped_kernel", gu, dn, sg, su, sd, xm, am, xm16, am16, P);
+    }
+    return launch_pdl(swiglu_grouped_kernel<BN, false, TOKM>, dim3(L.ctas), dim3(kThreads), S::kSmem, stream,
                       "swiglu_grouped_kernel", gu, dn, sg, su, sd, xm, am, xm16, am16, P);
 }
 
 }  // namespace
+
+// How many CTA pairs of the paired kernel can be resident at once on the
+// current device (clusters of two must share a GPC), 0 if none; cached per
+// device.
+int grouped_pair_clusters() {
+    static std::mutex mu;
+    static int cached[64];
+    static bool known[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (known[dev]) return cached[dev];
+    using S = GroupedShape<128, true>;
+    int n = 0;
+    // the first query may come while a stream of this thread is being
+    // captured: relaxed mode lets these non-stream calls run
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    if (ensure_dynamic_smem(swiglu_grouped_kernel<128, true, false>, S::kSmem, "cudaFuncSetAttribute(grouped)") ==
+        MOE_OK) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(2 * sm_count());
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = S::kSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, swiglu_grouped_kernel<128, true, false>, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaThreadExchangeStreamCaptureMode(&mode);
+    cudaGetLastError();  // a failed query leaves no sticky error
+    cached[dev] = n;
+    known[dev] = true;
+    return n;
+}
+
+bool grouped_swap_forced() {
+    const char *v = getenv("LRB_GROUPED_SWAP");
+    return v && v[0] == '1';
+}
+
+// The paired kernel (weights as an M = 256 operand split over two CTAs) can
+// serve the prefill widths (token tiles of 128, no K split, no in-kernel
+// gather or combine) when the widths divide into 256-row gate/up and 512-row
+// down blocks and pairs can be resident; the plan's item counts (mb1, mb2)
+// follow the choice.  It gives the same results as the single-CTA kernels and
+// measured no faster than them (the operand traffic it saves is not what
+// bounds the kernel), so it runs only with LRB_GROUPED_PAIRS=1 in the
+// environment (read at every call, so one process can run both).
+bool grouped_pairs_for(int bn, int ks, int inner, int hidden) {
+    const char *v = getenv("LRB_GROUPED_PAIRS");
+    const bool enabled = v && v[0] == '1';
+    return enabled && bn == 128 && ks == 1 && inner % (2 * kBM) == 0 && hidden % (4 * kBM) == 0 &&
+           grouped_pair_clusters() > 0;
+}
 
 int grouped_bn_for(int tokens) { return tokens <= 16 ? 16 : tokens <= 64 ? 32 : tokens <= 512 ? 64 : 128; }
 int grouped_ks_for(int tokens) { return tokens <= 4 ? 4 : tokens <= 8 ? 2 : 1; }
@@ -1034,13 +1290,28 @@ int launch_grouped(const GroupedLaunch &L, cudaStream_t stream) {
                 "grouped: address tables need both tables and the row counters, without gather_x");
     LRB_REQUIRE(L.ks == 1 || L.ks == 2 || L.ks == 4, "grouped: K split %d not in {1, 2, 4}", L.ks);
     LRB_REQUIRE(L.top_k <= 32, "grouped: top_k %d > 32", L.top_k);
+    if (L.pairs) {
+        LRB_REQUIRE(L.bn == 128 && L.ks == 1 && !L.gather_x && L.inner % (2 * kBM) == 0 && L.hidden % (4 * kBM) == 0 &&
+                        L.ctas >= 2,
+                    "grouped: the paired kernel needs 128-token tiles, no K split and no in-kernel gather");
+        return launch_bn<128, true>(L, stream);
+    }
     switch (L.bn) {
-        case 16: return launch_bn<16>(L, stream);
-        case 32: return launch_bn<32>(L, stream);
-        case 64: return launch_bn<64>(L, stream);
-        case 128: return launch_bn<128>(L, stream);
+        case 16: return launch_bn<16, false>(L, stream);
+        case 32: return launch_bn<32, false>(L, stream);
+        case 64: return launch_bn<64, false>(L, stream);
+        case 128:
+            // 128-token tiles run tokens-as-M unless LRB_GROUPED_SWAP=1
+            // (the swapped layout, for comparison; the results are the same)
+            if (L.ks == 1 && !L.gather_x && !grouped_swap_forced()) return launch_bn<128, false, true>(L, stream);
+            return launch_bn<128, false>(L, stream);
         default: return set_error(MOE_EINVAL, "grouped: unsupported token tile %d", L.bn);
     }
 }
 
 }  // namespace lrb
+
+extern "C" int moe_grouped_paired(int tokens, int inner, int hidden) {
+    if (tokens <= 0 || inner <= 0 || hidden <= 0) return 0;
+    return lrb::grouped_pairs_for(lrb::grouped_bn_for(tokens), lrb::grouped_ks_for(tokens), inner, hidden) ? 1 : 0;
+}

@@ -120,9 +120,14 @@ struct GroupedLaunch {
     int32_t *row_ready;
     int32_t *error_out;  // or null: set to 3 when a wait of the kernel gave up
     int tokens, top_k, hidden, inner, bn, ks, ctas;
+    // CTA pairs (grouped_pairs_for): the plan's items are 256 gate/up rows
+    // (mb1 = inner / 256) and 512 down rows (mb2 = hidden / 512)
+    int pairs;
 };
 struct PlanArgs;
 int grouped_bn_for(int tokens);
+int grouped_pair_clusters();
+bool grouped_pairs_for(int bn, int ks, int inner, int hidden);
 int grouped_ks_for(int tokens);
 int grouped_tiles_max(int tokens, int experts, int top_k, int inner);
 size_t grouped_part_floats(int tokens, int experts, int top_k, int inner);

@@ -318,8 +318,11 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     pa.tokens = tokens;
     pa.bn = bn;
     pa.ks = ks;
-    pa.mb1 = I / 128;
-    pa.mb2 = H / 256;  // phase-2 items cover 256 down rows
+    // items of the grouped kernel: 128 gate/up rows and 256 down rows, twice
+    // that for CTA pairs
+    const bool pairs = grouped_pairs_for(bn, ks, I, H);
+    pa.mb1 = I / (pairs ? 256 : 128);
+    pa.mb2 = H / (pairs ? 512 : 256);
     pa.halves = H / 1024;
     pa.groups = groups;
     pa.plan = plan;
@@ -500,6 +503,7 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.bn = bn;
     GL.ks = ks;
     GL.ctas = sm_count();
+    GL.pairs = pairs;
     if (int rc = launch_grouped(GL, s)) return rc;
     if (int rc = mark(5)) return rc;
     if (!fused_combine && !rows_mode) {

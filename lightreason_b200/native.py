@@ -93,6 +93,7 @@ _SIGNATURES = {
     "moe_combine": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p], _i),
     "moe_shared_expert_workspace_bytes": ([_i, _i], _sz),
     "moe_shared_expert": ([_p, _p, _p, _p, _p, _i, _i, _i, _p, _p, _p, _sz, _p], _i),
+    "moe_grouped_paired": ([_i, _i, _i], _i),
 }
 
 EXPORTED = tuple(_SIGNATURES)

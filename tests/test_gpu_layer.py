@@ -419,3 +419,28 @@ def test_layer_on_two_devices_in_one_process():
             torch.cuda.synchronize(dev)
     for tokens in (1, 16, 100):
         assert np.array_equal(got[0, tokens], got[1, tokens]), tokens
+
+
+@pytest.mark.parametrize("tokens", [700, 4096])
+def test_grouped_kernel_layouts_agree(dev, case14, tokens, monkeypatch):
+    """At 128-token tiles the grouped kernel runs tokens-as-M (the token tile
+    the M = 128 operand, the item's 256 weight rows one N = 256 operand); the
+    swapped layout (LRB_GROUPED_SWAP=1) and the CTA-pair kernel
+    (LRB_GROUPED_PAIRS=1, tcgen05.mma cta_group::2) compute the same products.
+    At a width with many partial token tiles (700 tokens, ~22 rows per
+    expert) and at configs[3] (4096) all three must agree bit for bit: every
+    output element is the same FP32 K-sum rounded at the same points."""
+    x = S.hidden_states(900 + tokens, tokens)
+    monkeypatch.delenv("LRB_GROUPED_SWAP", raising=False)
+    monkeypatch.delenv("LRB_GROUPED_PAIRS", raising=False)
+    assert native.lib().moe_grouped_paired(tokens, S.INNER, S.HIDDEN) == 0
+    tokm = case14.run(x)
+    monkeypatch.setenv("LRB_GROUPED_SWAP", "1")
+    swapped = case14.run(x)
+    monkeypatch.delenv("LRB_GROUPED_SWAP")
+    monkeypatch.setenv("LRB_GROUPED_PAIRS", "1")
+    assert native.lib().moe_grouped_paired(tokens, S.INNER, S.HIDDEN) == 1, "pairs not selectable at this width"
+    paired = case14.run(x)
+    for other, name in ((swapped, "swapped"), (paired, "paired")):
+        for a, b, what in zip(tokm, other, ("output", "ids", "scores", "logits")):
+            assert np.array_equal(a, b), f"tokens-as-M vs {name} {what} differ at T={tokens}"
