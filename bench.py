@@ -305,6 +305,44 @@ def timed_steps(run_step, steps, warmup, flush, world, n_events=0, event_slots=(
     return [s.elapsed_time(e) for s, e in ev], rows, wall
 
 
+def pipelined_e2e(step, xs_host, shape, dev, steps, warmup, world, capture=True):
+    """ms for `steps` steps through lightreason_b200.pipeline.HostStream: each
+    step's input copied host -> device and its output device -> host on side
+    streams, overlapped with the neighbouring steps' compute; every copy inside
+    the timed window, which is one CUDA-graph replay of all the steps
+    (eager when capture=False).  No L2 flush between steps: each step streams
+    expert banks larger than L2."""
+    from lightreason_b200.pipeline import HostStream
+
+    hs = HostStream(shape, shape, device=dev)
+    outs = [torch.empty(shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pool = len(xs_host)
+
+    def run(first, n):
+        hs.run(step, [xs_host[(first + i) % pool] for i in range(n)], [outs[i % 2] for i in range(n)])
+    run(0, warmup)
+    torch.cuda.synchronize()
+    g = None
+    if capture:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run(warmup, steps)
+        torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    if g is not None:
+        g.replay()
+    else:
+        run(warmup, steps)
+    b.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    del g
+    return a.elapsed_time(b)
+
+
 def between(rows, a, b):
     """Per-step ms between event slots a and b."""
     return [row[a].elapsed_time(row[b]) for row in rows]
@@ -555,6 +593,9 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
         _, krows, _ = timed_steps(hbm_step, steps, warmup, flush, 1, n_events=8, event_slots=(4, 5))
         _, srows, _ = timed_steps(hbm_step, steps, warmup, flush, 1, n_events=8, event_slots=tuple(range(8)))
         e2e_ms, _, _ = timed_steps(e2e_step_of(e2e_layer), steps, warmup, flush, 1)
+        pipe_ms = None
+        if host is None:
+            pipe_ms = pipelined_e2e(lambda x, o: hbm(x, out=o), xs_host, (tokens, HIDDEN), dev, steps, warmup, 1)
         e2e_stage = None
         if host is not None:
             _, grows, _ = timed_steps(e2e_step_of(host), steps, warmup, flush, 1, n_events=8, event_slots=(2, 3))
@@ -603,6 +644,15 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
                   "ms_per_step": round(e2e_total / steps, 4), "h2d_bytes_per_step": tokens * HIDDEN * 2,
                   "d2h_bytes_per_step": tokens * HIDDEN * 2,
                   "path": "moe_layer_forward, experts in HBM, x H2D from pinned memory + out D2H per step"}
+    if pipe_ms is not None:
+        rec["e2e"].update({
+            "value": round(tokens * steps / (pipe_ms / 1e3), 2), "ms_per_step": round(pipe_ms / steps, 4),
+            "serial_ms_per_step": round(e2e_total / steps, 4),
+            "serial_value": round(tokens * steps / (e2e_total / 1e3), 2),
+            "path": ("moe_layer_forward over pinned host batches through lightreason_b200.pipeline.HostStream: "
+                     "each step's x H2D and out D2H on side streams overlapped with the neighbouring steps; the "
+                     "steps as one CUDA-graph replay, no L2 flush between them (the expert banks streamed every "
+                     "step exceed L2); serial_*: one step at a time, copies in line, L2 flushed between steps")})
     if host is not None:
         banks = host.host_packed
         gathered = statistics.mean(sum(banks.expert_bytes(e) for e in set(idx_buf[j].cpu().numpy().reshape(-1)
@@ -713,14 +763,11 @@ def run_stack(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
 
 # ---------------------------------------------------- config 4 (default) ---
 
-def ep_weights(cfg, world, rank, dev):
-    """This rank's experts [El, 2I, H] / [El, H, I] on the device (each expert
+def ep_weights(cfg, mine, dev):
+    """The experts `mine` [El, 2I, H] / [El, H, I] on the device (each expert
     drawn from its own seed, on a thread pool) and the replicated parts."""
-    from lightreason_b200.expert_parallel import shard
-
     seed = cfg["seed"]
     w = S.layer_weights(seed, bias=cfg["bias"])
-    mine = shard(EXPERTS, world, rank)
     gu = torch.empty((len(mine), 2 * INNER, HIDDEN), dtype=torch.bfloat16, device=dev)
     dn = torch.empty((len(mine), HIDDEN, INNER), dtype=torch.bfloat16, device=dev)
 
@@ -731,13 +778,36 @@ def ep_weights(cfg, world, rank, dev):
         for j, a, b in pool.map(draw, range(len(mine))):
             gu[j].copy_(to_dev(a, dev))
             dn[j].copy_(to_dev(b, dev))
-    return w, mine, gu, dn
+    return w, gu, dn
 
 
-def build_ep(cfg, world, rank, dev, transport):
+def ep_placement(cfg, world, rank, dev, transport, mode):
+    """(owner rank per expert or None, this rank's experts, description).
+    "balanced" (peer exchange, N > 1): the routes per expert of the layer's
+    router over one calibration batch per rank (seeds no timed step uses),
+    summed over the ranks, placed by the longest-processing-time rule; else
+    contiguous ranges."""
+    from lightreason_b200.expert_parallel import balanced_placement, expert_loads, placement_experts, shard
+
+    if world == 1 or transport != "p2p" or mode == "contiguous":
+        return None, list(shard(EXPERTS, world, rank)), "contiguous: rank r owns experts [r*E/N, (r+1)*E/N)"
+    import torch.distributed as dist
+
+    w = S.layer_weights(cfg["seed"], bias=cfg["bias"])
+    x_cal = to_dev(S.hidden_states(900 + 17 * rank, cfg["tokens"], step=0), dev)
+    loads = expert_loads(to_dev(w.router, dev), x_cal, bias=torch.from_numpy(w.bias).to(dev), top_k=TOP_K)
+    dist.all_reduce(loads)
+    owner = balanced_placement(loads.cpu().tolist(), world)
+    return owner, placement_experts(owner, rank), ("balanced: routes per expert of the router over one "
+                                                   "calibration batch per rank (not a timed batch), summed "
+                                                   "over the ranks, longest-processing-time placement")
+
+
+def build_ep(cfg, world, rank, dev, transport, placement_mode="balanced"):
     from lightreason_b200.expert_parallel import ExpertParallelLayer, PeerExchange, TorchExchange
 
-    w, mine, gu, dn = ep_weights(cfg, world, rank, dev)
+    owner, mine, how = ep_placement(cfg, world, rank, dev, transport, placement_mode)
+    w, gu, dn = ep_weights(cfg, mine, dev)
     d = lambda a: to_dev(a, dev)  # noqa: E731
     peer = None
     if transport == "p2p":
@@ -749,7 +819,8 @@ def build_ep(cfg, world, rank, dev, transport):
     layer = ExpertParallelLayer(router=d(w.router), gate_up=gu, down=dn, shared_gate=d(w.sh_gate),
                                 shared_up=d(w.sh_up), shared_down=d(w.sh_down), shared_gate_w=d(w.sh_gate_w),
                                 bias=torch.from_numpy(w.bias).to(dev), rank=rank, world=world,
-                                tokens=cfg["tokens"], exchange=exchange)
+                                tokens=cfg["tokens"], exchange=exchange, placement=owner)
+    layer.placement_how = how
     return w, mine, layer, peer
 
 
@@ -794,6 +865,11 @@ def ep_parity(layer, w, out_host, x_dev, world, rank, dev, sample=64) -> dict:
         full_dn = torch.empty((EXPERTS, HIDDEN, INNER), dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(full_gu, layer.gate_up[:el].contiguous())
         dist.all_gather_into_tensor(full_dn, layer.down[:el].contiguous())
+        if layer.placement is not None:  # gathered in rank order: back to expert order
+            from lightreason_b200.expert_parallel import placement_experts
+            order = [e for r in range(world) for e in placement_experts(layer.placement, r)]
+            pos = torch.tensor(np.argsort(order), dtype=torch.int64, device=dev)
+            full_gu, full_dn = full_gu.index_select(0, pos), full_dn.index_select(0, pos)
     else:
         full_gu, full_dn = layer.gate_up[:EXPERTS], layer.down[:EXPERTS]
     sg, su = layer.gate_up[el, :INNER], layer.gate_up[el, INNER:]
@@ -847,7 +923,7 @@ def run_ep(args, world, rank, local) -> dict:
     tokens = cfg["tokens"]
     transport = args.transport if world > 1 else "p2p"
     t_setup = time.perf_counter()
-    w, mine, layer, peer = build_ep(cfg, world, rank, dev, transport)
+    w, mine, layer, peer = build_ep(cfg, world, rank, dev, transport, args.placement)
     xs_np = [S.hidden_states(input_seed(cfg, rank), tokens, step=i) for i in range(POOL)]
     xs = [to_dev(a, dev) for a in xs_np]
     xs_host = [pinned(a) for a in xs_np]
@@ -855,8 +931,8 @@ def run_ep(args, world, rank, local) -> dict:
     out_host = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16).pin_memory()
     xin = torch.empty_like(out)
     flush = l2_flusher(dev)
-    log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, experts "
-        f"{mine.start}..{mine.stop - 1}, transport {transport}")
+    log(f"[bench] ep setup {time.perf_counter() - t_setup:.1f}s, rank {rank}/{world}, {len(mine)} experts "
+        f"({layer.placement_how.split(':')[0]} placement), transport {transport}")
 
     # the expert kernel's own events: two around the grouped kernel on the
     # peer exchange, the local layer's eight stage events on NCCL
@@ -909,12 +985,16 @@ def run_ep(args, world, rank, local) -> dict:
             _, krows, _ = run(dev_step, k_events, k_slots)
             erows = None
             e2e_ms, _, _ = run(e2e_step)
+        out_last = out_host.clone()  # the serial loop's last timed step, for the parity check
+        pipe_ms = pipelined_e2e(lambda x, o: layer(x, out=o), xs_host, (tokens, HIDDEN), dev, args.steps,
+                                args.warmup, world, capture=transport == "p2p")
         if peer is not None:
             peer.check()
     clocks = sampler.summary()
     kern_ms = between(krows, *k_slots)
     total_ms = dist_max(sum(ms), world)
     e2e_total = dist_max(sum(e2e_ms), world)
+    pipe_total = dist_max(pipe_ms, world)
     value = world * tokens * args.steps / (total_ms / 1e3)
 
     # this rank's work in the last timed step
@@ -923,10 +1003,10 @@ def run_ep(args, world, rank, local) -> dict:
         per_sender = st["rows_per_sender"]
         received_rows = st["rows_received"]
         u_local = st["local_experts_with_rows"]
-        sent = layer.offsets.cpu().numpy()
-        el = EXPERTS // world
-        to_self = int(sent[(rank + 1) * el] - sent[rank * el])
-        leaving = int(sent[EXPERTS]) - to_self
+        # the step's own routes (the selection's ids) whose owner is another rank
+        ids = layer.idx[:tokens].cpu().numpy()
+        owner = (np.asarray(layer.placement)[ids] if layer.placement is not None else ids // (EXPERTS // world))
+        leaving = int(np.count_nonzero(owner != rank))
         from_peers = sum(per_sender) - per_sender[rank]
     else:
         m = layer.last_splits
@@ -966,7 +1046,7 @@ def run_ep(args, world, rank, local) -> dict:
 
     # parity of the last timed step (the e2e loop's, as the caller received it)
     last = (args.warmup + args.steps - 1) % POOL
-    parity = ep_parity(layer, w, out_host, xs[last], world, rank, dev)
+    parity = ep_parity(layer, w, out_last, xs[last], world, rank, dev)
     ok = (parity["bit_exact_vs_single_gpu"] and parity["ids_exact_vs_single_gpu"]
           and parity["ids_vs_torch_cpu_router"]["mismatched"] == 0)
     all_ok = dist_all(ok, world)
@@ -993,7 +1073,8 @@ def run_ep(args, world, rank, local) -> dict:
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, Zipf(1.1) router bias)",
         "config": {"workload": cfg["workload"], "tokens_per_gpu": tokens, "hidden": HIDDEN, "inner": INNER,
                    "experts": EXPERTS, "experts_per_gpu": len(mine), "top_k": TOP_K, "shared_expert": True,
-                   "parallelism": f"ep{world}", "transport": transport, "rank0_rows_received": received_rows,
+                   "parallelism": f"ep{world}", "transport": transport, "placement": layer.placement_how,
+                   "rank0_rows_received": received_rows,
                    "rank0_routes_leaving": leaving, "rank0_distinct_local_experts": u_local,
                    "grouped_kernel": grouped_mode(tokens + world * tokens * TOP_K),
                    "l2": "flushed between timed steps by reading a 256 MiB buffer, outside each step's event window",
@@ -1002,10 +1083,17 @@ def run_ep(args, world, rank, local) -> dict:
                              "and return over NVLink)", kernel_bytes,
                              kernel_flops, statistics.mean(kern_ms), pk, traffic=traffic,
                              traffic_source=traffic_src),
-        "e2e": {"value": round(world * tokens * args.steps / (e2e_total / 1e3), 2), "unit": "tokens/s",
-                "ms_per_step": round(e2e_total / args.steps, 4), "h2d_bytes_per_step": tokens * HIDDEN * 2,
+        "e2e": {"value": round(world * tokens * args.steps / (pipe_total / 1e3), 2), "unit": "tokens/s",
+                "ms_per_step": round(pipe_total / args.steps, 4), "h2d_bytes_per_step": tokens * HIDDEN * 2,
                 "d2h_bytes_per_step": tokens * HIDDEN * 2,
-                "path": "ExpertParallelLayer.forward per rank, x H2D from pinned memory + out D2H per step"},
+                "serial_ms_per_step": round(e2e_total / args.steps, 4),
+                "serial_value": round(world * tokens * args.steps / (e2e_total / 1e3), 2),
+                "path": ("ExpertParallelLayer.forward per rank over pinned host batches through "
+                         "lightreason_b200.pipeline.HostStream: each step's x H2D and out D2H on side streams "
+                         "overlapped with the neighbouring steps; the steps as one CUDA-graph replay (eager on "
+                         "NCCL), no L2 flush between them (each rank's expert banks, streamed every step, exceed "
+                         "L2); max over ranks.  serial_*: one step at a time, copies in line, L2 flushed between "
+                         "steps")},
         "parity": parity,
         "ep_stages_us": stages, "nvlink_rank0": nvlink,
         "gpu_launches": launches * args.steps,
@@ -1257,6 +1345,9 @@ def main():
                     help="at N = 1, skip the configs[0..3] sub-records of the default line")
     ap.add_argument("--transport", choices=("p2p", "nccl"), default="p2p",
                     help="expert-parallel exchange on N > 1 GPUs: NVLink peer memory (default) or NCCL all_to_all")
+    ap.add_argument("--placement", choices=("balanced", "contiguous"), default="balanced",
+                    help="expert placement of the peer exchange on N > 1 GPUs: balanced by the routes of a "
+                         "calibration batch (default) or contiguous ranges")
     ap.add_argument("--encode", action="store_true",
                     help="time the device codec encoders on one layer's expert banks instead of the layer")
     ap.add_argument("--profile", type=int, default=0, metavar="N",

@@ -430,7 +430,8 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
  *                       (t, k) the return row route_pos[t][k] = t * top_k +
  *                       (rank of its expert among the token's top_k) and
  *                       writes one entry (local expert, return row, token)
- *                       per route into the owning rank's meta, then releases
+ *                       per route into the owning rank's meta (owner and
+ *                       local index from `placement`), then releases
  *                       its flags_publish; no token row crosses a link here
  *                       and no permute is needed;
  *   moe_ep_p2p_experts  on the owner: waits for every sender, plans one group
@@ -451,7 +452,8 @@ int moe_ep_combine(const uint16_t *ret, const int32_t *route_pos, const uint16_t
  *                       token's routes summed in ascending return row, i.e.
  *                       ascending expert id).
  * Waits give up (1 s for the flags, 2 s inside the expert kernel) with
- * *error = 1 (publish), 2 (return) or 3 (expert kernel); the GPU is never
+ * *error = 1 (publish), 2 (return) or 3 (expert kernel), and 4 when the
+ * placement table names an owner or local index out of range; the GPU is never
  * left waiting. */
 typedef struct moe_ep_p2p {
     const int64_t *peers;
@@ -459,6 +461,11 @@ typedef struct moe_ep_p2p {
     int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
     int32_t *sync, *error;
+    /* Expert placement (device int32[experts], or NULL): entry e = (owner rank
+     * << 16) | (e's index among its owner's local experts).  NULL: rank r owns
+     * experts [r * local_experts, (r + 1) * local_experts).  Every rank owns
+     * local_experts experts, and every rank passes the same table. */
+    const int32_t *placement;
 } moe_ep_p2p;
 
 int moe_ipc_alloc(size_t bytes, void **ptr, void *handle64);

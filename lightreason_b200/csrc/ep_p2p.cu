@@ -20,8 +20,9 @@
 //            t * K + (rank of the route's expert among the token's K), so
 //            the ordered combine, which sums in ascending row, adds them in
 //            ascending expert id (the eager order); each route to expert e
-//            goes to rank d = e / El as an entry of d.meta[r] (local expert,
-//            return row, token), slots taken per CTA with one atomic per
+//            goes to its owner d (e / El, or the placement table's entry) as
+//            an entry of d.meta[r] (local expert, return row, token), slots
+//            taken per CTA with one atomic per
 //            destination; the last CTA writes d.count[r] and releases
 //            d.flags_publish[r] = step.  No token row moves here, and no
 //            permute of the own routes is needed.
@@ -152,7 +153,7 @@ __global__ void __launch_bounds__(256) ep_p2p_select_kernel(EpP2PArgs a, const u
     if (threadIdx.x < W) cta_cnt[threadIdx.x] = 0;
     __syncthreads();
     const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-    int e = -1, row = -1, d = 0, slot = 0;
+    int e = -1, row = -1, d = 0, le = 0, slot = 0;
     if (t < tokens) {
         float w;
         select_token<VPL>(t, logits, bias, tokens, a.experts, K, idx, nullptr, scores, x, gate_w, a.hidden, sig, part,
@@ -168,8 +169,19 @@ __global__ void __launch_bounds__(256) ep_p2p_select_kernel(EpP2PArgs a, const u
         if (lane < K) {
             row = t * K + rank;
             route_pos[static_cast<size_t>(t) * K + lane] = row;
-            d = e / El;
-            slot = atomicAdd(&cta_cnt[d], 1);
+            if (a.placement) {
+                const int pl = __ldg(a.placement + e);
+                d = pl >> 16;
+                le = pl & 0xffff;
+                if (d < 0 || d >= W || le >= El) {  // a malformed table: the route is dropped, the step fails
+                    atomicExch(a.error, 4);
+                    row = -1;
+                }
+            } else {
+                d = e / El;
+                le = e - d * El;
+            }
+            if (row >= 0) slot = atomicAdd(&cta_cnt[d], 1);
         }
     }
     __syncthreads();
@@ -180,7 +192,7 @@ __global__ void __launch_bounds__(256) ep_p2p_select_kernel(EpP2PArgs a, const u
         const int j = cta_base[d] + slot;
         if (j < a.capacity) {  // cannot be exceeded: a rank sends at most own_rows * K routes
             int4 *meta = reinterpret_cast<int4 *>(peer_base(a, d) + a.off_meta) + static_cast<size_t>(a.rank) * a.capacity;
-            meta[j] = make_int4(e - d * El, row, t, 0);
+            meta[j] = make_int4(le, row, t, 0);
         }
     }
     if (last_cta(a.sync + 0)) {
@@ -405,6 +417,7 @@ lrb::EpP2PArgs args_of(const moe_ep_p2p *p) {
     a.step = p->step;
     a.sync = p->sync;
     a.error = p->error;
+    a.placement = p->placement;
     return a;
 }
 

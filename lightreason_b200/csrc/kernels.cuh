@@ -143,6 +143,7 @@ struct EpP2PArgs {
     int world, rank, capacity, hidden, top_k, experts, local_experts, own_rows;
     uint32_t *step;
     int32_t *sync, *error;
+    const int32_t *placement;  // (owner << 16) | local index per expert, or null: contiguous
 };
 // BF16 tensor map: dims[0] innermost, 128-byte swizzle, box {64, box_rows(, 1)}.
 int make_map_bf16(CUtensorMap *map, const void *base, int rank, const uint64_t *dims, const uint64_t *strides_bytes,

@@ -53,6 +53,56 @@ def shard(experts: int, world: int, rank: int) -> range:
     return range(rank * el, (rank + 1) * el)
 
 
+def balanced_placement(loads, world: int) -> list[int]:
+    """The owner rank of every expert, each rank owning len(loads) / world
+    experts, with the per-rank sums of `loads` (routes per expert, measured on
+    a calibration batch) balanced by the longest-processing-time rule:
+    experts in descending load (ties: lower id first), each to the least
+    loaded rank that still has room (ties: the lower rank)."""
+    loads = [int(v) for v in loads]
+    experts = len(loads)
+    _require(world >= 1 and experts % world == 0, f"{experts} experts do not shard evenly over {world} ranks")
+    room = [experts // world] * world
+    sums = [0] * world
+    owner = [0] * experts
+    for e in sorted(range(experts), key=lambda e: (-loads[e], e)):
+        r = min((q for q in range(world) if room[q] > 0), key=lambda q: (sums[q], q))
+        owner[e] = r
+        sums[r] += loads[e]
+        room[r] -= 1
+    return owner
+
+
+def placement_experts(owner, rank: int) -> list[int]:
+    """The experts rank `rank` owns, ascending (its local order)."""
+    return [e for e, r in enumerate(owner) if r == rank]
+
+
+def placement_table(owner) -> list[int]:
+    """moe_ep_p2p.placement: (owner << 16) | index among the owner's experts."""
+    seen: dict[int, int] = {}
+    table = []
+    for r in owner:
+        table.append((int(r) << 16) | seen.get(r, 0))
+        seen[r] = seen.get(r, 0) + 1
+    return table
+
+
+def expert_loads(router: torch.Tensor, x: torch.Tensor, *, bias=None, top_k: int = 8) -> torch.Tensor:
+    """Routes per expert (int64 [E], on the device) of the layer's router over
+    the tokens x [T, H]: the load a placement balances."""
+    native._cuda_bf16(router, "router")
+    native._cuda_bf16(x, "x")
+    experts, hidden = router.shape
+    tokens = x.shape[0]
+    d = x.device
+    logits = torch.empty((tokens, experts), dtype=torch.bfloat16, device=d)
+    idx = torch.empty((tokens, top_k), dtype=torch.int64, device=d)
+    check(lib().moe_router_topk(_ptr(x), _ptr(router), _ptr(bias), None, tokens, hidden, experts, top_k,
+                                _ptr(logits), _ptr(idx), None, None, None, native._stream(d)), "moe_router_topk")
+    return torch.bincount(idx.view(-1), minlength=experts)
+
+
 class TorchExchange:
     """The all-to-all steps over a torch.distributed process group (NCCL for
     CUDA tensors, gloo for CPU ones).  Rows travel as int32 views (gloo has
@@ -103,16 +153,28 @@ def exchange_step(state, ex, compute) -> list[list[int]]:
 class ExpertParallelLayer:
     """One rank's share of the expert-parallel layer (device BF16 tensors).
 
-    gate_up [El, 2I, H] and down [El, H, I]: this rank's experts; router
-    [E, H], bias (f32 [E] or None) and the shared expert are replicas.
-    `tokens` bounds the per-step token count (it sizes the buffers)."""
+    gate_up [El, 2I, H] and down [El, H, I]: this rank's experts in ascending
+    id -- shard(E, world, rank), or with `placement` (owner rank per expert,
+    e.g. balanced_placement of measured loads; peer exchange only) the
+    experts it assigns to this rank; router [E, H], bias (f32 [E] or None)
+    and the shared expert are replicas.  `tokens` bounds the per-step token
+    count (it sizes the buffers)."""
 
     def __init__(self, *, router, gate_up, down, shared_gate, shared_up, shared_down, shared_gate_w, rank, world,
-                 tokens, bias=None, top_k=8, exchange=None):
+                 tokens, bias=None, top_k=8, exchange=None, placement=None):
         native._cuda_bf16(router, "router")
         self.experts, self.hidden = router.shape
         self.rank, self.world, self.top_k = rank, world, top_k
-        self.local_experts = len(shard(self.experts, world, rank))
+        self.placement = None
+        if placement is not None:
+            owner = [int(r) for r in placement]
+            _require(len(owner) == self.experts and all(0 <= r < world for r in owner) and
+                     all(owner.count(r) == self.experts // world for r in range(world)),
+                     "placement must give every rank E / world experts")
+            self.placement = owner
+        self.expert_ids = (placement_experts(self.placement, rank) if self.placement is not None
+                           else list(shard(self.experts, world, rank)))
+        self.local_experts = len(self.expert_ids)
         _require(tuple(gate_up.shape[:1]) == (self.local_experts,) and tuple(down.shape[:1]) == (self.local_experts,),
                  "gate_up/down must hold this rank's experts")
         _require(shared_gate.shape[0] == gate_up.shape[1] // 2,
@@ -156,6 +218,7 @@ class ExpertParallelLayer:
 
     # -- phases (split out so that one process can drive several virtual ranks)
     def dispatch(self, x: torch.Tensor) -> None:
+        _require(self.placement is None, "an expert placement runs with the peer exchange only")
         native._cuda_bf16(x, "x")
         tokens = x.shape[0]
         _require(tokens <= self.max_tokens and x.shape[1] == self.hidden, "x must be [T <= tokens, H]")
@@ -232,6 +295,10 @@ class ExpertParallelLayer:
         ws = lib().moe_ep_p2p_workspace_bytes(ctypes.byref(ex.args), inner)
         _require(ws > 0, "peer exchange: workspace query failed")
         self.p_ws = torch.empty(ws, dtype=torch.uint8, device=d)
+        self.p_place = None
+        if self.placement is not None:
+            self.p_place = torch.tensor(placement_table(self.placement), dtype=torch.int32, device=d)
+        ex.args.placement = self.p_place.data_ptr() if self.p_place is not None else None
         self._peer_ready = True
 
     def _forward_peer(self, x, out, stage_events, ep_events=None):
@@ -354,7 +421,8 @@ class PeerExchange:
         code = int(self.error.item())
         if code:
             what = {1: "a sender never published its routes", 2: "an owner never returned its rows",
-                    3: "the expert kernel gave up waiting"}.get(code, "unknown")
+                    3: "the expert kernel gave up waiting",
+                    4: "the expert placement table is malformed"}.get(code, "unknown")
             raise RuntimeError(f"expert-parallel exchange failed ({code}): {what}")
 
     def close(self) -> None:
@@ -401,4 +469,5 @@ def run_virtual_ranks(layers: list[ExpertParallelLayer], xs: list[torch.Tensor],
     return [layer.combine(o) for layer, o in zip(layers, outs)]
 
 
-__all__ = ["EP_STAGES", "ExpertParallelLayer", "PeerExchange", "TorchExchange", "exchange_step", "run_virtual_ranks", "shard"]
+__all__ = ["EP_STAGES", "ExpertParallelLayer", "PeerExchange", "TorchExchange", "balanced_placement",
+           "exchange_step", "expert_loads", "placement_experts", "placement_table", "run_virtual_ranks", "shard"]

@@ -40,7 +40,7 @@ class EpP2P(ctypes.Structure):
                 ("off_count", ctypes.c_int64), ("off_meta", ctypes.c_int64), ("off_tokens", ctypes.c_int64),
                 ("off_ret", ctypes.c_int64), ("world", _i), ("rank", _i), ("capacity", _i), ("hidden", _i),
                 ("top_k", _i), ("experts", _i), ("local_experts", _i), ("own_rows", _i), ("step", _p),
-                ("sync", _p), ("error", _p)]
+                ("sync", _p), ("error", _p), ("placement", _p)]
 
 
 class LayerIO(ctypes.Structure):

@@ -113,3 +113,31 @@ def test_expert_parallel_exchange_matches_single_layer(world):
     while not failures.empty():
         errs.append(failures.get())
     assert not errs, errs
+
+
+def test_balanced_placement_rule():
+    """Expert placement by the longest-processing-time rule: every rank owns
+    E / world experts, every expert exactly one owner, the heaviest experts
+    land on distinct ranks, and the per-rank load is within one expert's load
+    of the mean (the rule's bound when every rank has the same room)."""
+    from lightreason_b200.expert_parallel import balanced_placement, placement_experts, placement_table
+
+    rng = np.random.default_rng(3)
+    loads = (1000 / np.arange(1, 257) ** 1.1 * rng.uniform(0.5, 1.5, 256)).astype(np.int64)
+    rng.shuffle(loads)
+    for world in (2, 4, 8):
+        owner = balanced_placement(loads, world)
+        assert sorted(set(owner)) == list(range(world))
+        assert all(owner.count(r) == 256 // world for r in range(world))
+        sums = np.bincount(owner, weights=loads, minlength=world)
+        assert sums.max() - sums.mean() <= loads.max(), (world, sums)
+        top = np.argsort(-loads, kind="stable")[:world]
+        assert len({owner[e] for e in top}) == world
+        # the table the kernels read: (owner << 16) | index among the owner's experts, ascending ids
+        table = placement_table(owner)
+        for r in range(world):
+            mine = placement_experts(owner, r)
+            assert mine == sorted(mine)
+            assert [table[e] for e in mine] == [(r << 16) | j for j in range(len(mine))]
+    # equal loads: ties go to the lower rank, i.e. round robin
+    assert balanced_placement([5] * 8, 4) == [0, 1, 2, 3, 0, 1, 2, 3]

@@ -45,13 +45,17 @@ class Weights:
                                    shared_gate=self.sh[0], shared_up=self.sh[1], shared_down=self.sh[2],
                                    shared_gate_w=self.sh[3])
 
-    def rank_layer(self, rank: int, world: int, tokens: int, exchange=None, device=None):
-        s = shard(256, world, rank)
+    def rank_layer(self, rank: int, world: int, tokens: int, exchange=None, device=None, placement=None):
+        from lightreason_b200.expert_parallel import placement_experts
+
+        mine = placement_experts(placement, rank) if placement is not None else list(shard(256, world, rank))
+        sel = torch.tensor(mine, dtype=torch.int64, device=self.gu_dev.device)
         mv = (lambda t: t.to(device)) if device is not None else (lambda t: t)  # noqa: E731
-        return ExpertParallelLayer(router=mv(self.router), gate_up=mv(self.gu_dev[s.start:s.stop]),
-                                   down=mv(self.dn_dev[s.start:s.stop]), shared_gate=mv(self.sh[0]),
+        return ExpertParallelLayer(router=mv(self.router), gate_up=mv(self.gu_dev.index_select(0, sel)),
+                                   down=mv(self.dn_dev.index_select(0, sel)), shared_gate=mv(self.sh[0]),
                                    shared_up=mv(self.sh[1]), shared_down=mv(self.sh[2]), shared_gate_w=mv(self.sh[3]),
-                                   bias=mv(self.bias), rank=rank, world=world, tokens=tokens, exchange=exchange)
+                                   bias=mv(self.bias), rank=rank, world=world, tokens=tokens, exchange=exchange,
+                                   placement=placement)
 
 
 @pytest.fixture(scope="module")
@@ -180,7 +184,7 @@ def test_peer_exchange_one_rank_equals_single_gpu_layer(dev, weights):
         ex.close()
 
 
-def _peer_rank(rank: int, world: int, port: int, tokens: int, failures) -> None:
+def _peer_rank(rank: int, world: int, port: int, tokens: int, failures, balanced: bool = False) -> None:
     import torch.distributed as dist
 
     from lightreason_b200.expert_parallel import PeerExchange
@@ -194,8 +198,17 @@ def _peer_rank(rank: int, world: int, port: int, tokens: int, failures) -> None:
     ex = None
     try:
         w = Weights(41, dev)
+        placement = None
+        if balanced:
+            from lightreason_b200.expert_parallel import balanced_placement, expert_loads
+
+            loads = expert_loads(w.router, to_dev(S.hidden_states(6900 + rank, tokens), dev), bias=w.bias)
+            dist.all_reduce(loads)
+            placement = balanced_placement(loads.cpu().tolist(), world)
+            if placement == [e * world // 256 for e in range(256)]:
+                failures.put(f"rank {rank}: the balanced placement is the contiguous one; the test needs another")
         ex = PeerExchange(world=world, rank=rank, tokens=tokens, top_k=8, hidden=2048, experts=256, device=dev)
-        layer = w.rank_layer(rank, world, tokens, exchange=ex)
+        layer = w.rank_layer(rank, world, tokens, exchange=ex, placement=placement)
         for step in range(3):
             x = to_dev(S.hidden_states(6000 + 10 * step + rank, tokens - step), dev)
             out = layer(x)
@@ -215,13 +228,18 @@ def _peer_rank(rank: int, world: int, port: int, tokens: int, failures) -> None:
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_peer_exchange_ranks_equal_single_gpu_layer():
+@pytest.mark.parametrize("balanced", [False, True], ids=["contiguous", "balanced"])
+def test_peer_exchange_ranks_equal_single_gpu_layer(balanced):
+    """Real ranks over NVLink peer memory, bit-exact against the single-GPU
+    layer: contiguous expert ranges, and a placement balanced on measured
+    routes (experts of one rank scattered over the id range)."""
     import torch.multiprocessing as mp
 
     world = min(torch.cuda.device_count(), 8)
     ctx = mp.get_context("spawn")
     failures = ctx.SimpleQueue()
-    mp.start_processes(_peer_rank, args=(world, _free_port(), 128, failures), nprocs=world, start_method="spawn")
+    mp.start_processes(_peer_rank, args=(world, _free_port(), 128, failures, balanced), nprocs=world,
+                       start_method="spawn")
     errs = []
     while not failures.empty():
         errs.append(failures.get())

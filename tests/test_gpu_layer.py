@@ -444,3 +444,32 @@ def test_grouped_kernel_layouts_agree(dev, case14, tokens, monkeypatch):
     for other, name in ((swapped, "swapped"), (paired, "paired")):
         for a, b, what in zip(tokm, other, ("output", "ids", "scores", "logits")):
             assert np.array_equal(a, b), f"tokens-as-M vs {name} {what} differ at T={tokens}"
+
+
+def test_host_stream_overlapped_transfers_equal_per_batch_calls(dev, case13):
+    """pipeline.HostStream runs the layer over host batches with each batch's
+    copies on side streams overlapped with its neighbours' compute, eagerly
+    and as one captured CUDA graph; every output equals the layer's own call
+    on that batch, bit for bit, and nothing is left unwritten."""
+    from lightreason_b200.pipeline import HostStream
+
+    tokens, n = 64, 5
+    xs = [S.hidden_states(1300 + i, tokens) for i in range(n)]
+    want = [bits(case13.layer(to_dev(x, dev))) for x in xs]
+    host_in = [torch.from_numpy(np.ascontiguousarray(x).view(np.int16)).view(torch.bfloat16).pin_memory()
+               for x in xs]
+    hs = HostStream((tokens, 2048), (tokens, 2048), device=dev)
+    for captured in (False, True):
+        host_out = [torch.full((tokens, 2048), float("nan"), dtype=torch.bfloat16).pin_memory() for _ in range(n)]
+        if captured:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                hs.run(lambda x, o: case13.layer(x, out=o), host_in, host_out)
+            for o in host_out:
+                o.fill_(float("nan"))
+            g.replay()
+        else:
+            hs.run(lambda x, o: case13.layer(x, out=o), host_in, host_out)
+        torch.cuda.synchronize()
+        for i in range(n):
+            assert np.array_equal(host_out[i].view(torch.int16).numpy().view(np.uint16), want[i]), (captured, i)
