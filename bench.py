@@ -594,7 +594,10 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
         _, srows, _ = timed_steps(hbm_step, steps, warmup, flush, 1, n_events=8, event_slots=tuple(range(8)))
         e2e_ms, _, _ = timed_steps(e2e_step_of(e2e_layer), steps, warmup, flush, 1)
         pipe_ms = None
-        if host is None:
+        # overlapped only where a step's working set exceeds L2 (no flush between
+        # its steps): from T = 512 a step reads nearly all 256 experts (1.6 GB);
+        # at decode widths (57 MB at T = 1) it would sit in the 126 MB L2
+        if host is None and tokens >= 512:
             pipe_ms = pipelined_e2e(lambda x, o: hbm(x, out=o), xs_host, (tokens, HIDDEN), dev, steps, warmup, 1)
         e2e_stage = None
         if host is not None:
@@ -924,6 +927,7 @@ def run_ep(args, world, rank, local) -> dict:
     transport = args.transport if world > 1 else "p2p"
     t_setup = time.perf_counter()
     w, mine, layer, peer = build_ep(cfg, world, rank, dev, transport, args.placement)
+    placement_how = layer.placement_how
     xs_np = [S.hidden_states(input_seed(cfg, rank), tokens, step=i) for i in range(POOL)]
     xs = [to_dev(a, dev) for a in xs_np]
     xs_host = [pinned(a) for a in xs_np]
@@ -1073,7 +1077,7 @@ def run_ep(args, world, rank, local) -> dict:
         "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations, Zipf(1.1) router bias)",
         "config": {"workload": cfg["workload"], "tokens_per_gpu": tokens, "hidden": HIDDEN, "inner": INNER,
                    "experts": EXPERTS, "experts_per_gpu": len(mine), "top_k": TOP_K, "shared_expert": True,
-                   "parallelism": f"ep{world}", "transport": transport, "placement": layer.placement_how,
+                   "parallelism": f"ep{world}", "transport": transport, "placement": placement_how,
                    "rank0_rows_received": received_rows,
                    "rank0_routes_leaving": leaving, "rank0_distinct_local_experts": u_local,
                    "grouped_kernel": grouped_mode(tokens + world * tokens * TOP_K),
