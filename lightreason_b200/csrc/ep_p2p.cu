@@ -316,6 +316,7 @@ __global__ void __launch_bounds__(1024) ep_p2p_plan_kernel(EpP2PArgs a, EpPlanOu
         o.plan->done2_total = 0;
         o.plan->xs_ready = 0;
         o.plan->act_ready = 0;
+        o.plan->work2 = 0;
         if (o.stats) {
             o.stats[0] = routed;
             o.stats[1] = n_active;

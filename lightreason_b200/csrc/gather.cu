@@ -176,7 +176,8 @@ __global__ void __launch_bounds__(1024) gather_row_codec_kernel(const int64_t *_
 
 // The layer's host-resident stage with packed banks: active expert g (g-th
 // ascending id) decodes from descriptors[bank][active[g]] into HBM slot g of
-// bank 0 (gate_up) or 1 (down).  Grid (stripes, 2, max_slots), 256 threads.
+// bank 0 (gate_up) or 1 (down), bank = bank0 + blockIdx.y.  Grid (stripes,
+// banks, max_slots), 256 threads.
 //
 // The packed bytes cross the host link as large bulk copies: thread 0 streams
 // the CTA's share of the sign/fraction and exponent-delta regions into a ring
@@ -195,7 +196,7 @@ __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__r
                                                               const int32_t *__restrict__ slot_of_entry,
                                                               uint16_t *gate_up_slots, uint16_t *down_slots,
                                                               int64_t gate_up_bytes, int64_t down_bytes,
-                                                              int32_t *error) {
+                                                              int32_t *error, int bank0) {
     __shared__ __align__(128) uint8_t sf_buf[kStageRing][kStageUnits * 8];
     __shared__ __align__(128) uint8_t dl_buf[kStageRing][kStageUnits * 4];
     __shared__ __align__(8) uint64_t bars[kStageRing];
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__r
     grid_dependency_trigger();
     const int g = blockIdx.z;
     if (g >= *num_active) return;
-    const int bank = blockIdx.y;
+    const int bank = bank0 + static_cast<int>(blockIdx.y);
     const int64_t *d = descriptors + (static_cast<int64_t>(bank) * experts + active[g]) * 3;
     const uint8_t *src = reinterpret_cast<const uint8_t *>(d[0]);
     const int64_t base = d[1], escapes = d[2];
@@ -295,10 +296,11 @@ __global__ void __launch_bounds__(256) stage_row_codec_kernel(const int64_t *__r
 
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
                            int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
-                           int64_t down_bytes, int32_t *error, cudaStream_t stream, const int32_t *slot_of_entry) {
-    return launch_pdl(stage_row_codec_kernel, dim3(64, 2, max_slots), dim3(256), 0, stream, "stage_row_codec_kernel",
-                      descriptors, active, num_active, experts, slot_of_entry, gate_up_slots, down_slots,
-                      gate_up_bytes, down_bytes, error);
+                           int64_t down_bytes, int32_t *error, cudaStream_t stream, const int32_t *slot_of_entry,
+                           int bank0, int banks) {
+    return launch_pdl(stage_row_codec_kernel, dim3(64, banks, max_slots), dim3(256), 0, stream,
+                      "stage_row_codec_kernel", descriptors, active, num_active, experts, slot_of_entry, gate_up_slots,
+                      down_slots, gate_up_bytes, down_bytes, error, bank0);
 }
 
 template <bool AllowCompact>

@@ -13,7 +13,9 @@
 // routed tokens the N operand ("swap AB"), so decode widths (a handful of
 // tokens per expert) and prefill widths (hundreds) share one tile shape.
 //
-// Work items, handed out in this order from a device counter:
+// Work items, handed out in this order from a device counter (a launch may
+// run phase 1 only, or phases 2-3 only after a phase-1 launch of the plan, so
+// that other work can run between them):
 //   phase 1  (group, 128-row block of gate and of up, token tile, K split)
 //   phase 2  (group, 256-row block of down, token tile)
 //   phase 3  (token, 1024-column half; decode widths only)
@@ -124,6 +126,7 @@ struct GroupedParams {
     int32_t *row_ready;              // [num_groups] rows gathered per group (address-table mode)
     int32_t *error_out;              // or null: set to 3 when a wait of this kernel gave up
     int tokens, top_k, hidden, inner, ks;
+    int phases;                      // 3 all items, 1 phase 1 only, 2 phases 2-3 only
 };
 
 __device__ __forceinline__ uint64_t now_ns() {
@@ -431,7 +434,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t stage = 0, sphase = 0;
             uint32_t issued_parity[8];
             bool issued[8] = {false, false, false, false, false, false, false, false};
-            int next = leader ? atomicAdd(&P.plan->work, 1) : 0;
+            // the items of this launch: [lo, hi), fetched from their own counter
+            const int lo = P.phases == 2 ? items1 : 0, hi = P.phases == 1 ? items1 : total;
+            int32_t *ctr = P.phases == 2 ? &P.plan->work2 : &P.plan->work;
+            int next = leader ? lo + atomicAdd(ctr, 1) : 0;
             for (int it = 0;; ++it) {
                 const int slot = it & 3;
                 int item;
@@ -442,8 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     sm100::mbar_arrive_cluster(sm100::mapa(&tail->iempty[slot], 0));
                 } else {
                     item = next;
-                    if (item >= total) item = -1;
-                    else next = atomicAdd(&P.plan->work, 1);  // in flight while this item streams
+                    if (item >= hi) item = -1;
+                    else next = lo + atomicAdd(ctr, 1);  // in flight while this item streams
                     if (PAIR ? !wait_bar_cluster(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort)
                              : !wait_bar(&tail->iempty[slot], ((it >> 2) & 1) ^ 1, abort))
                         break;
@@ -1182,6 +1188,7 @@ int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
     P.hidden = L.hidden;
     P.inner = L.inner;
     P.ks = L.ks;
+    P.phases = L.phases == 1 || L.phases == 2 ? L.phases : 3;
     if constexpr (PAIR) {
         const int pairs = std::min(L.ctas / 2, grouped_pair_clusters());
         return launch_pdl_cluster2(swiglu_grouped_kernel<BN, true, false>, dim3(2 * pairs), dim3(kThreads), S::kSmem, stream,

@@ -29,6 +29,22 @@ int check_launch(const char *where) {
     return err == cudaSuccess ? MOE_OK : cuda_error(err, where);
 }
 
+cudaStream_t side_stream() {
+    static std::mutex mu;
+    static cudaStream_t streams[64] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!streams[device]) {
+        // not a stream operation: allowed while a stream of this thread captures
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        if (cudaStreamCreateWithFlags(&streams[device], cudaStreamNonBlocking) != cudaSuccess) streams[device] = nullptr;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+    }
+    return streams[device];
+}
+
 int sm_count() {
     static int cached[64] = {};
     int device = 0;

@@ -52,6 +52,7 @@ struct GroupedPlan {
     int32_t num_groups, items1, items2, items3, work, error, done2_total;
     int32_t xs_ready;   // epilogue warps that finished the in-kernel token gather
     int32_t act_ready;  // CTAs of the fused decode kernel that published their activations
+    int32_t work2;      // item counter of a launch that runs phases 2-3 only
 };
 
 // The grouped kernel's plan read as pointer groups, for the warp-per-row
@@ -123,6 +124,9 @@ struct GroupedLaunch {
     // CTA pairs (grouped_pairs_for): the plan's items are 256 gate/up rows
     // (mb1 = inner / 256) and 512 down rows (mb2 = hidden / 512)
     int pairs;
+    // which items this launch runs: 3 (0) all, 1 phase 1 only, 2 phases 2-3
+    // only (after a phase-1 launch of the same plan)
+    int phases;
 };
 struct PlanArgs;
 int grouped_bn_for(int tokens);
@@ -157,7 +161,10 @@ int sm_count();
 int launch_stage_row_codec(const int64_t *descriptors, const int32_t *active, const int32_t *num_active, int experts,
                            int max_slots, uint16_t *gate_up_slots, uint16_t *down_slots, int64_t gate_up_bytes,
                            int64_t down_bytes, int32_t *error, cudaStream_t stream,
-                           const int32_t *slot_of_entry = nullptr);
+                           const int32_t *slot_of_entry = nullptr, int bank0 = 0, int banks = 2);
+// A non-blocking stream per device for work the library overlaps with the
+// caller's stream (created on first use, kept for the process).
+cudaStream_t side_stream();
 
 int launch_router_logits(const uint16_t *x, const uint16_t *router, const uint16_t *gate_w, int tokens, int hidden,
                          int experts, uint16_t *logits, uint16_t *sig, cudaStream_t stream);

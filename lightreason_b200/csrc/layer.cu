@@ -96,10 +96,56 @@ T *at(void *base, size_t offset) {
     return reinterpret_cast<T *>(static_cast<char *>(base) + offset);
 }
 
+// Work forked from the caller's stream onto the library's side stream and
+// joined back: begin() creates the two events (allowed while the caller's
+// stream captures; the side stream then joins the capture through the first
+// wait), to_side() orders the side stream after the caller's work so far,
+// side_done() marks the side work's end, join() makes the caller's stream wait
+// for it.  The events are destroyed on every exit path; a wait already
+// enqueued keeps its dependency.
+struct SideFork {
+    cudaStream_t side = nullptr;
+    cudaEvent_t forked = nullptr, done = nullptr;
+
+    int begin(cudaStream_t) {
+        side = side_stream();
+        LRB_REQUIRE(side != nullptr, "moe_layer_forward: no side stream on this device");
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        cudaError_t e = cudaEventCreateWithFlags(&forked, cudaEventDisableTiming);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&done, cudaEventDisableTiming);
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        if (e != cudaSuccess) return cuda_error(e, "cudaEventCreateWithFlags(side fork)");
+        return MOE_OK;
+    }
+    int to_side(cudaStream_t s) {
+        LRB_CUDA(cudaEventRecord(forked, s));
+        LRB_CUDA(cudaStreamWaitEvent(side, forked, 0));
+        return MOE_OK;
+    }
+    int side_done() {
+        LRB_CUDA(cudaEventRecord(done, side));
+        return MOE_OK;
+    }
+    int join(cudaStream_t s) {
+        LRB_CUDA(cudaStreamWaitEvent(s, done, 0));
+        return MOE_OK;
+    }
+    ~SideFork() {
+        if (!forked && !done) return;
+        cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+        cudaThreadExchangeStreamCaptureMode(&mode);
+        if (forked) cudaEventDestroy(forked);
+        if (done) cudaEventDestroy(done);
+        cudaThreadExchangeStreamCaptureMode(&mode);
+    }
+};
+
 }  // namespace
 
 // Copy every active expert's gate_up and down rows from the mapped host banks
-// into HBM slot g (g-th active expert).  Grid (stripes, 2 banks, max_slots);
+// into HBM slot g (g-th active expert).  Grid (stripes, banks, max_slots), bank
+// bank0 + blockIdx.y (0 gate_up, 1 down);
 // 16-byte loads over the host link, four in flight per thread.
 // Entry g < *num_active copies expert active[g] into slot slot_of_entry[g]
 // (or slot g when slot_of_entry is null).
@@ -110,7 +156,7 @@ __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__res
                                                             int64_t gate_up_stride, int64_t down_stride,
                                                             int64_t gate_up_bytes, int64_t down_bytes,
                                                             uint16_t *gate_up_slots, uint16_t *down_slots,
-                                                            int32_t *overflow) {
+                                                            int32_t *overflow, int bank0) {
     grid_dependency_wait();
     grid_dependency_trigger();
     const int g = blockIdx.z;
@@ -118,7 +164,7 @@ __global__ void __launch_bounds__(256) stage_experts_kernel(const int32_t *__res
     if (g == 0 && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *overflow = n > static_cast<int>(gridDim.z);
     if (g >= n) return;
     const int64_t e = active[g];
-    const bool gu = blockIdx.y == 0;
+    const bool gu = bank0 + static_cast<int>(blockIdx.y) == 0;
     const uint4 *src = reinterpret_cast<const uint4 *>(gu ? host_gate_up + e * gate_up_stride
                                                           : host_down + e * down_stride);
     const int64_t bytes = gu ? gate_up_bytes : down_bytes;
@@ -284,13 +330,14 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     // external record node keeps the event usable for timing each replay.
     cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
     if (io->stage_events) LRB_CUDA(cudaStreamIsCapturing(s, &capturing));
-    auto mark = [&](int i) -> int {
+    auto mark_on = [&](int i, cudaStream_t st) -> int {
         if (io->stage_events && i < io->num_stage_events && io->stage_events[i])
-            LRB_CUDA(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(io->stage_events[i]), s,
+            LRB_CUDA(cudaEventRecordWithFlags(static_cast<cudaEvent_t>(io->stage_events[i]), st,
                                               capturing == cudaStreamCaptureStatusActive ? cudaEventRecordExternal
                                                                                          : cudaEventRecordDefault));
         return MOE_OK;
     };
+    auto mark = [&](int i) -> int { return mark_on(i, s); };
     if (int rc = mark(0)) return rc;
 
     void *ws = workspace;
@@ -415,25 +462,42 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
         stage_slot = ss;
         stage_count = counters + 5;
     }
-    if (packed_host) {
-        if (int rc = launch_stage_row_codec(io->host_descriptors, stage_list, stage_count, E, max_groups,
-                                            io->gate_up_slots, io->down_slots, static_cast<int64_t>(2) * I * H * 2,
-                                            static_cast<int64_t>(H) * I * 2, counters + 2, s, stage_slot))
-            return rc;
-    } else if (staged) {
-        if (int rc = launch_pdl(stage_experts_kernel, dim3(64, 2, max_groups), dim3(256), 0, s,
-                                "stage_experts_kernel", stage_list, stage_count, stage_slot, io->host_gate_up,
-                                io->host_down, gu_stride, dn_stride, static_cast<int64_t>(2) * I * H * 2,
-                                static_cast<int64_t>(H) * I * 2, io->gate_up_slots, io->down_slots, counters + 3))
-            return rc;
-    }
+    auto stage_banks = [&](int bank0, int banks, cudaStream_t st) -> int {
+        if (packed_host)
+            return launch_stage_row_codec(io->host_descriptors, stage_list, stage_count, E, max_groups,
+                                          io->gate_up_slots, io->down_slots, static_cast<int64_t>(2) * I * H * 2,
+                                          static_cast<int64_t>(H) * I * 2, counters + 2, st, stage_slot, bank0, banks);
+        return launch_pdl(stage_experts_kernel, dim3(64, banks, max_groups), dim3(256), 0, st, "stage_experts_kernel",
+                          stage_list, stage_count, stage_slot, io->host_gate_up, io->host_down, gu_stride, dn_stride,
+                          static_cast<int64_t>(2) * I * H * 2, static_cast<int64_t>(H) * I * 2, io->gate_up_slots,
+                          io->down_slots, counters + 3, bank0);
+    };
+    // Host-resident experts on the grouped path: the gate/up banks cross the
+    // host link first on the caller's stream; the down banks follow on the
+    // library's side stream while the grouped kernel runs phase 1 (gate/up,
+    // which reads no down bank), and phases 2-3 wait for them.  The link stays
+    // busy throughout and the gate/up products leave the critical path.
+    const bool split = staged && !gemv;
+    SideFork fork;
     if (staged) {
+        if (split) {
+            if (int rc = fork.begin(s)) return rc;
+            if (int rc = stage_banks(0, 1, s)) return rc;
+            if (int rc = fork.to_side(s)) return rc;
+            if (int rc = stage_banks(1, 1, fork.side)) return rc;
+            if (int rc = mark_on(3, fork.side)) return rc;  // both banks staged
+            if (int rc = fork.side_done()) return rc;
+        } else {
+            if (int rc = stage_banks(0, 2, s)) return rc;
+            if (int rc = mark(3)) return rc;
+        }
         gu_base = io->gate_up_slots;
         dn_base = io->down_slots;
         gu_str = static_cast<int64_t>(2) * I * H;
         dn_str = static_cast<int64_t>(H) * I;
+    } else if (int rc = mark(3)) {
+        return rc;
     }
-    if (int rc = mark(3)) return rc;
     uint16_t *xs = at<uint16_t>(ws, L.xs), *act = at<uint16_t>(ws, L.act), *y = at<uint16_t>(ws, L.y);
     // At decode widths the grouped kernel gathers the token rows itself (its
     // epilogue warps are idle while the first weight tiles stream in).
@@ -504,7 +568,14 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
     GL.ks = ks;
     GL.ctas = sm_count();
     GL.pairs = pairs;
+    GL.phases = split ? 1 : 3;
     if (int rc = launch_grouped(GL, s)) return rc;
+    if (split) {
+        if (int rc = fork.join(s)) return rc;  // the down banks are in their slots
+        GL.phases = 2;
+        GL.gather_x = 0;  // phase 1 gathered the token rows
+        if (int rc = launch_grouped(GL, s)) return rc;
+    }
     if (int rc = mark(5)) return rc;
     if (!fused_combine && !rows_mode) {
         if (int rc = launch_combine(y, route_pos, scores, tokens, K, H, shared ? y + static_cast<size_t>(R) * H : nullptr,

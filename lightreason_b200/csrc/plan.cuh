@@ -82,6 +82,7 @@ __device__ __forceinline__ void plan_block(const PlanArgs &a, int *scratch) {
         a.plan->done2_total = 0;
         a.plan->xs_ready = 0;
         a.plan->act_ready = 0;
+        a.plan->work2 = 0;
     }
     __syncthreads();
 }
@@ -187,6 +188,7 @@ __device__ void route_plan_block(IdxOf idx_of, int tokens, int top_k, int expert
         a.plan->done2_total = 0;
         a.plan->xs_ready = 0;
         a.plan->act_ready = 0;
+        a.plan->work2 = 0;
     }
     if (a.shared)
         for (int t = threadIdx.x; t < a.tokens; t += blockDim.x) a.route_token[a.routes + t] = t;
