@@ -80,7 +80,7 @@ constexpr int kSmemGroups = 257;         // plans up to this many groups are sta
 // 256 product and half of its token tile, so a token tile feeds 512 weight
 // rows per load and every CTA reads fewer operand bytes per FLOP from shared
 // memory, the limit of the single-CTA tile at prefill widths.
-template <int BN, bool PAIR = false>
+template <int BN, bool PAIR = false, bool TOKM = false>
 struct GroupedShape {
     static constexpr int kBRows = PAIR ? BN / 2 : BN;  // token rows of a tile held by one CTA
     static constexpr int kBTile = kBRows * kBK * 2 < 1024 ? 1024 : kBRows * kBK * 2;
@@ -91,7 +91,11 @@ struct GroupedShape {
     static constexpr int kBufs = 4 * BN <= 512 ? 2 : 1;
     static constexpr int kTmemCols = 2 * BN * kBufs < 32 ? 32 : 2 * BN * kBufs;
     static constexpr int kPlanBytes = 2 * (kSmemGroups + 1) * 4 + kSmemGroups * 16;
-    static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 512 /*barriers*/ + kPlanBytes;
+    // tokens-as-M in address-table mode: 4 KB per epilogue warp to turn its
+    // 32 rows x 64 columns into 128-byte row segments for the stores into the
+    // senders' memory
+    static constexpr int kEpiBytes = TOKM ? 4 * 4096 : 0;
+    static constexpr int kSmem = kStages * kStage + 1024 /*align*/ + 512 /*barriers*/ + kPlanBytes + kEpiBytes;
 };
 
 struct GroupedSmemTail {
@@ -337,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_x16,
                           const __grid_constant__ CUtensorMap tm_act16, const GroupedParams P) {
     static_assert(!TOKM || (BN == 128 && !PAIR), "tokens-as-M runs single CTAs on 128-token tiles");
-    using S = GroupedShape<BN, PAIR>;
+    using S = GroupedShape<BN, PAIR, TOKM>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     GroupedSmemTail *tail = reinterpret_cast<GroupedSmemTail *>(smem + S::kStages * S::kStage);
@@ -804,11 +808,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 o[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                             }
                         }
+                    } else if (P.dst_rows) {
+                        // address tables: the rows go to the senders' memory
+                        // over NVLink; 64 columns of the warp's 32 rows pass
+                        // through shared memory so that eight lanes store one
+                        // row's 128 contiguous bytes (one lane per row would
+                        // send 32 separate 16-byte pieces per instruction)
+                        uint8_t *stg = smem + S::kStages * S::kStage + 512 + S::kPlanBytes + (warp - 2) * 4096;
+                        const int64_t mine = valid ? P.dst_rows[p0 + tk] : 0;
+#pragma unroll 1
+                        for (int c0 = 0; c0 < 2 * kBM; c0 += 64) {
+#pragma unroll
+                            for (int sub = 0; sub < 4; ++sub) {
+                                float v[16];
+                                __syncwarp();
+                                sm100::tmem_ld16(t_gate + c0 + sub * 16, v);
+                                sm100::tmem_wait_ld();
+                                uint32_t pk[8];
+#pragma unroll
+                                for (int j = 0; j < 8; ++j)
+                                    pk[j] = static_cast<uint32_t>(f2bf(v[2 * j])) |
+                                            (static_cast<uint32_t>(f2bf(v[2 * j + 1])) << 16);
+                                // piece p of row r at slot p ^ (r & 7): the lanes'
+                                // writes spread over the banks
+                                uint8_t *row = stg + lane * 128;
+                                const int p0s = 2 * sub, sw = lane & 7;
+                                *reinterpret_cast<uint4 *>(row + ((p0s ^ sw) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                                *reinterpret_cast<uint4 *>(row + (((p0s + 1) ^ sw) << 4)) =
+                                    make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                            }
+                            __syncwarp();
+#pragma unroll
+                            for (int it = 0; it < 8; ++it) {
+                                const int r = it * 4 + (lane >> 3), seg = lane & 7;  // row of the warp, 16-byte piece
+                                const int64_t rowp = __shfl_sync(0xffffffffu, mine, r);
+                                const uint4 val = *reinterpret_cast<const uint4 *>(stg + r * 128 + ((seg ^ (r & 7)) << 4));
+                                if (q * 32 + r < nvalid)
+                                    reinterpret_cast<uint4 *>(reinterpret_cast<uint16_t *>(rowp) + ip.mb * 2 * kBM +
+                                                              c0)[seg] = val;
+                            }
+                            __syncwarp();
+                        }
                     } else {
                         uint16_t *dst = nullptr;  // this token's output row
                         if (valid) {
-                            if (P.dst_rows) dst = reinterpret_cast<uint16_t *>(P.dst_rows[p0 + tk]);
-                            else if (P.rows_out) dst = P.rows_out + static_cast<size_t>(P.route_token[p0 + tk]) * P.hidden;
+                            if (P.rows_out) dst = P.rows_out + static_cast<size_t>(P.route_token[p0 + tk]) * P.hidden;
                             else dst = P.y + static_cast<size_t>(p0 + tk) * P.hidden;
                             dst += ip.mb * 2 * kBM;
                         }
@@ -1116,7 +1160,7 @@ namespace {
 
 template <int BN, bool PAIR, bool TOKM = false>
 int launch_bn(const GroupedLaunch &L, cudaStream_t stream) {
-    using S = GroupedShape<BN, PAIR>;
+    using S = GroupedShape<BN, PAIR, TOKM>;
     CUtensorMap gu{}, dn{}, sg{}, su{}, sd{}, xm{}, am{}, xm16{}, am16{};
     const uint64_t H = L.hidden, I = L.inner, rows = static_cast<uint64_t>(L.rows);
     {
