@@ -689,6 +689,59 @@ def run_layer(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None)
     return rec
 
 
+def run_decode_widths(args, dev, widths=(2, 4, 8)) -> dict:
+    """The decode widths between configs[0] (T = 1) and configs[1] (T = 16):
+    the same layer (configs[0]/[1] weights, experts in HBM), each width timed
+    as those are (one CUDA-graph replay per step, L2 flushed between steps),
+    with the whole layer's bytes over the step time and the expert kernel's
+    algorithmic bytes over its own event-bracketed time."""
+    from lightreason_b200 import native
+
+    pk = peaks()
+    cfg = CONFIGS[0]
+    w, gu, dn = host_layer(cfg["seed"], cfg["bias"])
+    d = lambda a: to_dev(a, dev)  # noqa: E731
+    layer = native.Layer(router=d(w.router), gate_up=d(gu), down=d(dn), bias=torch.from_numpy(w.bias).to(dev),
+                         shared_gate=d(w.sh_gate), shared_up=d(w.sh_up), shared_down=d(w.sh_down),
+                         shared_gate_w=d(w.sh_gate_w))
+    flush = l2_flusher(dev)
+    out = {}
+    for tokens in widths:
+        xs = [d(S.hidden_states(cfg["seed"], tokens, step=i)) for i in range(POOL)]
+        y = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=dev)
+        idx = [torch.empty((tokens, TOP_K), dtype=torch.int64, device=dev) for _ in range(POOL)]
+
+        def step(i, ev):
+            layer(xs[i % POOL], out=y, idx_out=idx[i % POOL], stage_events=ev)
+
+        for i in range(args.warmup):
+            step(i, None)
+        ms, _, _ = timed_steps(step, args.steps, args.warmup, flush, 1)
+        _, krows, _ = timed_steps(step, args.steps, args.warmup, flush, 1, n_events=8, event_slots=(4, 5))
+        kernel_ms = between(krows, 4, 5)
+        used = [(args.warmup + i) % POOL for i in range(args.steps)]
+        u = [len(set(idx[j].cpu().numpy().reshape(-1).tolist())) for j in used]
+        kb = statistics.mean(layer_algo(tokens, x)[0] for x in u)
+        layer_gbs = statistics.mean(layer_bytes(tokens, x) / (m / 1e3) / 1e9 for x, m in zip(u, ms))
+        kernel_gbs = kb / (statistics.mean(kernel_ms) / 1e3) / 1e9
+        out[f"T{tokens}"] = {
+            "tokens": tokens, "us_per_step": round(1e3 * statistics.mean(ms), 2),
+            "value": round(tokens / (statistics.mean(ms) / 1e3), 2), "unit": "tokens/s",
+            "distinct_experts_per_step": round(float(np.mean(u)), 2),
+            "expert_kernel": ("fused_decode_kernel" if tokens <= FUSED_DECODE_MAX_TOKENS else
+                              "swiglu_grouped_kernel (" + grouped_mode(tokens) + ")"),
+            "expert_kernel_us": round(1e3 * statistics.mean(kernel_ms), 2),
+            "expert_kernel_hbm_frac": round(kernel_gbs / pk["hbm"], 4),
+            "layer_gbs": round(layer_gbs, 1), "layer_hbm_frac": round(layer_gbs / pk["hbm"], 4),
+            "gpu_launches": launches_per_step(tokens) * args.steps,
+        }
+    del layer
+    return {"workload": "one MoE layer at the decode widths between configs[0] (T=1) and configs[1] (T=16), "
+                        "experts in HBM, seeded as configs[0]",
+            "peak_hbm_gbs": pk["hbm"], "l2": "flushed between timed steps by reading a 256 MiB buffer",
+            "widths": out}
+
+
 # -------------------------------------------------------------- config 2 ---
 
 def run_stack(args, cfg, dev, *, with_cpu=True, cpu_steps=None, cpu_warmup=None) -> dict:
@@ -1129,6 +1182,10 @@ def run_subconfigs(args, dev) -> dict:
             out[key] = rec
         torch.cuda.empty_cache()
         log(f"[bench] {key} {time.perf_counter() - t:.1f}s")
+    t = time.perf_counter()
+    out["decode_widths"] = run_decode_widths(args, dev)
+    torch.cuda.empty_cache()
+    log(f"[bench] decode widths {time.perf_counter() - t:.1f}s")
     t = time.perf_counter()
     out["config2"] = run_stack(args, CONFIGS[2], dev, **cpu)
     torch.cuda.empty_cache()
