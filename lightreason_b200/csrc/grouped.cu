@@ -1304,7 +1304,20 @@ bool grouped_pairs_for(int bn, int ks, int inner, int hidden) {
 }
 
 int grouped_bn_for(int tokens) { return tokens <= 16 ? 16 : tokens <= 64 ? 32 : tokens <= 512 ? 64 : 128; }
-int grouped_ks_for(int tokens) { return tokens <= 4 ? 4 : tokens <= 8 ? 2 : 1; }
+// K splits of the phase-1 items at the narrowest grouped widths, so that
+// more SMs stream weights while few experts are active: two up to 4 tokens,
+// none from 5 (one box, grouped-kernel step at T = 4 / 8 / 16 with 1, 2 or 4
+// splits: 66.5 / 62.0 / 64.0, 76.1 / 79.1 / 81.0 and 99.6 / 109.2 / 110.4 us;
+// the FP32 partials and their last-split sum cost more than the extra SMs
+// gain from T = 5 on).  LRB_GROUPED_KS=1, 2 or 4 (read at every call)
+// overrides the choice for 3 to 16 tokens, for measurement.
+int grouped_ks_for(int tokens) {
+    if (tokens > 2 && tokens <= 16) {
+        const char *v = getenv("LRB_GROUPED_KS");
+        if (v && (v[0] == '1' || v[0] == '2' || v[0] == '4') && v[1] == 0) return v[0] - '0';
+    }
+    return tokens <= 4 ? 2 : 1;
+}
 
 // Upper bound of phase-1 tiles times splits times 2 * BN * 128 floats.
 size_t grouped_part_floats(int tokens, int experts, int top_k, int inner) {
