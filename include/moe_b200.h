@@ -14,6 +14,11 @@
  *     failure (RuntimeError, as edge35b/native_bf16_gather.py:25-29 _checked),
  *     MOE_EARCH when the device is not sm_100; moe_last_error() describes the
  *     last failure on the calling thread;
+ *   - an empty batch (tokens == 0) is a no-op for the router, permute, layer,
+ *     combine and shared-expert entry points, as it is for the eager module:
+ *     their per-token arrays may then be NULL (shapes are still checked; the
+ *     permute still writes zero offsets and num_active); the expert-parallel
+ *     step needs at least one token per rank;
  *   - no entry point allocates device memory unless its comment says so.
  *     Scratch lives in a caller-owned workspace sized by a *_workspace_bytes
  *     query; entry points that read routing counts do so on the device, so a

@@ -294,9 +294,10 @@ extern "C" {
 
 int moe_combine(const uint16_t *y, const int32_t *route_pos, const uint16_t *scores, const uint16_t *shared_rows,
                 const uint16_t *sig, int tokens, int top_k, int hidden, uint16_t *out, void *stream) {
-    LRB_REQUIRE(y && route_pos && scores && out && (!shared_rows || sig), "moe_combine: null pointer");
+    LRB_REQUIRE(tokens == 0 || (y && route_pos && scores && out && (!shared_rows || sig)), "moe_combine: null pointer");
     LRB_REQUIRE(hidden > 0 && hidden % 8 == 0 && tokens >= 0 && top_k >= 1 && top_k <= 16,
                 "moe_combine: bad shape");
+    if (tokens == 0) return MOE_OK;
     if (int rc = lrb::require_sm100()) return rc;
     return lrb::launch_combine(y, route_pos, scores, tokens, top_k, hidden, shared_rows, sig, out,
                                lrb::as_stream(stream));
@@ -309,7 +310,7 @@ size_t moe_shared_expert_workspace_bytes(int tokens, int inner) {
 int moe_shared_expert(const uint16_t *x, const uint16_t *gate, const uint16_t *up, const uint16_t *down,
                       const uint16_t *gate_w, int tokens, int hidden, int inner, uint16_t *out, uint16_t *sig,
                       void *workspace, size_t workspace_bytes, void *stream) {
-    LRB_REQUIRE(x && gate && up && down && out && (!gate_w || sig), "moe_shared_expert: null pointer");
+    LRB_REQUIRE(gate && up && down && (tokens == 0 || (x && out && (!gate_w || sig))), "moe_shared_expert: null pointer");
     LRB_REQUIRE(tokens >= 0 && tokens <= lrb::kMaxParamGroups, "moe_shared_expert: tokens %d outside [0, %d]", tokens,
                 lrb::kMaxParamGroups);
     LRB_REQUIRE((hidden == 1024 || hidden == 2048 || hidden == 4096) && (inner == 256 || inner == 512 || inner == 1024),

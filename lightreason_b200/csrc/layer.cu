@@ -282,7 +282,8 @@ size_t moe_layer_workspace_bytes(int tokens, int experts, int top_k, int hidden,
 int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens, uint16_t *out,
                       const moe_layer_io *io, void *workspace, size_t workspace_bytes, void *stream) {
     using namespace lrb;
-    LRB_REQUIRE(w && x && out, "moe_layer_forward: weights, x and out are required");
+    // an empty batch is a no-op: x, out and the workspace may then be NULL
+    LRB_REQUIRE(w && (tokens == 0 || (x && out)), "moe_layer_forward: weights, x and out are required");
     const moe_layer_io none{};
     if (!io) io = &none;
     const int E = w->experts, H = w->hidden, I = w->inner, K = w->top_k;
@@ -320,10 +321,10 @@ int moe_layer_forward(const moe_layer_weights *w, const uint16_t *x, int tokens,
                     a16(io->host_down) && a16(io->gate_up_slots) && a16(io->down_slots) && gu_stride % 8 == 0 &&
                     dn_stride % 8 == 0,
                 "moe_layer_forward: row pointers must be 16-byte aligned and expert strides multiples of 8");
+    if (tokens == 0) return MOE_OK;
     const Layout L = layout(tokens, E, K, H, I);
     LRB_REQUIRE(workspace && workspace_bytes >= L.total, "moe_layer_forward: workspace %zu < %zu bytes",
                 workspace_bytes, L.total);
-    if (tokens == 0) return MOE_OK;
     if (int rc = require_sm100()) return rc;
     cudaStream_t s = as_stream(stream);
     // Under stream capture an ordinary record is only a dependency node; an

@@ -246,7 +246,9 @@ extern "C" int moe_permute(const int64_t *idx, int tokens, int top_k, int expert
     LRB_REQUIRE(experts >= 1 && experts <= 1024, "moe_permute: experts %d outside [1, 1024]", experts);
     LRB_REQUIRE(top_k >= 1 && tokens >= 0, "moe_permute: bad tokens %d / top_k %d", tokens, top_k);
     LRB_REQUIRE(static_cast<int64_t>(tokens) * top_k < (1 << 30), "moe_permute: too many routes");
-    LRB_REQUIRE(idx && offsets && perm_token && perm_slot && route_pos && active && num_active,
+    // an empty batch still writes offsets (zeros) and num_active (0); its
+    // per-route arrays may be NULL
+    LRB_REQUIRE(offsets && active && num_active && (tokens == 0 || (idx && perm_token && perm_slot && route_pos)),
                 "moe_permute: null output");
     if (int rc = lrb::require_sm100()) return rc;
     if (tokens == 0) {

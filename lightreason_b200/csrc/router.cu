@@ -326,7 +326,8 @@ int moe_router_topk(const uint16_t *x, const uint16_t *router, const float *bias
                     int tokens, int hidden, int experts, int top_k, uint16_t *logits, int64_t *idx,
                     float *scores_f32, uint16_t *scores_bf16, uint16_t *sig, void *stream) {
     if (int rc = lrb::check_router_args(tokens, hidden, experts, top_k)) return rc;
-    LRB_REQUIRE(x && router && logits && idx, "moe_router_topk: x, router, logits and idx are required");
+    LRB_REQUIRE(router && (tokens == 0 || (x && logits && idx)),
+                "moe_router_topk: x, router, logits and idx are required");
     LRB_REQUIRE(!shared_gate_w || sig, "moe_router_topk: shared_gate_w needs a sig output");
     if (tokens == 0) return MOE_OK;
     if (int rc = lrb::require_sm100()) return rc;
@@ -372,7 +373,7 @@ int moe_router_topk_ws(const uint16_t *x, const uint16_t *router, const float *b
 int moe_router_select(const uint16_t *logits, const float *bias, int tokens, int experts, int top_k, int64_t *idx,
                       float *scores_f32, uint16_t *scores_bf16, void *stream) {
     if (int rc = lrb::check_router_args(tokens, 2048, experts, top_k)) return rc;
-    LRB_REQUIRE(logits && idx, "moe_router_select: logits and idx are required");
+    LRB_REQUIRE(tokens == 0 || (logits && idx), "moe_router_select: logits and idx are required");
     if (tokens == 0) return MOE_OK;
     if (int rc = lrb::require_sm100()) return rc;
     return lrb::launch_router_select(logits, bias, tokens, experts, top_k, idx, scores_f32, scores_bf16,

@@ -94,3 +94,27 @@ def test_layer_rejects_misaligned_rows_before_device_use(so):
                    dict(gate_up_stride=2 * 512 * 2048 + 4)):
         assert call(**kwargs) == native.MOE_EINVAL, kwargs
         assert b"16-byte aligned" in so.moe_last_error(), kwargs
+
+
+def test_empty_batch_is_a_no_op_before_device_use(so):
+    """tokens == 0 is an empty batch, as the eager module takes it: the
+    router, permute checks, layer, combine and shared-expert entry points
+    return MOE_OK with NULL per-token arrays (an empty CUDA tensor's data
+    pointer) and touch no device, while a bad shape in an empty batch is
+    still an argument error."""
+    good = ctypes.c_void_p(1 << 20)
+    w = native.LayerWeights(router=1 << 20, gate_up=1 << 20, down=1 << 20, experts=256, hidden=2048, inner=512,
+                            top_k=8)
+    assert so.moe_layer_forward(ctypes.byref(w), None, 0, None, None, None, 0, None) == native.MOE_OK
+    bad = native.LayerWeights(router=1 << 20, gate_up=1 << 20, down=1 << 20, experts=256, hidden=2048, inner=384,
+                              top_k=8)
+    assert so.moe_layer_forward(ctypes.byref(bad), None, 0, None, None, None, 0, None) == native.MOE_EINVAL
+    assert so.moe_router_topk(None, good, None, None, 0, 2048, 256, 8, None, None, None, None, None,
+                              None) == native.MOE_OK
+    assert so.moe_router_topk(None, good, None, None, 0, 3000, 256, 8, None, None, None, None, None,
+                              None) == native.MOE_EINVAL
+    assert so.moe_router_select(None, None, 0, 256, 8, None, None, None, None) == native.MOE_OK
+    assert so.moe_combine(None, None, None, None, None, 0, 8, 2048, None, None) == native.MOE_OK
+    assert so.moe_combine(None, None, None, None, None, 0, 8, 2047, None, None) == native.MOE_EINVAL
+    assert so.moe_shared_expert(None, good, good, good, None, 0, 2048, 512, None, None, None, 0,
+                                None) == native.MOE_OK

@@ -320,6 +320,33 @@ def test_route_in_is_the_experts_forward(dev, case13):
     assert_close(bits(out), want, what="experts forward")
 
 
+def test_empty_batch(dev, case13):
+    """An empty batch (T = 0), as the eager module takes it: the whole block
+    (router and shared expert), the experts forward with given routes, the
+    permute (zero offsets, no active expert) and the combine return empty
+    results of the right shapes without error, and the next call of the same
+    layer still matches the oracle."""
+    x = torch.empty((0, 2048), dtype=torch.bfloat16, device=dev)
+    assert tuple(case13.layer(x).shape) == (0, 2048)
+    idx = torch.empty((0, 8), dtype=torch.int64, device=dev)
+    wts = torch.empty((0, 8), dtype=torch.bfloat16, device=dev)
+    assert tuple(case13.layer(x, route_in=idx, weights_in=wts).shape) == (0, 2048)
+    for wide in (False, True):
+        offsets, _, _, rpos, _, n_active, bad = native.permute(idx, 256, wide=wide)
+        torch.cuda.synchronize()
+        assert offsets.cpu().numpy().tolist() == [0] * 257 and int(n_active.item()) == 0 and int(bad.item()) == 0
+        assert tuple(rpos.shape) == (0, 8)
+    y = torch.empty((0, 2048), dtype=torch.bfloat16, device=dev)
+    assert tuple(native.combine(y, rpos, wts).shape) == (0, 2048)
+    torch.cuda.synchronize()
+    xb = S.hidden_states(990, 3)
+    out, idx3, _, _ = case13.run(xb)
+    w_out, w_idx, _, w_lg = case13.oracle(xb)
+    compare_ids(idx3, w_idx, S.bf16_bits_to_f32(w_lg) + case13.w.bias, slack_ulps=1.0, case="after an empty batch")
+    same = np.all(idx3 == w_idx, axis=1)
+    assert_close(out[same], w_out[same], what="layer after an empty batch")
+
+
 def oracle_with_routes(w, x_bits, idx, scores):
     """The oracle's expert path, combine and shared expert for given routes
     (ids and BF16 scores), for tokens whose selection the GPU decided through
